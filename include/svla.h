@@ -1,0 +1,219 @@
+/*
+ * svla.h -- C ABI of libsvla.so, the sm_100a kernels of the quantized SmolVLA sample_actions path.
+ *
+ * Conventions (same status codes as the reference's launch helpers,
+ * deploy/cuda/fused_rope_layout.cu:566-570):
+ *   return 0 = success, 1 = bad argument / shape / alignment, 2 = CUDA launch or runtime error.
+ *   svla_last_error() returns a message for the last nonzero status of the calling thread.
+ * Every entry point is stream-ordered (no host synchronisation) and allocates no memory: all buffers,
+ * including scratch ("workspace"), are passed in by the caller, like the TensorRT plugin enqueue it
+ * replaces (deploy/cuda/smoothquant_qkv_plugin_serialized_smoke.cu:346-402).  All pointers are device
+ * pointers unless stated otherwise.  Tensors are row-major; "ld" values are row strides in elements.
+ * bf16 tensors are passed as void* (IEEE bfloat16 bit patterns).
+ */
+#ifndef SVLA_H_
+#define SVLA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* svla_stream_t; /* == cudaStream_t */
+
+#define SVLA_OK 0
+#define SVLA_ERR_ARG 1
+#define SVLA_ERR_CUDA 2
+
+/* operand kinds of svla_gemm */
+#define SVLA_KIND_I8 0    /* int8 x int8 -> int32 (SmoothQuant W8A8) */
+#define SVLA_KIND_BF16 1  /* bf16 x bf16 -> fp32 */
+#define SVLA_KIND_W8A16 2 /* bf16 activations x int8 weights dequantised to bf16(q * w_s) in shared memory */
+
+/* epilogues of svla_gemm (v = acc * a * w_s[n] + b[n] for I8, acc + b[n] otherwise) */
+#define SVLA_EPI_BF16 0      /* out = bf16(v) [then bf16(out * post_scale)] */
+#define SVLA_EPI_I32 1       /* out = raw int32 accumulators (I8 only) */
+#define SVLA_EPI_ROPE 2      /* out = bf16(rotate_half_rope(bf16(v), pos[m])) on segments with rope = 1 */
+#define SVLA_EPI_RESID 3     /* out = bf16(bf16(v) + resid) */
+#define SVLA_EPI_SILU_MUL 4  /* pair: out = bf16(bf16(silu(bf16(v_gate))) * bf16(v_up)) */
+#define SVLA_EPI_GELU_QUANT 5 /* g = bf16(gelu_tanh(bf16(v))); qout = round((g / q_smooth[n]) / q_act) */
+#define SVLA_EPI_EULER 6     /* x_t[m, n] += dt * v (fp32), x_t_bf16 = bf16(x_t) */
+#define SVLA_EPI_SILU 7      /* out = bf16(silu(bf16(v))) */
+#define SVLA_EPI_F32 8       /* out = v in fp32 */
+
+/* -------------------------------------------------------------------------------------------------
+ * Library
+ * ------------------------------------------------------------------------------------------------*/
+const char* svla_last_error(void);
+/* Version string of the build (compile flags and arch). */
+const char* svla_version(void);
+/* Reads (and with reset != 0 clears) the device error word that bounded waits and bounds checks
+ * write (0 = none).  Synchronises the current device. */
+int32_t svla_device_error(int32_t* code, int32_t reset);
+
+/* -------------------------------------------------------------------------------------------------
+ * SmoothQuant primitives
+ * ------------------------------------------------------------------------------------------------*/
+
+/* Per-output-channel int8 weight packing with optional SmoothQuant fold; replaces
+ * W8A8Linear.__init__ / quantize_weight_per_out_channel (deploy/linear_only_quant.py:43-54, :140-144):
+ * W' = W * smooth[None, :];  wscale[n] = max(max_k |W'[n,k]|, 1e-8) / 127;
+ * qweight = round(W' / wscale[n]).clamp(-127, 127).  weight bf16 [N, K]; smooth fp32 [K] or NULL. */
+int32_t svla_pack_weight_i8(const void* weight, const float* smooth, int32_t n, int32_t k, int8_t* qweight,
+                            float* wscale, svla_stream_t stream);
+
+/* SmoothQuant activation quantisation; replaces smoothQuantActivationKernel
+ * (deploy/cuda/smoothquant_linear_epilogue.cu:108-119) with bf16 input:
+ * q[m,k] = round((x[m,k] / smooth[k]) / act_scale).clamp(-128, 127).  K % 8 == 0. */
+int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, float act_scale, int8_t* q,
+                             int32_t ldq, int32_t m, int32_t k, svla_stream_t stream);
+
+/* int8 x int8 -> int32 GEMM acc[m,n] = sum_k qx[m,k] * qw[n,k]; replaces int8GemmInt32Kernel
+ * (deploy/cuda/smoothquant_linear_epilogue.cu:121-137) and the cuBLASLt CUBLAS_COMPUTE_32I call
+ * (deploy/cuda/smoothquant_linear_cublaslt.cu:230-306).  tcgen05 kind::i8. */
+int32_t svla_gemm_i8_i32(const int8_t* qx, const int8_t* qw, int32_t m, int32_t n, int32_t k, int32_t* acc,
+                         svla_stream_t stream);
+
+/* Scratch bytes svla_sq_linear_w8a8 needs for (m, k). */
+size_t svla_sq_linear_w8a8_workspace_size(int32_t m, int32_t k);
+
+/* SmoothQuant W8A8 linear, quantise + tcgen05 int8 GEMM + fused dequant/bias epilogue; replaces the
+ * quantize -> int8GemmFusedEpilogueKernel pipeline (deploy/cuda/smoothquant_linear_epilogue.cu:108-168)
+ * and W8A8Linear.forward (deploy/linear_only_quant.py:104-116):
+ * y[m,n] = bf16((acc[m,n] * act_scale) * wscale[n] + bias[n]),  x / y bf16, bias bf16 or NULL.
+ * workspace >= svla_sq_linear_w8a8_workspace_size(m, k) bytes, 256-byte aligned. */
+int32_t svla_sq_linear_w8a8(const void* x, const float* smooth, float act_scale, const int8_t* qweight,
+                            const float* wscale, const void* bias, int32_t m, int32_t n, int32_t k, void* y,
+                            void* workspace, size_t workspace_bytes, svla_stream_t stream);
+
+/* W8A16 linear; replaces W8A16Linear.forward (deploy/linear_only_quant.py:119-137):
+ * y = bf16(x @ bf16(qweight * wscale[:,None])^T + bias). */
+int32_t svla_w8a16_linear(const void* x, const int8_t* qweight, const float* wscale, const void* bias, int32_t m,
+                          int32_t n, int32_t k, void* y, svla_stream_t stream);
+
+/* -------------------------------------------------------------------------------------------------
+ * General fused GEMM (the launch the sample_actions runner uses for every linear)
+ * ------------------------------------------------------------------------------------------------*/
+typedef struct svla_gemm_seg {
+  const void* a;          /* A operand [M, lda]: int8 (I8) or bf16 */
+  int32_t lda;
+  const void* b;          /* weights [n, ldb]: int8 (I8, W8A16) or bf16 (BF16) */
+  int32_t ldb;
+  const float* wscale;    /* [n] per-output-channel weight scale (I8, W8A16) */
+  const void* bias;       /* bf16 [n] or NULL */
+  const float* bias_f32;  /* fp32 [n] or NULL, added after bias */
+  void* out;              /* output [M, ldo] (bf16, int32 or fp32 by epilogue) */
+  int32_t ldo;
+  int32_t n;              /* columns, multiple of 16 */
+  float act_scale;        /* I8: activation scale a */
+  int32_t rope;           /* EPI_ROPE: rotate this segment (n % 64 == 0) */
+} svla_gemm_seg;
+
+typedef struct svla_gemm_desc {
+  int32_t kind, epi;
+  int32_t m, k;
+  int32_t nseg;           /* 1..3 segments sharing M and K, each with its own A and weights */
+  int32_t pair;           /* 1: seg[0] (gate) and seg[1] (up) form one SILU_MUL tile pair */
+  svla_gemm_seg seg[3];
+  int32_t block_n;        /* 64 or 128; 0 = choose */
+  /* output row remap: row = (m / rows_per_group) * group_stride + m % rows_per_group + row_offset */
+  int32_t rows_per_group, group_stride, row_offset;
+  float post_scale;       /* EPI_BF16: 0 = off */
+  const void* resid;      /* EPI_RESID: bf16 residual, may alias seg[0].out */
+  int32_t ldr, resid_rows; /* resid_rows > 0: residual row = m % resid_rows */
+  const float* rope_cs;   /* EPI_ROPE: [max_pos][32] float2 (cos, sin) */
+  const int32_t* pos;     /* EPI_ROPE: [M] */
+  int32_t max_pos;
+  const float* q_smooth;  /* EPI_GELU_QUANT */
+  float q_act;
+  int8_t* qout;
+  int32_t ldq;
+  float dt;               /* EPI_EULER */
+  float* xt;
+  void* xt_bf16;
+} svla_gemm_desc;
+
+int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream);
+
+/* -------------------------------------------------------------------------------------------------
+ * Norm + SmoothQuant quantise (RMSNorm: SmolVLM2 text / expert; LayerNorm: SigLIP).  One launch emits the
+ * bf16 normalised rows and up to three int8 tensors, each with its own smooth vector and activation
+ * scale (per-projection SmoothQuant of q/k/v, deploy/cuda/smoothquant_qkv_cublaslt.cu:245-247).
+ * ------------------------------------------------------------------------------------------------*/
+typedef struct svla_norm_desc {
+  const void* x; int32_t ldx;
+  const void* weight;     /* bf16 [K] */
+  const void* bias;       /* bf16 [K] (LayerNorm) or NULL */
+  float eps;
+  int32_t layernorm;      /* 0 = RMSNorm, 1 = LayerNorm */
+  int32_t m, k;
+  void* y; int32_t ldy;   /* bf16 output or NULL */
+  int32_t nq;
+  int8_t* q[3];
+  int32_t ldq;
+  const float* smooth[3];
+  float act[3];
+  int32_t pixel_shuffle;  /* 0, or the SmolVLM connector shuffle factor (int8 outputs only) */
+  int32_t ps_grid;        /* tokens per side of the input grid */
+} svla_norm_desc;
+
+int32_t svla_norm_quant(const svla_norm_desc* desc, svla_stream_t stream);
+
+/* -------------------------------------------------------------------------------------------------
+ * Attention; replaces the fused RoPE attention plugins (deploy/cuda/fused_rope_layout.h:44-50,
+ * fused_rope_layout.cu:271-543) for post-RoPE q/k (RoPE is fused into the QKV GEMM epilogue).
+ * Masked GQA, head_dim 64; keys from one or two sources (cached prefix, then current suffix).
+ * ------------------------------------------------------------------------------------------------*/
+typedef struct svla_attn_desc {
+  const void* q; int64_t q_bs; int32_t q_rs;
+  const void* k1; const void* v1; int64_t kv1_bs; int32_t kv1_rs; int32_t l1;
+  const void* k2; const void* v2; int64_t kv2_bs; int32_t kv2_rs; int32_t l2;
+  const uint8_t* mask; int64_t mask_bs; int32_t mask_rs; /* bool mask [B, Lq, l1 + l2] or NULL */
+  void* o; int64_t o_bs; int32_t o_rs;                   /* bf16 context or NULL */
+  int8_t* qo; int64_t qo_bs; int32_t qo_rs;              /* int8 context (next W8A8 input) or NULL */
+  const float* qo_smooth; float qo_act;
+  int32_t batch, lq, hq, hkv;
+  float scale;                                           /* 0 = head_dim^-1/2 */
+} svla_attn_desc;
+
+int32_t svla_attention(const svla_attn_desc* desc, svla_stream_t stream);
+
+/* RoPE + layout; replaces launchFusedRopeLayout (deploy/cuda/fused_rope_layout.h:32-34,
+ * fused_rope_layout.cu:81-124) for bf16 tensors and int32 positions:
+ * q_raw [B, L, Hq*64] -> q_out [B, Hq, L, 64]; k_raw [B, L, Hkv*64] -> k_out [B, Hq, 64, L]
+ * (GQA-expanded and transposed), rotate-half with theta_i = pos / max_wavelength^(2i/64). */
+int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* pos, void* q_out, void* k_out,
+                         int32_t batch, int32_t seq_len, int32_t q_heads, int32_t kv_heads,
+                         float max_wavelength, svla_stream_t stream);
+
+/* -------------------------------------------------------------------------------------------------
+ * sample_actions glue
+ * ------------------------------------------------------------------------------------------------*/
+/* cs[p][i] = (cos, sin)(p / max_wavelength^(2i/64)), p < max_pos, i < 32 */
+int32_t svla_rope_table(float* cs, int32_t max_pos, float max_wavelength, svla_stream_t stream);
+
+/* Masks and positions of one call (deploy/diagnose_3_4_numeric_baseline.py:42-46, :117-146, :171-172).
+ * img_mask0/1 bool [B], lang_mask bool [B, n_lang]; prefix length Lp = 2*n_img + n_lang + 1. */
+int32_t svla_build_masks(const uint8_t* img_mask0, const uint8_t* img_mask1, const uint8_t* lang_mask,
+                         int32_t batch, int32_t n_img, int32_t n_lang, int32_t chunk, uint8_t* prefix_mask,
+                         int32_t* prefix_pos, uint8_t* self_mask, uint8_t* cross_mask, int32_t* suffix_pos,
+                         int32_t* cross_pos, svla_stream_t stream);
+
+/* out[b*rows_per_batch + row_offset + t] = bf16(table[tokens[b,t]] * scale); tokens int64 [B, T] */
+int32_t svla_embed_tokens(const int64_t* tokens, int32_t batch, int32_t t, const void* table, int32_t vocab,
+                          int32_t hidden, float scale, void* out, int32_t rows_per_batch, int32_t row_offset,
+                          svla_stream_t stream);
+
+/* images fp32 [N, C, S, S] -> bf16 patches [N*(S/P)^2, C*P*P] in Conv2d (c, kh, kw) order */
+int32_t svla_im2col(const float* images, int32_t n, int32_t c, int32_t s, int32_t p, void* out,
+                    svla_stream_t stream);
+
+int32_t svla_f32_to_bf16(const float* x, void* y, int64_t n, svla_stream_t stream);
+int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n, svla_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SVLA_H_ */

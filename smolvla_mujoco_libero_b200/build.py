@@ -1,0 +1,61 @@
+"""Build libsvla.so in-tree with nvcc for sm_100a.
+
+    python -m smolvla_mujoco_libero_b200.build [--debug]
+
+The library lands next to this file so that it travels with the source tree.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+OUT = PKG / "libsvla.so"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [PKG.parent / "include" / "svla.h"]
+
+
+def up_to_date() -> bool:
+    if not OUT.exists():
+        return False
+    t = OUT.stat().st_mtime
+    return all(p.stat().st_mtime <= t for p in sources())
+
+
+def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Path:
+    if not force and not debug and up_to_date():
+        return OUT
+    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+           "-o", str(OUT), str(CSRC / "svla.cu")]
+    if debug:
+        cmd.insert(1, "-DSVLA_BOUNDS_CHECK")
+    if verbose:
+        cmd.append("-Xptxas=-v")
+    subprocess.run(cmd, check=True)
+    return OUT
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--debug", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, debug=a.debug, verbose=a.verbose))
+    sys.exit(0)

@@ -1,0 +1,206 @@
+// Small kernels around the GEMMs: RoPE tables, prefix / suffix masks and positions, token embedding
+// gather, SigLIP patch extraction, dtype conversions.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace svla {
+
+// cs[p][i] = (cos(p / w^(2i/64)), sin(p / w^(2i/64))), fp32 like the reference's apply_rope
+// (deploy/validate_fused_rope_layout_math.py:28-42): freq = (2/64)*i, timescale = w^freq,
+// radians = p / timescale.
+__global__ void rope_table_kernel(float2* cs, int max_pos, float max_wavelength) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= max_pos * 32) return;
+  const int p = idx / 32, i = idx % 32;
+  const float freq = __fmul_rn(2.0f / 64.0f, static_cast<float>(i));
+  const float ts = powf(max_wavelength, freq);
+  const float rad = __fdiv_rn(static_cast<float>(p), ts);
+  cs[idx] = make_float2(cosf(rad), sinf(rad));
+}
+
+// Masks and positions for one sample_actions call (deploy/diagnose_3_4_numeric_baseline.py:42-46,
+// :117-146, :171-172).  Prefix tokens: 2 x n_img image tokens, n_lang language tokens, 1 state token.
+//   pad   = [img0_mask]*n_img + [img1_mask]*n_img + lang_mask + [1]
+//   att   = 0 ... 0, 1 (state)            cum = cumsum(att)
+//   prefix_mask[q, k] = cum[k] <= cum[q] && pad[q] && pad[k]           [B, Lp, Lp]
+//   prefix_pos[i]     = cumsum(pad)[i] - 1                              [B, Lp]
+//   suffix (chunk tokens, all att = 1, all pad = 1):
+//   self_mask[q, k]   = k < Lp ? pad[k] : (k - Lp) <= q                  [B, Ls, Lp + Ls]
+//   cross_mask[q, k]  = pad[k]                                          [B, Ls, Lp]
+//   suffix_pos[i]     = sum(pad) + i;   cross_pos[i] = i
+struct MaskArgs {
+  const uint8_t* img_mask0;  // [B]
+  const uint8_t* img_mask1;  // [B]
+  const uint8_t* lang_mask;  // [B, n_lang]
+  int B, n_img, n_lang, Ls;
+  uint8_t* prefix_mask;  // [B, Lp, Lp]
+  int* prefix_pos;       // [B * Lp]
+  uint8_t* self_mask;    // [B, Ls, Lp + Ls]
+  uint8_t* cross_mask;   // [B, Ls, Lp]
+  int* suffix_pos;       // [B * Ls]
+  int* cross_pos;        // [B * Ls]
+};
+
+__device__ __forceinline__ int prefix_pad(const MaskArgs& a, int b, int i) {
+  if (i < a.n_img) return a.img_mask0[b] != 0;
+  if (i < 2 * a.n_img) return a.img_mask1[b] != 0;
+  if (i < 2 * a.n_img + a.n_lang) return a.lang_mask[b * a.n_lang + (i - 2 * a.n_img)] != 0;
+  return 1;
+}
+
+// one block per batch row
+__global__ void masks_kernel(const MaskArgs a) {
+  const int b = blockIdx.x;
+  const int Lp = 2 * a.n_img + a.n_lang + 1;
+  extern __shared__ int sh[];  // pad[Lp], cum[Lp]
+  int* pad = sh;
+  int* cum = sh + Lp;
+  for (int i = threadIdx.x; i < Lp; i += blockDim.x) {
+    pad[i] = prefix_pad(a, b, i);
+    cum[i] = (i == Lp - 1) ? 1 : 0;  // att cumsum: only the state token has att = 1
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int c = 0;
+    for (int i = 0; i < Lp; ++i) {
+      c += pad[i];
+      a.prefix_pos[b * Lp + i] = c - 1;
+    }
+    for (int i = 0; i < a.Ls; ++i) {
+      a.suffix_pos[b * a.Ls + i] = c + i;
+      a.cross_pos[b * a.Ls + i] = i;
+    }
+  }
+  for (int idx = threadIdx.x; idx < Lp * Lp; idx += blockDim.x) {
+    const int q = idx / Lp, k = idx % Lp;
+    a.prefix_mask[static_cast<size_t>(b) * Lp * Lp + idx] = (cum[k] <= cum[q]) && pad[q] && pad[k];
+  }
+  const int Lt = Lp + a.Ls;
+  for (int idx = threadIdx.x; idx < a.Ls * Lt; idx += blockDim.x) {
+    const int q = idx / Lt, k = idx % Lt;
+    a.self_mask[static_cast<size_t>(b) * a.Ls * Lt + idx] = (k < Lp) ? pad[k] : ((k - Lp) <= q);
+  }
+  for (int idx = threadIdx.x; idx < a.Ls * Lp; idx += blockDim.x) {
+    const int k = idx % Lp;
+    a.cross_mask[static_cast<size_t>(b) * a.Ls * Lp + idx] = pad[k];
+  }
+}
+
+// out[b*row_stride + row_offset + t] = bf16(float(E[tok[b, t]]) * scale) ; one warp per token, 8 per lane
+__global__ void embed_tokens_kernel(const long long* tokens, int B, int T, const __nv_bfloat16* table, int vocab,
+                                    int H, float scale, __nv_bfloat16* out, int rows_per_batch, int row_offset,
+                                    int* err) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (w >= B * T) return;
+  const int b = w / T, t = w % T;
+  long long tok = tokens[w];
+  if (tok < 0 || tok >= vocab) {
+    record_error(err, kErrBadShape);
+    tok = 0;
+  }
+  const __nv_bfloat16* src = table + static_cast<size_t>(tok) * H;
+  __nv_bfloat16* dst = out + (static_cast<size_t>(b) * rows_per_batch + row_offset + t) * H;
+  for (int k = lane * 8; k < H; k += 256) {
+    const int4 raw = *reinterpret_cast<const int4*>(src + k);
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    uint32_t pk[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      __nv_bfloat162 v = __floats2bfloat162_rn(__fmul_rn(__bfloat162float(h[2 * u]), scale),
+                                               __fmul_rn(__bfloat162float(h[2 * u + 1]), scale));
+      pk[u] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    *reinterpret_cast<int4*>(dst + k) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+  }
+}
+
+// SigLIP patch extraction: images fp32 [N, C, S, S] -> bf16 patches [N * (S/P)^2, C*P*P] in the
+// (c, kh, kw) order of a Conv2d weight [out, C, P, P] flattened.  One thread per 8 outputs (8 kw).
+__global__ void im2col_kernel(const float* img, int N, int C, int S, int P, __nv_bfloat16* out) {
+  const int G = S / P;
+  const long long total = static_cast<long long>(N) * G * G * C * P * (P / 8);
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  long long r = idx;
+  const int kw8 = static_cast<int>(r % (P / 8)); r /= (P / 8);
+  const int kh = static_cast<int>(r % P); r /= P;
+  const int c = static_cast<int>(r % C); r /= C;
+  const int px = static_cast<int>(r % G); r /= G;
+  const int py = static_cast<int>(r % G); r /= G;
+  const int n = static_cast<int>(r);
+  const float* src = img + ((static_cast<size_t>(n) * C + c) * S + (py * P + kh)) * S + px * P + kw8 * 8;
+  const float4 a0 = *reinterpret_cast<const float4*>(src);
+  const float4 a1 = *reinterpret_cast<const float4*>(src + 4);
+  uint32_t pk[4] = {0, 0, 0, 0};
+  {
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(a0.x, a0.y), h1 = __floats2bfloat162_rn(a0.z, a0.w);
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(a1.x, a1.y), h3 = __floats2bfloat162_rn(a1.z, a1.w);
+    pk[0] = *reinterpret_cast<uint32_t*>(&h0);
+    pk[1] = *reinterpret_cast<uint32_t*>(&h1);
+    pk[2] = *reinterpret_cast<uint32_t*>(&h2);
+    pk[3] = *reinterpret_cast<uint32_t*>(&h3);
+  }
+  const size_t row = (static_cast<size_t>(n) * G + py) * G + px;
+  const int col = (c * P + kh) * P + kw8 * 8;
+  *reinterpret_cast<int4*>(out + row * (C * P * P) + col) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+}
+
+__global__ void f32_to_bf16_kernel(const float* x, __nv_bfloat16* y, long long n) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// x_t = noise (fp32 copy) and its bf16 image
+__global__ void euler_init_kernel(const float* noise, float* xt, __nv_bfloat16* xt_bf16, long long n) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float v = noise[i];
+    xt[i] = v;
+    xt_bf16[i] = __float2bfloat16_rn(v);
+  }
+}
+
+}  // namespace svla
+
+namespace svla {
+
+// Plugin-semantics RoPE + layout (deploy/cuda/fused_rope_layout.cu:81-124): q_raw [B, L, Hq*64] ->
+// q_out [B, Hq, L, 64]; k_raw [B, L, Hkv*64] -> k_out [B, Hq, 64, L] with kv head j expanded to query
+// heads j*g .. j*g+g-1 (g = Hq / Hkv).  One thread per rotation pair.
+__global__ void rope_layout_kernel(const __nv_bfloat16* q_raw, const __nv_bfloat16* k_raw, const int* pos,
+                                   __nv_bfloat16* q_out, __nv_bfloat16* k_out, int B, int L, int Hq, int Hkv,
+                                   float max_wavelength) {
+  const long long nq = static_cast<long long>(B) * L * Hq * 32;
+  const long long nk = static_cast<long long>(B) * L * Hkv * 32;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= nq + nk) return;
+  const bool is_q = idx < nq;
+  long long r = is_q ? idx : idx - nq;
+  const int H = is_q ? Hq : Hkv;
+  const int i = static_cast<int>(r % 32); r /= 32;
+  const int h = static_cast<int>(r % H); r /= H;
+  const int l = static_cast<int>(r % L);
+  const int b = static_cast<int>(r / L);
+  const float freq = __fmul_rn(2.0f / 64.0f, static_cast<float>(i));
+  const float rad = __fdiv_rn(static_cast<float>(pos[b * L + l]), powf(max_wavelength, freq));
+  const float c = cosf(rad), s = sinf(rad);
+  const __nv_bfloat16* src = (is_q ? q_raw : k_raw) + (static_cast<size_t>(b) * L + l) * H * 64 + h * 64;
+  const float x1 = __bfloat162float(src[i]), x2 = __bfloat162float(src[i + 32]);
+  const __nv_bfloat16 o1 = __float2bfloat16_rn(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+  const __nv_bfloat16 o2 = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
+  if (is_q) {
+    __nv_bfloat16* dst = q_out + ((static_cast<size_t>(b) * Hq + h) * L + l) * 64;
+    dst[i] = o1;
+    dst[i + 32] = o2;
+  } else {
+    const int gsz = Hq / Hkv;
+    for (int j = 0; j < gsz; ++j) {
+      __nv_bfloat16* dst = k_out + (static_cast<size_t>(b) * Hq + h * gsz + j) * 64 * L;
+      dst[static_cast<size_t>(i) * L + l] = o1;
+      dst[static_cast<size_t>(i + 32) * L + l] = o2;
+    }
+  }
+}
+
+}  // namespace svla

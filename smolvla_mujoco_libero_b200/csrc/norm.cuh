@@ -1,0 +1,190 @@
+// Row normalisation fused with SmoothQuant activation quantisation.
+//
+// One warp per row; each lane holds NV vectors of 8 bf16 in registers (K <= NV * 256).
+//   RMSNorm  (SmolVLM2 text / expert, transformers LlamaRMSNorm):
+//       h = bf16(x * (1 / sqrt(mean(x^2) + eps)));  y = bf16(w * h)
+//   LayerNorm (SigLIP):  y = bf16((x - mean) * rstd * w + b)
+// Outputs (any subset): y in bf16, and up to three int8 tensors
+//       q_i = round((y / s_i[k]) / a_i).clamp(-128, 127)
+// each with its own smooth vector s_i and activation scale a_i -- the per-projection SmoothQuant
+// of q/k/v (or gate/up) that W8A8Linear.forward applies (deploy/linear_only_quant.py:104-116).
+// The smooth divide runs on the bf16-rounded y, exactly as the unfused reference does.
+//
+// Optional pixel-shuffle remap of the int8 output (SmolVLM connector, scale 4 on a 32x32 grid):
+// input token t = hh*32 + ww of image i goes to output row i*64 + (hh/4)*8 + ww/4, columns
+// ((hh%4)*4 + ww%4) * K ..., with the smooth vector indexed by the output column.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace svla {
+
+struct NormQuantArgs {
+  const __nv_bfloat16* x;  // [M, ldx]
+  int ldx;
+  const __nv_bfloat16* w;  // [K]
+  const __nv_bfloat16* b;  // [K] (LayerNorm) or nullptr
+  float eps;
+  int M, K;
+  __nv_bfloat16* y;        // optional [M, ldy]
+  int ldy;
+  int nq;                  // number of int8 outputs (0..3)
+  int8_t* q[3];
+  int ldq;
+  const float* smooth[3];
+  float act[3];
+  int pixel_shuffle;       // 0 or the shuffle factor (4)
+  int ps_grid;             // tokens per side of the input grid (32)
+};
+
+template <int NV, bool LAYERNORM>
+__global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= a.M) return;
+  const int m = warp;
+  const __nv_bfloat16* xr = a.x + static_cast<size_t>(m) * a.ldx;
+  float v[NV][8];
+  float ss = 0.f, sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int k = (i * 32 + lane) * 8;
+    if (k < a.K) {
+      const int4 raw = *reinterpret_cast<const int4*>(xr + k);
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[i][j] = __bfloat162float(h[j]);
+        sum += v[i][j];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+    }
+  }
+  float mean = 0.f;
+  if constexpr (LAYERNORM) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    mean = __fdiv_rn(sum, static_cast<float>(a.K));
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int k = (i * 32 + lane) * 8;
+    if (k < a.K) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = LAYERNORM ? (v[i][j] - mean) : v[i][j];
+        ss = fmaf(d, d, ss);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float var = __fdiv_rn(ss, static_cast<float>(a.K));
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+
+  // output row / column remap for the pixel shuffle
+  int qrow = m, qcol0 = 0;
+  if (a.pixel_shuffle > 0) {
+    const int s = a.pixel_shuffle, g = a.ps_grid;
+    const int per_img = g * g;
+    const int img = m / per_img, t = m % per_img;
+    const int hh = t / g, ww = t % g;
+    const int out_side = g / s;
+    qrow = img * out_side * out_side + (hh / s) * out_side + (ww / s);
+    qcol0 = ((hh % s) * s + (ww % s)) * a.K;
+  }
+
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int k = (i * 32 + lane) * 8;
+    if (k >= a.K) continue;
+    const int4 wr = *reinterpret_cast<const int4*>(a.w + k);
+    const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wr);
+    float y[8];
+    if constexpr (LAYERNORM) {
+      const int4 br = *reinterpret_cast<const int4*>(a.b + k);
+      const __nv_bfloat16* bh = reinterpret_cast<const __nv_bfloat16*>(&br);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        y[j] = bf16_round(__fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i][j], mean), rstd), __bfloat162float(wh[j])),
+                                    __bfloat162float(bh[j])));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = bf16_round(__fmul_rn(__bfloat162float(wh[j]), bf16_round(__fmul_rn(v[i][j], rstd))));
+    }
+    if (a.y) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * u], y[2 * u + 1]);
+        pk[u] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<int4*>(a.y + static_cast<size_t>(m) * a.ldy + k) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    for (int qi = 0; qi < a.nq; ++qi) {
+      const int col = qcol0 + k;
+      const float4 s0 = *reinterpret_cast<const float4*>(a.smooth[qi] + col);
+      const float4 s1 = *reinterpret_cast<const float4*>(a.smooth[qi] + col + 4);
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      int8_t qv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) qv[j] = smooth_quant(y[j], sv[j], a.act[qi]);
+      *reinterpret_cast<int2*>(a.q[qi] + static_cast<size_t>(qrow) * a.ldq + col) = *reinterpret_cast<int2*>(qv);
+    }
+  }
+}
+
+// Standalone SmoothQuant activation quantiser (deploy/cuda/smoothquant_linear_epilogue.cu:108-119):
+// q[m, k] = round((x[m, k] / s[k]) / a).clamp(-128, 127), x in bf16.  8 elements per thread.
+__global__ void smooth_quant_kernel(const __nv_bfloat16* x, int ldx, const float* s, float act, int8_t* q, int ldq,
+                                    int M, int K) {
+  const int kv = K / 8;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<long long>(M) * kv) return;
+  const int m = static_cast<int>(idx / kv), k = static_cast<int>(idx % kv) * 8;
+  const int4 raw = *reinterpret_cast<const int4*>(x + static_cast<size_t>(m) * ldx + k);
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+  int8_t qv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) qv[j] = smooth_quant(__bfloat162float(h[j]), s ? s[k + j] : 1.0f, act);
+  *reinterpret_cast<int2*>(q + static_cast<size_t>(m) * ldq + k) = *reinterpret_cast<int2*>(qv);
+}
+
+// Per-output-channel int8 weight packing with an optional SmoothQuant fold
+// (deploy/linear_only_quant.py:43-53, :140-144):  W' = W * s[None, :];
+// w_s[n] = max(max_k |W'[n, k]|, 1e-8) / 127;  q = round(W' / w_s[n]).clamp(-127, 127).
+// One block per output row.
+__global__ void __launch_bounds__(256) pack_weight_kernel(const __nv_bfloat16* w, int K, const float* smooth,
+                                                          int8_t* q, float* wscale) {
+  const int n = blockIdx.x;
+  const __nv_bfloat16* wr = w + static_cast<size_t>(n) * K;
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    float v = __bfloat162float(wr[k]);
+    if (smooth) v = __fmul_rn(v, fmaxf(smooth[k], 1e-8f));
+    amax = fmaxf(amax, fabsf(v));
+  }
+  __shared__ float red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float scale = __fdiv_rn(fmaxf(red[0], 1e-8f), 127.0f);
+  if (threadIdx.x == 0) wscale[n] = scale;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    float v = __bfloat162float(wr[k]);
+    if (smooth) v = __fmul_rn(v, fmaxf(smooth[k], 1e-8f));
+    q[static_cast<size_t>(n) * K + k] = static_cast<int8_t>(quant_rn_clamp(__fdiv_rn(v, scale), -127, 127));
+  }
+}
+
+}  // namespace svla

@@ -1,0 +1,517 @@
+// libsvla.so: C-ABI entry points (include/svla.h) over the sm_100a kernels.
+//
+// Host-side responsibilities: argument validation (status 1 with a message), TMA tensor-map encoding,
+// template dispatch, and launch-error reporting (status 2).  Nothing here allocates device memory.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/svla.h"
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "misc.cuh"
+#include "norm.cuh"
+
+namespace svla {
+
+__device__ int g_device_error = 0;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int32_t fail(int32_t code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int32_t fail(int32_t code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int32_t check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return SVLA_OK;
+}
+
+int* device_error_ptr() {
+  // one device-error word per device; the symbol address is per device
+  static int* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+// ---------------------------------------------------------------- TMA descriptors
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2D row-major [rows, cols] tensor, box [box_rows, box_cols]; cols is the contiguous dimension.
+int32_t make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
+                  uint64_t rows, uint64_t ld_elems, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SVLA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(SVLA_ERR_ARG, "TMA base address not 16-byte aligned");
+  if ((ld_elems * elem_bytes) % 16 != 0) return fail(SVLA_ERR_ARG, "TMA row stride %llu bytes not a multiple of 16",
+                                                    (unsigned long long)(ld_elems * elem_bytes));
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld_elems * elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SVLA_ERR_ARG, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return SVLA_OK;
+}
+
+// ---------------------------------------------------------------- GEMM dispatch
+template <Kind K, int BN, int P>
+constexpr int stages_for() {
+  constexpr int a = 128 * 128, b = BN * 128, raw = KindTraits<K>::kConvert ? BN * 64 : 0;
+  constexpr int stage = P * (a + b + raw);
+  constexpr int s = (200 * 1024) / stage;
+  return s > 8 ? 8 : (s < 2 ? 2 : s);
+}
+
+template <Kind K, int BN, int P, Epi E>
+int32_t launch_gemm_inst(const GemmArgs& args, dim3 grid, cudaStream_t stream) {
+  constexpr int ST = stages_for<K, BN, P>();
+  using S = GemmSmem<K, BN, P, ST>;
+  auto kern = gemm_sm100_kernel<K, BN, P, ST, E>;
+  static bool configured[64] = {false};  // the attribute is per function and per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
+    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  kern<<<grid, 192, S::kBytes, stream>>>(args);
+  return check_launch("gemm_sm100_kernel");
+}
+
+template <Kind K, int BN, int P>
+int32_t dispatch_epi(Epi e, const GemmArgs& args, dim3 grid, cudaStream_t st) {
+  if constexpr (P == 2) {
+    if (e == Epi::SiluMul) return launch_gemm_inst<K, BN, 2, Epi::SiluMul>(args, grid, st);
+    return fail(SVLA_ERR_ARG, "pair GEMMs support only the SILU_MUL epilogue");
+  } else {
+    switch (e) {
+      case Epi::Bf16: return launch_gemm_inst<K, BN, 1, Epi::Bf16>(args, grid, st);
+      case Epi::Rope: return launch_gemm_inst<K, BN, 1, Epi::Rope>(args, grid, st);
+      case Epi::Resid: return launch_gemm_inst<K, BN, 1, Epi::Resid>(args, grid, st);
+      case Epi::F32: return launch_gemm_inst<K, BN, 1, Epi::F32>(args, grid, st);
+      default: break;
+    }
+    if constexpr (K == Kind::I8) {
+      if (e == Epi::I32) return launch_gemm_inst<K, BN, 1, Epi::I32>(args, grid, st);
+      if (e == Epi::GeluQuant) return launch_gemm_inst<K, BN, 1, Epi::GeluQuant>(args, grid, st);
+    }
+    if constexpr (K == Kind::BF16) {
+      if (e == Epi::SiluBf16) return launch_gemm_inst<K, BN, 1, Epi::SiluBf16>(args, grid, st);
+      if (e == Epi::Euler) return launch_gemm_inst<K, BN, 1, Epi::Euler>(args, grid, st);
+    }
+    return fail(SVLA_ERR_ARG, "epilogue %d not available for operand kind %d", static_cast<int>(e),
+                static_cast<int>(K));
+  }
+}
+
+template <Kind K>
+int32_t dispatch_bn(int bn, int pair, Epi e, const GemmArgs& args, dim3 grid, cudaStream_t st) {
+  if (pair) {
+    if (bn != 64) return fail(SVLA_ERR_ARG, "pair GEMMs use block_n 64");
+    return dispatch_epi<K, 64, 2>(e, args, grid, st);
+  }
+  if (bn == 64) return dispatch_epi<K, 64, 1>(e, args, grid, st);
+  if (bn == 128) return dispatch_epi<K, 128, 1>(e, args, grid, st);
+  return fail(SVLA_ERR_ARG, "block_n must be 64 or 128 (got %d)", bn);
+}
+
+}  // namespace
+
+int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
+  if (!d) return fail(SVLA_ERR_ARG, "null gemm descriptor");
+  if (d->kind < 0 || d->kind > 2) return fail(SVLA_ERR_ARG, "bad operand kind %d", d->kind);
+  const Kind kind = static_cast<Kind>(d->kind);
+  const Epi epi = static_cast<Epi>(d->epi);
+  if (d->m <= 0 || d->k <= 0) return fail(SVLA_ERR_ARG, "bad shape m=%d k=%d", d->m, d->k);
+  if (d->nseg < 1 || d->nseg > 3) return fail(SVLA_ERR_ARG, "nseg must be 1..3");
+  if (d->pair && d->nseg != 2) return fail(SVLA_ERR_ARG, "a pair needs exactly 2 segments");
+  if (epi == Epi::SiluMul && !d->pair) return fail(SVLA_ERR_ARG, "SILU_MUL needs pair = 1");
+  if (epi == Epi::I32 && kind != Kind::I8) return fail(SVLA_ERR_ARG, "I32 epilogue needs kind I8");
+  int bn = d->block_n;
+  if (bn == 0) {
+    int total_n = 0;
+    for (int s = 0; s < d->nseg; ++s) total_n += d->seg[s].n;
+    bn = (d->pair || epi == Epi::Rope || d->m <= 512 || total_n < 1024) ? 64 : 128;
+    if (d->pair) bn = 64;
+  }
+  const int elem_a = (kind == Kind::I8) ? 1 : 2;
+  const int elem_b = (kind == Kind::BF16) ? 2 : 1;
+  const int bk = (kind == Kind::I8) ? 128 : 64;
+  GemmArgs args;
+  std::memset(&args, 0, sizeof(args));
+  int tiles = 0;
+  for (int s = 0; s < d->nseg; ++s) {
+    const svla_gemm_seg& g = d->seg[s];
+    if (g.n <= 0 || g.n % 16 != 0) return fail(SVLA_ERR_ARG, "segment %d: n=%d must be a positive multiple of 16", s, g.n);
+    if (!g.a || !g.b) return fail(SVLA_ERR_ARG, "segment %d: null operand", s);
+    if (!g.out && epi != Epi::GeluQuant && epi != Epi::Euler)
+      return fail(SVLA_ERR_ARG, "segment %d: null output", s);
+    if (g.lda < d->k || g.ldb < d->k) return fail(SVLA_ERR_ARG, "segment %d: lda/ldb smaller than k", s);
+    if (epi == Epi::Rope && g.rope && g.n % 64 != 0) return fail(SVLA_ERR_ARG, "RoPE segment n must be a multiple of 64");
+    if (kind == Kind::I8 && g.act_scale <= 0.f) return fail(SVLA_ERR_ARG, "segment %d: act_scale must be > 0", s);
+    int32_t rc;
+    const CUtensorMapDataType dta = (kind == Kind::I8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    rc = make_tmap(&args.ta[s], g.a, dta, elem_a, d->k, d->m, g.lda, bk, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if (kind == Kind::W8A16) {
+      rc = make_tmap(&args.tb[s], g.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d->k, g.n, g.ldb, 64, bn,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+      const CUtensorMapDataType dtb = (kind == Kind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      rc = make_tmap(&args.tb[s], g.b, dtb, elem_b, d->k, g.n, g.ldb, bk, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (rc) return rc;
+    GemmSeg& o = args.seg[s];
+    o.wscale = g.wscale;
+    o.bias = static_cast<const __nv_bfloat16*>(g.bias);
+    o.bias_f32 = g.bias_f32;
+    o.out = g.out;
+    o.ldo = g.ldo;
+    o.n = g.n;
+    o.tile_begin = d->pair ? 0 : tiles;
+    o.act_scale = (kind == Kind::I8) ? g.act_scale : 1.0f;
+    o.rope = g.rope;
+    if (!d->pair) tiles += (g.n + bn - 1) / bn;
+  }
+  if (d->pair) {
+    if (d->seg[0].n != d->seg[1].n) return fail(SVLA_ERR_ARG, "pair segments must have equal n");
+    tiles = (d->seg[0].n + bn - 1) / bn;
+  }
+  args.nseg = d->nseg;
+  args.M = d->m;
+  args.K = d->k;
+  args.rows_per_group = d->rows_per_group;
+  args.group_stride = d->group_stride;
+  args.row_offset = d->row_offset;
+  args.post_scale = d->post_scale;
+  args.resid = static_cast<const __nv_bfloat16*>(d->resid);
+  args.ldr = d->ldr;
+  args.resid_rows = d->resid_rows;
+  args.rope_cs = reinterpret_cast<const float2*>(d->rope_cs);
+  args.pos = d->pos;
+  args.max_pos = d->max_pos;
+  args.q_smooth = d->q_smooth;
+  args.q_act = d->q_act;
+  args.qout = d->qout;
+  args.ldq = d->ldq;
+  args.dt = d->dt;
+  args.xt = d->xt;
+  args.xt_bf16 = static_cast<__nv_bfloat16*>(d->xt_bf16);
+  args.err = device_error_ptr();
+  if (epi == Epi::Resid && !d->resid) return fail(SVLA_ERR_ARG, "RESID needs a residual");
+  if (epi == Epi::Rope && (!d->rope_cs || !d->pos || d->max_pos <= 0)) return fail(SVLA_ERR_ARG, "ROPE needs rope_cs/pos");
+  if (epi == Epi::GeluQuant && (!d->q_smooth || !d->qout || d->q_act <= 0.f)) return fail(SVLA_ERR_ARG, "GELU_QUANT needs q_smooth/qout/q_act");
+  if (epi == Epi::Euler && (!d->xt || !d->xt_bf16)) return fail(SVLA_ERR_ARG, "EULER needs xt/xt_bf16");
+  dim3 grid((d->m + 127) / 128, tiles);
+  switch (kind) {
+    case Kind::I8: return dispatch_bn<Kind::I8>(bn, d->pair, epi, args, grid, stream);
+    case Kind::BF16: return dispatch_bn<Kind::BF16>(bn, d->pair, epi, args, grid, stream);
+    case Kind::W8A16: return dispatch_bn<Kind::W8A16>(bn, d->pair, epi, args, grid, stream);
+  }
+  return fail(SVLA_ERR_ARG, "unreachable");
+}
+
+}  // namespace svla
+
+using namespace svla;
+
+static inline cudaStream_t cs(svla_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+extern "C" {
+
+const char* svla_last_error(void) { return t_last_error.c_str(); }
+
+const char* svla_version(void) { return "svla 0.1 sm_100a (tcgen05 kind::i8 / kind::f16, TMA, mma.sync attention)"; }
+
+int32_t svla_device_error(int32_t* code, int32_t reset) {
+  int* p = device_error_ptr();
+  if (!p) return fail(SVLA_ERR_CUDA, "device error word unavailable");
+  int v = 0;
+  if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(SVLA_ERR_CUDA, "reading the device error word failed");
+  if (code) *code = v;
+  if (reset) {
+    int z = 0;
+    if (cudaMemcpy(p, &z, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(SVLA_ERR_CUDA, "clearing the device error word failed");
+  }
+  return SVLA_OK;
+}
+
+int32_t svla_pack_weight_i8(const void* weight, const float* smooth, int32_t n, int32_t k, int8_t* qweight,
+                            float* wscale, svla_stream_t stream) {
+  if (!weight || !qweight || !wscale || n <= 0 || k <= 0) return fail(SVLA_ERR_ARG, "svla_pack_weight_i8: bad args");
+  pack_weight_kernel<<<n, 256, 0, cs(stream)>>>(static_cast<const __nv_bfloat16*>(weight), k, smooth, qweight, wscale);
+  return check_launch("pack_weight_kernel");
+}
+
+int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, float act_scale, int8_t* q, int32_t ldq,
+                             int32_t m, int32_t k, svla_stream_t stream) {
+  if (!x || !q || m <= 0 || k <= 0 || k % 8 || ldx % 8 || ldq % 8 || act_scale <= 0.f)
+    return fail(SVLA_ERR_ARG, "svla_quantize_smooth: bad args (k, ldx, ldq must be multiples of 8)");
+  const long long total = static_cast<long long>(m) * (k / 8);
+  smooth_quant_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, cs(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, smooth, act_scale, q, ldq, m, k);
+  return check_launch("smooth_quant_kernel");
+}
+
+int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream) { return run_gemm(desc, cs(stream)); }
+
+int32_t svla_gemm_i8_i32(const int8_t* qx, const int8_t* qw, int32_t m, int32_t n, int32_t k, int32_t* acc,
+                         svla_stream_t stream) {
+  svla_gemm_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.kind = SVLA_KIND_I8;
+  d.epi = SVLA_EPI_I32;
+  d.m = m;
+  d.k = k;
+  d.nseg = 1;
+  d.seg[0].a = qx;
+  d.seg[0].lda = k;
+  d.seg[0].b = qw;
+  d.seg[0].ldb = k;
+  d.seg[0].out = acc;
+  d.seg[0].ldo = n;
+  d.seg[0].n = n;
+  d.seg[0].act_scale = 1.0f;
+  return run_gemm(&d, cs(stream));
+}
+
+size_t svla_sq_linear_w8a8_workspace_size(int32_t m, int32_t k) {
+  return (static_cast<size_t>(m) * k + 255) / 256 * 256;
+}
+
+int32_t svla_sq_linear_w8a8(const void* x, const float* smooth, float act_scale, const int8_t* qweight,
+                            const float* wscale, const void* bias, int32_t m, int32_t n, int32_t k, void* y,
+                            void* workspace, size_t workspace_bytes, svla_stream_t stream) {
+  if (!workspace || workspace_bytes < svla_sq_linear_w8a8_workspace_size(m, k))
+    return fail(SVLA_ERR_ARG, "svla_sq_linear_w8a8: workspace too small (%zu < %zu)", workspace_bytes,
+                svla_sq_linear_w8a8_workspace_size(m, k));
+  int8_t* qx = static_cast<int8_t*>(workspace);
+  int32_t rc = svla_quantize_smooth(x, k, smooth, act_scale, qx, k, m, k, stream);
+  if (rc) return rc;
+  svla_gemm_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.kind = SVLA_KIND_I8;
+  d.epi = SVLA_EPI_BF16;
+  d.m = m;
+  d.k = k;
+  d.nseg = 1;
+  d.seg[0] = svla_gemm_seg{qx, k, qweight, k, wscale, bias, nullptr, y, n, n, act_scale, 0};
+  return run_gemm(&d, cs(stream));
+}
+
+int32_t svla_w8a16_linear(const void* x, const int8_t* qweight, const float* wscale, const void* bias, int32_t m,
+                          int32_t n, int32_t k, void* y, svla_stream_t stream) {
+  svla_gemm_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.kind = SVLA_KIND_W8A16;
+  d.epi = SVLA_EPI_BF16;
+  d.m = m;
+  d.k = k;
+  d.nseg = 1;
+  d.seg[0] = svla_gemm_seg{x, k, qweight, k, wscale, bias, nullptr, y, n, n, 1.0f, 0};
+  return run_gemm(&d, cs(stream));
+}
+
+int32_t svla_norm_quant(const svla_norm_desc* d, svla_stream_t stream) {
+  if (!d || !d->x || !d->weight || d->m <= 0 || d->k <= 0) return fail(SVLA_ERR_ARG, "svla_norm_quant: bad args");
+  if (d->k % 8 || d->ldx % 8 || (d->y && d->ldy % 8) || (d->nq && d->ldq % 8))
+    return fail(SVLA_ERR_ARG, "svla_norm_quant: k and row strides must be multiples of 8");
+  if (d->nq < 0 || d->nq > 3) return fail(SVLA_ERR_ARG, "svla_norm_quant: nq must be 0..3");
+  if (d->layernorm && !d->bias) return fail(SVLA_ERR_ARG, "svla_norm_quant: LayerNorm needs a bias");
+  if (d->pixel_shuffle && (d->ps_grid % d->pixel_shuffle || d->m % (d->ps_grid * d->ps_grid)))
+    return fail(SVLA_ERR_ARG, "svla_norm_quant: pixel shuffle grid mismatch");
+  NormQuantArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.x = static_cast<const __nv_bfloat16*>(d->x);
+  a.ldx = d->ldx;
+  a.w = static_cast<const __nv_bfloat16*>(d->weight);
+  a.b = static_cast<const __nv_bfloat16*>(d->bias);
+  a.eps = d->eps;
+  a.M = d->m;
+  a.K = d->k;
+  a.y = static_cast<__nv_bfloat16*>(d->y);
+  a.ldy = d->ldy;
+  a.nq = d->nq;
+  for (int i = 0; i < 3; ++i) {
+    a.q[i] = d->q[i];
+    a.smooth[i] = d->smooth[i];
+    a.act[i] = d->act[i];
+    if (i < d->nq && (!d->q[i] || !d->smooth[i] || d->act[i] <= 0.f))
+      return fail(SVLA_ERR_ARG, "svla_norm_quant: quant output %d incomplete", i);
+  }
+  a.ldq = d->ldq;
+  a.pixel_shuffle = d->pixel_shuffle;
+  a.ps_grid = d->ps_grid;
+  const int nv = (d->k + 255) / 256;
+  const unsigned blocks = static_cast<unsigned>((d->m + 7) / 8);
+  cudaStream_t st = cs(stream);
+#define SVLA_NORM(NV)                                                             \
+  if (nv <= NV) {                                                                 \
+    if (d->layernorm) norm_quant_kernel<NV, true><<<blocks, 256, 0, st>>>(a);     \
+    else norm_quant_kernel<NV, false><<<blocks, 256, 0, st>>>(a);                 \
+    return check_launch("norm_quant_kernel");                                     \
+  }
+  SVLA_NORM(3)
+  SVLA_NORM(4)
+  SVLA_NORM(12)
+#undef SVLA_NORM
+  return fail(SVLA_ERR_ARG, "svla_norm_quant: k=%d too large (max 3072)", d->k);
+}
+
+int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
+  if (!d || !d->q || !d->k1 || !d->v1 || d->batch <= 0 || d->lq <= 0 || d->l1 <= 0 || d->hq <= 0 || d->hkv <= 0)
+    return fail(SVLA_ERR_ARG, "svla_attention: bad args");
+  if (d->hq % d->hkv) return fail(SVLA_ERR_ARG, "svla_attention: hq must be a multiple of hkv");
+  if (d->l2 > 0 && (!d->k2 || !d->v2)) return fail(SVLA_ERR_ARG, "svla_attention: second key source missing");
+  if (!d->o && !d->qo) return fail(SVLA_ERR_ARG, "svla_attention: no output");
+  if (d->qo && (!d->qo_smooth || d->qo_act <= 0.f)) return fail(SVLA_ERR_ARG, "svla_attention: qo needs smooth/act");
+  if ((d->q_rs % 8) || (d->kv1_rs % 8) || (d->l2 > 0 && d->kv2_rs % 8))
+    return fail(SVLA_ERR_ARG, "svla_attention: row strides must be multiples of 8");
+  AttnArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = static_cast<const __nv_bfloat16*>(d->q);
+  a.q_bs = d->q_bs;
+  a.q_rs = d->q_rs;
+  a.k1 = static_cast<const __nv_bfloat16*>(d->k1);
+  a.v1 = static_cast<const __nv_bfloat16*>(d->v1);
+  a.kv1_bs = d->kv1_bs;
+  a.kv1_rs = d->kv1_rs;
+  a.L1 = d->l1;
+  a.k2 = static_cast<const __nv_bfloat16*>(d->k2);
+  a.v2 = static_cast<const __nv_bfloat16*>(d->v2);
+  a.kv2_bs = d->kv2_bs;
+  a.kv2_rs = d->kv2_rs;
+  a.L2 = d->l2 > 0 ? d->l2 : 0;
+  a.mask = d->mask;
+  a.mask_bs = d->mask_bs;
+  a.mask_rs = d->mask_rs;
+  a.o = static_cast<__nv_bfloat16*>(d->o);
+  a.o_bs = d->o_bs;
+  a.o_rs = d->o_rs;
+  a.qo = d->qo;
+  a.qo_bs = d->qo_bs;
+  a.qo_rs = d->qo_rs;
+  a.qo_smooth = d->qo_smooth;
+  a.qo_act = d->qo_act;
+  a.Lq = d->lq;
+  a.Hq = d->hq;
+  a.Hkv = d->hkv;
+  a.scale = d->scale > 0.f ? d->scale : 0.125f;
+  dim3 grid((d->lq + 63) / 64, d->hq, d->batch);
+  attention_kernel<<<grid, 128, 0, cs(stream)>>>(a);
+  return check_launch("attention_kernel");
+}
+
+int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* pos, void* q_out, void* k_out,
+                         int32_t batch, int32_t seq_len, int32_t q_heads, int32_t kv_heads, float max_wavelength,
+                         svla_stream_t stream) {
+  if (!q_raw || !k_raw || !pos || !q_out || !k_out || batch <= 0 || seq_len <= 0 || q_heads <= 0 || kv_heads <= 0 ||
+      q_heads % kv_heads || max_wavelength <= 0.f)
+    return fail(SVLA_ERR_ARG, "svla_rope_layout: bad args");
+  const long long total = static_cast<long long>(batch) * seq_len * (q_heads + kv_heads) * 32;
+  rope_layout_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, cs(stream)>>>(
+      static_cast<const __nv_bfloat16*>(q_raw), static_cast<const __nv_bfloat16*>(k_raw), pos,
+      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out), batch, seq_len, q_heads, kv_heads,
+      max_wavelength);
+  return check_launch("rope_layout_kernel");
+}
+
+int32_t svla_rope_table(float* c, int32_t max_pos, float max_wavelength, svla_stream_t stream) {
+  if (!c || max_pos <= 0 || max_wavelength <= 0.f) return fail(SVLA_ERR_ARG, "svla_rope_table: bad args");
+  rope_table_kernel<<<(max_pos * 32 + 255) / 256, 256, 0, cs(stream)>>>(reinterpret_cast<float2*>(c), max_pos,
+                                                                         max_wavelength);
+  return check_launch("rope_table_kernel");
+}
+
+int32_t svla_build_masks(const uint8_t* img_mask0, const uint8_t* img_mask1, const uint8_t* lang_mask, int32_t batch,
+                         int32_t n_img, int32_t n_lang, int32_t chunk, uint8_t* prefix_mask, int32_t* prefix_pos,
+                         uint8_t* self_mask, uint8_t* cross_mask, int32_t* suffix_pos, int32_t* cross_pos,
+                         svla_stream_t stream) {
+  if (!img_mask0 || !img_mask1 || !lang_mask || !prefix_mask || !prefix_pos || !self_mask || !cross_mask ||
+      !suffix_pos || !cross_pos || batch <= 0 || n_img < 0 || n_lang < 0 || chunk <= 0)
+    return fail(SVLA_ERR_ARG, "svla_build_masks: bad args");
+  MaskArgs a{img_mask0, img_mask1, lang_mask, batch, n_img, n_lang, chunk, prefix_mask, prefix_pos,
+             self_mask, cross_mask, suffix_pos, cross_pos};
+  const int lp = 2 * n_img + n_lang + 1;
+  masks_kernel<<<batch, 256, 2 * lp * sizeof(int), cs(stream)>>>(a);
+  return check_launch("masks_kernel");
+}
+
+int32_t svla_embed_tokens(const int64_t* tokens, int32_t batch, int32_t t, const void* table, int32_t vocab,
+                          int32_t hidden, float scale, void* out, int32_t rows_per_batch, int32_t row_offset,
+                          svla_stream_t stream) {
+  if (!tokens || !table || !out || batch <= 0 || t <= 0 || vocab <= 0 || hidden <= 0 || hidden % 8)
+    return fail(SVLA_ERR_ARG, "svla_embed_tokens: bad args");
+  const long long threads = static_cast<long long>(batch) * t * 32;
+  embed_tokens_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, cs(stream)>>>(
+      reinterpret_cast<const long long*>(tokens), batch, t, static_cast<const __nv_bfloat16*>(table), vocab, hidden,
+      scale, static_cast<__nv_bfloat16*>(out), rows_per_batch, row_offset, device_error_ptr());
+  return check_launch("embed_tokens_kernel");
+}
+
+int32_t svla_im2col(const float* images, int32_t n, int32_t c, int32_t s, int32_t p, void* out, svla_stream_t stream) {
+  if (!images || !out || n <= 0 || c <= 0 || p <= 0 || p % 8 || s % p) return fail(SVLA_ERR_ARG, "svla_im2col: bad args");
+  const long long total = static_cast<long long>(n) * (s / p) * (s / p) * c * p * (p / 8);
+  im2col_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, cs(stream)>>>(images, n, c, s, p,
+                                                                                     static_cast<__nv_bfloat16*>(out));
+  return check_launch("im2col_kernel");
+}
+
+int32_t svla_f32_to_bf16(const float* x, void* y, int64_t n, svla_stream_t stream) {
+  if (!x || !y || n <= 0) return fail(SVLA_ERR_ARG, "svla_f32_to_bf16: bad args");
+  f32_to_bf16_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cs(stream)>>>(x, static_cast<__nv_bfloat16*>(y), n);
+  return check_launch("f32_to_bf16_kernel");
+}
+
+int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n, svla_stream_t stream) {
+  if (!noise || !xt || !xt_bf16 || n <= 0) return fail(SVLA_ERR_ARG, "svla_euler_init: bad args");
+  euler_init_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cs(stream)>>>(noise, xt,
+                                                                                    static_cast<__nv_bfloat16*>(xt_bf16), n);
+  return check_launch("euler_init_kernel");
+}
+
+}  // extern "C"

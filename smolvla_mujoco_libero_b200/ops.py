@@ -1,0 +1,250 @@
+"""torch-facing wrappers of the libsvla.so C ABI.
+
+Each function checks devices / dtypes / contiguity, allocates its outputs with torch (the only allocation in
+this layer), and launches on torch's current CUDA stream through ctypes.  The most used ops are also
+registered as ``torch.ops.svla.*`` custom ops.  Nothing here computes on the CPU: a missing library or a
+CPU tensor raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib as L
+from ._lib import check, lib
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str, contiguous: bool = True) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path)")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+# ----------------------------------------------------------------------------- SmoothQuant primitives
+
+def pack_weight_i8(weight: torch.Tensor, smooth: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """int8 per-output-channel weights with an optional SmoothQuant fold (deploy/linear_only_quant.py:43-54)."""
+    _need(weight, torch.bfloat16, "weight")
+    n, k = weight.shape
+    if smooth is not None:
+        _need(smooth, torch.float32, "smooth")
+    q = torch.empty(n, k, dtype=torch.int8, device=weight.device)
+    ws = torch.empty(n, dtype=torch.float32, device=weight.device)
+    check(lib().svla_pack_weight_i8(_p(weight), _p(smooth), n, k, _p(q), _p(ws), _stream()), "pack_weight_i8")
+    return q, ws
+
+
+def quantize_smooth(x: torch.Tensor, smooth: torch.Tensor | None, act_scale: float) -> torch.Tensor:
+    _need(x, torch.bfloat16, "x")
+    m, k = x.shape
+    q = torch.empty(m, k, dtype=torch.int8, device=x.device)
+    check(lib().svla_quantize_smooth(_p(x), k, _p(smooth), float(act_scale), _p(q), k, m, k, _stream()),
+          "quantize_smooth")
+    return q
+
+
+def gemm_i8_i32(qx: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
+    _need(qx, torch.int8, "qx")
+    _need(qw, torch.int8, "qw")
+    m, k = qx.shape
+    n = qw.shape[0]
+    acc = torch.empty(m, n, dtype=torch.int32, device=qx.device)
+    check(lib().svla_gemm_i8_i32(_p(qx), _p(qw), m, n, k, _p(acc), _stream()), "gemm_i8_i32")
+    return acc
+
+
+def sq_linear_w8a8(x: torch.Tensor, smooth: torch.Tensor | None, act_scale: float, qweight: torch.Tensor,
+                   wscale: torch.Tensor, bias: torch.Tensor | None = None,
+                   workspace: torch.Tensor | None = None) -> torch.Tensor:
+    _need(x, torch.bfloat16, "x")
+    m, k = x.shape
+    n = qweight.shape[0]
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    need = int(lib().svla_sq_linear_w8a8_workspace_size(m, k))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    check(lib().svla_sq_linear_w8a8(_p(x), _p(smooth), float(act_scale), _p(qweight), _p(wscale), _p(bias), m, n, k,
+                                    _p(y), _p(workspace), workspace.numel(), _stream()), "sq_linear_w8a8")
+    return y
+
+
+def w8a16_linear(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.Tensor,
+                 bias: torch.Tensor | None = None) -> torch.Tensor:
+    _need(x, torch.bfloat16, "x")
+    m, k = x.shape
+    n = qweight.shape[0]
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    check(lib().svla_w8a16_linear(_p(x), _p(qweight), _p(wscale), _p(bias), m, n, k, _p(y), _stream()),
+          "w8a16_linear")
+    return y
+
+
+# ----------------------------------------------------------------------------- general GEMM
+
+@dataclass
+class Seg:
+    a: torch.Tensor              # [M, lda]
+    b: torch.Tensor              # [n, ldb]
+    out: torch.Tensor | None     # [M', ldo]
+    n: int
+    wscale: torch.Tensor | None = None
+    bias: torch.Tensor | None = None
+    bias_f32: torch.Tensor | None = None
+    act_scale: float = 1.0
+    rope: int = 0
+    lda: int | None = None
+    ldb: int | None = None
+    ldo: int | None = None
+
+
+def gemm_desc(kind: int, epi: int, m: int, k: int, segs: list[Seg], pair: bool = False, block_n: int = 0,
+              **extra) -> L.GemmDesc:
+    d = L.GemmDesc()
+    d.kind, d.epi, d.m, d.k, d.nseg, d.pair, d.block_n = kind, epi, m, k, len(segs), int(pair), block_n
+    for i, s in enumerate(segs):
+        g = d.seg[i]
+        g.a, g.b = s.a.data_ptr(), s.b.data_ptr()
+        g.lda = s.lda if s.lda is not None else s.a.stride(0)
+        g.ldb = s.ldb if s.ldb is not None else s.b.stride(0)
+        g.wscale, g.bias, g.bias_f32 = _p(s.wscale), _p(s.bias), _p(s.bias_f32)
+        g.out = _p(s.out)
+        g.ldo = s.ldo if s.ldo is not None else (s.out.stride(0) if s.out is not None else s.n)
+        g.n, g.act_scale, g.rope = s.n, float(s.act_scale), int(s.rope)
+    for key, val in extra.items():
+        if isinstance(val, torch.Tensor):
+            val = val.data_ptr()
+        setattr(d, key, val)
+    return d
+
+
+def gemm(desc: L.GemmDesc) -> None:
+    check(lib().svla_gemm(ctypes.byref(desc), _stream()), "svla_gemm")
+
+
+# ----------------------------------------------------------------------------- norm + quant
+
+def norm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, bias: torch.Tensor | None = None,
+               quants: list[tuple[torch.Tensor, float]] = (), want_y: bool = True, pixel_shuffle: int = 0,
+               ps_grid: int = 0, y: torch.Tensor | None = None, q_out: list[torch.Tensor] | None = None):
+    _need(x, torch.bfloat16, "x", contiguous=False)
+    m, k = x.shape
+    d = L.NormDesc()
+    d.x, d.ldx, d.weight, d.bias, d.eps = x.data_ptr(), x.stride(0), weight.data_ptr(), _p(bias), float(eps)
+    d.layernorm, d.m, d.k = int(bias is not None), m, k
+    if want_y and y is None:
+        y = torch.empty(m, k, dtype=torch.bfloat16, device=x.device)
+    d.y, d.ldy = _p(y), (y.stride(0) if y is not None else 0)
+    outs = []
+    qm, qk = (m // (pixel_shuffle ** 2), k * pixel_shuffle ** 2) if pixel_shuffle else (m, k)
+    for i, (smooth, act) in enumerate(quants):
+        q = q_out[i] if q_out is not None else torch.empty(qm, qk, dtype=torch.int8, device=x.device)
+        outs.append(q)
+        d.q[i], d.smooth[i], d.act[i] = q.data_ptr(), smooth.data_ptr(), float(act)
+    d.nq, d.ldq = len(quants), (outs[0].stride(0) if outs else 0)
+    d.pixel_shuffle, d.ps_grid = pixel_shuffle, ps_grid
+    check(lib().svla_norm_quant(ctypes.byref(d), _stream()), "svla_norm_quant")
+    return y, outs
+
+
+# ----------------------------------------------------------------------------- attention / RoPE
+
+def attention_desc(q: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor, batch: int, lq: int, hq: int, hkv: int,
+                   mask: torch.Tensor | None = None, k2: torch.Tensor | None = None, v2: torch.Tensor | None = None,
+                   o: torch.Tensor | None = None, qo: torch.Tensor | None = None,
+                   qo_smooth: torch.Tensor | None = None, qo_act: float = 0.0, scale: float = 0.0) -> L.AttnDesc:
+    """q [B, Lq, >=hq*64] (row stride = stride(1)), k/v [B, L, >=hkv*64], mask [B, Lq, L1+L2] (uint8/bool)."""
+    d = L.AttnDesc()
+    d.q, d.q_bs, d.q_rs = q.data_ptr(), q.stride(0), q.stride(1)
+    d.k1, d.v1, d.kv1_bs, d.kv1_rs, d.l1 = k1.data_ptr(), v1.data_ptr(), k1.stride(0), k1.stride(1), k1.shape[1]
+    assert v1.stride() == k1.stride()
+    if k2 is not None:
+        assert v2 is not None and v2.stride() == k2.stride()
+        d.k2, d.v2, d.kv2_bs, d.kv2_rs, d.l2 = k2.data_ptr(), v2.data_ptr(), k2.stride(0), k2.stride(1), k2.shape[1]
+    if mask is not None:
+        d.mask, d.mask_bs, d.mask_rs = mask.data_ptr(), mask.stride(0), mask.stride(1)
+    if o is not None:
+        d.o, d.o_bs, d.o_rs = o.data_ptr(), o.stride(0), o.stride(1)
+    if qo is not None:
+        d.qo, d.qo_bs, d.qo_rs = qo.data_ptr(), qo.stride(0), qo.stride(1)
+        d.qo_smooth, d.qo_act = qo_smooth.data_ptr(), float(qo_act)
+    d.batch, d.lq, d.hq, d.hkv, d.scale = batch, lq, hq, hkv, float(scale)
+    return d
+
+
+def attention_run(desc: L.AttnDesc) -> None:
+    check(lib().svla_attention(ctypes.byref(desc), _stream()), "svla_attention")
+
+
+def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smooth=None, qo_act=0.0):
+    """bf16 context [B, Lq, hq*64] (and the int8 context when qo_smooth is given)."""
+    b, lq = q.shape[0], q.shape[1]
+    o = torch.empty(b, lq, hq * 64, dtype=torch.bfloat16, device=q.device)
+    qo = torch.empty(b, lq, hq * 64, dtype=torch.int8, device=q.device) if qo_smooth is not None else None
+    if mask is not None and mask.dtype == torch.bool:
+        mask = mask.view(torch.uint8)
+    attention_run(attention_desc(q, k1, v1, b, lq, hq, hkv, mask=mask, k2=k2, v2=v2, o=o, qo=qo,
+                                 qo_smooth=qo_smooth, qo_act=qo_act))
+    return (o, qo) if qo is not None else o
+
+
+def rope_layout(q_raw: torch.Tensor, k_raw: torch.Tensor, pos: torch.Tensor, q_heads: int, kv_heads: int,
+                max_wavelength: float = 10000.0):
+    """Plugin semantics of SmolVLAFusedRopeLayout (deploy/cuda/fused_rope_layout.h:32-34)."""
+    _need(q_raw, torch.bfloat16, "q_raw")
+    _need(k_raw, torch.bfloat16, "k_raw")
+    _need(pos, torch.int32, "pos")
+    b, l, _ = q_raw.shape
+    q_out = torch.empty(b, q_heads, l, 64, dtype=torch.bfloat16, device=q_raw.device)
+    k_out = torch.empty(b, q_heads, 64, l, dtype=torch.bfloat16, device=q_raw.device)
+    check(lib().svla_rope_layout(_p(q_raw), _p(k_raw), _p(pos), _p(q_out), _p(k_out), b, l, q_heads, kv_heads,
+                                 float(max_wavelength), _stream()), "rope_layout")
+    return q_out, k_out
+
+
+def rope_table(max_pos: int, max_wavelength: float, device) -> torch.Tensor:
+    cs = torch.empty(max_pos, 32, 2, dtype=torch.float32, device=device)
+    check(lib().svla_rope_table(_p(cs), max_pos, float(max_wavelength), _stream()), "rope_table")
+    return cs
+
+
+# ----------------------------------------------------------------------------- torch custom ops
+
+@torch.library.custom_op("svla::sq_linear_w8a8", mutates_args=())
+def _sq_linear_op(x: torch.Tensor, smooth: torch.Tensor, act_scale: float, qweight: torch.Tensor,
+                  wscale: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    return sq_linear_w8a8(x, smooth, act_scale, qweight, wscale, bias)
+
+
+@_sq_linear_op.register_fake
+def _(x, smooth, act_scale, qweight, wscale, bias):
+    return x.new_empty(x.shape[0], qweight.shape[0])
+
+
+@torch.library.custom_op("svla::w8a16_linear", mutates_args=())
+def _w8a16_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    return w8a16_linear(x, qweight, wscale, bias)
+
+
+@_w8a16_op.register_fake
+def _(x, qweight, wscale, bias):
+    return x.new_empty(x.shape[0], qweight.shape[0])
+
+
+@torch.library.custom_op("svla::rope_layout", mutates_args=())
+def _rope_layout_op(q_raw: torch.Tensor, k_raw: torch.Tensor, pos: torch.Tensor, q_heads: int, kv_heads: int,
+                    max_wavelength: float) -> tuple[torch.Tensor, torch.Tensor]:
+    return rope_layout(q_raw, k_raw, pos, q_heads, kv_heads, max_wavelength)

@@ -1,0 +1,364 @@
+"""Parity of the sm_100a kernels (through the C ABI) with the CPU oracle.
+
+Bars (stated per test):
+  * int8 activations, int8 weights, weight scales and int32 accumulators: bit-exact.
+  * W8A8 output: bit-exact with bf16 of the fp32 integer-dequant form (acc*a)*w_s + b that the kernel
+    computes; against the reference's bf16 fake-dequant output: cosine >= 0.9999, max-abs <= 2 bf16 ulps
+    of the output magnitude.
+  * bf16 GEMMs / W8A16: against an fp32 torch reference of the same bf16 operands, |diff| <= 1 bf16 ulp
+    (relative 2^-8) plus 1e-6 absolute.
+  * norms / attention: stated in each test.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import quant as Q
+from smolvla_mujoco_libero_b200 import _lib as L
+from smolvla_mujoco_libero_b200 import ops, synthetic
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def bf16_ulp_close(got: torch.Tensor, ref: torch.Tensor, ulps: float = 1.0, atol: float = 1e-6) -> tuple[bool, float]:
+    got = got.float().cpu()
+    ref = ref.float().cpu()
+    tol = ref.abs() * (ulps * 2.0 ** -8) + atol
+    bad = (got - ref).abs() > tol
+    return (not bool(bad.any())), float(bad.float().mean())
+
+
+def cosine(a, b):
+    return float(F.cosine_similarity(a.float().flatten().cpu(), b.float().flatten().cpu(), dim=0))
+
+
+def _bf16(a):
+    return torch.from_numpy(np.asarray(a)).view(torch.bfloat16)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    L.device_error(reset=True)
+    yield
+    torch.cuda.synchronize()
+    assert L.device_error(reset=True) == 0
+
+
+# ----------------------------------------------------------------------------- SmoothQuant primitives
+
+def test_pack_weight_bit_exact_with_smoothing():
+    case = synthetic.smoothquant_linear_case()
+    smooth = torch.rand(960, generator=synthetic.generator(5)) * 4 + 0.1
+    q_ref, ws_ref = Q.pack_w8a8_weight(case.weight, smooth)
+    q, ws = ops.pack_weight_i8(case.weight.to(DEV), smooth.to(DEV))
+    assert torch.equal(q.cpu(), q_ref)
+    assert torch.equal(ws.cpu(), ws_ref)
+    q2, ws2 = ops.pack_weight_i8(case.weight.to(DEV))
+    q2_ref, ws2_ref = Q.quantize_weight_per_out_channel(case.weight)
+    assert torch.equal(q2.cpu(), q2_ref) and torch.equal(ws2.cpu(), ws2_ref)
+
+
+def test_quantize_smooth_bit_exact(golden):
+    g = golden["linear_full"]
+    case = synthetic.smoothquant_linear_case()
+    smooth = torch.tensor(g["smooth_scale"], dtype=torch.float32)
+    q = ops.quantize_smooth(case.x.to(DEV), smooth.to(DEV), g["act_scale"])
+    assert torch.equal(q.cpu(), Q.smooth_quantize_activation(case.x, smooth, g["act_scale"]))
+
+
+@pytest.mark.parametrize("m,k,n", [(177, 960, 2560), (177, 960, 320), (1, 128, 64), (3, 960, 960),
+                                   (50, 720, 960), (300, 2560, 960), (129, 12288, 960), (1024, 768, 3072)])
+def test_gemm_i8_i32_bit_exact(m, k, n):
+    g = synthetic.generator(m * 7 + k + n)
+    qx = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    acc = ops.gemm_i8_i32(qx.to(DEV), qw.to(DEV))
+    assert torch.equal(acc.cpu(), Q.int_gemm(qx, qw))
+
+
+def test_sq_linear_single_linear_workload(golden):
+    """The single-linear workload (X [177,960] with outliers, W [2560,960], alpha 0.85, p99.99 over 32 batches)."""
+    g = golden["linear_full"]
+    case = synthetic.smoothquant_linear_case()
+    smooth = torch.tensor(g["smooth_scale"], dtype=torch.float32)
+    lin = Q.W8A8Linear(case.weight, None, g["act_scale"], smooth)
+    qw, ws = ops.pack_weight_i8(case.weight.to(DEV), smooth.to(DEV))
+    y = ops.sq_linear_w8a8(case.x.to(DEV), smooth.to(DEV), g["act_scale"], qw, ws)
+    qx = lin.quantize_input(case.x)
+    y_int = Q.w8a8_int_dequant(Q.int_gemm(qx, lin.qweight), g["act_scale"], lin.weight_scale, None)
+    assert torch.equal(y.cpu(), y_int.to(torch.bfloat16))          # kernel == fp32 int-dequant form, rounded
+    y_ref = lin(case.x)                                              # reference bf16 fake-dequant
+    assert cosine(y, y_ref) >= 0.9999
+    ok, frac = bf16_ulp_close(y, y_ref, ulps=2.0, atol=2e-3)
+    assert ok, frac
+
+
+def test_sq_linear_golden_small_with_bias(golden_dir):
+    d = np.load(golden_dir / "linear_small.npz")
+    x, w, b = _bf16(d["x_bf16"]), _bf16(d["weight_bf16"]), _bf16(d["bias_bf16"])
+    a = float(d["act_scale"][0])
+    smooth = torch.from_numpy(d["smooth_scale"])
+    qw, ws = ops.pack_weight_i8(w.to(DEV), smooth.to(DEV))
+    assert torch.equal(qw.cpu(), torch.from_numpy(d["qweight"]))
+    assert torch.equal(ws.cpu(), torch.from_numpy(d["weight_scale"]))
+    qx = ops.quantize_smooth(x.to(DEV), smooth.to(DEV), a)
+    assert torch.equal(qx.cpu().float() * torch.tensor(a, dtype=torch.float32), torch.from_numpy(d["x_deq"]))
+    y = ops.sq_linear_w8a8(x.to(DEV), smooth.to(DEV), a, qw, ws, b.to(DEV))
+    y_ref = torch.from_numpy(d["y_bf16"]).view(torch.bfloat16)
+    assert cosine(y, y_ref) >= 0.9999
+    ok, frac = bf16_ulp_close(y, y_ref, ulps=2.0, atol=2e-3)
+    assert ok, frac
+
+
+# ----------------------------------------------------------------------------- W8A16 / bf16
+
+def test_w8a16_golden(golden_dir):
+    d = np.load(golden_dir / "w8a16_small.npz")
+    x, w, b = _bf16(d["x_bf16"]), _bf16(d["weight_bf16"]), _bf16(d["bias_bf16"])
+    qw, ws = ops.pack_weight_i8(w.to(DEV))
+    y = ops.w8a16_linear(x.to(DEV), qw, ws, b.to(DEV))
+    w_deq = _bf16(d["weight_deq_bf16"]).float()
+    ref = (x.float() @ w_deq.t() + b.float()).to(torch.bfloat16)
+    ok, frac = bf16_ulp_close(y, ref, ulps=1.0)
+    assert ok, frac
+    assert cosine(y, _bf16(d["y_bf16"])) >= 0.99999
+
+
+@pytest.mark.parametrize("m,k,n", [(50, 720, 960), (50, 720, 320), (50, 2048, 720), (177, 2560, 960),
+                                   (177, 320, 320), (3, 64, 16), (600, 720, 4096)])
+def test_w8a16_shapes(m, k, n):
+    g = synthetic.generator(m + 3 * k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    lin = Q.W8A16Linear(w, b)
+    qw, ws = ops.pack_weight_i8(w.to(DEV))
+    assert torch.equal(qw.cpu(), lin.qweight)
+    y = ops.w8a16_linear(x.to(DEV), qw, ws, b.to(DEV))
+    ref = (x.float() @ lin.weight.float().t() + b.float()).to(torch.bfloat16)
+    ok, frac = bf16_ulp_close(y, ref, ulps=1.0)
+    assert ok, frac
+
+
+@pytest.mark.parametrize("m,k,n", [(50, 32, 720), (50, 1440, 720), (1, 32, 960), (2048, 768, 768)])
+def test_bf16_gemm(m, k, n):
+    g = synthetic.generator(m + k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.05).to(torch.bfloat16)
+    xd, wd, bd = x.to(DEV), w.to(DEV), b.to(DEV)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_BF16, L.EPI_BF16, m, k, [ops.Seg(a=xd, b=wd, out=out, n=n, bias=bd)]))
+    ref = (x.float() @ w.float().t() + b.float()).to(torch.bfloat16)
+    ok, frac = bf16_ulp_close(out, ref, ulps=1.0)
+    assert ok, frac
+
+
+# ----------------------------------------------------------------------------- epilogues
+
+def _rand_i8(shape, g):
+    return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
+
+
+def test_epilogue_rope_qkv_segments():
+    """q/k/v as three segments with their own int8 A, weights and scales; RoPE on q and k."""
+    g = synthetic.generator(11)
+    m, k = 177, 960
+    pos = torch.arange(m, dtype=torch.int32)
+    cs = ops.rope_table(256, 10000.0, DEV)
+    segs, refs = [], []
+    for n, rope in ((960, 1), (320, 1), (320, 0)):
+        qx, qw = _rand_i8((m, k), g), _rand_i8((n, k), g)
+        ws = torch.rand(n, generator=g) * 1e-3
+        a = 0.01 + torch.rand(1, generator=g).item() * 0.01
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+        segs.append(ops.Seg(a=qx.to(DEV), b=qw.to(DEV), out=out, n=n, wscale=ws.to(DEV), act_scale=a, rope=rope))
+        y = Q.w8a8_int_dequant(Q.int_gemm(qx, qw), a, ws, None).to(torch.bfloat16)
+        if rope:
+            from oracle.model import apply_rope
+            y = apply_rope(y.view(1, m, n // 64, 64), pos.long()[None]).reshape(m, n)
+        refs.append(y)
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_ROPE, m, k, segs, rope_cs=cs, pos=pos.to(DEV), max_pos=256))
+    for s, ref in zip(segs, refs):
+        ok, frac = bf16_ulp_close(s.out, ref, ulps=1.0, atol=1e-5)
+        assert ok, frac
+
+
+def test_epilogue_resid_silu_mul_gelu_quant_euler_f32():
+    g = synthetic.generator(12)
+    m, k, n = 177, 960, 320
+    qx, qw = _rand_i8((m, k), g), _rand_i8((n, k), g)
+    ws = torch.rand(n, generator=g) * 1e-3
+    a = 0.02
+    y_int = Q.w8a8_int_dequant(Q.int_gemm(qx, qw), a, ws, None)
+    yb = y_int.to(torch.bfloat16)
+    qxd, qwd, wsd = qx.to(DEV), qw.to(DEV), ws.to(DEV)
+    # residual (in place)
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    out = res.to(DEV).clone()
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_RESID, m, k, [ops.Seg(a=qxd, b=qwd, out=out, n=n, wscale=wsd, act_scale=a)],
+                           resid=out, ldr=n))
+    ok, _ = bf16_ulp_close(out, (yb.float() + res.float()).to(torch.bfloat16), ulps=1.0)
+    assert ok
+    # SiLU-gate pair
+    qx2, qw2 = _rand_i8((m, k), g), _rand_i8((n, k), g)
+    ws2 = torch.rand(n, generator=g) * 1e-3
+    u = Q.w8a8_int_dequant(Q.int_gemm(qx2, qw2), 0.03, ws2, None).to(torch.bfloat16)
+    h = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_SILU_MUL, m, k,
+                           [ops.Seg(a=qxd, b=qwd, out=h, n=n, wscale=wsd, act_scale=a),
+                            ops.Seg(a=qx2.to(DEV), b=qw2.to(DEV), out=h, n=n, wscale=ws2.to(DEV), act_scale=0.03)],
+                           pair=True))
+    ref = (F.silu(yb) * u)
+    ok, frac = bf16_ulp_close(h, ref, ulps=1.0, atol=1e-5)
+    assert ok, frac
+    # GELU(tanh) + quantise for the next linear
+    smooth = torch.rand(n, generator=g) + 0.5
+    qout = torch.empty(m, n, dtype=torch.int8, device=DEV)
+    ybf = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_GELU_QUANT, m, k, [ops.Seg(a=qxd, b=qwd, out=ybf, n=n, wscale=wsd, act_scale=a)],
+                           q_smooth=smooth.to(DEV), q_act=0.01, qout=qout, ldq=n))
+    gref = F.gelu(yb, approximate="tanh")
+    ok, frac = bf16_ulp_close(ybf, gref, ulps=1.0, atol=1e-5)
+    assert ok, frac
+    q_from_got = Q.smooth_quantize_activation(ybf.cpu(), smooth, 0.01)
+    assert torch.equal(qout.cpu(), q_from_got)   # quantiser bit-exact given the bf16 value
+    # fp32 output and the Euler update
+    xb = torch.randn(50, 720, generator=g).to(torch.bfloat16)
+    wb = (torch.randn(32, 720, generator=g) * 0.05).to(torch.bfloat16)
+    bb = (torch.randn(32, generator=g) * 0.05).to(torch.bfloat16)
+    v_ref = xb.float() @ wb.float().t() + bb.float()
+    f32 = torch.empty(50, 32, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_BF16, L.EPI_F32, 50, 720, [ops.Seg(a=xb.to(DEV), b=wb.to(DEV), out=f32, n=32, bias=bb.to(DEV))]))
+    assert torch.allclose(f32.cpu(), v_ref, rtol=1e-5, atol=1e-5)
+    xt0 = torch.randn(50, 32, generator=g)
+    xt = xt0.to(DEV).clone()
+    xtb = torch.empty(50, 32, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_BF16, L.EPI_EULER, 50, 720, [ops.Seg(a=xb.to(DEV), b=wb.to(DEV), out=None, n=32, bias=bb.to(DEV), ldo=32)],
+                           dt=-0.1, xt=xt, xt_bf16=xtb))
+    x_ref = xt0 + (-0.1) * v_ref
+    assert torch.allclose(xt.cpu(), x_ref, rtol=1e-5, atol=1e-5)
+    assert torch.equal(xtb.cpu(), xt.cpu().to(torch.bfloat16))
+
+
+def test_row_remap_and_post_scale():
+    """Connector-style output: rows scattered into the prefix buffer, then bf16(y) * 31 rounded again."""
+    g = synthetic.generator(13)
+    m, k, n = 256, 256, 64
+    qx, qw = _rand_i8((m, k), g), _rand_i8((n, k), g)
+    ws = torch.rand(n, generator=g) * 1e-3
+    y = Q.w8a8_int_dequant(Q.int_gemm(qx, qw), 0.01, ws, None).to(torch.bfloat16)
+    ref = (y.float() * 31.0).to(torch.bfloat16)
+    buf = torch.zeros(2 * 177, n, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_BF16, m, k, [ops.Seg(a=qx.to(DEV), b=qw.to(DEV), out=buf, n=n, wscale=ws.to(DEV), act_scale=0.01)],
+                           rows_per_group=128, group_stride=177, post_scale=31.0))
+    buf = buf.cpu()
+    assert torch.equal(buf[0:128], ref[0:128])
+    assert torch.equal(buf[177:177 + 128], ref[128:256])
+    assert buf[128:177].abs().sum() == 0
+
+
+# ----------------------------------------------------------------------------- norms
+
+def test_rmsnorm_quant_three_outputs():
+    from oracle.model import rms_norm
+    g = synthetic.generator(21)
+    ch = synthetic.outlier_channels(960, 8, g)
+    x = synthetic.outlier_activations(177, 960, ch, 30.0, g)
+    w = (1.0 + 0.1 * torch.randn(960, generator=g)).to(torch.bfloat16)
+    smooths = [torch.rand(960, generator=g) * 3 + 0.2 for _ in range(3)]
+    acts = [0.02, 0.03, 0.05]
+    y, qs = ops.norm_quant(x.to(DEV), w.to(DEV), 1e-5, quants=[(s.to(DEV), a) for s, a in zip(smooths, acts)])
+    ref = rms_norm(x, w, 1e-5)
+    ok, frac = bf16_ulp_close(y, ref, ulps=1.0)
+    assert ok, frac
+    assert float((y.cpu() != ref).float().mean()) < 1e-3   # sum order may flip a rare rounding
+    for q, s, a in zip(qs, smooths, acts):
+        assert torch.equal(q.cpu(), Q.smooth_quantize_activation(y.cpu(), s, a))
+
+
+def test_layernorm_and_pixel_shuffle_quant():
+    from oracle.model import pixel_shuffle
+    g = synthetic.generator(22)
+    x = torch.randn(2 * 1024, 768, generator=g).to(torch.bfloat16)
+    w = (1.0 + 0.1 * torch.randn(768, generator=g)).to(torch.bfloat16)
+    b = (0.1 * torch.randn(768, generator=g)).to(torch.bfloat16)
+    smooth = torch.rand(768 * 16, generator=g) + 0.5
+    y, (q,) = ops.norm_quant(x.to(DEV), w.to(DEV), 1e-6, bias=b.to(DEV), quants=[(smooth.to(DEV), 0.02)],
+                             pixel_shuffle=4, ps_grid=32)
+    ref = F.layer_norm(x.float(), (768,), w.float(), b.float(), 1e-6).to(torch.bfloat16)
+    ok, frac = bf16_ulp_close(y, ref, ulps=1.0, atol=1e-5)
+    assert ok, frac
+    shuffled = pixel_shuffle(y.cpu().view(2, 1024, 768), 4).reshape(128, 768 * 16)
+    assert torch.equal(q.cpu(), Q.smooth_quantize_activation(shuffled, smooth, 0.02))
+
+
+# ----------------------------------------------------------------------------- attention
+
+def _attn_ref(q, k, v, mask, hq, hkv):
+    from oracle.model import eager_attention
+    return eager_attention(q, k, v, mask, hq, hkv)
+
+
+@pytest.mark.parametrize("b,lq,lk,hq,hkv,masked", [(1, 177, 177, 15, 5, True), (2, 50, 177, 15, 5, True),
+                                                  (1, 1024, 1024, 12, 12, False), (3, 5, 9, 15, 5, True)])
+def test_attention_single_source(b, lq, lk, hq, hkv, masked):
+    g = synthetic.generator(b * 1000 + lq + lk)
+    q = torch.randn(b, lq, hq * 64, generator=g).to(torch.bfloat16)
+    k = torch.randn(b, lk, hkv * 64, generator=g).to(torch.bfloat16)
+    v = torch.randn(b, lk, hkv * 64, generator=g).to(torch.bfloat16)
+    mask = (torch.rand(b, lq, lk, generator=g) > 0.3) if masked else None
+    if masked:
+        mask[:, 0, :] = False   # a fully masked row: uniform over all keys, as the reference
+    o = ops.attention(q.to(DEV), k.to(DEV), v.to(DEV), hq, hkv, mask=None if mask is None else mask.to(DEV))
+    ref = _attn_ref(q, k, v, mask, hq, hkv)
+    assert cosine(o, ref) >= 0.9999
+    assert float((o.cpu().float() - ref.float()).abs().max()) <= 2e-2
+
+
+def test_attention_two_sources_and_quant_out():
+    g = synthetic.generator(31)
+    b, lq, l1, l2, hq, hkv = 2, 50, 177, 50, 15, 5
+    q = torch.randn(b, lq, hq * 64, generator=g).to(torch.bfloat16)
+    k1 = torch.randn(b, l1, hkv * 64, generator=g).to(torch.bfloat16)
+    v1 = torch.randn(b, l1, hkv * 64, generator=g).to(torch.bfloat16)
+    k2 = torch.randn(b, l2, hkv * 64, generator=g).to(torch.bfloat16)
+    v2 = torch.randn(b, l2, hkv * 64, generator=g).to(torch.bfloat16)
+    mask = torch.ones(b, lq, l1 + l2, dtype=torch.bool)
+    mask[:, :, l1:] = torch.tril(torch.ones(lq, l2, dtype=torch.bool))
+    smooth = torch.rand(hq * 64, generator=g) + 0.5
+    o, qo = ops.attention(q.to(DEV), k1.to(DEV), v1.to(DEV), hq, hkv, mask=mask.to(DEV), k2=k2.to(DEV), v2=v2.to(DEV),
+                          qo_smooth=smooth.to(DEV), qo_act=0.01)
+    ref = _attn_ref(q, torch.cat([k1, k2], 1), torch.cat([v1, v2], 1), mask, hq, hkv)
+    assert cosine(o, ref) >= 0.9999
+    qo_ref = Q.smooth_quantize_activation(o.cpu().reshape(-1, hq * 64), smooth, 0.01).reshape(b, lq, -1)
+    assert torch.equal(qo.cpu(), qo_ref)
+
+
+# ----------------------------------------------------------------------------- RoPE / layout
+
+def test_rope_layout_against_reference_kat(golden_dir):
+    """validate_fused_rope_layout_math.py inputs (seed 1000, L = 177) through the plugin-semantics kernel."""
+    torch.manual_seed(1000)
+    q_raw = torch.randn(1, 177, 15 * 64)
+    k_raw = torch.randn(1, 177, 5 * 64)
+    d = np.load(golden_dir / "rope_kat.npz")
+    rows = torch.from_numpy(d["rows"])
+    qb, kb = q_raw.to(torch.bfloat16), k_raw.to(torch.bfloat16)
+    pos = torch.arange(177, dtype=torch.int32)[None]
+    q_out, k_out = ops.rope_layout(qb.to(DEV), kb.to(DEV), pos.to(DEV), 15, 5, 10000.0)
+    q_rot = q_out.cpu().float().transpose(1, 2)[0, rows]                 # [rows, 15, 64]
+    k_rot = k_out.cpu().float().permute(0, 3, 1, 2)[0, rows][:, ::3]     # [rows, 5, 64] (undo GQA expansion)
+    # the kernel rotates bf16 inputs: compare within bf16 rounding of the fp32 reference KAT values
+    assert cosine(q_rot, torch.from_numpy(d["q_rot"])) >= 0.9999
+    assert cosine(k_rot, torch.from_numpy(d["k_rot"])) >= 0.9999
+    assert float((q_rot - torch.from_numpy(d["q_rot"])).abs().max()) < 0.05
+    # GQA expansion: the three query heads of each kv head hold identical keys
+    kk = k_out.cpu()
+    for j in range(5):
+        assert torch.equal(kk[0, 3 * j], kk[0, 3 * j + 1]) and torch.equal(kk[0, 3 * j], kk[0, 3 * j + 2])
