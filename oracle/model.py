@@ -108,3 +108,209 @@ def sinusoidal_time_embedding(t: torch.Tensor, dim: int, min_period: float, max_
     scaling = 1.0 / period * 2 * math.pi
     sin_input = scaling[None, :] * t.to(torch.float64)[:, None]
     return torch.cat([torch.sin(sin_input), torch.cos(sin_input)], dim=1)
+
+
+# ----------------------------------------------------------------------------- full core
+
+class OracleSmolVLA:
+    """sample_actions of SmolVLA on the CPU.
+
+    mode = "quant": the deployed recipe -- SmoothQuant W8A8 (oracle.quant.W8A8Linear) on the vision tower,
+                    connector and text q/k/v/o/gate/up; W8A16 on text down_proj and every expert linear;
+                    bf16 state / action / time projections.
+    mode = "bf16":  every linear in bf16 (the unquantised model, used for calibration).
+    ``collector(module, x)`` (optional) sees the input of every W8A8-recipe linear, which is what the
+    reference's PerChannelLinearInputCollector hooks (calibrate_smolvla_activation_channel_scales.py:62-84).
+    """
+
+    def __init__(self, cfg, weights: dict[str, torch.Tensor], scales: dict | None = None, mode: str = "quant"):
+        from smolvla_mujoco_libero_b200.weights import linear_specs
+        from . import quant as Q
+
+        self.cfg, self.w, self.mode = cfg, weights, mode
+        self.lin = {}
+        for name, _n, k, has_bias, q in linear_specs(cfg):
+            wt, b = weights[f"{name}.weight"], weights.get(f"{name}.bias") if has_bias else None
+            if mode == "bf16" or q == "bf16":
+                self.lin[name] = Q.Bf16Linear(wt, b)
+            elif q == "w8a16":
+                self.lin[name] = Q.W8A16Linear(wt, b)
+            else:
+                if scales is None or name not in scales:
+                    raise KeyError(f"missing calibrated activation scale for quantized module: {name}")
+                entry = Q.select_activation_scale_for_linear(scales[name], k)
+                self.lin[name] = Q.W8A8Linear(wt, b, entry["scale"], torch.tensor(entry["smooth_scale"]))
+        self.collector = None
+
+    # -- helpers
+    def _linear(self, name: str, x: torch.Tensor) -> torch.Tensor:
+        if self.collector is not None and self.mode == "bf16":
+            from smolvla_mujoco_libero_b200.weights import w8a8_modules
+            if not hasattr(self, "_w8a8"):
+                self._w8a8 = set(w8a8_modules(self.cfg))
+            if name in self._w8a8:
+                self.collector(name, x)
+        return self.lin[name](x)
+
+    # -- vision
+    def embed_image(self, image: torch.Tensor) -> torch.Tensor:
+        """SigLIP + pixel-shuffle connector: fp32 [B,3,S,S] -> bf16 [B, n_img_tokens, hidden]."""
+        from smolvla_mujoco_libero_b200.config import CONNECTOR, VISION
+        c, w = self.cfg, self.w
+        pe = f"{VISION}.embeddings"
+        x = F.conv2d(image.to(torch.bfloat16), w[f"{pe}.patch_embedding.weight"], w[f"{pe}.patch_embedding.bias"],
+                     stride=c.patch)
+        h = x.flatten(2).transpose(1, 2) + w[f"{pe}.position_embedding.weight"][None]
+        b = h.shape[0]
+        for i in range(c.vis_layers):
+            p = f"{VISION}.encoder.layers.{i}"
+            r = h
+            y = layer_norm(h, w[f"{p}.layer_norm1.weight"], w[f"{p}.layer_norm1.bias"], c.vis_eps)
+            q = self._linear(f"{p}.self_attn.q_proj", y)
+            k = self._linear(f"{p}.self_attn.k_proj", y)
+            v = self._linear(f"{p}.self_attn.v_proj", y)
+            ctx = eager_attention(q, k, v, None, c.vis_heads, c.vis_heads)
+            h = r + self._linear(f"{p}.self_attn.out_proj", ctx)
+            r = h
+            y = layer_norm(h, w[f"{p}.layer_norm2.weight"], w[f"{p}.layer_norm2.bias"], c.vis_eps)
+            f1 = F.gelu(self._linear(f"{p}.mlp.fc1", y), approximate="tanh")
+            h = r + self._linear(f"{p}.mlp.fc2", f1)
+        h = layer_norm(h, w[f"{VISION}.post_layernorm.weight"], w[f"{VISION}.post_layernorm.bias"], c.vis_eps)
+        h = pixel_shuffle(h, c.scale_factor)
+        return self._linear(CONNECTOR, h)
+
+    # -- prefix
+    def embed_prefix(self, images, img_masks, lang_tokens, lang_masks, state):
+        """deploy/diagnose_3_4_numeric_baseline.py:72-115 (image embeddings from embed_image)."""
+        from smolvla_mujoco_libero_b200.config import TEXT
+        c = self.cfg
+        embs, pads, att = [], [], []
+        for img, m in zip(images, img_masks):
+            e = self.embed_image(img)
+            e = e * torch.tensor(e.shape[-1] ** 0.5, dtype=e.dtype)
+            embs.append(e)
+            pads.append(m[:, None].expand(e.shape[0], e.shape[1]))
+            att += [0] * e.shape[1]
+        lang = F.embedding(lang_tokens, self.w[f"{TEXT}.embed_tokens.weight"])
+        lang = lang * math.sqrt(lang.shape[-1])
+        embs.append(lang)
+        pads.append(lang_masks)
+        att += [0] * lang.shape[1]
+        st = self.lin["model.state_proj"](state.to(torch.bfloat16))[:, None, :]
+        embs.append(st)
+        pads.append(torch.ones(st.shape[0], 1, dtype=torch.bool))
+        att += [1]
+        prefix = torch.cat(embs, dim=1)
+        pad = torch.cat(pads, dim=1)
+        att_t = torch.tensor(att, dtype=torch.bool)[None].expand(prefix.shape[0], -1)
+        return prefix, pad, att_t
+
+    def _mlp(self, p: str, y: torch.Tensor) -> torch.Tensor:
+        return self._linear(f"{p}.mlp.down_proj",
+                            F.silu(self._linear(f"{p}.mlp.gate_proj", y)) * self._linear(f"{p}.mlp.up_proj", y))
+
+    def prefix_forward(self, prefix, pad, att):
+        """VLM layers with KV fill (lerobot forward_attn_layer, fill_kv_cache=True)."""
+        from smolvla_mujoco_libero_b200.config import TEXT
+        c, w = self.cfg, self.w
+        mask = make_att_2d_masks(pad, att)
+        pos = torch.cumsum(pad.to(torch.int64), dim=1) - 1
+        b, L, _ = prefix.shape
+        h = prefix
+        cache = []
+        for i in range(c.text_layers):
+            p = f"{TEXT}.layers.{i}"
+            y = rms_norm(h, w[f"{p}.input_layernorm.weight"], c.rms_eps)
+            q = self._linear(f"{p}.self_attn.q_proj", y).view(b, L, c.heads, c.head_dim)
+            k = self._linear(f"{p}.self_attn.k_proj", y).view(b, L, c.kv_heads, c.head_dim)
+            v = self._linear(f"{p}.self_attn.v_proj", y)
+            q = apply_rope(q, pos, c.rope_wavelength).reshape(b, L, -1)
+            k = apply_rope(k, pos, c.rope_wavelength).reshape(b, L, -1)
+            cache.append((k, v))
+            ctx = eager_attention(q, k, v, mask, c.heads, c.kv_heads)
+            h = h + self._linear(f"{p}.self_attn.o_proj", ctx)
+            y = rms_norm(h, w[f"{p}.post_attention_layernorm.weight"], c.rms_eps)
+            h = h + self._mlp(p, y)
+        prefix_out = rms_norm(h, w[f"{TEXT}.norm.weight"], c.rms_eps)
+        return cache, prefix_out, mask, pos
+
+    # -- suffix / expert
+    def embed_suffix(self, x_t: torch.Tensor, t: float) -> torch.Tensor:
+        c = self.cfg
+        a = self.lin["model.action_in_proj"](x_t.to(torch.bfloat16))
+        tt = torch.tensor([t], dtype=torch.float32).expand(x_t.shape[0])
+        te = sinusoidal_time_embedding(tt, c.expert_hidden, c.min_period, c.max_period).to(a.dtype)
+        at = torch.cat([a, te[:, None, :].expand_as(a)], dim=2)
+        at = F.silu(self.lin["model.action_time_mlp_in"](at))
+        return self.lin["model.action_time_mlp_out"](at)
+
+    def denoise_step(self, cache, pad, x_t: torch.Tensor, t: float) -> torch.Tensor:
+        from smolvla_mujoco_libero_b200.config import EXPERT
+        c, w = self.cfg, self.w
+        h = self.embed_suffix(x_t, t)
+        b, S, _ = h.shape
+        Lp = pad.shape[1]
+        n_valid = pad.to(torch.int64).sum(-1, keepdim=True)
+        spos = n_valid + torch.arange(S)[None]
+        cpos = torch.arange(S)[None].expand(b, S)
+        self_mask = torch.cat([pad[:, None, :].expand(b, S, Lp), torch.tril(torch.ones(S, S, dtype=torch.bool))[None].expand(b, S, S)], dim=2)
+        cross_mask = pad[:, None, :].expand(b, S, Lp)
+        for i in range(c.expert_layers):
+            p = f"{EXPERT}.layers.{i}"
+            y = rms_norm(h, w[f"{p}.input_layernorm.weight"], c.rms_eps)
+            q = self._linear(f"{p}.self_attn.q_proj", y).view(b, S, c.heads, c.head_dim)
+            kp, vp = cache[i]
+            if c.is_cross_layer(i):
+                q = apply_rope(q, cpos, c.rope_wavelength).reshape(b, S, -1)
+                k = self._linear(f"{p}.self_attn.k_proj", kp)
+                v = self._linear(f"{p}.self_attn.v_proj", vp)
+                ctx = eager_attention(q, k, v, cross_mask, c.heads, c.kv_heads)
+            else:
+                q = apply_rope(q, spos, c.rope_wavelength).reshape(b, S, -1)
+                k = self._linear(f"{p}.self_attn.k_proj", y).view(b, S, c.kv_heads, c.head_dim)
+                k = apply_rope(k, spos, c.rope_wavelength).reshape(b, S, -1)
+                v = self._linear(f"{p}.self_attn.v_proj", y)
+                ctx = eager_attention(q, torch.cat([kp, k], 1), torch.cat([vp, v], 1), self_mask, c.heads, c.kv_heads)
+            h = h + self._linear(f"{p}.self_attn.o_proj", ctx)
+            y = rms_norm(h, w[f"{p}.post_attention_layernorm.weight"], c.rms_eps)
+            h = h + self._mlp(p, y)
+        out = rms_norm(h, w[f"{EXPERT}.norm.weight"], c.rms_eps)
+        wo = self.lin["model.action_out_proj"]
+        return out.float() @ wo.weight.float().t() + wo.bias.float()
+
+    @torch.no_grad()
+    def sample_actions(self, images, img_masks, lang_tokens, lang_masks, state, noise, taps: dict | None = None):
+        """Returns the fp32 chunk [B, chunk, max_action_dim] (callers slice the first action_dim)."""
+        c = self.cfg
+        prefix, pad, att = self.embed_prefix(images, img_masks, lang_tokens, lang_masks, state)
+        cache, prefix_out, _, _ = self.prefix_forward(prefix, pad, att)
+        if taps is not None:
+            taps["prefix_embs"] = prefix
+            taps["prefix_out"] = prefix_out
+            taps["kv"] = cache
+        dt = -1.0 / c.num_steps
+        x_t = noise.to(torch.float32)
+        for step in range(c.num_steps):
+            t = float(torch.tensor(1.0 + step * dt, dtype=torch.float32))
+            v_t = self.denoise_step(cache, pad, x_t, t)
+            x_t = x_t + dt * v_t
+            if taps is not None:
+                taps[f"v_t_step_{step:02d}"] = v_t
+                taps[f"x_t_step_{step:02d}"] = x_t
+        return x_t
+
+
+def calibrate(cfg, weights, observations, percentile: float | None = None, alpha: float | None = None):
+    """Reference calibration semantics on the bf16 model: per-call per-channel percentile of every W8A8-recipe
+    linear input, elementwise max over calls, then SmoothQuant build_entry -> scale JSON dict."""
+    from . import quant as Q
+    percentile = cfg.percentile if percentile is None else percentile
+    alpha = cfg.alpha if alpha is None else alpha
+    m = OracleSmolVLA(cfg, weights, mode="bf16")
+    col = Q.PerChannelCollector(percentile)
+    m.collector = lambda name, x: [col.observe(name, x[i:i + 1]) for i in range(x.shape[0])]
+    for obs in observations:
+        m.sample_actions(obs.images, obs.img_masks, obs.lang_tokens, obs.lang_masks, obs.state, obs.noise)
+    rows = col.rows()
+    entries = [Q.build_smoothquant_entry(r, weights[f"{r['module']}.weight"], alpha) for r in rows]
+    return {"smoothquant_alpha": alpha, "linear_call_scales": entries}
