@@ -1,0 +1,366 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized SmolVLA sample_actions path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch 64] [--impl svla|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...          (one process per GPU)
+
+Metric: action chunks/s at batch 64 independent synthetic observations per GPU (whole job, weak scaling,
+no collective on the data path), with batch-1 sample_actions p50 latency reported beside it.  A "step" is
+one sample_actions call at batch 64 (SigLIP on 128 images, 16 text layers, 10 flow steps x 16 expert
+layers) replayed as one CUDA graph; inputs and activations (> 2 GB) exceed L2, so no flush is needed.
+
+--impl reference times the CPU oracle (restatement of the reference's fake-quant path) on the host cores
+on rank 0 only: each step is one observation of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "action chunks/s at bs64 per GPU (sample_actions, SmolVLA SmoothQuant W8A8/W8A16)"
+UNIT = "chunks/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--impl", default="svla", choices=["svla", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--calib-samples", type=int, default=4)
+    ap.add_argument("--b1-iters", type=int, default=30)
+    ap.add_argument("--cpu-iters", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, local_index: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        self.idx = ids[local_index] if local_index < len(ids) else str(local_index)
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_observations(cfg, batch, seed):
+    from smolvla_mujoco_libero_b200 import synthetic
+    return synthetic.observations(batch, seed=seed, image_size=cfg.image_size, n_tokens=cfg.n_lang)
+
+
+def cpu_baseline(cfg, state, scales_json, iters: int):
+    """The oracle (CPU restatement of the reference fake-quant path) on the host cores, batch 1."""
+    from oracle import quant as Q
+    from oracle.model import OracleSmolVLA
+    torch.set_num_threads(os.cpu_count() or 1)
+    m = OracleSmolVLA(cfg, state, Q.load_activation_scales_by_module(scales_json))
+    o = make_observations(cfg, 1, 10_000)
+    times = []
+    for i in range(iters + 1):
+        t0 = time.perf_counter()
+        m.sample_actions(o.images, o.img_masks, o.lang_tokens, o.lang_masks, o.state, o.noise)
+        if i > 0:
+            times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": 1.0 / med, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{iters} timed batch-1 sample_actions calls after 1 warm-up (the bs64 workload per "
+                      f"observation), median {med:.2f} s/chunk, fp32/bf16 torch CPU oracle"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    from smolvla_mujoco_libero_b200.calibrate import calibrate
+    from smolvla_mujoco_libero_b200.config import BENCH
+    from smolvla_mujoco_libero_b200.weights import random_weights
+    from oracle import quant as Q
+    from oracle.model import OracleSmolVLA, calibrate as oracle_calibrate
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = BENCH
+    state = random_weights(cfg, args.seed)
+    js = oracle_calibrate(cfg, state, [make_observations(cfg, 1, 100 + i) for i in range(2)])
+    m = OracleSmolVLA(cfg, state, Q.load_activation_scales_by_module(js))
+    o = make_observations(cfg, 1, 10_000)
+    for _ in range(args.warmup):
+        m.sample_actions(o.images, o.img_masks, o.lang_tokens, o.lang_masks, o.state, o.noise)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.sample_actions(o.images, o.img_masks, o.lang_tokens, o.lang_masks, o.state, o.noise)
+    el = time.perf_counter() - t0
+    value = args.steps / el
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8/bf16", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "sample_actions, SmolVLA SigLIP-12x768 + text 16x960 + expert 16x720, "
+                                   "10 flow steps; each step one batch-1 observation on the host cores"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": "one batch-1 observation per step (bounded sample of the bs64 workload)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def time_kernel(fn, iters=20, warm=3):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    from smolvla_mujoco_libero_b200 import _lib as L
+    from smolvla_mujoco_libero_b200.calibrate import calibrate, load_scale_json
+    from smolvla_mujoco_libero_b200.config import BENCH
+    from smolvla_mujoco_libero_b200.model import DeviceWeights, SmolVLARunner
+    from smolvla_mujoco_libero_b200.weights import random_weights
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    cfg = BENCH
+    B = args.batch
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
+
+    state = random_weights(cfg, args.seed)
+    js = calibrate(cfg, state, [make_observations(cfg, 1, 100 + i) for i in range(args.calib_samples)], device=dev)
+    weights = DeviceWeights(cfg, state, load_scale_json(js), device=dev)
+
+    # ---------------- batch-64 throughput (inputs resident in HBM)
+    runner = SmolVLARunner(weights, B)
+    obs = make_observations(cfg, B, 1_000_000 + rank * B)
+    dev_in = ([im.to(dev) for im in obs.images], [m.to(dev) for m in obs.img_masks], obs.lang_tokens.to(dev),
+              obs.lang_masks.to(dev), obs.state.to(dev), obs.noise.to(dev))
+    runner.load_inputs(*dev_in)
+    runner.capture()
+    for _ in range(args.warmup):
+        runner.run()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        runner.run()
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert torch.isfinite(runner.actions()).all(), "non-finite actions"
+    assert L.device_error() == 0, "device error word set"
+    value = B * world * args.steps / (ms / 1e3)
+    launches = runner.n_launches * args.steps
+
+    # ---------------- end to end through the public call with host (pinned) buffers
+    host = ([im.pin_memory() for im in obs.images], [m.pin_memory() for m in obs.img_masks],
+            obs.lang_tokens.pin_memory(), obs.lang_masks.pin_memory(), obs.state.pin_memory(), obs.noise.pin_memory())
+    out_host = torch.empty(B, cfg.chunk, cfg.action_dim, dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (*host[0], *host[1], *host[2:]))
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        runner.load_inputs(*host)
+        runner.run()
+        out_host.copy_(runner.actions()[:, :, :cfg.action_dim], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = B * world * args.steps / (e2e_ms / 1e3)
+
+    # ---------------- batch-1 latency (p50 over individually timed calls)
+    r1 = SmolVLARunner(weights, 1)
+    o1 = make_observations(cfg, 1, 2_000_000 + rank)
+    r1.load_inputs([im.to(dev) for im in o1.images], [m.to(dev) for m in o1.img_masks], o1.lang_tokens.to(dev),
+                   o1.lang_masks.to(dev), o1.state.to(dev), o1.noise.to(dev))
+    r1.capture()
+    lat = []
+    for i in range(args.b1_iters + 5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        r1.run()
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 5:
+            lat.append(a.elapsed_time(b))
+    lat.sort()
+    p50 = lat[len(lat) // 2]
+    p95 = lat[min(len(lat) - 1, int(round(0.95 * (len(lat) - 1))))]
+
+    # ---------------- roofline of the dominant kernel, timed live (same launch as in the graph)
+    roof = dominant_kernel_roofline(runner, peaks)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8/bf16", "data": "synthetic (seeded observations, random-init weights, GPU-calibrated SmoothQuant scales)",
+        "config": {"workload": f"sample_actions bs{B} per GPU: SigLIP 12x768 on {B * cfg.n_cams} images 512px + connector, "
+                               f"text 16x960 (L=177), expert 16x720 x 10 flow steps",
+                   "global_batch": B * world, "seq_len": cfg.prefix_len, "parallelism": f"dp{world} (replicas, no collectives)",
+                   "l2": "inputs+activations > L2 (no flush needed)", "cuda_graph": True},
+        "batch1_p50_ms": p50, "batch1_p95_ms": p95,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "roofline": roof,
+        "clocks": clk,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, state, js, args.cpu_iters)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def measure_int8_peak(dev) -> float | None:
+    """Dense int8 tensor throughput of the library GEMM (torch._int_mm, cuBLASLt) on 8192^3: a measurement
+    reference for the roofline only, never on the product path."""
+    try:
+        a = torch.randint(-128, 127, (8192, 8192), dtype=torch.int8, device=dev)
+        b = torch.randint(-128, 127, (8192, 8192), dtype=torch.int8, device=dev)
+        ms = time_kernel(lambda: torch._int_mm(a, b), iters=10)
+        return 2 * 8192 ** 3 / (ms / 1e3) / 1e12
+    except Exception:  # noqa: BLE001 - any failure just means "no measured int8 peak"
+        return None
+
+
+def dominant_kernel_roofline(runner, peaks):
+    """Time the largest W8A8 GEMM launch of the step (SigLIP fc1 / fc2 class) on its own with CUDA events."""
+    from smolvla_mujoco_libero_b200 import _lib as L
+    best = None
+    for fn, a in runner.launches:
+        if fn is L.lib().svla_gemm:
+            d = a[0]
+            n = sum(d.seg[i].n for i in range(d.nseg))
+            flops = 2.0 * d.m * n * d.k * (2 if d.pair else 1)
+            if best is None or flops > best[0]:
+                best = (flops, d)
+    flops, d = best
+    stream = torch.cuda.current_stream().cuda_stream
+    import ctypes
+    fn = L.lib().svla_gemm
+    ms = time_kernel(lambda: fn(ctypes.byref(d), stream), iters=20)
+    achieved = flops / (ms / 1e3) / 1e12
+    int8 = d.kind == L.KIND_I8
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    if int8:
+        lib_int8 = measure_int8_peak(torch.device("cuda", torch.cuda.current_device()))
+        if lib_int8 is not None and lib_int8 >= bf16:
+            peak, src = lib_int8, "measured in this run: torch._int_mm (cuBLASLt) int8 8192^3, dense"
+        else:
+            peak, src = 2 * bf16, f"provisional 2 x MEASURED_PEAKS bf16 (cuBLASLt int8 measured {lib_int8})"
+    else:
+        peak, src = bf16, "MEASURED_PEAKS.json bf16_tflops (burst)"
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": None, "kernel": f"gemm_sm100 kind={'i8' if int8 else d.kind} M={d.m} N={sum(d.seg[i].n for i in range(d.nseg))} K={d.k}",
+            "ms_per_launch": ms, "peak_source": src}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

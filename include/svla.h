@@ -38,7 +38,7 @@ typedef struct CUstream_st* svla_stream_t; /* == cudaStream_t */
 #define SVLA_EPI_ROPE 2      /* out = bf16(rotate_half_rope(bf16(v), pos[m])) on segments with rope = 1 */
 #define SVLA_EPI_RESID 3     /* out = bf16(bf16(v) + resid) */
 #define SVLA_EPI_SILU_MUL 4  /* pair: out = bf16(bf16(silu(bf16(v_gate))) * bf16(v_up)) */
-#define SVLA_EPI_GELU_QUANT 5 /* g = bf16(gelu_tanh(bf16(v))); qout = round((g / q_smooth[n]) / q_act) */
+#define SVLA_EPI_GELU_QUANT 5 /* g = bf16(gelu_tanh(bf16(v))); out = g (if set); qout = round((g / q_smooth[n]) / q_act) (if set) */
 #define SVLA_EPI_EULER 6     /* x_t[m, n] += dt * v (fp32), x_t_bf16 = bf16(x_t) */
 #define SVLA_EPI_SILU 7      /* out = bf16(silu(bf16(v))) */
 #define SVLA_EPI_F32 8       /* out = v in fp32 */
@@ -155,7 +155,7 @@ typedef struct svla_norm_desc {
   int32_t ldq;
   const float* smooth[3];
   float act[3];
-  int32_t pixel_shuffle;  /* 0, or the SmolVLM connector shuffle factor (int8 outputs only) */
+  int32_t pixel_shuffle;  /* 0, or the SmolVLM connector shuffle factor (remaps y and the int8 outputs) */
   int32_t ps_grid;        /* tokens per side of the input grid */
 } svla_norm_desc;
 

@@ -27,7 +27,7 @@ enum class Epi : int {
   Rope = 2,       // Bf16, then rotate-half RoPE on segments flagged rope (64-column heads)
   Resid = 3,      // out = bf16(bf16(y) + resid)
   SiluMul = 4,    // pairs: out = bf16(bf16(silu(bf16(g))) * bf16(u))
-  GeluQuant = 5,  // g = bf16(gelu_tanh(bf16(y))); qout = smooth_quant(g) (+ optional bf16 out)
+  GeluQuant = 5,  // g = bf16(gelu_tanh(bf16(y))); optional qout = smooth_quant(g), optional bf16 out
   Euler = 6,      // v = acc + b (fp32); x_t += dt * v; x_t_bf16 = bf16(x_t)
   SiluBf16 = 7,   // out = bf16(silu(bf16(y)))
   F32 = 8,        // out = v in fp32
@@ -393,14 +393,15 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], __bfloat162float(rs[j]));
           } else if constexpr (EPI == Epi::GeluQuant) {
-            int8_t qv[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              v[j] = bf16_round(gelu_tanh_f(v[j]));
-              qv[j] = smooth_quant(v[j], args.q_smooth[nb + j], args.q_act);
+            for (int j = 0; j < 16; ++j) v[j] = bf16_round(gelu_tanh_f(v[j]));
+            if (args.qout != nullptr) {
+              int8_t qv[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) qv[j] = smooth_quant(v[j], args.q_smooth[nb + j], args.q_act);
+              *reinterpret_cast<int4*>(args.qout + static_cast<size_t>(orow) * args.ldq + nb) =
+                  *reinterpret_cast<int4*>(qv);
             }
-            *reinterpret_cast<int4*>(args.qout + static_cast<size_t>(orow) * args.ldq + nb) =
-                *reinterpret_cast<int4*>(qv);
             if (sg.out == nullptr) continue;
           } else if constexpr (EPI == Epi::Bf16) {
             if (args.post_scale != 0.0f) {

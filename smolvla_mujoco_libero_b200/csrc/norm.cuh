@@ -10,7 +10,7 @@
 // of q/k/v (or gate/up) that W8A8Linear.forward applies (deploy/linear_only_quant.py:104-116).
 // The smooth divide runs on the bf16-rounded y, exactly as the unfused reference does.
 //
-// Optional pixel-shuffle remap of the int8 output (SmolVLM connector, scale 4 on a 32x32 grid):
+// Optional pixel-shuffle remap of the outputs (SmolVLM connector, scale 4 on a 32x32 grid):
 // input token t = hh*32 + ww of image i goes to output row i*64 + (hh/4)*8 + ww/4, columns
 // ((hh%4)*4 + ww%4) * K ..., with the smooth vector indexed by the output column.
 #pragma once
@@ -121,7 +121,8 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) 
         __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * u], y[2 * u + 1]);
         pk[u] = *reinterpret_cast<uint32_t*>(&h);
       }
-      *reinterpret_cast<int4*>(a.y + static_cast<size_t>(m) * a.ldy + k) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<int4*>(a.y + static_cast<size_t>(qrow) * a.ldy + qcol0 + k) =
+          make_int4(pk[0], pk[1], pk[2], pk[3]);
     }
     for (int qi = 0; qi < a.nq; ++qi) {
       const int col = qcol0 + k;

@@ -133,9 +133,9 @@ int32_t dispatch_epi(Epi e, const GemmArgs& args, dim3 grid, cudaStream_t st) {
       case Epi::F32: return launch_gemm_inst<K, BN, 1, Epi::F32>(args, grid, st);
       default: break;
     }
+    if (e == Epi::GeluQuant) return launch_gemm_inst<K, BN, 1, Epi::GeluQuant>(args, grid, st);
     if constexpr (K == Kind::I8) {
       if (e == Epi::I32) return launch_gemm_inst<K, BN, 1, Epi::I32>(args, grid, st);
-      if (e == Epi::GeluQuant) return launch_gemm_inst<K, BN, 1, Epi::GeluQuant>(args, grid, st);
     }
     if constexpr (K == Kind::BF16) {
       if (e == Epi::SiluBf16) return launch_gemm_inst<K, BN, 1, Epi::SiluBf16>(args, grid, st);
@@ -242,7 +242,9 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   args.err = device_error_ptr();
   if (epi == Epi::Resid && !d->resid) return fail(SVLA_ERR_ARG, "RESID needs a residual");
   if (epi == Epi::Rope && (!d->rope_cs || !d->pos || d->max_pos <= 0)) return fail(SVLA_ERR_ARG, "ROPE needs rope_cs/pos");
-  if (epi == Epi::GeluQuant && (!d->q_smooth || !d->qout || d->q_act <= 0.f)) return fail(SVLA_ERR_ARG, "GELU_QUANT needs q_smooth/qout/q_act");
+  if (epi == Epi::GeluQuant && d->qout && (!d->q_smooth || d->q_act <= 0.f))
+    return fail(SVLA_ERR_ARG, "GELU_QUANT with qout needs q_smooth and q_act > 0");
+  if (epi == Epi::GeluQuant && !d->qout && !d->seg[0].out) return fail(SVLA_ERR_ARG, "GELU_QUANT needs qout or out");
   if (epi == Epi::Euler && (!d->xt || !d->xt_bf16)) return fail(SVLA_ERR_ARG, "EULER needs xt/xt_bf16");
   dim3 grid((d->m + 127) / 128, tiles);
   switch (kind) {
