@@ -75,9 +75,7 @@ def calibrate(cfg: SmolVLAConfig, state: dict[str, torch.Tensor], observations: 
         b = obs.state.shape[0]
         if runner is None or runner.B != b:
             runner = SmolVLARunner(dw, b, mode="bf16")
-        runner(obs.images, obs.img_masks, obs.lang_tokens, obs.lang_masks, obs.state, obs.noise)
-        torch.cuda.synchronize()
-        for mods, buf in runner._taps:
+        def observe(mods, buf, runner=runner, b=b):
             rows = buf.shape[0]
             if buf is runner.conn_in:
                 per = cfg.n_img_tokens
@@ -89,6 +87,9 @@ def calibrate(cfg: SmolVLAConfig, state: dict[str, torch.Tensor], observations: 
                 chunk = buf[start:start + per]
                 for m in mods:
                     stats.observe(m, chunk)
+
+        runner(obs.images, obs.img_masks, obs.lang_tokens, obs.lang_masks, obs.state, obs.noise, observer=observe)
+    torch.cuda.synchronize()
     specs = {name: (n, k) for name, n, k, _, q in linear_specs(cfg) if q == "w8a8"}
     entries = []
     for module, c in stats.calls.items():

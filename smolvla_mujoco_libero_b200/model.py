@@ -219,6 +219,11 @@ class SmolVLARunner:
     def _add(self, fn, *args):
         self.launches.append((fn, args))
 
+    def _tap(self, mods, buf):
+        """A point in the launch list where ``buf`` holds the input of ``mods`` (bf16 mode / debug taps);
+        the observer passed to run() sees it in stream order, before later launches reuse the buffer."""
+        self.launches.append((_TAP, (list(mods), buf)))
+
     def _gemm(self, kind, epi, m, k, segs, **kw):
         d = ops.gemm_desc(kind, epi, m, k, segs, **kw)
         self._keep.append(segs)
@@ -257,9 +262,9 @@ class SmolVLARunner:
         else:
             target = y if y is not None else outs[0]
             d.y, d.ldy = target.data_ptr(), target.stride(0)
-            if tap is not None:
-                self._taps.append((tap, target))
         self._add(L.lib().svla_norm_quant, d)
+        if tap is not None and not (self.mode == "quant" and quant_mods):
+            self._tap(tap, target)
 
     def _attn(self, q, k1, v1, lq, hq, hkv, mask=None, k2=None, v2=None, out_mod=None, out=None, tap=None):
         """attention; in quant mode with out_mod the context is quantised for that W8A8 linear.
@@ -279,15 +284,15 @@ class SmolVLARunner:
                                    qo_smooth=p.smooth, qo_act=p.act_scale)
         else:
             d = ops.attention_desc(qv, k1v, v1v, B, lq, hq, hkv, mask=mask, k2=k2v, v2=v2v, o=ov)
-            if tap is not None:
-                self._taps.append((tap, out))
         self._add(L.lib().svla_attention, d)
+        if tap is not None and not (self.mode == "quant" and out_mod is not None):
+            self._tap(tap, out)
 
     # ------------------------------------------------------------------ the call
     def _build(self):
         c, B, w = self.cfg, self.B, self.w
         lib = L.lib()
-        self._keep, self._taps = [], []
+        self._keep = []
         q_mode = self.mode == "quant"
         Lp, S, H, E = c.prefix_len, c.chunk, c.hidden, c.expert_hidden
         NI = B * c.n_cams
@@ -329,7 +334,7 @@ class SmolVLARunner:
             else:
                 self._gemm(L.KIND_BF16, L.EPI_GELU_QUANT, NV, c.vis_hidden,
                            [self._linear_seg(f"{p}.mlp.fc1", self.v_fc1_in, self.v_fc2_in)])
-                self._taps.append(([f"{p}.mlp.fc2"], self.v_fc2_in))
+                self._tap([f"{p}.mlp.fc2"], self.v_fc2_in)
             self._gemm(self._kind(f"{p}.mlp.fc2"), L.EPI_RESID, NV, c.vis_mlp,
                        [self._linear_seg(f"{p}.mlp.fc2", self.v_fc2_in, self.vh)], resid=self.vh, ldr=c.vis_hidden)
         # post LayerNorm + pixel shuffle + connector quantisation
@@ -349,7 +354,7 @@ class SmolVLARunner:
                    [self._linear_seg("model.state_proj", self.state_bf, self.h)], rows_per_group=1,
                    group_stride=Lp, row_offset=Lp - 1)
         if self.debug:
-            self._taps.append((["prefix_embs"], self.h))
+            self._tap(["prefix_embs"], self.h)
         # ---------------- text layers (KV fill)
         for i in range(c.text_layers):
             p = f"{TEXT}.layers.{i}"
@@ -377,7 +382,7 @@ class SmolVLARunner:
                        [self._linear_seg(f"{p}.mlp.down_proj", self.t_mlp, self.h)], resid=self.h, ldr=H)
         if self.debug:
             self._norm(self.h, w.t[f"{TEXT}.norm.weight"], c.rms_eps, y=self.prefix_out)
-            self._taps.append((["prefix_out"], self.prefix_out))
+            self._tap(["prefix_out"], self.prefix_out)
         # ---------------- cross-attention K/V of the cached prefix (step-invariant)
         for i in self.ck:
             p = f"{EXPERT}.layers.{i}.self_attn"
@@ -428,11 +433,16 @@ class SmolVLARunner:
     # ------------------------------------------------------------------ execution
     @property
     def n_launches(self) -> int:
-        return len(self.launches)
+        """Kernel launches per call (taps are not launches)."""
+        return sum(1 for fn, _ in self.launches if fn is not _TAP)
 
-    def _run_launches(self):
+    def _run_launches(self, observer=None):
         stream = torch.cuda.current_stream(self.dev).cuda_stream
         for fn, args in self.launches:
+            if fn is _TAP:
+                if observer is not None:
+                    observer(*args)
+                continue
             if isinstance(args[0], ctypes_structs):
                 rc = fn(ctypes_byref(args[0]), stream)
             else:
@@ -465,12 +475,13 @@ class SmolVLARunner:
         self.in_state.copy_(st, non_blocking=True)
         self.in_noise.copy_(noise.reshape(B, c.chunk, c.max_action_dim), non_blocking=True)
 
-    def run(self):
-        """Launch the call on the current stream (graph replay when captured)."""
-        if self.graph is not None:
+    def run(self, observer=None):
+        """Launch the call on the current stream (graph replay when captured).  ``observer(mods, buf)`` is
+        called at every tap point (direct launches only)."""
+        if self.graph is not None and observer is None:
             self.graph.replay()
         else:
-            self._run_launches()
+            self._run_launches(observer)
 
     def capture(self, warmup: int = 1):
         """Record the launch list as one CUDA graph (inputs and outputs are the static buffers)."""
@@ -489,13 +500,14 @@ class SmolVLARunner:
     def actions(self) -> torch.Tensor:
         return self.xt.view(self.B, self.cfg.chunk, self.cfg.max_action_dim)
 
-    def __call__(self, images, img_masks, lang_tokens, lang_masks, state, noise) -> torch.Tensor:
+    def __call__(self, images, img_masks, lang_tokens, lang_masks, state, noise, observer=None) -> torch.Tensor:
         self.load_inputs(images, img_masks, lang_tokens, lang_masks, state, noise)
-        self.run()
+        self.run(observer)
         return self.actions()
 
 
 import ctypes as _ct  # noqa: E402
 
 ctypes_structs = (L.GemmDesc, L.NormDesc, L.AttnDesc)
+_TAP = object()  # marker of a tap entry in the launch list
 ctypes_byref = _ct.byref

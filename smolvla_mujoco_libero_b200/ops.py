@@ -145,13 +145,18 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, bias: torch.Te
     d = L.NormDesc()
     d.x, d.ldx, d.weight, d.bias, d.eps = x.data_ptr(), x.stride(0), weight.data_ptr(), _p(bias), float(eps)
     d.layernorm, d.m, d.k = int(bias is not None), m, k
+    # with a pixel shuffle every output (bf16 and int8) is in the shuffled [m / s^2, k * s^2] layout
+    qm, qk = (m // (pixel_shuffle ** 2), k * pixel_shuffle ** 2) if pixel_shuffle else (m, k)
     if want_y and y is None:
-        y = torch.empty(m, k, dtype=torch.bfloat16, device=x.device)
+        y = torch.empty(qm, qk, dtype=torch.bfloat16, device=x.device)
+    if y is not None and (y.shape[0] < qm or y.stride(0) < qk):
+        raise ValueError(f"y must hold [{qm}, {qk}]")
     d.y, d.ldy = _p(y), (y.stride(0) if y is not None else 0)
     outs = []
-    qm, qk = (m // (pixel_shuffle ** 2), k * pixel_shuffle ** 2) if pixel_shuffle else (m, k)
     for i, (smooth, act) in enumerate(quants):
         q = q_out[i] if q_out is not None else torch.empty(qm, qk, dtype=torch.int8, device=x.device)
+        if q.shape[0] < qm or q.stride(0) < qk:
+            raise ValueError(f"int8 output {i} must hold [{qm}, {qk}]")
         outs.append(q)
         d.q[i], d.smooth[i], d.act[i] = q.data_ptr(), smooth.data_ptr(), float(act)
     d.nq, d.ldq = len(quants), (outs[0].stride(0) if outs else 0)

@@ -294,10 +294,11 @@ def test_layernorm_and_pixel_shuffle_quant():
     y, (q,) = ops.norm_quant(x.to(DEV), w.to(DEV), 1e-6, bias=b.to(DEV), quants=[(smooth.to(DEV), 0.02)],
                              pixel_shuffle=4, ps_grid=32)
     ref = F.layer_norm(x.float(), (768,), w.float(), b.float(), 1e-6).to(torch.bfloat16)
-    ok, frac = bf16_ulp_close(y, ref, ulps=1.0, atol=1e-5)
+    ref_shuffled = pixel_shuffle(ref.view(2, 1024, 768), 4).reshape(128, 768 * 16)
+    assert y.shape == (128, 768 * 16)          # the bf16 output is written in the shuffled layout too
+    ok, frac = bf16_ulp_close(y, ref_shuffled, ulps=1.0, atol=1e-5)
     assert ok, frac
-    shuffled = pixel_shuffle(y.cpu().view(2, 1024, 768), 4).reshape(128, 768 * 16)
-    assert torch.equal(q.cpu(), Q.smooth_quantize_activation(shuffled, smooth, 0.02))
+    assert torch.equal(q.cpu(), Q.smooth_quantize_activation(y.cpu(), smooth, 0.02))
 
 
 # ----------------------------------------------------------------------------- attention
