@@ -88,6 +88,17 @@ int32_t svla_sq_linear_w8a8(const void* x, const float* smooth, float act_scale,
                             const float* wscale, const void* bias, int32_t m, int32_t n, int32_t k, void* y,
                             void* workspace, size_t workspace_bytes, svla_stream_t stream);
 
+/* The same SmoothQuant W8A8 linear for callers that cannot allocate device memory (a fixed-rate control
+ * loop that must not allocate after start-up, or a binding that only holds the pointers it was given).
+ * No counterpart in the reference.  Takes no workspace: the int8 activations go to one 4 MiB
+ * (4194304-byte) array built into the library, held on every GPU that loads the library until exit.
+ * Rejects m*k above 4194304 with status 1.  All calls on a device share the array, so calls that overlap
+ * on the GPU race; nothing needs clearing between calls.  The first call on each device looks up the
+ * array's device address and should come before any stream capture. */
+int32_t svla_sq_linear_w8a8_static_scratch(const void* x, const float* smooth, float act_scale,
+                                           const int8_t* qweight, const float* wscale, const void* bias, int32_t m,
+                                           int32_t n, int32_t k, void* y, svla_stream_t stream);
+
 /* W8A16 linear; replaces W8A16Linear.forward (deploy/linear_only_quant.py:119-137):
  * y = bf16(x @ bf16(qweight * wscale[:,None])^T + bias). */
 int32_t svla_w8a16_linear(const void* x, const int8_t* qweight, const float* wscale, const void* bias, int32_t m,

@@ -69,6 +69,8 @@ SIGNATURES = {
     "svla_sq_linear_w8a8_workspace_size": (c_size_t, [c_int32, c_int32]),
     "svla_sq_linear_w8a8": (c_int32, [c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                                       c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "svla_sq_linear_w8a8_static_scratch": (c_int32, [c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
+                                                     c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "svla_w8a16_linear": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,
                                     c_void_p]),
     "svla_gemm": (c_int32, [POINTER(GemmDesc), c_void_p]),

@@ -517,3 +517,80 @@ int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// SmoothQuant W8A8 linear with built-in scratch, for callers that cannot allocate device memory.
+//
+// Some callers cannot call cudaMalloc: a robot's fixed-rate control loop that must not allocate
+// after start-up (an allocation can block for milliseconds or fail under fragmentation), or a
+// foreign-language binding that only holds the device pointers it was handed and has no allocator.
+// This entry point takes the same inputs and outputs as svla_sq_linear_w8a8 but no workspace: the
+// int8 activations live in one fixed array compiled into the library.
+//
+// The array is kStaticScratchBytes (4 MiB) of device memory, reserved on every GPU that loads
+// the library until the process exits, and shared by every call on that device.  So calls whose
+// m * k exceeds 4 MiB are rejected, and calls that overlap on the GPU (two streams, or two
+// threads) race on the same bytes and must be serialised by the caller.  Each call overwrites
+// every byte it later reads (the quantiser writes all m * k values before the GEMM reads them,
+// in stream order), so nothing has to be cleared between calls.
+//
+// In host code the array's name is only a stand-in symbol, not a device address.  The first call
+// on each device asks the runtime for the device address (cudaGetSymbolAddress, with that device
+// current) and caches it; that first call should therefore come before any stream capture.
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) int8_t g_sq_linear_static_scratch[kStaticScratchBytes];
+
+int8_t* static_scratch_address(int32_t* status) {
+  static int8_t* addr[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = fail(SVLA_ERR_CUDA, "svla_sq_linear_w8a8_static_scratch: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_sq_linear_static_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *status = fail(SVLA_ERR_CUDA, "svla_sq_linear_w8a8_static_scratch: cudaGetSymbolAddress failed: %s",
+                     cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = static_cast<int8_t*>(p);
+  }
+  *status = SVLA_OK;
+  return addr[dev];
+}
+
+}  // namespace
+
+extern "C" int32_t svla_sq_linear_w8a8_static_scratch(const void* x, const float* smooth, float act_scale,
+                                                      const int8_t* qweight, const float* wscale, const void* bias,
+                                                      int32_t m, int32_t n, int32_t k, void* y,
+                                                      svla_stream_t stream) {
+  if (m <= 0 || k <= 0 || n <= 0) return fail(SVLA_ERR_ARG, "svla_sq_linear_w8a8_static_scratch: bad shape");
+  const size_t need = static_cast<size_t>(m) * static_cast<size_t>(k);
+  if (need > kStaticScratchBytes)
+    return fail(SVLA_ERR_ARG,
+                "svla_sq_linear_w8a8_static_scratch: m*k = %zu bytes of int8 activations exceeds the fixed "
+                "scratch of %zu bytes; use svla_sq_linear_w8a8 with a caller-provided workspace",
+                need, kStaticScratchBytes);
+  int32_t rc = SVLA_OK;
+  int8_t* qx = static_scratch_address(&rc);
+  if (!qx) return rc;
+  rc = svla_quantize_smooth(x, k, smooth, act_scale, qx, k, m, k, stream);
+  if (rc) return rc;
+  svla_gemm_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.kind = SVLA_KIND_I8;
+  d.epi = SVLA_EPI_BF16;
+  d.m = m;
+  d.k = k;
+  d.nseg = 1;
+  d.seg[0] = svla_gemm_seg{qx, k, qweight, k, wscale, bias, nullptr, y, n, n, act_scale, 0};
+  return run_gemm(&d, cs(stream));
+}
