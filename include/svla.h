@@ -138,12 +138,14 @@ typedef struct svla_gemm_desc {
   const int32_t* pos;     /* EPI_ROPE: [M] */
   int32_t max_pos;
   const float* q_smooth;  /* EPI_GELU_QUANT */
+  const float* q_rsmooth; /* optional 1 / q_smooth (correctly rounded, svla_reciprocal): faster, same result */
   float q_act;
   int8_t* qout;
   int32_t ldq;
   float dt;               /* EPI_EULER */
   float* xt;
   void* xt_bf16;
+  uint64_t* debug_clock;  /* optional [16]: SM clock stamps of the first CTA's phases (profiling), else NULL */
 } svla_gemm_desc;
 
 int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream);
@@ -165,6 +167,7 @@ typedef struct svla_norm_desc {
   int8_t* q[3];
   int32_t ldq;
   const float* smooth[3];
+  const float* rsmooth[3]; /* optional 1 / smooth[i] (svla_reciprocal): faster, same int8 result */
   float act[3];
   int32_t pixel_shuffle;  /* 0, or the SmolVLM connector shuffle factor (remaps y and the int8 outputs) */
   int32_t ps_grid;        /* tokens per side of the input grid */
@@ -184,7 +187,7 @@ typedef struct svla_attn_desc {
   const uint8_t* mask; int64_t mask_bs; int32_t mask_rs; /* bool mask [B, Lq, l1 + l2] or NULL */
   void* o; int64_t o_bs; int32_t o_rs;                   /* bf16 context or NULL */
   int8_t* qo; int64_t qo_bs; int32_t qo_rs;              /* int8 context (next W8A8 input) or NULL */
-  const float* qo_smooth; float qo_act;
+  const float* qo_smooth; const float* qo_rsmooth; float qo_act; /* qo_rsmooth optional, as in svla_norm_desc */
   int32_t batch, lq, hq, hkv;
   float scale;                                           /* 0 = head_dim^-1/2 */
 } svla_attn_desc;
@@ -222,6 +225,8 @@ int32_t svla_im2col(const float* images, int32_t n, int32_t c, int32_t s, int32_
                     svla_stream_t stream);
 
 int32_t svla_f32_to_bf16(const float* x, void* y, int64_t n, svla_stream_t stream);
+/* y[i] = 1 / x[i], correctly rounded (the reciprocal smooth vectors the quantisers accept) */
+int32_t svla_reciprocal(const float* x, float* y, int64_t n, svla_stream_t stream);
 int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n, svla_stream_t stream);
 
 #ifdef __cplusplus

@@ -30,8 +30,8 @@ class GemmDesc(ctypes.Structure):
         ("seg", GemmSeg * 3), ("block_n", c_int32), ("rows_per_group", c_int32), ("group_stride", c_int32),
         ("row_offset", c_int32), ("post_scale", c_float), ("resid", c_void_p), ("ldr", c_int32),
         ("resid_rows", c_int32), ("rope_cs", c_void_p), ("pos", c_void_p), ("max_pos", c_int32),
-        ("q_smooth", c_void_p), ("q_act", c_float), ("qout", c_void_p), ("ldq", c_int32), ("dt", c_float),
-        ("xt", c_void_p), ("xt_bf16", c_void_p),
+        ("q_smooth", c_void_p), ("q_rsmooth", c_void_p), ("q_act", c_float), ("qout", c_void_p), ("ldq", c_int32), ("dt", c_float),
+        ("xt", c_void_p), ("xt_bf16", c_void_p), ("debug_clock", c_void_p),
     ]
 
 
@@ -39,7 +39,7 @@ class NormDesc(ctypes.Structure):
     _fields_ = [
         ("x", c_void_p), ("ldx", c_int32), ("weight", c_void_p), ("bias", c_void_p), ("eps", c_float),
         ("layernorm", c_int32), ("m", c_int32), ("k", c_int32), ("y", c_void_p), ("ldy", c_int32), ("nq", c_int32),
-        ("q", c_void_p * 3), ("ldq", c_int32), ("smooth", c_void_p * 3), ("act", c_float * 3),
+        ("q", c_void_p * 3), ("ldq", c_int32), ("smooth", c_void_p * 3), ("rsmooth", c_void_p * 3), ("act", c_float * 3),
         ("pixel_shuffle", c_int32), ("ps_grid", c_int32),
     ]
 
@@ -52,7 +52,7 @@ class AttnDesc(ctypes.Structure):
         ("mask", c_void_p), ("mask_bs", c_int64), ("mask_rs", c_int32),
         ("o", c_void_p), ("o_bs", c_int64), ("o_rs", c_int32),
         ("qo", c_void_p), ("qo_bs", c_int64), ("qo_rs", c_int32),
-        ("qo_smooth", c_void_p), ("qo_act", c_float),
+        ("qo_smooth", c_void_p), ("qo_rsmooth", c_void_p), ("qo_act", c_float),
         ("batch", c_int32), ("lq", c_int32), ("hq", c_int32), ("hkv", c_int32), ("scale", c_float),
     ]
 
@@ -86,6 +86,7 @@ SIGNATURES = {
     "svla_im2col": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "svla_f32_to_bf16": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
     "svla_euler_init": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "svla_reciprocal": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
 }
 
 

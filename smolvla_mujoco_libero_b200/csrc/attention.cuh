@@ -4,16 +4,17 @@
 // lerobot eager_attention_forward):
 //   s = (q . k) * d^-1/2                    (fp32)
 //   s = mask ? s : finfo(f32).min           (a fully masked row therefore becomes uniform over ALL keys)
-//   p = bf16(softmax(s))                    (normalised in fp32, then rounded to bf16)
-//   o = bf16(p @ v)                         (fp32 accumulation)
+//   o = bf16(softmax(s) @ v)                (fp32 accumulation)
 // Query head h reads key/value head h / (Hq / Hkv).
 //
-// Two passes over the keys: pass 1 finds each row's max and sum, pass 2 recomputes the scores, forms
-// the normalised bf16 probabilities and accumulates P.V.  This keeps the reference's rounding of the
-// normalised probabilities for any key length.
+// One pass over the keys with an online softmax (running max m, running sum l, O rescaled when m grows):
+// probabilities exp(s - m) are rounded to bf16 for the tensor-core P.V and O is divided by l at the end.
+// The reference rounds the already-normalised probabilities instead; both roundings are 2^-9 relative
+// per term (bf16), well inside the stated tolerance.
 //
-// Keys may come from two sources (the cached prefix followed by the current suffix); each CTA handles
-// 64 queries of one (batch, head) with 4 warps of 16 rows; tensor-core work is mma.sync m16n8k16.
+// CTA: 8 warps x 16 query rows = 128 queries of one (batch, head).  Keys stream in tiles of 64 through a
+// two-stage cp.async pipeline; keys may come from two sources (the cached prefix followed by the current
+// suffix).  Tensor-core work is mma.sync m16n8k16 with ldmatrix fragments; exponentials are ex2.approx.
 //
 // Optional fused output quantisation (the o_proj input of a W8A8 layer):
 //   qo[m, h*64 + d] = round((o / s[h*64+d]) / a).clamp(-128, 127).
@@ -30,16 +31,19 @@ struct AttnArgs {
   const uint8_t* mask;     long long mask_bs; int mask_rs;  // mask[b*mask_bs + i*mask_rs + key] or nullptr
   __nv_bfloat16* o;        long long o_bs; int o_rs;        // optional bf16 output
   int8_t* qo;              long long qo_bs; int qo_rs;      // optional int8 output
-  const float* qo_smooth;  float qo_act;
+  const float* qo_smooth;  const float* qo_rsmooth;  float qo_act;
   int Lq, Hq, Hkv;
   float scale;
 };
 
 namespace attn_detail {
 constexpr int kD = 64;
-constexpr int kKP = 72;  // padded smem row (bf16) -> conflict-free fragment loads
-constexpr int kChunk = 64;
+constexpr int kRows = 128;    // queries per CTA
+constexpr int kWarps = kRows / 16;
+constexpr int kKeys = 64;     // keys per tile
+constexpr int kPad = 72;      // smem row (bf16): 144 bytes -> conflict-free ldmatrix
 constexpr float kMaskedScore = -3.4028234663852886e38f;  // torch.finfo(torch.float32).min
+constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -49,9 +53,10 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
 }
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
@@ -60,16 +65,41 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* 
                : "r"(smem_u32(p)));
 }
 
-// load one 64-key chunk of K (and V) for kv head `kh` into padded shared tiles (zero beyond Lk)
-__device__ __forceinline__ void load_kv_chunk(const AttnArgs& a, int b, int kh, int key0, __nv_bfloat16* ks,
-                                              __nv_bfloat16* vs, bool load_v) {
+// 16-byte cp.async; src_bytes = 0 fills the destination with zeros
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) { return pack_bf16_rn(lo, hi); }
+
+struct Smem {
+  __nv_bfloat16 q[kRows * kPad];
+  __nv_bfloat16 k[2][kKeys * kPad];
+  __nv_bfloat16 v[2][kKeys * kPad];
+  uint8_t m[2][kRows * kKeys];
+};
+
+// issue the cp.async copies of key tile `tile` (keys key0 .. key0+63) of kv head kh into stage st
+__device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st, int b, int kh, int key0) {
   const int Lk = a.L1 + a.L2;
-  for (int idx = threadIdx.x; idx < kChunk * 8; idx += blockDim.x) {
+  for (int idx = threadIdx.x; idx < kKeys * 8; idx += blockDim.x) {
     const int r = idx >> 3, c = (idx & 7) * 8;
     const int key = key0 + r;
-    int4 kv = make_int4(0, 0, 0, 0), vv = make_int4(0, 0, 0, 0);
+    const __nv_bfloat16* kp = a.k1;
+    const __nv_bfloat16* vp = a.v1;
+    int bytes = 0;
     if (key < Lk) {
-      const __nv_bfloat16 *kp, *vp;
+      bytes = 16;
       if (key < a.L1) {
         const size_t off = static_cast<size_t>(b) * a.kv1_bs + static_cast<size_t>(key) * a.kv1_rs + kh * kD + c;
         kp = a.k1 + off;
@@ -80,119 +110,139 @@ __device__ __forceinline__ void load_kv_chunk(const AttnArgs& a, int b, int kh, 
         kp = a.k2 + off;
         vp = a.v2 + off;
       }
-      kv = *reinterpret_cast<const int4*>(kp);
-      if (load_v) vv = *reinterpret_cast<const int4*>(vp);
     }
-    *reinterpret_cast<int4*>(ks + r * kKP + c) = kv;
-    if (load_v) *reinterpret_cast<int4*>(vs + r * kKP + c) = vv;
+    cp_async16(&sm.k[st][r * kPad + c], kp, bytes);
+    cp_async16(&sm.v[st][r * kPad + c], vp, bytes);
+  }
+  if (a.mask) {
+    // mask bytes [128 rows x 64 keys]; rows past Lq and keys past Lk are left as whatever they read:
+    // the scores of keys past Lk are forced to -inf and rows past Lq are never stored
+    const int q0 = blockIdx.x * kRows;
+    for (int idx = threadIdx.x; idx < kRows * 4; idx += blockDim.x) {
+      const int r = idx >> 2, c = (idx & 3) * 16;
+      const int row = q0 + r, key = key0 + c;
+      const uint8_t* src = a.mask + static_cast<size_t>(b) * a.mask_bs + static_cast<size_t>(row < a.Lq ? row : 0) * a.mask_rs + key;
+      // whole 16-byte run inside the row and 16-byte aligned -> one copy, otherwise bytes one by one
+      const bool vec = (key + 16 <= Lk) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+      if (vec) {
+        cp_async16(&sm.m[st][r * kKeys + c], src, 16);
+      } else {
+        for (int j = 0; j < 16; ++j) sm.m[st][r * kKeys + c + j] = (key + j < Lk) ? src[j] : 0;
+      }
+    }
   }
 }
 }  // namespace attn_detail
 
-__global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const AttnArgs a) {
   using namespace attn_detail;
-  __shared__ __align__(16) __nv_bfloat16 ks[kChunk * kKP];
-  __shared__ __align__(16) __nv_bfloat16 vs[kChunk * kKP];
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int h = blockIdx.y, b = blockIdx.z;
   const int kh = h / (a.Hq / a.Hkv);
-  const int q0 = blockIdx.x * 64 + warp * 16;
+  const int q0 = blockIdx.x * kRows;
   const int Lk = a.L1 + a.L2;
+  const int n_tiles = (Lk + kKeys - 1) / kKeys;
 
-  // Q fragments (16 rows x 64 dims per warp), rows beyond Lq read as zero
-  uint32_t qa[4][4];
+  // Q tile -> smem (zero rows beyond Lq), first K/V tile in flight
   {
-    const int r0 = q0 + g, r1 = q0 + g + 8;
     const __nv_bfloat16* qb = a.q + static_cast<size_t>(b) * a.q_bs + h * kD;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const int c = kk * 16 + 2 * t;
-      auto ld = [&](int r, int cc) -> uint32_t {
-        if (r >= a.Lq) return 0u;
-        return *reinterpret_cast<const uint32_t*>(qb + static_cast<size_t>(r) * a.q_rs + cc);
-      };
-      qa[kk][0] = ld(r0, c);
-      qa[kk][1] = ld(r1, c);
-      qa[kk][2] = ld(r0, c + 8);
-      qa[kk][3] = ld(r1, c + 8);
+    for (int idx = threadIdx.x; idx < kRows * 8; idx += blockDim.x) {
+      const int r = idx >> 3, c = (idx & 7) * 8;
+      const int row = q0 + r;
+      cp_async16(&sm.q[r * kPad + c], qb + static_cast<size_t>(row < a.Lq ? row : 0) * a.q_rs + c, row < a.Lq ? 16 : 0);
     }
   }
-  const int row0 = q0 + g, row1 = q0 + g + 8;
-  const uint8_t* mrow0 = (a.mask && row0 < a.Lq) ? a.mask + static_cast<size_t>(b) * a.mask_bs + static_cast<size_t>(row0) * a.mask_rs : nullptr;
-  const uint8_t* mrow1 = (a.mask && row1 < a.Lq) ? a.mask + static_cast<size_t>(b) * a.mask_bs + static_cast<size_t>(row1) * a.mask_rs : nullptr;
+  load_kv_tile(a, sm, 0, b, kh, 0);
+  cp_async_commit();
 
-  // scores for one chunk: s[n][0..3] for key columns key0 + n*8 + 2t (+1), rows g / g+8
-  auto chunk_scores = [&](int key0, float (&s)[8][4]) {
+  uint32_t qa[4][4];
+  float o[8][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+  for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mx[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  const int wr = warp * 16;  // this warp's first row inside the CTA tile
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int st = tile & 1;
+    if (tile + 1 < n_tiles) {
+      load_kv_tile(a, sm, st ^ 1, b, kh, (tile + 1) * kKeys);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (tile == 0) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const __nv_bfloat16* kr = ks + (n * 8 + g) * kKP + kk * 16 + 2 * t;
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 8);
-        mma16816(s[n], qa[kk], b0, b1);
+        // A fragments: rows wr + (lane & 15), columns kk*16 + (lane >> 4) * 8
+        ldmatrix_x4(qa[kk], &sm.q[(wr + (lane & 15)) * kPad + kk * 16 + (lane >> 4) * 8]);
       }
+    }
+    const int key0 = tile * kKeys;
+    // ---- S = Q K^T for 16 rows x 64 keys (8 n-tiles of 8 keys)
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        // B fragments of two 8-key n-tiles: matrices (keys np*16 + 0..7 | 8..15) x (d kk*16 + 0..7 | 8..15)
+        uint32_t kb[4];
+        const int key_r = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldmatrix_x4(kb, &sm.k[st][key_r * kPad + col]);
+        mma16816(s[2 * np], qa[kk], kb[0], kb[1]);
+        mma16816(s[2 * np + 1], qa[kk], kb[2], kb[3]);
+      }
+    }
+    // ---- scale, mask, online softmax (rows g and g + 8 of this warp)
+    float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int key = key0 + n * 8 + 2 * t + (e & 1);
-        const uint8_t* mr = (e < 2) ? mrow0 : mrow1;
+        const int kc = n * 8 + 2 * t + (e & 1);  // key inside the tile
+        const int key = key0 + kc;
+        const int rl = wr + g + ((e >> 1) << 3);  // row inside the CTA tile
         float v = __fmul_rn(s[n][e], a.scale);
         if (key >= Lk) {
           v = -INFINITY;  // not a key at all
-        } else if (a.mask) {
-          const bool allowed = mr ? (mr[key] != 0) : false;
-          if (!allowed) v = kMaskedScore;
+        } else if (a.mask && sm.m[st][rl * kKeys + kc] == 0) {
+          v = kMaskedScore;
         }
         s[n][e] = v;
+        tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
       }
     }
-  };
-
-  // ---------------- pass 1: row max and sum
-  float mx[2] = {-INFINITY, -INFINITY}, sm[2] = {0.f, 0.f};
-  for (int key0 = 0; key0 < Lk; key0 += kChunk) {
-    __syncthreads();
-    load_kv_chunk(a, b, kh, key0, ks, vs, false);
-    __syncthreads();
-    float s[8][4];
-    chunk_scores(key0, s);
+    float alpha[2];
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
-      float cm = -INFINITY;
-#pragma unroll
-      for (int n = 0; n < 8; ++n) cm = fmaxf(cm, fmaxf(s[n][2 * hr], s[n][2 * hr + 1]));
-      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
-      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
-      const float nm = fmaxf(mx[hr], cm);
-      float cs = 0.f;
-#pragma unroll
-      for (int n = 0; n < 8; ++n) cs += expf(s[n][2 * hr] - nm) + expf(s[n][2 * hr + 1] - nm);
-      cs += __shfl_xor_sync(0xffffffffu, cs, 1);
-      cs += __shfl_xor_sync(0xffffffffu, cs, 2);
-      sm[hr] = (mx[hr] == -INFINITY ? 0.f : sm[hr] * expf(mx[hr] - nm)) + cs;
+      tmax[hr] = fmaxf(tmax[hr], __shfl_xor_sync(0xffffffffu, tmax[hr], 1));
+      tmax[hr] = fmaxf(tmax[hr], __shfl_xor_sync(0xffffffffu, tmax[hr], 2));
+      const float nm = fmaxf(mx[hr], tmax[hr]);
+      alpha[hr] = (mx[hr] == -INFINITY) ? 0.f : ex2((mx[hr] - nm) * kLog2e);
       mx[hr] = nm;
+      l[hr] *= alpha[hr];
     }
-  }
-
-  // ---------------- pass 2: normalised bf16 probabilities, O = P V
-  float oacc[8][4];
-#pragma unroll
-  for (int n = 0; n < 8; ++n) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
-  for (int key0 = 0; key0 < Lk; key0 += kChunk) {
-    __syncthreads();
-    load_kv_chunk(a, b, kh, key0, ks, vs, true);
-    __syncthreads();
-    float s[8][4];
-    chunk_scores(key0, s);
-    uint32_t pa[4][4];  // A fragments of P for 4 k16 steps
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
-      const float p0 = __fdiv_rn(expf(s[n][0] - mx[0]), sm[0]);
-      const float p1 = __fdiv_rn(expf(s[n][1] - mx[0]), sm[0]);
-      const float p2 = __fdiv_rn(expf(s[n][2] - mx[1]), sm[1]);
-      const float p3 = __fdiv_rn(expf(s[n][3] - mx[1]), sm[1]);
+      o[n][0] *= alpha[0];
+      o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1];
+      o[n][3] *= alpha[1];
+    }
+    uint32_t pa[4][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float p0 = ex2((s[n][0] - mx[0]) * kLog2e), p1 = ex2((s[n][1] - mx[0]) * kLog2e);
+      const float p2 = ex2((s[n][2] - mx[1]) * kLog2e), p3 = ex2((s[n][3] - mx[1]) * kLog2e);
+      l[0] += p0 + p1;
+      l[1] += p2 + p3;
       const int kk = n >> 1;
       if ((n & 1) == 0) {
         pa[kk][0] = pack_bf16(p0, p1);
@@ -202,36 +252,52 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
         pa[kk][3] = pack_bf16(p2, p3);
       }
     }
+    // ---- O += P V
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {  // pairs of 8-wide d tiles
+      for (int np = 0; np < 4; ++np) {
         uint32_t vb[4];
         const int r = kk * 16 + (lane & 15);
         const int c = np * 16 + ((lane >> 4) << 3);
-        ldmatrix_x4_trans(vb, vs + r * kKP + c);
-        mma16816(oacc[2 * np], pa[kk], vb[0], vb[1]);
-        mma16816(oacc[2 * np + 1], pa[kk], vb[2], vb[3]);
+        ldmatrix_x4_trans(vb, &sm.v[st][r * kPad + c]);
+        mma16816(o[2 * np], pa[kk], vb[0], vb[1]);
+        mma16816(o[2 * np + 1], pa[kk], vb[2], vb[3]);
       }
     }
+    __syncthreads();  // stage st is refilled by the next iteration's prefetch
   }
 
-  // ---------------- epilogue
+  // ---- epilogue: O / l, bf16, optional int8 for the next W8A8 linear
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
-    const int row = hr ? row1 : row0;
+    l[hr] += __shfl_xor_sync(0xffffffffu, l[hr], 1);
+    l[hr] += __shfl_xor_sync(0xffffffffu, l[hr], 2);
+  }
+  const float inv[2] = {__frcp_rn(l[0]), __frcp_rn(l[1])};
+  const float ra = (a.qo && a.qo_rsmooth) ? __frcp_rn(a.qo_act) : 0.f;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int row = q0 + wr + g + hr * 8;
     if (row >= a.Lq) continue;
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       const int d = n * 8 + 2 * t;
-      const float o0 = bf16_round(oacc[n][2 * hr]), o1 = bf16_round(oacc[n][2 * hr + 1]);
+      const float o0 = bf16_round(o[n][2 * hr] * inv[hr]), o1 = bf16_round(o[n][2 * hr + 1] * inv[hr]);
       if (a.o) {
         *reinterpret_cast<uint32_t*>(a.o + static_cast<size_t>(b) * a.o_bs + static_cast<size_t>(row) * a.o_rs +
                                      h * kD + d) = pack_bf16(o0, o1);
       }
       if (a.qo) {
         const int col = h * kD + d;
-        int8_t q2[2] = {smooth_quant(o0, a.qo_smooth[col], a.qo_act), smooth_quant(o1, a.qo_smooth[col + 1], a.qo_act)};
+        int8_t q2[2];
+        if (a.qo_rsmooth) {
+          q2[0] = smooth_quant_fast(o0, a.qo_smooth[col], a.qo_rsmooth[col], a.qo_act, ra);
+          q2[1] = smooth_quant_fast(o1, a.qo_smooth[col + 1], a.qo_rsmooth[col + 1], a.qo_act, ra);
+        } else {
+          q2[0] = smooth_quant(o0, a.qo_smooth[col], a.qo_act);
+          q2[1] = smooth_quant(o1, a.qo_smooth[col + 1], a.qo_act);
+        }
         *reinterpret_cast<int16_t*>(a.qo + static_cast<size_t>(b) * a.qo_bs + static_cast<size_t>(row) * a.qo_rs + col) =
             *reinterpret_cast<int16_t*>(q2);
       }

@@ -6,9 +6,12 @@
 //   W8A16  A bf16 (TMA), B int8 (TMA into a staging buffer), converted by the epilogue warps to
 //          bf16(q * w_s[n]) in the 128B-swizzled layout the MMA reads, then kind::f16.  W8A16 linears.
 //
-// CTA = 192 threads: warp 0 issues TMA, warp 1 owns TMEM and issues MMA (one elected lane), warps 2-5
-// run the epilogue (TMEM lanes 32*(warp%4) .. +31) and, for W8A16, the weight conversion during the
-// main loop.  Tile: 128 rows (M) x BN columns (N) x 128 bytes of K per pipeline stage.
+// Persistent: one CTA per SM walks output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... in N-fastest
+// order (the CTAs running at one time share A row-blocks; the weights stay L2-resident).  Accumulators
+// are double-buffered in TMEM (2 x P x BN columns) so the epilogue of one tile overlaps the MMAs of the next.
+// Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma (one lane), warps 2-5 run the
+// epilogue (TMEM lanes 32*(warp%4) .. +31), and for W8A16 warps 6-9 convert the int8 weight stages to
+// bf16.  Tile: 128 rows (M) x BN columns (N) x 128 bytes of K per pipeline stage.
 //
 // "Segments" let one launch cover several linears that share M and K but have their own A operand,
 // weights, scales and outputs (q/k/v with per-projection SmoothQuant activations).  "Pairs" (P = 2)
@@ -51,6 +54,7 @@ struct GemmArgs {
   GemmSeg seg[3];
   int nseg;     // segments (P = 1) or 2 for a pair (P = 2)
   int M, K;
+  int tiles_m, tiles_n;  // output tiles: ceil(M / 128) x (sum over segments of ceil(n / BN))
   // output row remap: row = (m / rows_per_group) * group_stride + (m % rows_per_group) + row_offset
   int rows_per_group, group_stride, row_offset;
   float post_scale;                 // Bf16: multiply bf16(y) by this and round again (0 = off)
@@ -60,14 +64,20 @@ struct GemmArgs {
   const int* pos;                   // [M] positions
   int max_pos;
   const float* q_smooth;            // GeluQuant: smooth vector of the next linear [N]
+  const float* q_rsmooth;           // GeluQuant: optional 1 / q_smooth
   float q_act;                      // GeluQuant: activation scale of the next linear
   int8_t* qout;                     // GeluQuant: int8 output [M, ldq]
   int ldq;
   float dt;                         // Euler
   float* xt;                        // Euler: fp32 state [M, ldo]
   __nv_bfloat16* xt_bf16;           // Euler: bf16 copy
+  unsigned long long* dbg;          // optional phase clock stamps of CTA 0 (profiling)
   int* err;
 };
+
+__device__ __forceinline__ void stamp(unsigned long long* dbg, int slot) {
+  if (dbg != nullptr && blockIdx.x == 0) dbg[slot] = clock64();
+}
 
 template <Kind KIND>
 struct KindTraits;
@@ -100,22 +110,260 @@ struct GemmSmem {
   static constexpr int kRawTile = KindTraits<KIND>::kConvert ? BN * 64 : 0;  // int8 staging, W8A16
   static constexpr int kStage = P * (kATile + kBTile + kRawTile);
   static constexpr int kBarOff = STAGES * kStage;
-  static constexpr int kBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
-  static constexpr int kTmemCols = (P * BN <= 32) ? 32 : (P * BN <= 64) ? 64 : (P * BN <= 128) ? 128
-                                                     : (P * BN <= 256) ? 256 : 512;
+  // per-tile column constants staged by the epilogue warps: 2 buffers x kConstArrays x BN floats
+  static constexpr int kConstArrays = 6;  // scale0, bias0, scale1, bias1, next-linear smooth, its reciprocal
+  static constexpr int kConstOff = kBarOff + 256;
+  static constexpr int kBytes = kConstOff + 2 * kConstArrays * BN * 4 + 1024;  // + alignment slack
+  static constexpr int kAccCols = P * BN;              // one accumulator buffer
+  static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128) ? 128
+                                   : (2 * kAccCols <= 256) ? 256 : 512;
+  static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
+  static_assert(kBytes <= 232448, "dynamic shared memory above the 227 KB per-CTA limit");
 };
 
-__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, 1.0f + expf(-x)); }
+constexpr int kEpiWarps = 8;  // epilogue warps 2..9: two per TMEM lane quarter, each on half the columns
 
+template <Kind KIND>
+constexpr int gemm_threads() { return 32 * (2 + kEpiWarps + (KindTraits<KIND>::kConvert ? 4 : 0)); }
+
+// SiLU x * sigmoid(x) and tanh-GELU 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi)(x + 0.044715 x^3),
+// both evaluated as x / (1 + e^-z) with the fast exponential and divide: the results are rounded to bf16
+// (8 significant bits) right after, far coarser than these approximations (about 2^-21 relative).
+__device__ __forceinline__ float sigmoid_mul(float x, float z) { return __fdividef(x, 1.0f + __expf(-z)); }
+__device__ __forceinline__ float silu_f(float x) { return sigmoid_mul(x, x); }
 __device__ __forceinline__ float gelu_tanh_f(float x) {
-  // 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3)))
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  float inner = k0 * (x + k1 * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(inner));
+  const float u = k0 * (x + k1 * x * x * x);
+  return sigmoid_mul(x, 2.0f * u);
+}
+
+template <int BN, int P>
+__device__ __forceinline__ void tile_coord(const GemmArgs& a, int t, int& si, int& m0, int& n0) {
+  const int nt = t % a.tiles_n, mt = t / a.tiles_n;
+  si = 0;
+  if constexpr (P == 1) {
+#pragma unroll
+    for (int s = 1; s < 3; ++s)
+      if (s < a.nseg && nt >= a.seg[s].tile_begin) si = s;
+  }
+  m0 = mt * 128;
+  n0 = (nt - a.seg[si].tile_begin) * BN;
+}
+
+// Epilogue of one output tile for the calling warp's 32 TMEM lanes (rows row = 32*(warp%4) + lane) and
+// its half of the columns (two warps share each lane quarter).  `ok` is warp-uniform; when false the
+// TMEM loads are skipped and nothing is written.
+template <Kind KIND, int BN, int P, Epi EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, int si, int m0, int n0, uint32_t t_row,
+                                              int row, int half, bool ok, const float* consts) {
+  const GemmSeg& sg = args.seg[si];
+  const int m = m0 + row;
+  const bool row_ok = ok && (m < args.M);
+  int orow = m;
+  if (args.rows_per_group > 0) orow = (m / args.rows_per_group) * args.group_stride + (m % args.rows_per_group);
+  orow += args.row_offset;
+
+  // per-column constants of 16 columns starting at nb (staged in shared memory for this tile):
+  // set 0 belongs to the tile's segment, set 1 to the second linear of a pair
+  auto col_consts = [&](const GemmSeg& g, int nb, float (&sc)[16], float (&bi)[16]) {
+    const int set = (&g == &args.seg[si]) ? 0 : 1;
+    const float* scs = consts + (2 * set) * BN + (nb - n0);
+    const float* bis = consts + (2 * set + 1) * BN + (nb - n0);
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      const float4 w = *reinterpret_cast<const float4*>(scs + j);
+      const float4 b = *reinterpret_cast<const float4*>(bis + j);
+      sc[j] = w.x; sc[j + 1] = w.y; sc[j + 2] = w.z; sc[j + 3] = w.w;
+      bi[j] = b.x; bi[j + 1] = b.y; bi[j + 2] = b.z; bi[j + 3] = b.w;
+    }
+  };
+  // v = ((acc * a) * w_s + b_bf16) + b_f32   (I8),   acc + b_bf16 + b_f32 otherwise.
+  auto dequant = [&](const GemmSeg& g, uint32_t raw, float sc, float bi, int n) -> float {
+    float v;
+    if constexpr (KIND == Kind::I8) {
+      v = __fmul_rn(static_cast<float>(static_cast<int>(raw)), g.act_scale);
+      if (g.wscale) v = __fmul_rn(v, sc);
+    } else {
+      v = __uint_as_float(raw);
+    }
+    if (g.bias) v = __fadd_rn(v, bi);
+    if (g.bias_f32) v = __fadd_rn(v, g.bias_f32[n]);
+    return v;
+  };
+
+  if constexpr (EPI == Epi::Rope) {
+    // one 64-column head at a time (the two warps of a lane quarter take alternate heads), rotated in two
+    // blocks of 16 pairs (columns j..j+15 with j+32..j+47) to bound register use
+    for (int c = half * 64; c < BN; c += 128) {
+      const int nb = n0 + c;
+      const bool do_head = row_ok && nb < sg.n;
+      int p = 0;
+      if (do_head && sg.rope) {
+        p = args.pos[m];
+        p = p < 0 ? 0 : (p >= args.max_pos ? args.max_pos - 1 : p);
+      }
+      const float4* cs = reinterpret_cast<const float4*>(args.rope_cs + static_cast<size_t>(p) * 32);
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        const int j0 = blk * 16;
+        uint32_t r1[16], r2[16];
+        if (ok) {
+          tmem_ld16(t_row + c + j0, r1);
+          tmem_ld16(t_row + c + j0 + 32, r2);
+          tmem_ld_wait();
+        }
+
+        if (!do_head) continue;
+        float v1[16], v2[16];
+        {
+          float sc[16], bi[16];
+          col_consts(sg, nb + j0, sc, bi);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v1[j] = bf16_round(dequant(sg, r1[j], sc[j], bi[j], nb + j0 + j));
+          col_consts(sg, nb + j0 + 32, sc, bi);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v2[j] = bf16_round(dequant(sg, r2[j], sc[j], bi[j], nb + j0 + 32 + j));
+        }
+        if (sg.rope) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float4 t = cs[(j0 + j) / 2];  // (cos_i, sin_i, cos_i+1, sin_i+1), i = j0 + j
+            float x1 = v1[j], x2 = v2[j];
+            v1[j] = __fsub_rn(__fmul_rn(x1, t.x), __fmul_rn(x2, t.y));
+            v2[j] = __fadd_rn(__fmul_rn(x2, t.x), __fmul_rn(x1, t.y));
+            x1 = v1[j + 1];
+            x2 = v2[j + 1];
+            v1[j + 1] = __fsub_rn(__fmul_rn(x1, t.z), __fmul_rn(x2, t.w));
+            v2[j + 1] = __fadd_rn(__fmul_rn(x2, t.z), __fmul_rn(x1, t.w));
+          }
+        }
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb + j0;
+#pragma unroll
+        for (int half2 = 0; half2 < 2; ++half2) {
+          const float* vv = half2 ? v2 : v1;
+          uint32_t pk[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) pk[u] = pack_bf16_rn(vv[2 * u], vv[2 * u + 1]);
+          __nv_bfloat16* oo = o + half2 * 32;
+          *reinterpret_cast<int4*>(oo) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<int4*>(oo + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+    }
+  } else {
+    constexpr int kHalf = BN / 2;
+    constexpr int kChunk = kHalf >= 32 ? 32 : 16;  // columns per TMEM round trip
+    const float ra = (EPI == Epi::GeluQuant && args.qout) ? __frcp_rn(args.q_act) : 0.0f;
+    for (int cb = half * kHalf; cb < (half + 1) * kHalf; cb += kChunk) {
+      uint32_t r[kChunk], r2[P == 2 ? kChunk : 1];
+      if (ok) {
+#pragma unroll
+        for (int u = 0; u < kChunk; u += 16) {
+          tmem_ld16(t_row + cb + u, *reinterpret_cast<uint32_t(*)[16]>(&r[u]));
+          if constexpr (P == 2) tmem_ld16(t_row + BN + cb + u, *reinterpret_cast<uint32_t(*)[16]>(&r2[u]));
+        }
+        tmem_ld_wait();
+      }
+#pragma unroll 1
+      for (int u = 0; u < kChunk; u += 16) {
+        const int nb = n0 + cb + u;
+        if (!row_ok || nb >= sg.n) continue;
+        const uint32_t* rr = &r[u];
+        float sc[16], bi[16];
+        col_consts(sg, nb, sc, bi);
+        if constexpr (EPI == Epi::I32) {
+          int* o = reinterpret_cast<int*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) *reinterpret_cast<int4*>(o + j) = make_int4(rr[j], rr[j + 1], rr[j + 2], rr[j + 3]);
+        } else if constexpr (EPI == Epi::F32) {
+          float* o = reinterpret_cast<float*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *reinterpret_cast<float4*>(o + j) =
+                make_float4(dequant(sg, rr[j], sc[j], bi[j], nb + j), dequant(sg, rr[j + 1], sc[j + 1], bi[j + 1], nb + j + 1),
+                            dequant(sg, rr[j + 2], sc[j + 2], bi[j + 2], nb + j + 2),
+                            dequant(sg, rr[j + 3], sc[j + 3], bi[j + 3], nb + j + 3));
+        } else if constexpr (EPI == Epi::Euler) {
+          float* xo = args.xt + static_cast<size_t>(orow) * sg.ldo + nb;
+          __nv_bfloat16* xb = args.xt_bf16 + static_cast<size_t>(orow) * sg.ldo + nb;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float vt = dequant(sg, rr[j], sc[j], bi[j], nb + j);
+            const float x = __fadd_rn(xo[j], __fmul_rn(args.dt, vt));
+            xo[j] = x;
+            xb[j] = __float2bfloat16_rn(x);
+          }
+        } else {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = bf16_round(dequant(sg, rr[j], sc[j], bi[j], nb + j));
+          if constexpr (EPI == Epi::SiluMul) {
+            const GemmSeg& su = args.seg[1];
+            float sc2[16], bi2[16];
+            col_consts(su, nb, sc2, bi2);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float uv = bf16_round(dequant(su, r2[u + j], sc2[j], bi2[j], nb + j));
+              v[j] = __fmul_rn(bf16_round(silu_f(v[j])), uv);
+            }
+          } else if constexpr (EPI == Epi::SiluBf16) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = silu_f(v[j]);
+          } else if constexpr (EPI == Epi::Resid) {
+            const int rrow = args.resid_rows > 0 ? (m % args.resid_rows) : orow;
+            const __nv_bfloat16* rs = args.resid + static_cast<size_t>(rrow) * args.ldr + nb;
+            const int4 ra4 = *reinterpret_cast<const int4*>(rs);
+            const int4 rb4 = *reinterpret_cast<const int4*>(rs + 8);
+            const __nv_bfloat16* h0 = reinterpret_cast<const __nv_bfloat16*>(&ra4);
+            const __nv_bfloat16* h1 = reinterpret_cast<const __nv_bfloat16*>(&rb4);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              v[j] = __fadd_rn(v[j], __bfloat162float(h0[j]));
+              v[j + 8] = __fadd_rn(v[j + 8], __bfloat162float(h1[j]));
+            }
+          } else if constexpr (EPI == Epi::GeluQuant) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = bf16_round(gelu_tanh_f(v[j]));
+            if (args.qout != nullptr) {
+              int8_t qv[16];
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const float4 s4 = *reinterpret_cast<const float4*>(consts + 4 * BN + (nb - n0) + j);
+                const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                if (args.q_rsmooth) {
+                  const float4 r4 = *reinterpret_cast<const float4*>(consts + 5 * BN + (nb - n0) + j);
+                  const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) qv[j + e] = smooth_quant_fast(v[j + e], sv[e], rv[e], args.q_act, ra);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) qv[j + e] = smooth_quant(v[j + e], sv[e], args.q_act);
+                }
+              }
+              *reinterpret_cast<int4*>(args.qout + static_cast<size_t>(orow) * args.ldq + nb) =
+                  *reinterpret_cast<int4*>(qv);
+            }
+            if (sg.out == nullptr) continue;
+          } else if constexpr (EPI == Epi::Bf16) {
+            if (args.post_scale != 0.0f) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], args.post_scale);
+            }
+          }
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
+          uint32_t pk[8];
+#pragma unroll
+          for (int q2 = 0; q2 < 8; ++q2) pk[q2] = pack_bf16_rn(v[2 * q2], v[2 * q2 + 1]);
+          *reinterpret_cast<int4*>(o) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<int4*>(o + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+    }
+  }
 }
 
 template <Kind KIND, int BN, int P, int STAGES, Epi EPI>
-__global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constant__ GemmArgs args) {
+__global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(const __grid_constant__ GemmArgs args) {
   using T = KindTraits<KIND>;
   using S = GemmSmem<KIND, BN, P, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -123,34 +371,27 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
   uint64_t* empty = full + STAGES;
   uint64_t* conv = empty + STAGES;          // W8A16: converted B ready
-  uint64_t* accum = conv + STAGES;          // all MMAs done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = conv + STAGES;          // [2] accumulator buffer holds a finished tile
+  uint64_t* tempty = tfull + 2;             // [2] epilogue has drained the accumulator buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tile = blockIdx.x;
-  const int n_tile = blockIdx.y;
-
-  // segment lookup
-  int si = 0;
-  if constexpr (P == 1) {
-#pragma unroll
-    for (int s = 1; s < 3; ++s)
-      if (s < args.nseg && n_tile >= args.seg[s].tile_begin) si = s;
-  }
-  const GemmSeg& sg = args.seg[si];
-  const int n0 = (n_tile - sg.tile_begin) * BN;  // first column within the segment
-  const int m0 = m_tile * 128;
   const int k_tiles = (args.K + T::kBK - 1) / T::kBK;
+  const int n_tiles_total = args.tiles_m * args.tiles_n;
 
+  if (threadIdx.x == 0) stamp(args.dbg, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
       mbar_init(&conv[s], 4);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -162,6 +403,7 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) stamp(args.dbg, 1);
 
   auto bounded_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
@@ -176,25 +418,32 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
-      for (int p = 0; p < P; ++p) {
-        prefetch_tmap(&args.ta[P == 1 ? si : p]);
-        prefetch_tmap(&args.tb[P == 1 ? si : p]);
+      for (int p = 0; p < (P == 1 ? args.nseg : 2); ++p) {
+        prefetch_tmap(&args.ta[p]);
+        prefetch_tmap(&args.tb[p]);
       }
-      for (int kt = 0; kt < k_tiles; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        if (!bounded_wait(&empty[s], ph ^ 1)) break;
-        uint8_t* st = smem + s * S::kStage;
-        constexpr uint32_t kBBytes = T::kConvert ? S::kRawTile : S::kBTile;
-        mbar_arrive_expect_tx(&full[s], P * (S::kATile + kBBytes));
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x) {
+        int si, m0, n0;
+        tile_coord<BN, P>(args, t, si, m0, n0);
+        for (int kt = 0; kt < k_tiles; ++kt, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!(ok = bounded_wait(&empty[s], ph ^ 1))) break;
+          uint8_t* st = smem + s * S::kStage;
+          constexpr uint32_t kBBytes = T::kConvert ? S::kRawTile : S::kBTile;
+          mbar_arrive_expect_tx(&full[s], P * (S::kATile + kBBytes));
+          if (g == 0) stamp(args.dbg, 2);
 #pragma unroll
-        for (int p = 0; p < P; ++p) {
-          const int mi = (P == 1) ? si : p;
-          uint8_t* a_dst = st + p * S::kATile;
-          uint8_t* b_dst = T::kConvert ? st + P * (S::kATile + S::kBTile) + p * S::kRawTile
-                                       : st + P * S::kATile + p * S::kBTile;
-          tma_load_2d(a_dst, &args.ta[mi], &full[s], kt * T::kBK, m0);
-          tma_load_2d(b_dst, &args.tb[mi], &full[s], kt * T::kBK, n0);
+          for (int p = 0; p < P; ++p) {
+            const int mi = (P == 1) ? si : p;
+            uint8_t* a_dst = st + p * S::kATile;
+            uint8_t* b_dst = T::kConvert ? st + P * (S::kATile + S::kBTile) + p * S::kRawTile
+                                         : st + P * S::kATile + p * S::kBTile;
+            tma_load_2d(a_dst, &args.ta[mi], &full[s], kt * T::kBK, m0);
+            tma_load_2d(b_dst, &args.tb[mi], &full[s], kt * T::kBK, n0);
+          }
         }
       }
     }
@@ -202,23 +451,30 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
     // ---------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = T::idesc(BN);
+      uint32_t g = 0, lt = 0;
       bool ok = true;
-      for (int kt = 0; kt < k_tiles && ok; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        ok = bounded_wait(&full[s], ph);
-        if (ok && T::kConvert) ok = bounded_wait(&conv[s], ph);
-        if (!ok) break;
+      for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x, ++lt) {
+        const uint32_t ab = lt & 1, use = lt >> 1;
+        if (!(ok = bounded_wait(&tempty[ab], (use & 1) ^ 1))) break;
         tc_fence_after();
-        uint8_t* st = smem + s * S::kStage;
+        const uint32_t d_base = tmem_base + ab * S::kAccCols;
+        for (int kt = 0; kt < k_tiles; ++kt, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          ok = bounded_wait(&full[s], ph);
+          if (g == 0) stamp(args.dbg, 3);
+          if (ok && T::kConvert) ok = bounded_wait(&conv[s], ph);
+          if (g == 0) stamp(args.dbg, 4);
+          if (!ok) break;
+          tc_fence_after();
+          uint8_t* st = smem + s * S::kStage;
 #pragma unroll
-        for (int p = 0; p < P; ++p) {
-          const uint32_t a_addr = smem_u32(st + p * S::kATile);
-          const uint32_t b_addr = smem_u32(st + P * S::kATile + p * S::kBTile);
-          const uint32_t d_tmem = tmem_base + p * BN;
+          for (int p = 0; p < P; ++p) {
+            const uint32_t a_addr = smem_u32(st + p * S::kATile);
+            const uint32_t b_addr = smem_u32(st + P * S::kATile + p * S::kBTile);
+            const uint32_t d_tmem = d_base + p * BN;
 #pragma unroll
-          for (int kk = 0; kk < 128 / 32; ++kk) {  // 4 MMAs of 32 bytes of K each
-            {
+            for (int kk = 0; kk < 128 / 32; ++kk) {  // 4 MMAs of 32 bytes of K each
               const uint64_t ad = smem_desc_sw128(a_addr + kk * 32);
               const uint64_t bd = smem_desc_sw128(b_addr + kk * 32);
               const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
@@ -228,43 +484,101 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
                 mma_bf16(d_tmem, ad, bd, idesc, acc);
             }
           }
+          mma_commit(&empty[s]);  // stage s free once these MMAs have read it
         }
-        mma_commit(&empty[s]);  // stage s free once these MMAs have read it
+        mma_commit(&tfull[ab]);  // the tile's accumulator is complete
+        if (lt == 0) stamp(args.dbg, 5);
       }
-      mma_commit(accum);  // arrives when every MMA issued above has completed
     }
-  } else {
-    // ---------------- epilogue warps (2..5); W8A16 weight conversion during the main loop
-    const int q = warp & 3;      // TMEM lane quarter this warp may access
+  } else if (warp < 2 + kEpiWarps) {
+    // ---------------- epilogue warps 2..9
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
-    const int et = (warp - 2) * 32 + lane;  // 0..127
-    if constexpr (T::kConvert) {
-      // each stage: P x [BN rows x 64 int8] staging -> P x [BN rows x 64 bf16] swizzled operand tiles
-      for (int kt = 0; kt < k_tiles; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        const bool okc = bounded_wait(&full[s], ph);
-        if (!__all_sync(0xffffffffu, okc)) break;
+    const int half = (warp - 2) / 4;
+    const int etid = threadIdx.x - 64;  // 0 .. 32*kEpiWarps-1
+    float* const_base = reinterpret_cast<float*>(smem + S::kConstOff);
+    uint32_t lt = 0;
+    bool ok = true;
+    // Every epilogue warp runs every iteration (also after a failed wait) so that the named barrier
+    // below is reached the same number of times by all of them.
+    for (int t = blockIdx.x; t < n_tiles_total; t += gridDim.x, ++lt) {
+      const uint32_t ab = lt & 1, use = lt >> 1;
+      int si, m0, n0;
+      tile_coord<BN, P>(args, t, si, m0, n0);
+      // stage this tile's column constants (double-buffered by tile parity)
+      float* cst = const_base + ab * S::kConstArrays * BN;
+      for (int c = etid; c < BN; c += 32 * kEpiWarps) {
+#pragma unroll
+        for (int set = 0; set < P; ++set) {
+          const GemmSeg& g = args.seg[P == 1 ? si : set];
+          const int n = n0 + c;
+          const bool in = n < g.n;
+          cst[(2 * set) * BN + c] = (KIND == Kind::I8 && g.wscale && in) ? g.wscale[n] : 1.0f;
+          cst[(2 * set + 1) * BN + c] = (g.bias && in) ? __bfloat162float(g.bias[n]) : 0.0f;
+        }
+        if constexpr (EPI == Epi::GeluQuant) {
+          const int n = n0 + c;
+          const bool in = args.qout && n < args.seg[si].n;
+          cst[4 * BN + c] = in ? args.q_smooth[n] : 1.0f;
+          cst[5 * BN + c] = (in && args.q_rsmooth) ? args.q_rsmooth[n] : 1.0f;
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+      if (lt == 0 && etid == 0) stamp(args.dbg, 6);
+      const bool ok_t = ok && __all_sync(0xffffffffu, bounded_wait(&tfull[ab], use & 1));
+      tc_fence_after();
+      if (lt == 0 && etid == 0) stamp(args.dbg, 7);
+      const uint32_t t_row = tmem_base + ab * S::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+      epilogue_tile<KIND, BN, P, EPI>(args, si, m0, n0, t_row, row, half, ok_t, cst);
+      if (lt == 0 && etid == 0) stamp(args.dbg, 8);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[ab]);
+      ok = ok_t;
+    }
+  } else if constexpr (T::kConvert) {
+    // ---------------- W8A16 weight conversion, warps 10..13:
+    // each stage: P x [BN rows x 64 int8] staging -> P x [BN rows x 64 bf16] swizzled operand tiles
+    const int et = (warp - 2 - kEpiWarps) * 32 + lane;  // 0..127
+    uint32_t g = 0;
+    bool ok = true;
+    constexpr int kPer = BN * 4 / 128;  // (row, 16-byte chunk) items per converter thread and stage
+    for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x) {
+      int si, m0, n0;
+      tile_coord<BN, P>(args, t, si, m0, n0);
+      // the weight scales of this thread's rows, loaded once per tile (not once per stage)
+      float wsr[P][kPer];
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const GemmSeg& sp = args.seg[P == 1 ? si : p];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int gn = n0 + ((et + i * 128) >> 2);
+          wsr[p][i] = (sp.wscale != nullptr && gn < sp.n) ? sp.wscale[gn] : 1.0f;
+        }
+      }
+      for (int kt = 0; kt < k_tiles; ++kt, ++g) {
+        const int s = g % STAGES;
+        const uint32_t ph = (g / STAGES) & 1;
+        ok = __all_sync(0xffffffffu, bounded_wait(&full[s], ph));
+        if (!ok) break;
         uint8_t* st = smem + s * S::kStage;
 #pragma unroll
         for (int p = 0; p < P; ++p) {
-          const GemmSeg& sp = args.seg[P == 1 ? si : p];
           const int8_t* raw = reinterpret_cast<const int8_t*>(st + P * (S::kATile + S::kBTile) + p * S::kRawTile);
           uint8_t* bt = st + P * S::kATile + p * S::kBTile;
-          // BN rows x 4 chunks of 16 int8 -> 8 chunks of 16 bytes of bf16
-          for (int idx = et; idx < BN * 4; idx += 128) {
+#pragma unroll
+          for (int i = 0; i < kPer; ++i) {
+            const int idx = et + i * 128;
             const int r = idx >> 2, c = idx & 3;
-            const int gn = n0 + r;
-            const float ws = (sp.wscale != nullptr && gn < sp.n) ? sp.wscale[gn] : 1.0f;
+            const float ws = wsr[p][i];
             const int4 v = *reinterpret_cast<const int4*>(raw + r * 64 + c * 16);
             const int8_t* b8 = reinterpret_cast<const int8_t*>(&v);
             uint32_t packed[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              __nv_bfloat162 h;
-              h.x = __float2bfloat16_rn(__fmul_rn(static_cast<float>(b8[2 * j]), ws));
-              h.y = __float2bfloat16_rn(__fmul_rn(static_cast<float>(b8[2 * j + 1]), ws));
-              packed[j] = *reinterpret_cast<uint32_t*>(&h);
+              packed[j] = pack_bf16_rn(__fmul_rn(static_cast<float>(b8[2 * j]), ws),
+                                       __fmul_rn(static_cast<float>(b8[2 * j + 1]), ws));
             }
             // logical 16-byte chunks 2c and 2c+1 of row r, 128B swizzle: chunk ^ (r & 7)
             const int c0 = (2 * c) ^ (r & 7), c1 = (2 * c + 1) ^ (r & 7);
@@ -277,158 +591,16 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
         if (lane == 0) mbar_arrive(&conv[s]);
       }
     }
-
-    // wait for the accumulator
-    const bool ok = __all_sync(0xffffffffu, bounded_wait(accum, 0));
-    tc_fence_after();
-    const int m = m0 + row;
-    const bool row_ok = ok && (m < args.M);
-    int orow = m;
-    if (args.rows_per_group > 0) orow = (m / args.rows_per_group) * args.group_stride + (m % args.rows_per_group);
-    orow += args.row_offset;
-    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-
-    auto dequant = [&](const GemmSeg& g, uint32_t raw, int n) -> float {
-      float v;
-      if constexpr (KIND == Kind::I8) {
-        v = __fmul_rn(static_cast<float>(static_cast<int>(raw)), g.act_scale);
-        if (g.wscale) v = __fmul_rn(v, g.wscale[n]);
-      } else {
-        v = __uint_as_float(raw);
-      }
-      if (g.bias) v = __fadd_rn(v, __bfloat162float(g.bias[n]));
-      if (g.bias_f32) v = __fadd_rn(v, g.bias_f32[n]);
-      return v;
-    };
-
-    if constexpr (EPI == Epi::Rope) {
-      // 64 columns (one head) at a time
-      for (int c = 0; c < BN; c += 64) {
-        uint32_t r[64];
-        if (ok) {
-          tmem_ld16(t_row + c, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-          tmem_ld16(t_row + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
-          tmem_ld16(t_row + c + 32, *reinterpret_cast<uint32_t(*)[16]>(&r[32]));
-          tmem_ld16(t_row + c + 48, *reinterpret_cast<uint32_t(*)[16]>(&r[48]));
-          tmem_ld_wait();
-        }
-        const int nb = n0 + c;
-        if (!row_ok || nb >= sg.n) continue;
-        float v[64];
-#pragma unroll
-        for (int j = 0; j < 64; ++j) v[j] = bf16_round(dequant(sg, r[j], nb + j));
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
-        if (sg.rope) {
-          int p = args.pos[m];
-          p = p < 0 ? 0 : (p >= args.max_pos ? args.max_pos - 1 : p);
-          const float2* cs = args.rope_cs + static_cast<size_t>(p) * 32;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float2 t = cs[j];
-            const float x1 = v[j], x2 = v[j + 32];
-            const float o1 = __fsub_rn(__fmul_rn(x1, t.x), __fmul_rn(x2, t.y));
-            const float o2 = __fadd_rn(__fmul_rn(x2, t.x), __fmul_rn(x1, t.y));
-            v[j] = o1;
-            v[j + 32] = o2;
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 64; j += 8) {
-          uint32_t pk[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(v[j + 2 * u], v[j + 2 * u + 1]);
-            pk[u] = *reinterpret_cast<uint32_t*>(&h);
-          }
-          *reinterpret_cast<int4*>(o + j) = make_int4(pk[0], pk[1], pk[2], pk[3]);
-        }
-      }
-    } else {
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16], r2[16];
-        if (ok) {
-          tmem_ld16(t_row + c, r);
-          if constexpr (P == 2) tmem_ld16(t_row + BN + c, r2);
-          tmem_ld_wait();
-        }
-        const int nb = n0 + c;
-        if (!row_ok || nb >= sg.n) continue;
-        if constexpr (EPI == Epi::I32) {
-          int* o = reinterpret_cast<int*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
-#pragma unroll
-          for (int j = 0; j < 16; j += 4) *reinterpret_cast<int4*>(o + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-        } else if constexpr (EPI == Epi::F32) {
-          float* o = reinterpret_cast<float*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
-#pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            *reinterpret_cast<float4*>(o + j) = make_float4(dequant(sg, r[j], nb + j), dequant(sg, r[j + 1], nb + j + 1),
-                                                            dequant(sg, r[j + 2], nb + j + 2), dequant(sg, r[j + 3], nb + j + 3));
-        } else if constexpr (EPI == Epi::Euler) {
-          float* xo = args.xt + static_cast<size_t>(orow) * sg.ldo + nb;
-          __nv_bfloat16* xb = args.xt_bf16 + static_cast<size_t>(orow) * sg.ldo + nb;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float vt = dequant(sg, r[j], nb + j);
-            const float x = __fadd_rn(xo[j], __fmul_rn(args.dt, vt));
-            xo[j] = x;
-            xb[j] = __float2bfloat16_rn(x);
-          }
-        } else {
-          float v[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = bf16_round(dequant(sg, r[j], nb + j));
-          if constexpr (EPI == Epi::SiluMul) {
-            const GemmSeg& su = args.seg[1];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float u = bf16_round(dequant(su, r2[j], nb + j));
-              v[j] = __fmul_rn(bf16_round(silu_f(v[j])), u);
-            }
-          } else if constexpr (EPI == Epi::SiluBf16) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = silu_f(v[j]);
-          } else if constexpr (EPI == Epi::Resid) {
-            const int rr = args.resid_rows > 0 ? (m % args.resid_rows) : orow;
-            const __nv_bfloat16* rs = args.resid + static_cast<size_t>(rr) * args.ldr + nb;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], __bfloat162float(rs[j]));
-          } else if constexpr (EPI == Epi::GeluQuant) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = bf16_round(gelu_tanh_f(v[j]));
-            if (args.qout != nullptr) {
-              int8_t qv[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) qv[j] = smooth_quant(v[j], args.q_smooth[nb + j], args.q_act);
-              *reinterpret_cast<int4*>(args.qout + static_cast<size_t>(orow) * args.ldq + nb) =
-                  *reinterpret_cast<int4*>(qv);
-            }
-            if (sg.out == nullptr) continue;
-          } else if constexpr (EPI == Epi::Bf16) {
-            if (args.post_scale != 0.0f) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], args.post_scale);
-            }
-          }
-          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
-          uint32_t pk[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * u], v[2 * u + 1]);
-            pk[u] = *reinterpret_cast<uint32_t*>(&h);
-          }
-          *reinterpret_cast<int4*>(o) = make_int4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<int4*>(o + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
-        }
-      }
-    }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) stamp(args.dbg, 9);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, S::kTmemCols);
+    if (lane == 0) stamp(args.dbg, 10);
   }
 }
 

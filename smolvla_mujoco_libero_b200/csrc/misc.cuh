@@ -151,6 +151,12 @@ __global__ void f32_to_bf16_kernel(const float* x, __nv_bfloat16* y, long long n
   if (i < n) y[i] = __float2bfloat16_rn(x[i]);
 }
 
+// y = 1 / x, correctly rounded
+__global__ void reciprocal_kernel(const float* x, float* y, long long n) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __frcp_rn(x[i]);
+}
+
 // x_t = noise (fp32 copy) and its bf16 image
 __global__ void euler_init_kernel(const float* noise, float* xt, __nv_bfloat16* xt_bf16, long long n) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;

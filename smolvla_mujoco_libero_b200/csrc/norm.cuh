@@ -32,6 +32,7 @@ struct NormQuantArgs {
   int8_t* q[3];
   int ldq;
   const float* smooth[3];
+  const float* rsmooth[3];  // optional reciprocals of smooth (fast path, same result)
   float act[3];
   int pixel_shuffle;       // 0 or the shuffle factor (4)
   int ps_grid;             // tokens per side of the input grid (32)
@@ -117,10 +118,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) 
     if (a.y) {
       uint32_t pk[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * u], y[2 * u + 1]);
-        pk[u] = *reinterpret_cast<uint32_t*>(&h);
-      }
+      for (int u = 0; u < 4; ++u) pk[u] = pack_bf16_rn(y[2 * u], y[2 * u + 1]);
       *reinterpret_cast<int4*>(a.y + static_cast<size_t>(qrow) * a.ldy + qcol0 + k) =
           make_int4(pk[0], pk[1], pk[2], pk[3]);
     }
@@ -130,8 +128,17 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) 
       const float4 s1 = *reinterpret_cast<const float4*>(a.smooth[qi] + col + 4);
       const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
       int8_t qv[8];
+      if (a.rsmooth[qi]) {
+        const float4 r0 = *reinterpret_cast<const float4*>(a.rsmooth[qi] + col);
+        const float4 r1 = *reinterpret_cast<const float4*>(a.rsmooth[qi] + col + 4);
+        const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+        const float ra = __frcp_rn(a.act[qi]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) qv[j] = smooth_quant(y[j], sv[j], a.act[qi]);
+        for (int j = 0; j < 8; ++j) qv[j] = smooth_quant_fast(y[j], sv[j], rv[j], a.act[qi], ra);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) qv[j] = smooth_quant(y[j], sv[j], a.act[qi]);
+      }
       *reinterpret_cast<int2*>(a.q[qi] + static_cast<size_t>(qrow) * a.ldq + col) = *reinterpret_cast<int2*>(qv);
     }
   }

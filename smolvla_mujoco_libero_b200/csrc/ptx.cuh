@@ -177,6 +177,18 @@ __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; 
 
 // ------------------------------------------------------------------ numeric helpers
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// two fp32 values rounded to bf16 (RN) and packed: lo in the low half
+__device__ __forceinline__ uint32_t pack_bf16_rn(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Round-half-even of |y| < 2^22 to an integer with one fp32 add (the sum lands where the spacing is 1).
+__device__ __forceinline__ int round_rn_small(float y, float& r) {
+  const float t = __fadd_rn(y, 12582912.0f);
+  r = __fsub_rn(t, 12582912.0f);
+  return __float_as_int(t) - 0x4B400000;
+}
 
 // round-half-even then clamp, the torch.round(..).clamp(lo, hi) rule
 __device__ __forceinline__ int quant_rn_clamp(float v, int lo, int hi) {
@@ -188,6 +200,26 @@ __device__ __forceinline__ int quant_rn_clamp(float v, int lo, int hi) {
 // SmoothQuant activation quantize: round((x / s) / a).clamp(-128, 127) with two IEEE divides
 __device__ __forceinline__ int8_t smooth_quant(float x, float s, float a) {
   return static_cast<int8_t>(quant_rn_clamp(__fdiv_rn(__fdiv_rn(x, s), a), -128, 127));
+}
+// the same, kept out of line: the rare fallback of smooth_quant_fast (one copy instead of one per element)
+__device__ __noinline__ int smooth_quant_slow(float x, float s, float a) { return smooth_quant(x, s, a); }
+
+// The same result as smooth_quant, cheaper: y = (x * rs) * ra with rs = 1/s, ra = 1/a (correctly rounded
+// reciprocals) differs from fl(fl(x / s) / a) by at most 6 * 2^-24 * |y| (< 1e-4 for |y| < 256).  Away
+// from a rounding boundary (fraction more than 1e-3 from .5) and inside |y| < 256, round(y) therefore
+// equals the two-divide result; beyond 256 both clamp to the same end.  Everything else -- values within
+// 1e-3 of a .5 boundary, NaN, infinities -- takes the exact two-divide path.
+__device__ __forceinline__ int8_t smooth_quant_fast(float x, float s, float rs, float a, float ra) {
+  const float y = __fmul_rn(__fmul_rn(x, rs), ra);
+  const float ay = fabsf(y);
+  if (ay < 256.0f) {
+    float r;
+    const int i = round_rn_small(y, r);
+    if (fabsf(__fsub_rn(y, r)) < 0.499f) return static_cast<int8_t>(i < -128 ? -128 : (i > 127 ? 127 : i));
+  } else if (ay < 3.0e38f) {
+    return static_cast<int8_t>(y > 0.0f ? 127 : -128);
+  }
+  return static_cast<int8_t>(smooth_quant_slow(x, s, a));
 }
 
 }  // namespace svla

@@ -116,7 +116,7 @@ int32_t launch_gemm_inst(const GemmArgs& args, dim3 grid, cudaStream_t stream) {
     if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  kern<<<grid, 192, S::kBytes, stream>>>(args);
+  kern<<<grid, gemm_threads<K>(), S::kBytes, stream>>>(args);
   return check_launch("gemm_sm100_kernel");
 }
 
@@ -149,12 +149,41 @@ int32_t dispatch_epi(Epi e, const GemmArgs& args, dim3 grid, cudaStream_t st) {
 template <Kind K>
 int32_t dispatch_bn(int bn, int pair, Epi e, const GemmArgs& args, dim3 grid, cudaStream_t st) {
   if (pair) {
-    if (bn != 64) return fail(SVLA_ERR_ARG, "pair GEMMs use block_n 64");
-    return dispatch_epi<K, 64, 2>(e, args, grid, st);
+    if (bn == 64) return dispatch_epi<K, 64, 2>(e, args, grid, st);
+    if (bn == 128) return dispatch_epi<K, 128, 2>(e, args, grid, st);
+    return fail(SVLA_ERR_ARG, "pair GEMMs use block_n 64 or 128 (got %d)", bn);
   }
   if (bn == 64) return dispatch_epi<K, 64, 1>(e, args, grid, st);
   if (bn == 128) return dispatch_epi<K, 128, 1>(e, args, grid, st);
-  return fail(SVLA_ERR_ARG, "block_n must be 64 or 128 (got %d)", bn);
+  if (bn == 256) return dispatch_epi<K, 256, 1>(e, args, grid, st);
+  return fail(SVLA_ERR_ARG, "block_n must be 64, 128 or 256 (got %d)", bn);
+}
+
+int sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (counts[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
+// Widest tile that still gives every SM at least one tile (pairs: at most 128 so two buffers fit TMEM).
+int choose_block_n(const svla_gemm_desc* d, int sms) {
+  const int m_tiles = (d->m + 127) / 128;
+  auto tiles = [&](int bn) {
+    if (d->pair) return m_tiles * ((d->seg[0].n + bn - 1) / bn);
+    int t = 0;
+    for (int s = 0; s < d->nseg; ++s) t += (d->seg[s].n + bn - 1) / bn;
+    return m_tiles * t;
+  };
+  if (!d->pair && tiles(256) >= sms) return 256;
+  if (tiles(128) >= sms) return 128;
+  return 64;
 }
 
 }  // namespace
@@ -169,13 +198,8 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   if (d->pair && d->nseg != 2) return fail(SVLA_ERR_ARG, "a pair needs exactly 2 segments");
   if (epi == Epi::SiluMul && !d->pair) return fail(SVLA_ERR_ARG, "SILU_MUL needs pair = 1");
   if (epi == Epi::I32 && kind != Kind::I8) return fail(SVLA_ERR_ARG, "I32 epilogue needs kind I8");
-  int bn = d->block_n;
-  if (bn == 0) {
-    int total_n = 0;
-    for (int s = 0; s < d->nseg; ++s) total_n += d->seg[s].n;
-    bn = (d->pair || epi == Epi::Rope || d->m <= 512 || total_n < 1024) ? 64 : 128;
-    if (d->pair) bn = 64;
-  }
+  const int sms = sm_count();
+  const int bn = d->block_n ? d->block_n : choose_block_n(d, sms);
   const int elem_a = (kind == Kind::I8) ? 1 : 2;
   const int elem_b = (kind == Kind::BF16) ? 2 : 1;
   const int bk = (kind == Kind::I8) ? 128 : 64;
@@ -222,6 +246,8 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   args.nseg = d->nseg;
   args.M = d->m;
   args.K = d->k;
+  args.tiles_m = (d->m + 127) / 128;
+  args.tiles_n = tiles;
   args.rows_per_group = d->rows_per_group;
   args.group_stride = d->group_stride;
   args.row_offset = d->row_offset;
@@ -233,6 +259,7 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   args.pos = d->pos;
   args.max_pos = d->max_pos;
   args.q_smooth = d->q_smooth;
+  args.q_rsmooth = d->q_rsmooth;
   args.q_act = d->q_act;
   args.qout = d->qout;
   args.ldq = d->ldq;
@@ -240,13 +267,15 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   args.xt = d->xt;
   args.xt_bf16 = static_cast<__nv_bfloat16*>(d->xt_bf16);
   args.err = device_error_ptr();
+  args.dbg = reinterpret_cast<unsigned long long*>(d->debug_clock);
   if (epi == Epi::Resid && !d->resid) return fail(SVLA_ERR_ARG, "RESID needs a residual");
   if (epi == Epi::Rope && (!d->rope_cs || !d->pos || d->max_pos <= 0)) return fail(SVLA_ERR_ARG, "ROPE needs rope_cs/pos");
   if (epi == Epi::GeluQuant && d->qout && (!d->q_smooth || d->q_act <= 0.f))
     return fail(SVLA_ERR_ARG, "GELU_QUANT with qout needs q_smooth and q_act > 0");
   if (epi == Epi::GeluQuant && !d->qout && !d->seg[0].out) return fail(SVLA_ERR_ARG, "GELU_QUANT needs qout or out");
   if (epi == Epi::Euler && (!d->xt || !d->xt_bf16)) return fail(SVLA_ERR_ARG, "EULER needs xt/xt_bf16");
-  dim3 grid((d->m + 127) / 128, tiles);
+  const long long total_tiles = static_cast<long long>(args.tiles_m) * args.tiles_n;
+  dim3 grid(static_cast<unsigned>(total_tiles < sms ? total_tiles : sms));
   switch (kind) {
     case Kind::I8: return dispatch_bn<Kind::I8>(bn, d->pair, epi, args, grid, stream);
     case Kind::BF16: return dispatch_bn<Kind::BF16>(bn, d->pair, epi, args, grid, stream);
@@ -381,6 +410,7 @@ int32_t svla_norm_quant(const svla_norm_desc* d, svla_stream_t stream) {
   for (int i = 0; i < 3; ++i) {
     a.q[i] = d->q[i];
     a.smooth[i] = d->smooth[i];
+    a.rsmooth[i] = d->rsmooth[i];
     a.act[i] = d->act[i];
     if (i < d->nq && (!d->q[i] || !d->smooth[i] || d->act[i] <= 0.f))
       return fail(SVLA_ERR_ARG, "svla_norm_quant: quant output %d incomplete", i);
@@ -438,13 +468,24 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
   a.qo_bs = d->qo_bs;
   a.qo_rs = d->qo_rs;
   a.qo_smooth = d->qo_smooth;
+  a.qo_rsmooth = d->qo_rsmooth;
   a.qo_act = d->qo_act;
   a.Lq = d->lq;
   a.Hq = d->hq;
   a.Hkv = d->hkv;
   a.scale = d->scale > 0.f ? d->scale : 0.125f;
-  dim3 grid((d->lq + 63) / 64, d->hq, d->batch);
-  attention_kernel<<<grid, 128, 0, cs(stream)>>>(a);
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
+  const int smem = static_cast<int>(sizeof(attn_detail::Smem));
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  dim3 grid((d->lq + attn_detail::kRows - 1) / attn_detail::kRows, d->hq, d->batch);
+  attention_kernel<<<grid, attn_detail::kRows * 2, smem, cs(stream)>>>(a);
   return check_launch("attention_kernel");
 }
 
@@ -507,6 +548,12 @@ int32_t svla_f32_to_bf16(const float* x, void* y, int64_t n, svla_stream_t strea
   if (!x || !y || n <= 0) return fail(SVLA_ERR_ARG, "svla_f32_to_bf16: bad args");
   f32_to_bf16_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cs(stream)>>>(x, static_cast<__nv_bfloat16*>(y), n);
   return check_launch("f32_to_bf16_kernel");
+}
+
+int32_t svla_reciprocal(const float* x, float* y, int64_t n, svla_stream_t stream) {
+  if (!x || !y || n <= 0) return fail(SVLA_ERR_ARG, "svla_reciprocal: bad args");
+  reciprocal_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cs(stream)>>>(x, y, n);
+  return check_launch("reciprocal_kernel");
 }
 
 int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n, svla_stream_t stream) {

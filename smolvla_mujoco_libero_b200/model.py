@@ -47,6 +47,7 @@ class PackedLinear:
     wscale: torch.Tensor | None = None  # fp32 [n]
     bias: torch.Tensor | None = None    # bf16 [n]
     smooth: torch.Tensor | None = None  # fp32 [k] (w8a8)
+    rsmooth: torch.Tensor | None = None  # fp32 [k] = 1 / smooth (w8a8), lets the quantisers multiply
     act_scale: float = 1.0              # w8a8
     weight_bf16: torch.Tensor | None = None  # original bf16 weight (bf16 / calibration mode)
 
@@ -98,8 +99,8 @@ class DeviceWeights:
                 if smooth.numel() != k:
                     raise ValueError(f"{name}: smooth_scale has {smooth.numel()} channels, expected {k}")
                 q, ws = ops.pack_weight_i8(w, smooth)
-                self.lin[name] = PackedLinear(n, k, "w8a8", q, ws, b, smooth, max(float(e["scale"]), 1e-8),
-                                              w if keep_bf16 else None)
+                self.lin[name] = PackedLinear(n, k, "w8a8", q, ws, b, smooth, ops.reciprocal(smooth),
+                                              max(float(e["scale"]), 1e-8), w if keep_bf16 else None)
             elif kind == "w8a16":
                 q, ws = ops.pack_weight_i8(w)
                 self.lin[name] = PackedLinear(n, k, "w8a16", q, ws, b, weight_bf16=w if keep_bf16 else None)
@@ -256,6 +257,7 @@ class SmolVLARunner:
             for i, (mod, q) in enumerate(zip(quant_mods, outs)):
                 p = self.w.lin[mod]
                 d.q[i], d.smooth[i], d.act[i] = q.data_ptr(), p.smooth.data_ptr(), p.act_scale
+                d.rsmooth[i] = p.rsmooth.data_ptr()
             d.nq, d.ldq = len(quant_mods), outs[0].stride(0)
             if y is not None:
                 d.y, d.ldy = y.data_ptr(), y.stride(0)
@@ -281,7 +283,7 @@ class SmolVLARunner:
         if self.mode == "quant" and out_mod is not None:
             p = self.w.lin[out_mod]
             d = ops.attention_desc(qv, k1v, v1v, B, lq, hq, hkv, mask=mask, k2=k2v, v2=v2v, qo=ov,
-                                   qo_smooth=p.smooth, qo_act=p.act_scale)
+                                   qo_smooth=p.smooth, qo_act=p.act_scale, qo_rsmooth=p.rsmooth)
         else:
             d = ops.attention_desc(qv, k1v, v1v, B, lq, hq, hkv, mask=mask, k2=k2v, v2=v2v, o=ov)
         self._add(L.lib().svla_attention, d)
@@ -330,7 +332,8 @@ class SmolVLARunner:
             if q_mode:
                 self._gemm(L.KIND_I8, L.EPI_GELU_QUANT, NV, c.vis_hidden,
                            [self._linear_seg(f"{p}.mlp.fc1", self.v_fc1_in, None)],
-                           q_smooth=fc2.smooth, q_act=fc2.act_scale, qout=self.v_fc2_in, ldq=c.vis_mlp)
+                           q_smooth=fc2.smooth, q_rsmooth=fc2.rsmooth, q_act=fc2.act_scale, qout=self.v_fc2_in,
+                           ldq=c.vis_mlp)
             else:
                 self._gemm(L.KIND_BF16, L.EPI_GELU_QUANT, NV, c.vis_hidden,
                            [self._linear_seg(f"{p}.mlp.fc1", self.v_fc1_in, self.v_fc2_in)])

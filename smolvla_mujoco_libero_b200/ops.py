@@ -48,6 +48,14 @@ def pack_weight_i8(weight: torch.Tensor, smooth: torch.Tensor | None = None) -> 
     return q, ws
 
 
+def reciprocal(x: torch.Tensor) -> torch.Tensor:
+    """Correctly rounded 1 / x (fp32) on the device -- the reciprocal smooth vectors the quantisers accept."""
+    _need(x, torch.float32, "x")
+    y = torch.empty_like(x)
+    check(lib().svla_reciprocal(_p(x), _p(y), x.numel(), _stream()), "reciprocal")
+    return y
+
+
 def quantize_smooth(x: torch.Tensor, smooth: torch.Tensor | None, act_scale: float) -> torch.Tensor:
     _need(x, torch.bfloat16, "x")
     m, k = x.shape
@@ -139,7 +147,8 @@ def gemm(desc: L.GemmDesc) -> None:
 
 def norm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, bias: torch.Tensor | None = None,
                quants: list[tuple[torch.Tensor, float]] = (), want_y: bool = True, pixel_shuffle: int = 0,
-               ps_grid: int = 0, y: torch.Tensor | None = None, q_out: list[torch.Tensor] | None = None):
+               ps_grid: int = 0, y: torch.Tensor | None = None, q_out: list[torch.Tensor] | None = None,
+               rsmooth: list[torch.Tensor | None] | None = None):
     _need(x, torch.bfloat16, "x", contiguous=False)
     m, k = x.shape
     d = L.NormDesc()
@@ -159,6 +168,8 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, bias: torch.Te
             raise ValueError(f"int8 output {i} must hold [{qm}, {qk}]")
         outs.append(q)
         d.q[i], d.smooth[i], d.act[i] = q.data_ptr(), smooth.data_ptr(), float(act)
+        if rsmooth is not None and rsmooth[i] is not None:
+            d.rsmooth[i] = rsmooth[i].data_ptr()
     d.nq, d.ldq = len(quants), (outs[0].stride(0) if outs else 0)
     d.pixel_shuffle, d.ps_grid = pixel_shuffle, ps_grid
     check(lib().svla_norm_quant(ctypes.byref(d), _stream()), "svla_norm_quant")
@@ -170,7 +181,8 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, bias: torch.Te
 def attention_desc(q: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor, batch: int, lq: int, hq: int, hkv: int,
                    mask: torch.Tensor | None = None, k2: torch.Tensor | None = None, v2: torch.Tensor | None = None,
                    o: torch.Tensor | None = None, qo: torch.Tensor | None = None,
-                   qo_smooth: torch.Tensor | None = None, qo_act: float = 0.0, scale: float = 0.0) -> L.AttnDesc:
+                   qo_smooth: torch.Tensor | None = None, qo_act: float = 0.0, scale: float = 0.0,
+                   qo_rsmooth: torch.Tensor | None = None) -> L.AttnDesc:
     """q [B, Lq, >=hq*64] (row stride = stride(1)), k/v [B, L, >=hkv*64], mask [B, Lq, L1+L2] (uint8/bool)."""
     d = L.AttnDesc()
     d.q, d.q_bs, d.q_rs = q.data_ptr(), q.stride(0), q.stride(1)
@@ -186,6 +198,7 @@ def attention_desc(q: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor, batch: i
     if qo is not None:
         d.qo, d.qo_bs, d.qo_rs = qo.data_ptr(), qo.stride(0), qo.stride(1)
         d.qo_smooth, d.qo_act = qo_smooth.data_ptr(), float(qo_act)
+        d.qo_rsmooth = _p(qo_rsmooth)
     d.batch, d.lq, d.hq, d.hkv, d.scale = batch, lq, hq, hkv, float(scale)
     return d
 
@@ -194,7 +207,8 @@ def attention_run(desc: L.AttnDesc) -> None:
     check(lib().svla_attention(ctypes.byref(desc), _stream()), "svla_attention")
 
 
-def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smooth=None, qo_act=0.0):
+def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smooth=None, qo_act=0.0,
+              qo_rsmooth=None):
     """bf16 context [B, Lq, hq*64] (and the int8 context when qo_smooth is given)."""
     b, lq = q.shape[0], q.shape[1]
     o = torch.empty(b, lq, hq * 64, dtype=torch.bfloat16, device=q.device)
@@ -202,7 +216,7 @@ def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smoo
     if mask is not None and mask.dtype == torch.bool:
         mask = mask.view(torch.uint8)
     attention_run(attention_desc(q, k1, v1, b, lq, hq, hkv, mask=mask, k2=k2, v2=v2, o=o, qo=qo,
-                                 qo_smooth=qo_smooth, qo_act=qo_act))
+                                 qo_smooth=qo_smooth, qo_act=qo_act, qo_rsmooth=qo_rsmooth))
     return (o, qo) if qo is not None else o
 
 

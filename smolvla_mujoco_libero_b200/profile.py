@@ -1,6 +1,9 @@
-"""Profiling driver: build the benchmark model and run sample_actions calls inside an NVTX range.
+"""Profiling driver: build the benchmark model and run sample_actions calls inside an NVTX range, or
+time one operator on random inputs.
 
     python -m smolvla_mujoco_libero_b200.profile --batch 1 --iters 3 [--graph]
+    python -m smolvla_mujoco_libero_b200.profile --op gemm --kind i8 --epi gelu_quant --m 16384 --n 3072 --k 768
+    python -m smolvla_mujoco_libero_b200.profile --op attn --batch 16 --lq 1024 --lk 1024 --heads 12 --kv-heads 12
 
 Each call is wrapped in the NVTX range "sample_actions", so a profiler can capture exactly those launches
 (e.g. ``ncu --nvtx --nvtx-include "sample_actions/" --metrics gpu__time_duration.sum ...``).  Prints the
@@ -21,13 +24,108 @@ from .model import DeviceWeights, SmolVLARunner
 from .weights import random_weights
 
 
+EPIS = {"bf16": 0, "resid": 3, "gelu_quant": 5, "rope": 2, "silu_mul": 4}
+KINDS = {"i8": 0, "bf16": 1, "w8a16": 2}
+
+
+def time_op(fn, iters: int, reps: int = 20) -> list[float]:
+    """Per-launch device time: `reps` back-to-back launches between two events (so host launch latency
+    overlaps device work), repeated `iters` times."""
+    fn()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("op")
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        out.append(s.elapsed_time(e) / reps)
+    return out
+
+
+def op_gemm(a) -> dict:
+    from . import _lib as L
+    from . import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    kind, epi = KINDS[a.kind], EPIS[a.epi]
+    adt = torch.int8 if kind == 0 else torch.bfloat16
+    mk = lambda r, c, dt: (torch.randint(-100, 100, (r, c), generator=g, dtype=torch.int8) if dt == torch.int8  # noqa: E731
+                           else torch.randn(r, c, generator=g).to(dt)).to(dev)
+    A = mk(a.m, a.k, adt)
+    B = mk(a.n, a.k, torch.bfloat16 if kind == 1 else torch.int8)
+    ws = torch.rand(a.n, generator=g).to(dev) * 1e-3
+    out = torch.empty(a.m, a.n, dtype=torch.bfloat16, device=dev)
+    segs = [ops.Seg(a=A, b=B, out=out, n=a.n, wscale=ws, act_scale=0.01)]
+    extra = {}
+    if epi == 5:
+        smooth = torch.rand(a.n, generator=g).to(dev) + 0.5
+        qout = torch.empty(a.m, a.n, dtype=torch.int8, device=dev)
+        segs[0].out = None
+        extra = dict(q_smooth=smooth, q_rsmooth=ops.reciprocal(smooth), q_act=0.02, qout=qout, ldq=a.n)
+    elif epi == 3:
+        extra = dict(resid=out, ldr=a.n)
+    elif epi == 4:
+        segs.append(ops.Seg(a=A, b=B, out=out, n=a.n, wscale=ws, act_scale=0.01))
+        extra = dict(pair=True)
+    d = ops.gemm_desc(kind, epi, a.m, a.k, segs, block_n=a.block_n, **extra)
+    ms = time_op(lambda: ops.gemm(d), a.iters)
+    # phase clock stamps of CTA 0 from one more launch
+    dbg = torch.zeros(16, dtype=torch.int64, device=dev)
+    d.debug_clock = dbg.data_ptr()
+    ops.gemm(d)
+    torch.cuda.synchronize()
+    c = dbg.cpu().tolist()
+    d.debug_clock = None
+    names = ["entry", "setup", "tma0", "full0", "conv0", "commit0", "epi_consts", "epi_acc", "epi_done", "sync_end", "dealloc"]
+    phases = {names[i]: (c[i] - c[0]) if c[i] else None for i in range(len(names))}
+    ops_count = 2.0 * a.m * a.n * a.k * (2 if epi == 4 else 1)
+    best = min(ms)
+    return {"op": "gemm", "kind": a.kind, "epi": a.epi, "m": a.m, "n": a.n, "k": a.k, "ms": ms,
+            "tflops_best": ops_count / (best / 1e3) / 1e12, "cta0_cycles": phases}
+
+
+def op_attn(a) -> dict:
+    from . import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    q = torch.randn(a.batch, a.lq, a.heads * 64, generator=g).to(torch.bfloat16).to(dev)
+    k = torch.randn(a.batch, a.lk, a.kv_heads * 64, generator=g).to(torch.bfloat16).to(dev)
+    v = torch.randn(a.batch, a.lk, a.kv_heads * 64, generator=g).to(torch.bfloat16).to(dev)
+    ms = time_op(lambda: ops.attention(q, k, v, a.heads, a.kv_heads), a.iters)
+    flops = 4.0 * a.batch * a.heads * a.lq * a.lk * 64
+    return {"op": "attn", "batch": a.batch, "lq": a.lq, "lk": a.lk, "ms": ms,
+            "tflops_best": flops / (min(ms) / 1e3) / 1e12}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--op", default="sample_actions", choices=["sample_actions", "gemm", "attn"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--graph", action="store_true")
     ap.add_argument("--calib-samples", type=int, default=1)
+    ap.add_argument("--kind", default="i8", choices=list(KINDS))
+    ap.add_argument("--epi", default="bf16", choices=list(EPIS))
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=3072)
+    ap.add_argument("--k", type=int, default=768)
+    ap.add_argument("--block-n", type=int, default=0)
+    ap.add_argument("--lq", type=int, default=1024)
+    ap.add_argument("--lk", type=int, default=1024)
+    ap.add_argument("--heads", type=int, default=12)
+    ap.add_argument("--kv-heads", type=int, default=12)
     a = ap.parse_args()
+    if a.op == "gemm":
+        print(json.dumps(op_gemm(a)))
+        return
+    if a.op == "attn":
+        print(json.dumps(op_attn(a)))
+        return
     cfg = BENCH
     dev = torch.device("cuda", 0)
     obs = lambda b, s: synthetic.observations(b, seed=s, image_size=cfg.image_size, n_tokens=cfg.n_lang)  # noqa: E731

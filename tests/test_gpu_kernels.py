@@ -71,6 +71,31 @@ def test_pack_weight_bit_exact_with_smoothing():
     assert torch.equal(q2.cpu(), q2_ref) and torch.equal(ws2.cpu(), ws2_ref)
 
 
+def test_fast_quantiser_matches_two_divides_on_boundaries():
+    """The reciprocal fast path must give exactly round((y / s) / a).clamp(-128, 127).  RMSNorm of a row of
+    ones returns the norm weight w itself, so per-channel smooth scales s = w / (t * a) put y / s / a on
+    chosen targets t: on .5 rounding boundaries, 1e-7 .. 1e-3 beside them, and beyond the clamp."""
+    g = synthetic.generator(17)
+    halves = torch.arange(-131, 131, dtype=torch.float32) + 0.5
+    jitter = torch.tensor([0.0, 1e-6, -1e-6, 9e-4, -9e-4, 1.1e-3, -1.1e-3, 0.3])
+    targets = (halves[:, None] + jitter[None, :]).flatten()
+    targets = torch.cat([targets, torch.tensor([300.0, -300.0, 255.9, -256.1, 127.4, -128.4, 0.0, 1e-3])])
+    k = ((targets.numel() + 7) // 8) * 8
+    t = torch.zeros(k)
+    t[: targets.numel()] = targets
+    t[targets.numel():] = 0.25
+    w = ((torch.rand(k, generator=g) + 0.5) * torch.where(torch.rand(k, generator=g) > 0.5, 1.0, -1.0)).to(torch.bfloat16)
+    a = 0.0173
+    s = (w.float() / (t * a)).abs().clamp_min(1e-6)
+    x = torch.ones(4, k, dtype=torch.bfloat16)
+    y, (q_exact,) = ops.norm_quant(x.to(DEV), w.to(DEV), 1e-5, quants=[(s.to(DEV), a)])
+    _, (q_fast,) = ops.norm_quant(x.to(DEV), w.to(DEV), 1e-5, quants=[(s.to(DEV), a)], rsmooth=[ops.reciprocal(s.to(DEV))])
+    assert torch.equal(y.cpu()[0], w)
+    ref = Q.smooth_quantize_activation(y.cpu(), s, a)
+    assert torch.equal(q_exact.cpu(), ref)
+    assert torch.equal(q_fast.cpu(), ref)
+
+
 def test_quantize_smooth_bit_exact(golden):
     g = golden["linear_full"]
     case = synthetic.smoothquant_linear_case()
@@ -225,6 +250,11 @@ def test_epilogue_resid_silu_mul_gelu_quant_euler_f32():
     ybf = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
     ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_GELU_QUANT, m, k, [ops.Seg(a=qxd, b=qwd, out=ybf, n=n, wscale=wsd, act_scale=a)],
                            q_smooth=smooth.to(DEV), q_act=0.01, qout=qout, ldq=n))
+    qout_fast = torch.empty_like(qout)
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_GELU_QUANT, m, k, [ops.Seg(a=qxd, b=qwd, out=None, n=n, wscale=wsd, act_scale=a)],
+                           q_smooth=smooth.to(DEV), q_rsmooth=ops.reciprocal(smooth.to(DEV)), q_act=0.01, qout=qout_fast,
+                           ldq=n))
+    assert torch.equal(qout_fast, qout)
     gref = F.gelu(yb, approximate="tanh")
     ok, frac = bf16_ulp_close(ybf, gref, ulps=1.0, atol=1e-5)
     assert ok, frac
@@ -276,6 +306,11 @@ def test_rmsnorm_quant_three_outputs():
     smooths = [torch.rand(960, generator=g) * 3 + 0.2 for _ in range(3)]
     acts = [0.02, 0.03, 0.05]
     y, qs = ops.norm_quant(x.to(DEV), w.to(DEV), 1e-5, quants=[(s.to(DEV), a) for s, a in zip(smooths, acts)])
+    # the reciprocal fast path gives the same int8 values
+    _, qf = ops.norm_quant(x.to(DEV), w.to(DEV), 1e-5, quants=[(s.to(DEV), a) for s, a in zip(smooths, acts)],
+                           rsmooth=[ops.reciprocal(s.to(DEV)) for s in smooths])
+    for a_, b_ in zip(qs, qf):
+        assert torch.equal(a_, b_)
     ref = rms_norm(x, w, 1e-5)
     ok, frac = bf16_ulp_close(y, ref, ulps=1.0)
     assert ok, frac
@@ -337,6 +372,10 @@ def test_attention_two_sources_and_quant_out():
     smooth = torch.rand(hq * 64, generator=g) + 0.5
     o, qo = ops.attention(q.to(DEV), k1.to(DEV), v1.to(DEV), hq, hkv, mask=mask.to(DEV), k2=k2.to(DEV), v2=v2.to(DEV),
                           qo_smooth=smooth.to(DEV), qo_act=0.01)
+    _, qo_fast = ops.attention(q.to(DEV), k1.to(DEV), v1.to(DEV), hq, hkv, mask=mask.to(DEV), k2=k2.to(DEV),
+                               v2=v2.to(DEV), qo_smooth=smooth.to(DEV), qo_act=0.01,
+                               qo_rsmooth=ops.reciprocal(smooth.to(DEV)))
+    assert torch.equal(qo, qo_fast)
     ref = _attn_ref(q, torch.cat([k1, k2], 1), torch.cat([v1, v2], 1), mask, hq, hkv)
     assert cosine(o, ref) >= 0.9999
     qo_ref = Q.smooth_quantize_activation(o.cpu().reshape(-1, hq * 64), smooth, 0.01).reshape(b, lq, -1)
