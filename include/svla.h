@@ -5,6 +5,9 @@
  * deploy/cuda/fused_rope_layout.cu:566-570):
  *   return 0 = success, 1 = bad argument / shape / alignment, 2 = CUDA launch or runtime error.
  *   svla_last_error() returns a message for the last nonzero status of the calling thread.
+ * Kernels are launched with programmatic dependent launch (set SVLA_PDL=0 to disable): each one waits
+ * for the previous kernel in the stream before touching data it produced, so stream order is kept while
+ * kernel prologues overlap.
  * Every entry point is stream-ordered (no host synchronisation) and allocates no memory: all buffers,
  * including scratch ("workspace"), are passed in by the caller, like the TensorRT plugin enqueue it
  * replaces (deploy/cuda/smoothquant_qkv_plugin_serialized_smoke.cu:346-402).  All pointers are device
@@ -146,6 +149,8 @@ typedef struct svla_gemm_desc {
   float* xt;
   void* xt_bf16;
   uint64_t* debug_clock;  /* optional [16]: SM clock stamps of the first CTA's phases (profiling), else NULL */
+  int32_t weights_resident; /* 1: every B operand was written before the previously launched kernel started
+                               (packed weights), so its first tiles are fetched before waiting for that kernel */
 } svla_gemm_desc;
 
 int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream);

@@ -31,7 +31,7 @@ class GemmDesc(ctypes.Structure):
         ("row_offset", c_int32), ("post_scale", c_float), ("resid", c_void_p), ("ldr", c_int32),
         ("resid_rows", c_int32), ("rope_cs", c_void_p), ("pos", c_void_p), ("max_pos", c_int32),
         ("q_smooth", c_void_p), ("q_rsmooth", c_void_p), ("q_act", c_float), ("qout", c_void_p), ("ldq", c_int32), ("dt", c_float),
-        ("xt", c_void_p), ("xt_bf16", c_void_p), ("debug_clock", c_void_p),
+        ("xt", c_void_p), ("xt_bf16", c_void_p), ("debug_clock", c_void_p), ("weights_resident", c_int32),
     ]
 
 

@@ -135,6 +135,8 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st
 }  // namespace attn_detail
 
 __global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   using namespace attn_detail;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);

@@ -72,6 +72,7 @@ struct GemmArgs {
   float* xt;                        // Euler: fp32 state [M, ldo]
   __nv_bfloat16* xt_bf16;           // Euler: bf16 copy
   unsigned long long* dbg;          // optional phase clock stamps of CTA 0 (profiling)
+  int weights_resident;             // B operands were written before the previous kernel started
   int* err;
 };
 
@@ -153,12 +154,13 @@ __device__ __forceinline__ void tile_coord(const GemmArgs& a, int t, int& si, in
 // Epilogue of one output tile for the calling warp's 32 TMEM lanes (rows row = 32*(warp%4) + lane) and
 // its half of the columns (two warps share each lane quarter).  `ok` is warp-uniform; when false the
 // TMEM loads are skipped and nothing is written.
-template <Kind KIND, int BN, int P, Epi EPI>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, int si, int m0, int n0, uint32_t t_row,
-                                              int row, int half, bool ok, const float* consts) {
+template <Kind KIND, int BN, int P, Epi EPI, typename WaitAcc>
+__device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int m0, int n0, uint32_t t_row,
+                                              int row, int half, bool ok_in, const float* consts, WaitAcc&& wait_acc) {
   const GemmSeg& sg = args.seg[si];
   const int m = m0 + row;
-  const bool row_ok = ok && (m < args.M);
+  bool ok = ok_in;
+  bool row_ok = ok && (m < args.M);
   int orow = m;
   if (args.rows_per_group > 0) orow = (m / args.rows_per_group) * args.group_stride + (m % args.rows_per_group);
   orow += args.row_offset;
@@ -192,6 +194,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, int si, int 
   };
 
   if constexpr (EPI == Epi::Rope) {
+    ok = ok && wait_acc();
+    row_ok = ok && (m < args.M);
     // one 64-column head at a time (the two warps of a lane quarter take alternate heads), rotated in two
     // blocks of 16 pairs (columns j..j+15 with j+32..j+47) to bound register use
     for (int c = half * 64; c < BN; c += 128) {
@@ -253,17 +257,32 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, int si, int 
   } else {
     constexpr int kHalf = BN / 2;
     constexpr int kChunk = kHalf >= 32 ? 32 : 16;  // columns per TMEM round trip
+    constexpr int kNC = kHalf / kChunk;            // chunks per warp and tile
+    constexpr int kRes = (EPI == Epi::Resid) ? kChunk / 8 : 1;
     const float ra = (EPI == Epi::GeluQuant && args.qout) ? __frcp_rn(args.q_act) : 0.0f;
-    for (int cb = half * kHalf; cb < (half + 1) * kHalf; cb += kChunk) {
-      uint32_t r[kChunk], r2[P == 2 ? kChunk : 1];
+    const int c0 = half * kHalf;
+    const int rrow = (EPI == Epi::Resid && args.resid_rows > 0) ? (m % args.resid_rows) : orow;
+    // residual rows do not depend on the accumulator: fetch them ahead of it
+    auto load_res = [&](int4 (&res)[kRes], int cb) {
+      if constexpr (EPI == Epi::Resid) {
+        const bool in = ok && m < args.M;
+        const __nv_bfloat16* rs = args.resid + static_cast<size_t>(rrow) * args.ldr + n0 + cb;
+#pragma unroll
+        for (int u = 0; u < kRes; ++u)
+          res[u] = (in && n0 + cb + u * 8 < sg.n) ? *reinterpret_cast<const int4*>(rs + u * 8) : make_int4(0, 0, 0, 0);
+      }
+    };
+    auto tmem_load = [&](uint32_t (&r)[kChunk], uint32_t (&r2)[P == 2 ? kChunk : 1], int cb) {
       if (ok) {
 #pragma unroll
         for (int u = 0; u < kChunk; u += 16) {
           tmem_ld16(t_row + cb + u, *reinterpret_cast<uint32_t(*)[16]>(&r[u]));
           if constexpr (P == 2) tmem_ld16(t_row + BN + cb + u, *reinterpret_cast<uint32_t(*)[16]>(&r2[u]));
         }
-        tmem_ld_wait();
       }
+    };
+    auto process = [&](const uint32_t (&r)[kChunk], const uint32_t (&r2)[P == 2 ? kChunk : 1], const int4 (&res)[kRes],
+                       int cb) {
 #pragma unroll 1
       for (int u = 0; u < kChunk; u += 16) {
         const int nb = n0 + cb + u;
@@ -310,10 +329,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, int si, int 
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = silu_f(v[j]);
           } else if constexpr (EPI == Epi::Resid) {
-            const int rrow = args.resid_rows > 0 ? (m % args.resid_rows) : orow;
-            const __nv_bfloat16* rs = args.resid + static_cast<size_t>(rrow) * args.ldr + nb;
-            const int4 ra4 = *reinterpret_cast<const int4*>(rs);
-            const int4 rb4 = *reinterpret_cast<const int4*>(rs + 8);
+            const int4 ra4 = res[u / 8], rb4 = res[u / 8 + 1];
             const __nv_bfloat16* h0 = reinterpret_cast<const __nv_bfloat16*>(&ra4);
             const __nv_bfloat16* h1 = reinterpret_cast<const __nv_bfloat16*>(&rb4);
 #pragma unroll
@@ -358,8 +374,30 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, int si, int 
           *reinterpret_cast<int4*>(o + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
         }
       }
+    };
+    // tcgen05.ld writes its registers asynchronously until tcgen05.wait::ld, so each chunk's TMEM load is
+    // waited for before any other register work; the residual (an ordinary load) of the next chunk is
+    // requested before that wait so its latency overlaps it.
+    uint32_t r[kChunk], r2[P == 2 ? kChunk : 1];
+    int4 resA[kRes], resB[kRes];
+    load_res(resA, c0);
+    ok = ok && wait_acc();
+    row_ok = ok && (m < args.M);
+#pragma unroll 1
+    for (int i = 0; i < kNC; i += 2) {
+      tmem_load(r, r2, c0 + i * kChunk);
+      if (i + 1 < kNC) load_res(resB, c0 + (i + 1) * kChunk);
+      if (ok) tmem_ld_wait();
+      process(r, r2, resA, c0 + i * kChunk);
+      if (i + 1 < kNC) {
+        tmem_load(r, r2, c0 + (i + 1) * kChunk);
+        if (i + 2 < kNC) load_res(resA, c0 + (i + 2) * kChunk);
+        if (ok) tmem_ld_wait();
+        process(r, r2, resB, c0 + (i + 1) * kChunk);
+      }
     }
   }
+  return ok;
 }
 
 template <Kind KIND, int BN, int P, int STAGES, Epi EPI>
@@ -386,7 +424,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 4);
+      mbar_init(&conv[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -422,6 +460,27 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
         prefetch_tmap(&args.ta[p]);
         prefetch_tmap(&args.tb[p]);
       }
+      constexpr uint32_t kBBytes = T::kConvert ? S::kRawTile : S::kBTile;
+      auto b_dst = [&](uint8_t* st, int p) {
+        return T::kConvert ? st + P * (S::kATile + S::kBTile) + p * S::kRawTile : st + P * S::kATile + p * S::kBTile;
+      };
+      // Weights packed before the previous kernel started (weights_resident) do not depend on it: the first
+      // tile's first STAGES weight tiles are requested before waiting, so they stream in while it finishes.
+      int pre = 0;
+      if (args.weights_resident && blockIdx.x < n_tiles_total) {
+        int si, m0, n0;
+        tile_coord<BN, P>(args, blockIdx.x, si, m0, n0);
+        pre = k_tiles < STAGES ? k_tiles : STAGES;
+        for (int kt = 0; kt < pre; ++kt) {
+          uint8_t* st = smem + kt * S::kStage;
+          mbar_arrive_expect_tx(&full[kt], P * (S::kATile + kBBytes));
+#pragma unroll
+          for (int p = 0; p < P; ++p)
+            tma_load_2d(b_dst(st, p), &args.tb[(P == 1) ? si : p], &full[kt], kt * T::kBK, n0);
+        }
+      }
+      pdl_wait();
+      pdl_trigger();
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x) {
@@ -430,19 +489,21 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
         for (int kt = 0; kt < k_tiles; ++kt, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
-          if (!(ok = bounded_wait(&empty[s], ph ^ 1))) break;
           uint8_t* st = smem + s * S::kStage;
-          constexpr uint32_t kBBytes = T::kConvert ? S::kRawTile : S::kBTile;
+          if (static_cast<int>(g) < pre) {  // weights already requested: only the activations remain
+#pragma unroll
+            for (int p = 0; p < P; ++p)
+              tma_load_2d(st + p * S::kATile, &args.ta[(P == 1) ? si : p], &full[s], kt * T::kBK, m0);
+            if (g == 0) stamp(args.dbg, 2);
+            continue;
+          }
+          if (!(ok = bounded_wait(&empty[s], ph ^ 1))) break;
           mbar_arrive_expect_tx(&full[s], P * (S::kATile + kBBytes));
-          if (g == 0) stamp(args.dbg, 2);
 #pragma unroll
           for (int p = 0; p < P; ++p) {
             const int mi = (P == 1) ? si : p;
-            uint8_t* a_dst = st + p * S::kATile;
-            uint8_t* b_dst = T::kConvert ? st + P * (S::kATile + S::kBTile) + p * S::kRawTile
-                                         : st + P * S::kATile + p * S::kBTile;
-            tma_load_2d(a_dst, &args.ta[mi], &full[s], kt * T::kBK, m0);
-            tma_load_2d(b_dst, &args.tb[mi], &full[s], kt * T::kBK, n0);
+            tma_load_2d(st + p * S::kATile, &args.ta[mi], &full[s], kt * T::kBK, m0);
+            tma_load_2d(b_dst(st, p), &args.tb[mi], &full[s], kt * T::kBK, n0);
           }
         }
       }
@@ -499,6 +560,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
     float* const_base = reinterpret_cast<float*>(smem + S::kConstOff);
     uint32_t lt = 0;
     bool ok = true;
+    pdl_wait();  // residuals / outputs may be touched by the previous kernel
     // Every epilogue warp runs every iteration (also after a failed wait) so that the named barrier
     // below is reached the same number of times by all of them.
     for (int t = blockIdx.x; t < n_tiles_total; t += gridDim.x, ++lt) {
@@ -525,11 +587,14 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
       }
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
       if (lt == 0 && etid == 0) stamp(args.dbg, 6);
-      const bool ok_t = ok && __all_sync(0xffffffffu, bounded_wait(&tfull[ab], use & 1));
-      tc_fence_after();
-      if (lt == 0 && etid == 0) stamp(args.dbg, 7);
+      auto wait_acc = [&]() -> bool {
+        const bool w = __all_sync(0xffffffffu, bounded_wait(&tfull[ab], use & 1));
+        tc_fence_after();
+        if (lt == 0 && etid == 0) stamp(args.dbg, 7);
+        return w;
+      };
       const uint32_t t_row = tmem_base + ab * S::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<KIND, BN, P, EPI>(args, si, m0, n0, t_row, row, half, ok_t, cst);
+      const bool ok_t = epilogue_tile<KIND, BN, P, EPI>(args, si, m0, n0, t_row, row, half, ok, cst, wait_acc);
       if (lt == 0 && etid == 0) stamp(args.dbg, 8);
       tc_fence_before();
       __syncwarp();
@@ -537,28 +602,32 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
       ok = ok_t;
     }
   } else if constexpr (T::kConvert) {
-    // ---------------- W8A16 weight conversion, warps 10..13:
-    // each stage: P x [BN rows x 64 int8] staging -> P x [BN rows x 64 bf16] swizzled operand tiles
-    const int et = (warp - 2 - kEpiWarps) * 32 + lane;  // 0..127
+    // ---------------- W8A16 weight conversion, warps 10..13: converter warp cw owns the pipeline slots
+    // s with s % 4 == cw and converts every stage that lands in them (all BN rows), so up to four stages
+    // are converted concurrently.  Owning slots (not stage numbers) keeps each slot's phases in order in
+    // one warp, which the parity waits on full[s] rely on.  Each stage:
+    // P x [BN rows x 64 int8] staging -> P x [BN rows x 64 bf16] in the 128B-swizzled operand layout.
+    const int cw = warp - 2 - kEpiWarps;  // 0..3
+    constexpr int kPer = BN * 4 / 32;      // (row, 16-byte chunk) items per lane and stage
     uint32_t g = 0;
     bool ok = true;
-    constexpr int kPer = BN * 4 / 128;  // (row, 16-byte chunk) items per converter thread and stage
     for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x) {
       int si, m0, n0;
       tile_coord<BN, P>(args, t, si, m0, n0);
-      // the weight scales of this thread's rows, loaded once per tile (not once per stage)
+      // the weight scales of this lane's rows, loaded once per tile
       float wsr[P][kPer];
 #pragma unroll
       for (int p = 0; p < P; ++p) {
         const GemmSeg& sp = args.seg[P == 1 ? si : p];
 #pragma unroll
         for (int i = 0; i < kPer; ++i) {
-          const int gn = n0 + ((et + i * 128) >> 2);
+          const int gn = n0 + ((lane + i * 32) >> 2);
           wsr[p][i] = (sp.wscale != nullptr && gn < sp.n) ? sp.wscale[gn] : 1.0f;
         }
       }
       for (int kt = 0; kt < k_tiles; ++kt, ++g) {
         const int s = g % STAGES;
+        if ((s & 3) != cw) continue;
         const uint32_t ph = (g / STAGES) & 1;
         ok = __all_sync(0xffffffffu, bounded_wait(&full[s], ph));
         if (!ok) break;
@@ -567,19 +636,18 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
         for (int p = 0; p < P; ++p) {
           const int8_t* raw = reinterpret_cast<const int8_t*>(st + P * (S::kATile + S::kBTile) + p * S::kRawTile);
           uint8_t* bt = st + P * S::kATile + p * S::kBTile;
-#pragma unroll
+#pragma unroll 4
           for (int i = 0; i < kPer; ++i) {
-            const int idx = et + i * 128;
+            const int idx = lane + i * 32;
             const int r = idx >> 2, c = idx & 3;
             const float ws = wsr[p][i];
             const int4 v = *reinterpret_cast<const int4*>(raw + r * 64 + c * 16);
             const int8_t* b8 = reinterpret_cast<const int8_t*>(&v);
             uint32_t packed[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 8; ++j)
               packed[j] = pack_bf16_rn(__fmul_rn(static_cast<float>(b8[2 * j]), ws),
                                        __fmul_rn(static_cast<float>(b8[2 * j + 1]), ws));
-            }
             // logical 16-byte chunks 2c and 2c+1 of row r, 128B swizzle: chunk ^ (r & 7)
             const int c0 = (2 * c) ^ (r & 7), c1 = (2 * c + 1) ^ (r & 7);
             *reinterpret_cast<int4*>(bt + r * 128 + c0 * 16) = make_int4(packed[0], packed[1], packed[2], packed[3]);

@@ -10,6 +10,8 @@ namespace svla {
 // (deploy/validate_fused_rope_layout_math.py:28-42): freq = (2/64)*i, timescale = w^freq,
 // radians = p / timescale.
 __global__ void rope_table_kernel(float2* cs, int max_pos, float max_wavelength) {
+  pdl_wait();
+  pdl_trigger();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= max_pos * 32) return;
   const int p = idx / 32, i = idx % 32;
@@ -51,6 +53,8 @@ __device__ __forceinline__ int prefix_pad(const MaskArgs& a, int b, int i) {
 
 // one block per batch row
 __global__ void masks_kernel(const MaskArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   const int Lp = 2 * a.n_img + a.n_lang + 1;
   extern __shared__ int sh[];  // pad[Lp], cum[Lp]
@@ -91,6 +95,8 @@ __global__ void masks_kernel(const MaskArgs a) {
 __global__ void embed_tokens_kernel(const long long* tokens, int B, int T, const __nv_bfloat16* table, int vocab,
                                     int H, float scale, __nv_bfloat16* out, int rows_per_batch, int row_offset,
                                     int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (w >= B * T) return;
   const int b = w / T, t = w % T;
@@ -118,6 +124,8 @@ __global__ void embed_tokens_kernel(const long long* tokens, int B, int T, const
 // SigLIP patch extraction: images fp32 [N, C, S, S] -> bf16 patches [N * (S/P)^2, C*P*P] in the
 // (c, kh, kw) order of a Conv2d weight [out, C, P, P] flattened.  One thread per 8 outputs (8 kw).
 __global__ void im2col_kernel(const float* img, int N, int C, int S, int P, __nv_bfloat16* out) {
+  pdl_wait();
+  pdl_trigger();
   const int G = S / P;
   const long long total = static_cast<long long>(N) * G * G * C * P * (P / 8);
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -147,18 +155,24 @@ __global__ void im2col_kernel(const float* img, int N, int C, int S, int P, __nv
 }
 
 __global__ void f32_to_bf16_kernel(const float* x, __nv_bfloat16* y, long long n) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __float2bfloat16_rn(x[i]);
 }
 
 // y = 1 / x, correctly rounded
 __global__ void reciprocal_kernel(const float* x, float* y, long long n) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __frcp_rn(x[i]);
 }
 
 // x_t = noise (fp32 copy) and its bf16 image
 __global__ void euler_init_kernel(const float* noise, float* xt, __nv_bfloat16* xt_bf16, long long n) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) {
     const float v = noise[i];
@@ -177,6 +191,8 @@ namespace svla {
 __global__ void rope_layout_kernel(const __nv_bfloat16* q_raw, const __nv_bfloat16* k_raw, const int* pos,
                                    __nv_bfloat16* q_out, __nv_bfloat16* k_out, int B, int L, int Hq, int Hkv,
                                    float max_wavelength) {
+  pdl_wait();
+  pdl_trigger();
   const long long nq = static_cast<long long>(B) * L * Hq * 32;
   const long long nk = static_cast<long long>(B) * L * Hkv * 32;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;

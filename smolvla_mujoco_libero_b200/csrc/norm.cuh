@@ -40,6 +40,8 @@ struct NormQuantArgs {
 
 template <int NV, bool LAYERNORM>
 __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= a.M) return;
@@ -148,6 +150,8 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) 
 // q[m, k] = round((x[m, k] / s[k]) / a).clamp(-128, 127), x in bf16.  8 elements per thread.
 __global__ void smooth_quant_kernel(const __nv_bfloat16* x, int ldx, const float* s, float act, int8_t* q, int ldq,
                                     int M, int K) {
+  pdl_wait();
+  pdl_trigger();
   const int kv = K / 8;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<long long>(M) * kv) return;
@@ -166,6 +170,8 @@ __global__ void smooth_quant_kernel(const __nv_bfloat16* x, int ldx, const float
 // One block per output row.
 __global__ void __launch_bounds__(256) pack_weight_kernel(const __nv_bfloat16* w, int K, const float* smooth,
                                                           int8_t* q, float* wscale) {
+  pdl_wait();
+  pdl_trigger();
   const int n = blockIdx.x;
   const __nv_bfloat16* wr = w + static_cast<size_t>(n) * K;
   float amax = 0.f;

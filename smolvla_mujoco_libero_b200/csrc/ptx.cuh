@@ -31,6 +31,16 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// Kernels are launched with programmatic stream serialisation: a kernel may start while the previous one
+// in the stream is still running.  Every kernel calls pdl_wait() before it reads anything an earlier
+// kernel wrote or writes anything an earlier kernel may still read (pdl_wait returns once the previous
+// grid has completed and its memory is visible), and only then pdl_trigger(), so that when a kernel
+// starts, every kernel before its immediate predecessor has completed.  Without the launch attribute
+// both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

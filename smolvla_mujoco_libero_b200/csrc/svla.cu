@@ -7,7 +7,9 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <utility>
 #include <mutex>
 #include <string>
 
@@ -40,6 +42,34 @@ int32_t check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return SVLA_OK;
+}
+
+// Programmatic dependent launch (see pdl_wait in ptx.cuh): on by default, SVLA_PDL=0 turns it off.
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("SVLA_PDL");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+template <typename... KArgs, typename... Args>
+int32_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* name,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+  return check_launch(name);
 }
 
 int* device_error_ptr() {
@@ -116,8 +146,7 @@ int32_t launch_gemm_inst(const GemmArgs& args, dim3 grid, cudaStream_t stream) {
     if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  kern<<<grid, gemm_threads<K>(), S::kBytes, stream>>>(args);
-  return check_launch("gemm_sm100_kernel");
+  return launch(kern, grid, dim3(gemm_threads<K>()), S::kBytes, stream, "gemm_sm100_kernel", args);
 }
 
 template <Kind K, int BN, int P>
@@ -268,6 +297,7 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   args.xt_bf16 = static_cast<__nv_bfloat16*>(d->xt_bf16);
   args.err = device_error_ptr();
   args.dbg = reinterpret_cast<unsigned long long*>(d->debug_clock);
+  args.weights_resident = d->weights_resident;
   if (epi == Epi::Resid && !d->resid) return fail(SVLA_ERR_ARG, "RESID needs a residual");
   if (epi == Epi::Rope && (!d->rope_cs || !d->pos || d->max_pos <= 0)) return fail(SVLA_ERR_ARG, "ROPE needs rope_cs/pos");
   if (epi == Epi::GeluQuant && d->qout && (!d->q_smooth || d->q_act <= 0.f))
@@ -314,8 +344,7 @@ int32_t svla_device_error(int32_t* code, int32_t reset) {
 int32_t svla_pack_weight_i8(const void* weight, const float* smooth, int32_t n, int32_t k, int8_t* qweight,
                             float* wscale, svla_stream_t stream) {
   if (!weight || !qweight || !wscale || n <= 0 || k <= 0) return fail(SVLA_ERR_ARG, "svla_pack_weight_i8: bad args");
-  pack_weight_kernel<<<n, 256, 0, cs(stream)>>>(static_cast<const __nv_bfloat16*>(weight), k, smooth, qweight, wscale);
-  return check_launch("pack_weight_kernel");
+  return launch(pack_weight_kernel, dim3(n), dim3(256), 0, cs(stream), "pack_weight_kernel", static_cast<const __nv_bfloat16*>(weight), k, smooth, qweight, wscale);
 }
 
 int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, float act_scale, int8_t* q, int32_t ldq,
@@ -323,9 +352,8 @@ int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, fl
   if (!x || !q || m <= 0 || k <= 0 || k % 8 || ldx % 8 || ldq % 8 || act_scale <= 0.f)
     return fail(SVLA_ERR_ARG, "svla_quantize_smooth: bad args (k, ldx, ldq must be multiples of 8)");
   const long long total = static_cast<long long>(m) * (k / 8);
-  smooth_quant_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, cs(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, smooth, act_scale, q, ldq, m, k);
-  return check_launch("smooth_quant_kernel");
+  return launch(smooth_quant_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, cs(stream), "smooth_quant_kernel",
+                static_cast<const __nv_bfloat16*>(x), ldx, smooth, act_scale, q, ldq, m, k);
 }
 
 int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream) { return run_gemm(desc, cs(stream)); }
@@ -421,11 +449,10 @@ int32_t svla_norm_quant(const svla_norm_desc* d, svla_stream_t stream) {
   const int nv = (d->k + 255) / 256;
   const unsigned blocks = static_cast<unsigned>((d->m + 7) / 8);
   cudaStream_t st = cs(stream);
-#define SVLA_NORM(NV)                                                             \
-  if (nv <= NV) {                                                                 \
-    if (d->layernorm) norm_quant_kernel<NV, true><<<blocks, 256, 0, st>>>(a);     \
-    else norm_quant_kernel<NV, false><<<blocks, 256, 0, st>>>(a);                 \
-    return check_launch("norm_quant_kernel");                                     \
+#define SVLA_NORM(NV)                                                                                     \
+  if (nv <= NV) {                                                                                         \
+    if (d->layernorm) return launch(norm_quant_kernel<NV, true>, dim3(blocks), dim3(256), 0, st, "norm_quant_kernel", a); \
+    return launch(norm_quant_kernel<NV, false>, dim3(blocks), dim3(256), 0, st, "norm_quant_kernel", a);  \
   }
   SVLA_NORM(3)
   SVLA_NORM(4)
@@ -485,8 +512,7 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
     configured[dev] = true;
   }
   dim3 grid((d->lq + attn_detail::kRows - 1) / attn_detail::kRows, d->hq, d->batch);
-  attention_kernel<<<grid, attn_detail::kRows * 2, smem, cs(stream)>>>(a);
-  return check_launch("attention_kernel");
+  return launch(attention_kernel, dim3(grid), dim3(attn_detail::kRows * 2), smem, cs(stream), "attention_kernel", a);
 }
 
 int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* pos, void* q_out, void* k_out,
@@ -496,18 +522,16 @@ int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* po
       q_heads % kv_heads || max_wavelength <= 0.f)
     return fail(SVLA_ERR_ARG, "svla_rope_layout: bad args");
   const long long total = static_cast<long long>(batch) * seq_len * (q_heads + kv_heads) * 32;
-  rope_layout_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, cs(stream)>>>(
-      static_cast<const __nv_bfloat16*>(q_raw), static_cast<const __nv_bfloat16*>(k_raw), pos,
+  return launch(rope_layout_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, cs(stream), "rope_layout_kernel",
+                static_cast<const __nv_bfloat16*>(q_raw), static_cast<const __nv_bfloat16*>(k_raw), pos,
       static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out), batch, seq_len, q_heads, kv_heads,
       max_wavelength);
-  return check_launch("rope_layout_kernel");
 }
 
 int32_t svla_rope_table(float* c, int32_t max_pos, float max_wavelength, svla_stream_t stream) {
   if (!c || max_pos <= 0 || max_wavelength <= 0.f) return fail(SVLA_ERR_ARG, "svla_rope_table: bad args");
-  rope_table_kernel<<<(max_pos * 32 + 255) / 256, 256, 0, cs(stream)>>>(reinterpret_cast<float2*>(c), max_pos,
+  return launch(rope_table_kernel, dim3((max_pos * 32 + 255) / 256), dim3(256), 0, cs(stream), "rope_table_kernel", reinterpret_cast<float2*>(c), max_pos,
                                                                          max_wavelength);
-  return check_launch("rope_table_kernel");
 }
 
 int32_t svla_build_masks(const uint8_t* img_mask0, const uint8_t* img_mask1, const uint8_t* lang_mask, int32_t batch,
@@ -520,8 +544,7 @@ int32_t svla_build_masks(const uint8_t* img_mask0, const uint8_t* img_mask1, con
   MaskArgs a{img_mask0, img_mask1, lang_mask, batch, n_img, n_lang, chunk, prefix_mask, prefix_pos,
              self_mask, cross_mask, suffix_pos, cross_pos};
   const int lp = 2 * n_img + n_lang + 1;
-  masks_kernel<<<batch, 256, 2 * lp * sizeof(int), cs(stream)>>>(a);
-  return check_launch("masks_kernel");
+  return launch(masks_kernel, dim3(batch), dim3(256), 2 * lp * sizeof(int), cs(stream), "masks_kernel", a);
 }
 
 int32_t svla_embed_tokens(const int64_t* tokens, int32_t batch, int32_t t, const void* table, int32_t vocab,
@@ -530,37 +553,36 @@ int32_t svla_embed_tokens(const int64_t* tokens, int32_t batch, int32_t t, const
   if (!tokens || !table || !out || batch <= 0 || t <= 0 || vocab <= 0 || hidden <= 0 || hidden % 8)
     return fail(SVLA_ERR_ARG, "svla_embed_tokens: bad args");
   const long long threads = static_cast<long long>(batch) * t * 32;
-  embed_tokens_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, cs(stream)>>>(
-      reinterpret_cast<const long long*>(tokens), batch, t, static_cast<const __nv_bfloat16*>(table), vocab, hidden,
+  return launch(embed_tokens_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, cs(stream), "embed_tokens_kernel",
+                reinterpret_cast<const long long*>(tokens), batch, t, static_cast<const __nv_bfloat16*>(table), vocab, hidden,
       scale, static_cast<__nv_bfloat16*>(out), rows_per_batch, row_offset, device_error_ptr());
-  return check_launch("embed_tokens_kernel");
 }
 
 int32_t svla_im2col(const float* images, int32_t n, int32_t c, int32_t s, int32_t p, void* out, svla_stream_t stream) {
   if (!images || !out || n <= 0 || c <= 0 || p <= 0 || p % 8 || s % p) return fail(SVLA_ERR_ARG, "svla_im2col: bad args");
   const long long total = static_cast<long long>(n) * (s / p) * (s / p) * c * p * (p / 8);
-  im2col_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, cs(stream)>>>(images, n, c, s, p,
+  return launch(im2col_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, cs(stream), "im2col_kernel",
+                images, n, c, s, p,
                                                                                      static_cast<__nv_bfloat16*>(out));
-  return check_launch("im2col_kernel");
 }
 
 int32_t svla_f32_to_bf16(const float* x, void* y, int64_t n, svla_stream_t stream) {
   if (!x || !y || n <= 0) return fail(SVLA_ERR_ARG, "svla_f32_to_bf16: bad args");
-  f32_to_bf16_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cs(stream)>>>(x, static_cast<__nv_bfloat16*>(y), n);
-  return check_launch("f32_to_bf16_kernel");
+  return launch(f32_to_bf16_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, cs(stream), "f32_to_bf16_kernel",
+                x, static_cast<__nv_bfloat16*>(y), n);
 }
 
 int32_t svla_reciprocal(const float* x, float* y, int64_t n, svla_stream_t stream) {
   if (!x || !y || n <= 0) return fail(SVLA_ERR_ARG, "svla_reciprocal: bad args");
-  reciprocal_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cs(stream)>>>(x, y, n);
-  return check_launch("reciprocal_kernel");
+  return launch(reciprocal_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, cs(stream), "reciprocal_kernel",
+                x, y, n);
 }
 
 int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n, svla_stream_t stream) {
   if (!noise || !xt || !xt_bf16 || n <= 0) return fail(SVLA_ERR_ARG, "svla_euler_init: bad args");
-  euler_init_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cs(stream)>>>(noise, xt,
+  return launch(euler_init_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, cs(stream), "euler_init_kernel",
+                noise, xt,
                                                                                     static_cast<__nv_bfloat16*>(xt_bf16), n);
-  return check_launch("euler_init_kernel");
 }
 
 }  // extern "C"

@@ -226,7 +226,8 @@ class SmolVLARunner:
         self.launches.append((_TAP, (list(mods), buf)))
 
     def _gemm(self, kind, epi, m, k, segs, **kw):
-        d = ops.gemm_desc(kind, epi, m, k, segs, **kw)
+        # every B operand here is a packed weight, written when the model was built
+        d = ops.gemm_desc(kind, epi, m, k, segs, weights_resident=1, **kw)
         self._keep.append(segs)
         self._add(L.lib().svla_gemm, d)
 
