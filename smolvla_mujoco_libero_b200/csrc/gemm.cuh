@@ -283,7 +283,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
     };
     auto process = [&](const uint32_t (&r)[kChunk], const uint32_t (&r2)[P == 2 ? kChunk : 1], const int4 (&res)[kRes],
                        int cb) {
-#pragma unroll 1
+#pragma unroll
       for (int u = 0; u < kChunk; u += 16) {
         const int nb = n0 + cb + u;
         if (!row_ok || nb >= sg.n) continue;
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 1);
+      mbar_init(&conv[s], 4);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -602,32 +602,29 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
       ok = ok_t;
     }
   } else if constexpr (T::kConvert) {
-    // ---------------- W8A16 weight conversion, warps 10..13: converter warp cw owns the pipeline slots
-    // s with s % 4 == cw and converts every stage that lands in them (all BN rows), so up to four stages
-    // are converted concurrently.  Owning slots (not stage numbers) keeps each slot's phases in order in
-    // one warp, which the parity waits on full[s] rely on.  Each stage:
-    // P x [BN rows x 64 int8] staging -> P x [BN rows x 64 bf16] in the 128B-swizzled operand layout.
-    const int cw = warp - 2 - kEpiWarps;  // 0..3
-    constexpr int kPer = BN * 4 / 32;      // (row, 16-byte chunk) items per lane and stage
+    // ---------------- W8A16 weight conversion, warps 10..13, all four on every stage:
+    // P x [BN rows x 64 int8] staging -> P x [BN rows x 64 bf16(q * w_s[n])] in the 128B-swizzled operand
+    // layout.  The conversion uses integer / FMA arithmetic only (exact small-int -> fp32, fp32 multiply,
+    // integer round-to-nearest-even), which keeps it off the slow conversion unit.
+    const int et = (warp - 2 - kEpiWarps) * 32 + lane;  // 0..127
+    constexpr int kPer = BN * 4 / 128;                   // (row, 16-byte chunk) items per thread and stage
     uint32_t g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x) {
       int si, m0, n0;
       tile_coord<BN, P>(args, t, si, m0, n0);
-      // the weight scales of this lane's rows, loaded once per tile
-      float wsr[P][kPer];
+      float wsr[P][kPer];  // the weight scales of this thread's rows, loaded once per tile
 #pragma unroll
       for (int p = 0; p < P; ++p) {
         const GemmSeg& sp = args.seg[P == 1 ? si : p];
 #pragma unroll
         for (int i = 0; i < kPer; ++i) {
-          const int gn = n0 + ((lane + i * 32) >> 2);
+          const int gn = n0 + ((et + i * 128) >> 2);
           wsr[p][i] = (sp.wscale != nullptr && gn < sp.n) ? sp.wscale[gn] : 1.0f;
         }
       }
       for (int kt = 0; kt < k_tiles; ++kt, ++g) {
         const int s = g % STAGES;
-        if ((s & 3) != cw) continue;
         const uint32_t ph = (g / STAGES) & 1;
         ok = __all_sync(0xffffffffu, bounded_wait(&full[s], ph));
         if (!ok) break;
@@ -636,18 +633,20 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
         for (int p = 0; p < P; ++p) {
           const int8_t* raw = reinterpret_cast<const int8_t*>(st + P * (S::kATile + S::kBTile) + p * S::kRawTile);
           uint8_t* bt = st + P * S::kATile + p * S::kBTile;
-#pragma unroll 4
+#pragma unroll
           for (int i = 0; i < kPer; ++i) {
-            const int idx = lane + i * 32;
+            const int idx = et + i * 128;
             const int r = idx >> 2, c = idx & 3;
             const float ws = wsr[p][i];
             const int4 v = *reinterpret_cast<const int4*>(raw + r * 64 + c * 16);
             const int8_t* b8 = reinterpret_cast<const int8_t*>(&v);
             uint32_t packed[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              packed[j] = pack_bf16_rn(__fmul_rn(static_cast<float>(b8[2 * j]), ws),
-                                       __fmul_rn(static_cast<float>(b8[2 * j + 1]), ws));
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t lo = bf16_rn_bits(__fmul_rn(small_int_to_f32(b8[2 * j]), ws));
+              const uint32_t hi = bf16_rn_bits(__fmul_rn(small_int_to_f32(b8[2 * j + 1]), ws));
+              packed[j] = __byte_perm(lo, hi, 0x7632);
+            }
             // logical 16-byte chunks 2c and 2c+1 of row r, 128B swizzle: chunk ^ (r & 7)
             const int c0 = (2 * c) ^ (r & 7), c1 = (2 * c + 1) ^ (r & 7);
             *reinterpret_cast<int4*>(bt + r * 128 + c0 * 16) = make_int4(packed[0], packed[1], packed[2], packed[3]);

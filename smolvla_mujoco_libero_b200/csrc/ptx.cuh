@@ -193,6 +193,16 @@ __device__ __forceinline__ uint32_t pack_bf16_rn(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// The same rounding with integer operations only (for loops where the conversion unit is the bottleneck):
+// round-to-nearest-even of a finite fp32 to bf16, as the fp32 bit pattern with the low 16 bits clear.
+__device__ __forceinline__ uint32_t bf16_rn_bits(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+}
+// exact int32 -> fp32 for |i| < 2^22 without a conversion instruction: 0x4B400000 is 1.5 * 2^23, where
+// the fp32 spacing is exactly 1
+__device__ __forceinline__ float small_int_to_f32(int i) { return __int_as_float(0x4B400000 + i) - 12582912.0f; }
+
 // Round-half-even of |y| < 2^22 to an integer with one fp32 add (the sum lands where the spacing is 1).
 __device__ __forceinline__ int round_rn_small(float y, float& r) {
   const float t = __fadd_rn(y, 12582912.0f);
