@@ -9,9 +9,10 @@
 // Persistent: one CTA per SM walks output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... in N-fastest
 // order (the CTAs running at one time share A row-blocks; the weights stay L2-resident).  Accumulators
 // are double-buffered in TMEM (2 x P x BN columns) so the epilogue of one tile overlaps the MMAs of the next.
-// Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma (one lane), warps 2-5 run the
-// epilogue (TMEM lanes 32*(warp%4) .. +31), and for W8A16 warps 6-9 convert the int8 weight stages to
-// bf16.  Tile: 128 rows (M) x BN columns (N) x 128 bytes of K per pipeline stage.
+// Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma (one lane), warps 2-9 run the
+// epilogue (two warps per TMEM lane quarter 32*(warp%4) .. +31, each on half the tile's columns), and for
+// W8A16 warps 10-13 convert the int8 weight stages to bf16.  Tile: 128 rows (M) x BN columns (N) x 128
+// bytes of K per pipeline stage.
 //
 // "Segments" let one launch cover several linears that share M and K but have their own A operand,
 // weights, scales and outputs (q/k/v with per-projection SmoothQuant activations).  "Pairs" (P = 2)
@@ -128,14 +129,17 @@ template <Kind KIND>
 constexpr int gemm_threads() { return 32 * (2 + kEpiWarps + (KindTraits<KIND>::kConvert ? 4 : 0)); }
 
 // SiLU x * sigmoid(x) and tanh-GELU 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi)(x + 0.044715 x^3),
-// both evaluated as x / (1 + e^-z) with the fast exponential and divide: the results are rounded to bf16
-// (8 significant bits) right after, far coarser than these approximations (about 2^-21 relative).
-__device__ __forceinline__ float sigmoid_mul(float x, float z) { return __fdividef(x, 1.0f + __expf(-z)); }
-__device__ __forceinline__ float silu_f(float x) { return sigmoid_mul(x, x); }
+// both evaluated as x / (1 + 2^(-z log2 e)) with the hardware 2^x and reciprocal approximations: the results
+// are rounded to bf16 (8 significant bits) right after, far coarser than these (about 2^-20 relative).
+// For x -> -inf the exponential overflows to +inf and the quotient goes to -0, the limit of both.
+__device__ __forceinline__ float silu_f(float x) {
+  return __fmul_rn(x, rcp_approx(__fadd_rn(1.0f, ex2_approx(__fmul_rn(x, -1.4426950408889634f)))));
+}
 __device__ __forceinline__ float gelu_tanh_f(float x) {
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  const float u = k0 * (x + k1 * x * x * x);
-  return sigmoid_mul(x, 2.0f * u);
+  // -2 u log2(e) = x (c0 + c1 x^2), c0 = -2 sqrt(2/pi) log2(e), c1 = 0.044715 c0
+  constexpr float c0 = -2.302208198f, c1 = -0.1029432396f;
+  const float z = __fmul_rn(x, __fmaf_rn(c1, __fmul_rn(x, x), c0));
+  return __fmul_rn(x, rcp_approx(__fadd_rn(1.0f, ex2_approx(z))));
 }
 
 template <int BN, int P>
@@ -165,10 +169,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
   if (args.rows_per_group > 0) orow = (m / args.rows_per_group) * args.group_stride + (m % args.rows_per_group);
   orow += args.row_offset;
 
-  // per-column constants of 16 columns starting at nb (staged in shared memory for this tile):
-  // set 0 belongs to the tile's segment, set 1 to the second linear of a pair
-  auto col_consts = [&](const GemmSeg& g, int nb, float (&sc)[16], float (&bi)[16]) {
-    const int set = (&g == &args.seg[si]) ? 0 : 1;
+  // per-column constants of 16 columns starting at nb (staged in shared memory for this tile): set 0
+  // belongs to the tile's segment, set 1 to the second linear of a pair.  A missing weight scale is staged
+  // as 1 and a missing bias as -0, so both apply unconditionally as exact no-ops.
+  auto col_consts = [&](int set, int nb, float (&sc)[16], float (&bi)[16]) {
     const float* scs = consts + (2 * set) * BN + (nb - n0);
     const float* bis = consts + (2 * set + 1) * BN + (nb - n0);
 #pragma unroll
@@ -179,18 +183,34 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
       bi[j] = b.x; bi[j + 1] = b.y; bi[j + 2] = b.z; bi[j + 3] = b.w;
     }
   };
-  // v = ((acc * a) * w_s + b_bf16) + b_f32   (I8),   acc + b_bf16 + b_f32 otherwise.
-  auto dequant = [&](const GemmSeg& g, uint32_t raw, float sc, float bi, int n) -> float {
-    float v;
-    if constexpr (KIND == Kind::I8) {
-      v = __fmul_rn(static_cast<float>(static_cast<int>(raw)), g.act_scale);
-      if (g.wscale) v = __fmul_rn(v, sc);
-    } else {
-      v = __uint_as_float(raw);
+  // v = ((acc * a) * w_s + b_bf16) [+ b_f32]   (I8),   acc + b_bf16 [+ b_f32] otherwise; 16 columns.
+  auto dequant16 = [&](const GemmSeg& g, int set, const uint32_t* raw, int nb, float (&v)[16]) {
+    float sc[16], bi[16];
+    col_consts(set, nb, sc, bi);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float x;
+      if constexpr (KIND == Kind::I8)
+        x = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(raw[j])), g.act_scale), sc[j]);
+      else
+        x = __uint_as_float(raw[j]);
+      v[j] = __fadd_rn(x, bi[j]);
     }
-    if (g.bias) v = __fadd_rn(v, bi);
-    if (g.bias_f32) v = __fadd_rn(v, g.bias_f32[n]);
-    return v;
+    if (g.bias_f32 != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], g.bias_f32[nb + j]);
+    }
+  };
+  auto round16 = [](float (&v)[16]) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) bf16_round2(v[j], v[j + 1]);
+  };
+  auto store_bf16_16 = [](__nv_bfloat16* o, const float (&v)[16]) {
+    uint32_t pk[8];
+#pragma unroll
+    for (int q2 = 0; q2 < 8; ++q2) pk[q2] = pack_bf16_rn(v[2 * q2], v[2 * q2 + 1]);
+    *reinterpret_cast<int4*>(o) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+    *reinterpret_cast<int4*>(o + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
   };
 
   if constexpr (EPI == Epi::Rope) {
@@ -219,15 +239,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
 
         if (!do_head) continue;
         float v1[16], v2[16];
-        {
-          float sc[16], bi[16];
-          col_consts(sg, nb + j0, sc, bi);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v1[j] = bf16_round(dequant(sg, r1[j], sc[j], bi[j], nb + j0 + j));
-          col_consts(sg, nb + j0 + 32, sc, bi);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v2[j] = bf16_round(dequant(sg, r2[j], sc[j], bi[j], nb + j0 + 32 + j));
-        }
+        dequant16(sg, 0, r1, nb + j0, v1);
+        dequant16(sg, 0, r2, nb + j0 + 32, v2);
+        round16(v1);
+        round16(v2);
         if (sg.rope) {
 #pragma unroll
           for (int j = 0; j < 16; j += 2) {
@@ -242,16 +257,8 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
           }
         }
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb + j0;
-#pragma unroll
-        for (int half2 = 0; half2 < 2; ++half2) {
-          const float* vv = half2 ? v2 : v1;
-          uint32_t pk[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) pk[u] = pack_bf16_rn(vv[2 * u], vv[2 * u + 1]);
-          __nv_bfloat16* oo = o + half2 * 32;
-          *reinterpret_cast<int4*>(oo) = make_int4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<int4*>(oo + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
-        }
+        store_bf16_16(o, v1);
+        store_bf16_16(o + 32, v2);
       }
     }
   } else {
@@ -288,90 +295,90 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
         const int nb = n0 + cb + u;
         if (!row_ok || nb >= sg.n) continue;
         const uint32_t* rr = &r[u];
-        float sc[16], bi[16];
-        col_consts(sg, nb, sc, bi);
         if constexpr (EPI == Epi::I32) {
           int* o = reinterpret_cast<int*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
 #pragma unroll
           for (int j = 0; j < 16; j += 4) *reinterpret_cast<int4*>(o + j) = make_int4(rr[j], rr[j + 1], rr[j + 2], rr[j + 3]);
-        } else if constexpr (EPI == Epi::F32) {
+          continue;
+        }
+        float v[16];
+        dequant16(sg, 0, rr, nb, v);
+        if constexpr (EPI == Epi::F32) {
           float* o = reinterpret_cast<float*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
 #pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            *reinterpret_cast<float4*>(o + j) =
-                make_float4(dequant(sg, rr[j], sc[j], bi[j], nb + j), dequant(sg, rr[j + 1], sc[j + 1], bi[j + 1], nb + j + 1),
-                            dequant(sg, rr[j + 2], sc[j + 2], bi[j + 2], nb + j + 2),
-                            dequant(sg, rr[j + 3], sc[j + 3], bi[j + 3], nb + j + 3));
+          for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         } else if constexpr (EPI == Epi::Euler) {
           float* xo = args.xt + static_cast<size_t>(orow) * sg.ldo + nb;
           __nv_bfloat16* xb = args.xt_bf16 + static_cast<size_t>(orow) * sg.ldo + nb;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float vt = dequant(sg, rr[j], sc[j], bi[j], nb + j);
-            const float x = __fadd_rn(xo[j], __fmul_rn(args.dt, vt));
+            const float x = __fadd_rn(xo[j], __fmul_rn(args.dt, v[j]));
             xo[j] = x;
             xb[j] = __float2bfloat16_rn(x);
           }
         } else {
-          float v[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = bf16_round(dequant(sg, rr[j], sc[j], bi[j], nb + j));
           if constexpr (EPI == Epi::SiluMul) {
-            const GemmSeg& su = args.seg[1];
-            float sc2[16], bi2[16];
-            col_consts(su, nb, sc2, bi2);
+            float uv[16];
+            dequant16(args.seg[1], 1, &r2[u], nb, uv);
+            round16(v);
+            round16(uv);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float uv = bf16_round(dequant(su, r2[u + j], sc2[j], bi2[j], nb + j));
-              v[j] = __fmul_rn(bf16_round(silu_f(v[j])), uv);
-            }
+            for (int j = 0; j < 16; ++j) v[j] = silu_f(v[j]);
+            round16(v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], uv[j]);
           } else if constexpr (EPI == Epi::SiluBf16) {
+            round16(v);
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = silu_f(v[j]);
           } else if constexpr (EPI == Epi::Resid) {
+            round16(v);
             const int4 ra4 = res[u / 8], rb4 = res[u / 8 + 1];
-            const __nv_bfloat16* h0 = reinterpret_cast<const __nv_bfloat16*>(&ra4);
-            const __nv_bfloat16* h1 = reinterpret_cast<const __nv_bfloat16*>(&rb4);
+            const uint32_t rw[8] = {static_cast<uint32_t>(ra4.x), static_cast<uint32_t>(ra4.y),
+                                    static_cast<uint32_t>(ra4.z), static_cast<uint32_t>(ra4.w),
+                                    static_cast<uint32_t>(rb4.x), static_cast<uint32_t>(rb4.y),
+                                    static_cast<uint32_t>(rb4.z), static_cast<uint32_t>(rb4.w)};
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              v[j] = __fadd_rn(v[j], __bfloat162float(h0[j]));
-              v[j + 8] = __fadd_rn(v[j + 8], __bfloat162float(h1[j]));
+              v[2 * j] = __fadd_rn(v[2 * j], __uint_as_float(rw[j] << 16));
+              v[2 * j + 1] = __fadd_rn(v[2 * j + 1], __uint_as_float(rw[j] & 0xFFFF0000u));
             }
           } else if constexpr (EPI == Epi::GeluQuant) {
+            round16(v);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = bf16_round(gelu_tanh_f(v[j]));
+            for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_f(v[j]);
+            round16(v);
             if (args.qout != nullptr) {
-              int8_t qv[16];
+              uint32_t w[4] = {0u, 0u, 0u, 0u};
+              uint32_t slow = 0xFFFFu;  // every element exact when there is no reciprocal smooth vector
+              if (args.q_rsmooth != nullptr) {
+                slow = 0u;
+                const float* rsc = consts + 5 * BN + (nb - n0);
 #pragma unroll
-              for (int j = 0; j < 16; j += 4) {
-                const float4 s4 = *reinterpret_cast<const float4*>(consts + 4 * BN + (nb - n0) + j);
-                const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
-                if (args.q_rsmooth) {
-                  const float4 r4 = *reinterpret_cast<const float4*>(consts + 5 * BN + (nb - n0) + j);
-                  const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+                for (int k = 0; k < 4; ++k)
+                  w[k] = smooth_quant4_fast(&v[4 * k], *reinterpret_cast<const float4*>(rsc + 4 * k), ra, slow, 4 * k);
+              }
+              if (slow != 0u) {  // rare: values near a rounding boundary take the two-divide path one by one
+                const float* smc = consts + 4 * BN + (nb - n0);
 #pragma unroll
-                  for (int e = 0; e < 4; ++e) qv[j + e] = smooth_quant_fast(v[j + e], sv[e], rv[e], args.q_act, ra);
-                } else {
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) qv[j + e] = smooth_quant(v[j + e], sv[e], args.q_act);
+                for (int e = 0; e < 16; ++e) {
+                  if (slow & (1u << e)) {
+                    const uint32_t q8 = static_cast<uint32_t>(smooth_quant_slow(v[e], smc[e], args.q_act) & 0xFF);
+                    w[e / 4] = (w[e / 4] & ~(0xFFu << (8 * (e % 4)))) | (q8 << (8 * (e % 4)));
+                  }
                 }
               }
-              *reinterpret_cast<int4*>(args.qout + static_cast<size_t>(orow) * args.ldq + nb) =
-                  *reinterpret_cast<int4*>(qv);
+              *reinterpret_cast<int4*>(args.qout + static_cast<size_t>(orow) * args.ldq + nb) = make_int4(w[0], w[1], w[2], w[3]);
             }
             if (sg.out == nullptr) continue;
           } else if constexpr (EPI == Epi::Bf16) {
             if (args.post_scale != 0.0f) {
+              round16(v);
 #pragma unroll
               for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], args.post_scale);
             }
           }
-          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb;
-          uint32_t pk[8];
-#pragma unroll
-          for (int q2 = 0; q2 < 8; ++q2) pk[q2] = pack_bf16_rn(v[2 * q2], v[2 * q2 + 1]);
-          *reinterpret_cast<int4*>(o) = make_int4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<int4*>(o + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
+          store_bf16_16(reinterpret_cast<__nv_bfloat16*>(sg.out) + static_cast<size_t>(orow) * sg.ldo + nb, v);
         }
       }
     };
@@ -576,7 +583,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
           const int n = n0 + c;
           const bool in = n < g.n;
           cst[(2 * set) * BN + c] = (KIND == Kind::I8 && g.wscale && in) ? g.wscale[n] : 1.0f;
-          cst[(2 * set + 1) * BN + c] = (g.bias && in) ? __bfloat162float(g.bias[n]) : 0.0f;
+          cst[(2 * set + 1) * BN + c] = (g.bias && in) ? __bfloat162float(g.bias[n]) : -0.0f;  // x + -0 == x for every x
         }
         if constexpr (EPI == Epi::GeluQuant) {
           const int n = n0 + c;

@@ -226,20 +226,60 @@ __device__ __noinline__ int smooth_quant_slow(float x, float s, float a) { retur
 
 // The same result as smooth_quant, cheaper: y = (x * rs) * ra with rs = 1/s, ra = 1/a (correctly rounded
 // reciprocals) differs from fl(fl(x / s) / a) by at most 6 * 2^-24 * |y| (< 1e-4 for |y| < 256).  Away
-// from a rounding boundary (fraction more than 1e-3 from .5) and inside |y| < 256, round(y) therefore
+// from a rounding boundary (fraction more than 2^-12 from .5) and inside |y| < 256, round(y) therefore
 // equals the two-divide result; beyond 256 both clamp to the same end.  Everything else -- values within
-// 1e-3 of a .5 boundary, NaN, infinities -- takes the exact two-divide path.
+// 2^-12 of a .5 boundary, NaN, infinities -- takes the exact two-divide path.
 __device__ __forceinline__ int8_t smooth_quant_fast(float x, float s, float rs, float a, float ra) {
   const float y = __fmul_rn(__fmul_rn(x, rs), ra);
   const float ay = fabsf(y);
   if (ay < 256.0f) {
     float r;
     const int i = round_rn_small(y, r);
-    if (fabsf(__fsub_rn(y, r)) < 0.499f) return static_cast<int8_t>(i < -128 ? -128 : (i > 127 ? 127 : i));
+    if (fabsf(__fsub_rn(y, r)) <= 0.5f - 0.000244140625f) return static_cast<int8_t>(i < -128 ? -128 : (i > 127 ? 127 : i));
   } else if (ay < 3.0e38f) {
     return static_cast<int8_t>(y > 0.0f ? 127 : -128);
   }
   return static_cast<int8_t>(smooth_quant_slow(x, s, a));
+}
+
+// Branch-free form of smooth_quant_fast for four values, packed as four int8 bytes (x[0] in the low byte).
+// y is clamped to [-128, 127] before rounding -- the same result as rounding first and clamping after
+// (a NaN also lands on -128, as in smooth_quant) -- then rounded with one add: t = y + 1.5 * 2^23 holds
+// round(y) in its low mantissa bits, so the low byte of t's bit pattern is the int8 two's complement.
+// The fast y differs from the two-divide y by at most 6 * 2^-24 * 128.5 < 4.6e-5 inside the clamp range,
+// so only values within 2^-12 (5x that) of a .5 boundary can round differently: bit e of the returned
+// `slow` mask (bit 4k+e of the caller's group) marks those, and the caller recomputes them with smooth_quant.
+__device__ __forceinline__ uint32_t smooth_quant4_fast(const float* x, float4 rs, float ra, uint32_t& slow, int bit0) {
+  const float r4[4] = {rs.x, rs.y, rs.z, rs.w};
+  uint32_t b[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float y = fminf(fmaxf(__fmul_rn(__fmul_rn(x[e], r4[e]), ra), -128.0f), 127.0f);
+    const float t = __fadd_rn(y, 12582912.0f);
+    if (fabsf(__fsub_rn(y, __fsub_rn(t, 12582912.0f))) > 0.5f - 0.000244140625f) slow |= 1u << (bit0 + e);
+    b[e] = __float_as_uint(t);
+  }
+  return __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+}
+
+// Hardware approximations (PTX ex2.approx / rcp.approx, flush-to-zero): 2^x and 1/x with relative
+// errors around 2^-22, far below the bf16 rounding that follows every use here.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Round two fp32 values to bf16 (RN) and return them as fp32: one packed conversion for both.
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const uint32_t p = pack_bf16_rn(a, b);
+  a = __uint_as_float(p << 16);
+  b = __uint_as_float(p & 0xFFFF0000u);
 }
 
 }  // namespace svla
