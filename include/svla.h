@@ -67,6 +67,12 @@ int32_t svla_device_error(int32_t* code, int32_t reset);
 int32_t svla_pack_weight_i8(const void* weight, const float* smooth, int32_t n, int32_t k, int8_t* qweight,
                             float* wscale, svla_stream_t stream);
 
+/* The bf16 weight of a W8A16 linear: out[n,k] = bf16(float(qweight[n,k]) * wscale[n]); replaces
+ * dequantize_weight(qweight, scale).to(torch.bfloat16) in W8A16Linear.__init__
+ * (deploy/linear_only_quant.py:122-124, :147-148).  out bf16 [N, K]; K % 8 == 0. */
+int32_t svla_dequant_weight_bf16(const int8_t* qweight, const float* wscale, int32_t n, int32_t k, void* out,
+                                 svla_stream_t stream);
+
 /* SmoothQuant activation quantisation; replaces smoothQuantActivationKernel
  * (deploy/cuda/smoothquant_linear_epilogue.cu:108-119) with bf16 input:
  * q[m,k] = round((x[m,k] / smooth[k]) / act_scale).clamp(-128, 127).  K % 8 == 0. */
@@ -214,7 +220,10 @@ int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* po
 int32_t svla_rope_table(float* cs, int32_t max_pos, float max_wavelength, svla_stream_t stream);
 
 /* Masks and positions of one call (deploy/diagnose_3_4_numeric_baseline.py:42-46, :117-146, :171-172).
- * img_mask0/1 bool [B], lang_mask bool [B, n_lang]; prefix length Lp = 2*n_img + n_lang + 1. */
+ * img_mask0/1 bool [B], lang_mask bool [B, n_lang]; prefix length Lp = 2*n_img + n_lang + 1, Ls = chunk.
+ * prefix_mask [B, Lp, ld(Lp)], self_mask [B, Ls, ld(Lp + Ls)], cross_mask [B, Ls, ld(Lp)] bytes with the
+ * row stride ld(L) = L rounded up to a multiple of 16 (padding bytes 0); prefix_pos [B, Lp],
+ * suffix_pos / cross_pos [B, Ls]. */
 int32_t svla_build_masks(const uint8_t* img_mask0, const uint8_t* img_mask1, const uint8_t* lang_mask,
                          int32_t batch, int32_t n_img, int32_t n_lang, int32_t chunk, uint8_t* prefix_mask,
                          int32_t* prefix_pos, uint8_t* self_mask, uint8_t* cross_mask, int32_t* suffix_pos,

@@ -63,6 +63,7 @@ SIGNATURES = {
     "svla_version": (c_char_p, []),
     "svla_device_error": (c_int32, [POINTER(c_int32), c_int32]),
     "svla_pack_weight_i8": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
+    "svla_dequant_weight_bf16": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "svla_quantize_smooth": (c_int32, [c_void_p, c_int32, c_void_p, c_float, c_void_p, c_int32, c_int32, c_int32,
                                        c_void_p]),
     "svla_gemm_i8_i32": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),

@@ -116,18 +116,22 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st
   }
   if (a.mask) {
     // mask bytes [128 rows x 64 keys]; rows past Lq and keys past Lk are left as whatever they read:
-    // the scores of keys past Lk are forced to -inf and rows past Lq are never stored
+    // the scores of keys past Lk are forced to -inf and rows past Lq are never stored.  A 16-key run is
+    // one 16-byte copy when it is aligned and lies inside the row's storage (the row stride covers Lk
+    // rounded up to 16: then even the last, partial run stays in bounds); runs past Lk are zero-filled.
     const int q0 = blockIdx.x * kRows;
+    const bool padded_rows = a.mask_rs >= ((Lk + 15) & ~15);
     for (int idx = threadIdx.x; idx < kRows * 4; idx += blockDim.x) {
       const int r = idx >> 2, c = (idx & 3) * 16;
       const int row = q0 + r, key = key0 + c;
-      const uint8_t* src = a.mask + static_cast<size_t>(b) * a.mask_bs + static_cast<size_t>(row < a.Lq ? row : 0) * a.mask_rs + key;
-      // whole 16-byte run inside the row and 16-byte aligned -> one copy, otherwise bytes one by one
-      const bool vec = (key + 16 <= Lk) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
-      if (vec) {
-        cp_async16(&sm.m[st][r * kKeys + c], src, 16);
+      const uint8_t* src = a.mask + static_cast<size_t>(b) * a.mask_bs + static_cast<size_t>(row < a.Lq ? row : 0) * a.mask_rs;
+      uint8_t* dst = &sm.m[st][r * kKeys + c];
+      if (key >= Lk) {
+        cp_async16(dst, src, 0);
+      } else if ((key + 16 <= Lk || padded_rows) && ((reinterpret_cast<uintptr_t>(src + key) & 15) == 0)) {
+        cp_async16(dst, src + key, 16);
       } else {
-        for (int j = 0; j < 16; ++j) sm.m[st][r * kKeys + c + j] = (key + j < Lk) ? src[j] : 0;
+        for (int j = 0; j < 16; ++j) dst[j] = (key + j < Lk) ? src[key + j] : 0;
       }
     }
   }

@@ -31,18 +31,23 @@ __global__ void rope_table_kernel(float2* cs, int max_pos, float max_wavelength)
 //   self_mask[q, k]   = k < Lp ? pad[k] : (k - Lp) <= q                  [B, Ls, Lp + Ls]
 //   cross_mask[q, k]  = pad[k]                                          [B, Ls, Lp]
 //   suffix_pos[i]     = sum(pad) + i;   cross_pos[i] = i
+// Mask rows are stored at a stride of the row length rounded up to 16 bytes (padding bytes 0), so the
+// attention kernel can copy every 16-key run of a row with one aligned 16-byte transfer.
 struct MaskArgs {
   const uint8_t* img_mask0;  // [B]
   const uint8_t* img_mask1;  // [B]
   const uint8_t* lang_mask;  // [B, n_lang]
   int B, n_img, n_lang, Ls;
-  uint8_t* prefix_mask;  // [B, Lp, Lp]
+  uint8_t* prefix_mask;  // [B, Lp, mask_ld(Lp)]
   int* prefix_pos;       // [B * Lp]
-  uint8_t* self_mask;    // [B, Ls, Lp + Ls]
-  uint8_t* cross_mask;   // [B, Ls, Lp]
+  uint8_t* self_mask;    // [B, Ls, mask_ld(Lp + Ls)]
+  uint8_t* cross_mask;   // [B, Ls, mask_ld(Lp)]
   int* suffix_pos;       // [B * Ls]
   int* cross_pos;        // [B * Ls]
 };
+
+// row stride of a mask over L keys
+__host__ __device__ constexpr int mask_ld(int L) { return (L + 15) & ~15; }
 
 __device__ __forceinline__ int prefix_pad(const MaskArgs& a, int b, int i) {
   if (i < a.n_img) return a.img_mask0[b] != 0;
@@ -76,18 +81,19 @@ __global__ void masks_kernel(const MaskArgs a) {
       a.cross_pos[b * a.Ls + i] = i;
     }
   }
-  for (int idx = threadIdx.x; idx < Lp * Lp; idx += blockDim.x) {
-    const int q = idx / Lp, k = idx % Lp;
-    a.prefix_mask[static_cast<size_t>(b) * Lp * Lp + idx] = (cum[k] <= cum[q]) && pad[q] && pad[k];
+  const int ldp = mask_ld(Lp);
+  for (int idx = threadIdx.x; idx < Lp * ldp; idx += blockDim.x) {
+    const int q = idx / ldp, k = idx % ldp;
+    a.prefix_mask[static_cast<size_t>(b) * Lp * ldp + idx] = (k < Lp) && (cum[k] <= cum[q]) && pad[q] && pad[k];
   }
-  const int Lt = Lp + a.Ls;
-  for (int idx = threadIdx.x; idx < a.Ls * Lt; idx += blockDim.x) {
-    const int q = idx / Lt, k = idx % Lt;
-    a.self_mask[static_cast<size_t>(b) * a.Ls * Lt + idx] = (k < Lp) ? pad[k] : ((k - Lp) <= q);
+  const int Lt = Lp + a.Ls, ldt = mask_ld(Lt);
+  for (int idx = threadIdx.x; idx < a.Ls * ldt; idx += blockDim.x) {
+    const int q = idx / ldt, k = idx % ldt;
+    a.self_mask[static_cast<size_t>(b) * a.Ls * ldt + idx] = (k < Lp) ? pad[k] : (k < Lt && (k - Lp) <= q);
   }
-  for (int idx = threadIdx.x; idx < a.Ls * Lp; idx += blockDim.x) {
-    const int k = idx % Lp;
-    a.cross_mask[static_cast<size_t>(b) * a.Ls * Lp + idx] = pad[k];
+  for (int idx = threadIdx.x; idx < a.Ls * ldp; idx += blockDim.x) {
+    const int k = idx % ldp;
+    a.cross_mask[static_cast<size_t>(b) * a.Ls * ldp + idx] = (k < Lp) && pad[k];
   }
 }
 

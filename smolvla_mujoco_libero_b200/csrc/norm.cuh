@@ -201,4 +201,23 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const __nv_bfloat16* w
   }
 }
 
+// out[n, k] = bf16(float(q[n, k]) * wscale[n]) -- the bf16 weight a W8A16 linear multiplies by
+// (dequantize_weight(...).to(bfloat16), deploy/linear_only_quant.py:122-124, :147-148).  8 per thread.
+__global__ void __launch_bounds__(256) dequant_weight_kernel(const int8_t* q, const float* wscale, int N, int K,
+                                                             __nv_bfloat16* out) {
+  pdl_wait();
+  pdl_trigger();
+  const long long i8 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (i8 >= static_cast<long long>(N) * K) return;
+  const int n = static_cast<int>(i8 / K);
+  const float ws = wscale[n];
+  const int2 raw = *reinterpret_cast<const int2*>(q + i8);
+  const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+  uint32_t pk[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    pk[j] = pack_bf16_rn(__fmul_rn(static_cast<float>(b[2 * j]), ws), __fmul_rn(static_cast<float>(b[2 * j + 1]), ws));
+  *reinterpret_cast<int4*>(out + i8) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+}
+
 }  // namespace svla

@@ -347,6 +347,15 @@ int32_t svla_pack_weight_i8(const void* weight, const float* smooth, int32_t n, 
   return launch(pack_weight_kernel, dim3(n), dim3(256), 0, cs(stream), "pack_weight_kernel", static_cast<const __nv_bfloat16*>(weight), k, smooth, qweight, wscale);
 }
 
+int32_t svla_dequant_weight_bf16(const int8_t* qweight, const float* wscale, int32_t n, int32_t k, void* out,
+                                 svla_stream_t stream) {
+  if (!qweight || !wscale || !out || n <= 0 || k <= 0 || k % 8)
+    return fail(SVLA_ERR_ARG, "svla_dequant_weight_bf16: bad args (k must be a multiple of 8)");
+  const long long groups = static_cast<long long>(n) * k / 8;
+  return launch(dequant_weight_kernel, dim3(static_cast<unsigned>((groups + 255) / 256)), dim3(256), 0, cs(stream),
+                "dequant_weight_kernel", qweight, wscale, n, k, static_cast<__nv_bfloat16*>(out));
+}
+
 int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, float act_scale, int8_t* q, int32_t ldq,
                              int32_t m, int32_t k, svla_stream_t stream) {
   if (!x || !q || m <= 0 || k <= 0 || k % 8 || ldx % 8 || ldq % 8 || act_scale <= 0.f)

@@ -50,6 +50,7 @@ class PackedLinear:
     rsmooth: torch.Tensor | None = None  # fp32 [k] = 1 / smooth (w8a8), lets the quantisers multiply
     act_scale: float = 1.0              # w8a8
     weight_bf16: torch.Tensor | None = None  # original bf16 weight (bf16 / calibration mode)
+    weight_deq: torch.Tensor | None = None   # w8a16: bf16(q * wscale), the weight W8A16Linear multiplies by
 
 
 def time_embedding_bf16(cfg: SmolVLAConfig) -> torch.Tensor:
@@ -103,7 +104,8 @@ class DeviceWeights:
                                               max(float(e["scale"]), 1e-8), w if keep_bf16 else None)
             elif kind == "w8a16":
                 q, ws = ops.pack_weight_i8(w)
-                self.lin[name] = PackedLinear(n, k, "w8a16", q, ws, b, weight_bf16=w if keep_bf16 else None)
+                self.lin[name] = PackedLinear(n, k, "w8a16", q, ws, b, weight_bf16=w if keep_bf16 else None,
+                                              weight_deq=ops.dequant_weight_bf16(q, ws))
             else:
                 self.lin[name] = PackedLinear(n, k, "bf16", w, None, b, weight_bf16=w)
         self.t: dict[str, torch.Tensor] = {}
@@ -119,7 +121,7 @@ class DeviceWeights:
     def nbytes(self) -> int:
         tot = 0
         for p in self.lin.values():
-            for t in (p.weight, p.wscale, p.bias, p.smooth):
+            for t in (p.weight, p.wscale, p.bias, p.smooth, p.weight_deq):
                 if t is not None:
                     tot += t.numel() * t.element_size()
         return tot + sum(t.numel() * t.element_size() for t in self.t.values())
@@ -127,6 +129,8 @@ class DeviceWeights:
 
 class SmolVLARunner:
     """Static buffers + launch list for one batch size."""
+
+    W8A16_BF16_ROWS = 512  # M from which W8A16 linears run as bf16 GEMMs on the dequantized weight
 
     def __init__(self, weights: DeviceWeights, batch: int, mode: str = "quant", debug_taps: bool = False):
         if weights.cfg.expert_layers != weights.cfg.text_layers:
@@ -161,9 +165,11 @@ class SmolVLARunner:
         self.in_state = z(B, c.max_state_dim, dt=f32)
         self.in_noise = z(B, S, c.max_action_dim, dt=f32)
         self.state_bf = z(B, c.max_state_dim)
-        self.prefix_mask = z(B, Lp, Lp, dt=torch.uint8)
-        self.self_mask = z(B, S, Lp + S, dt=torch.uint8)
-        self.cross_mask = z(B, S, Lp, dt=torch.uint8)
+        # mask rows are stored at 16-byte strides (the layout svla_build_masks writes); the views cover L keys
+        ld = lambda n: (n + 15) // 16 * 16  # noqa: E731
+        self.prefix_mask = z(B, Lp, ld(Lp), dt=torch.uint8)[:, :, :Lp]
+        self.self_mask = z(B, S, ld(Lp + S), dt=torch.uint8)[:, :, :Lp + S]
+        self.cross_mask = z(B, S, ld(Lp), dt=torch.uint8)[:, :, :Lp]
         self.prefix_pos = z(B * Lp, dt=torch.int32)
         self.suffix_pos = z(B * S, dt=torch.int32)
         self.cross_pos = z(B * S, dt=torch.int32)
@@ -231,17 +237,26 @@ class SmolVLARunner:
         self._keep.append(segs)
         self._add(L.lib().svla_gemm, d)
 
+    def _deq_rows(self, p: PackedLinear, m: int) -> bool:
+        """W8A16 linears with at least W8A16_BF16_ROWS rows multiply by the stored bf16(q * wscale) weight
+        (a plain bf16 GEMM; the reference's W8A16Linear keeps exactly that buffer) instead of converting
+        the int8 weight inside every output tile: the same operands, so the same results, and at large M
+        the per-tile conversion would cost more than the weight bytes it saves."""
+        return p.kind == "w8a16" and m >= self.W8A16_BF16_ROWS
+
     def _linear_seg(self, name: str, a: torch.Tensor, out, rope=0, n=None):
         p = self.w.lin[name]
         if self.mode == "bf16" or p.kind == "bf16":
             return ops.Seg(a=a, b=p.weight_bf16, out=out, n=p.n if n is None else n, bias=p.bias, rope=rope)
+        if self._deq_rows(p, a.shape[0]):
+            return ops.Seg(a=a, b=p.weight_deq, out=out, n=p.n, bias=p.bias, rope=rope)
         if p.kind == "w8a16":
             return ops.Seg(a=a, b=p.weight, out=out, n=p.n, wscale=p.wscale, bias=p.bias, rope=rope)
         return ops.Seg(a=a, b=p.weight, out=out, n=p.n, wscale=p.wscale, bias=p.bias, act_scale=p.act_scale, rope=rope)
 
-    def _kind(self, name: str) -> int:
+    def _kind(self, name: str, m: int) -> int:
         p = self.w.lin[name]
-        if self.mode == "bf16" or p.kind == "bf16":
+        if self.mode == "bf16" or p.kind == "bf16" or self._deq_rows(p, m):
             return L.KIND_BF16
         return L.KIND_I8 if p.kind == "w8a8" else L.KIND_W8A16
 
@@ -320,11 +335,11 @@ class SmolVLARunner:
             self._norm(self.vh, w.t[f"{p}.layer_norm1.weight"], c.vis_eps, bias=w.t[f"{p}.layer_norm1.bias"],
                        quant_mods=mods, outs=self.v_in, tap=mods)
             a_in = self.v_in if q_mode else [self.v_in[0]] * 3
-            self._gemm(self._kind(mods[0]), L.EPI_BF16, NV, c.vis_hidden,
+            self._gemm(self._kind(mods[0], NV), L.EPI_BF16, NV, c.vis_hidden,
                        [self._linear_seg(m, a, o) for m, a, o in zip(mods, a_in, self.v_qkv)])
             self._attn(self.v_qkv[0], self.v_qkv[1], self.v_qkv[2], c.n_patches, c.vis_heads, c.vis_heads,
                        out_mod=f"{p}.self_attn.out_proj", out=self.v_ctx, tap=[f"{p}.self_attn.out_proj"])
-            self._gemm(self._kind(f"{p}.self_attn.out_proj"), L.EPI_RESID, NV, c.vis_hidden,
+            self._gemm(self._kind(f"{p}.self_attn.out_proj", NV), L.EPI_RESID, NV, c.vis_hidden,
                        [self._linear_seg(f"{p}.self_attn.out_proj", self.v_ctx, self.vh)], resid=self.vh,
                        ldr=c.vis_hidden)
             self._norm(self.vh, w.t[f"{p}.layer_norm2.weight"], c.vis_eps, bias=w.t[f"{p}.layer_norm2.bias"],
@@ -339,7 +354,7 @@ class SmolVLARunner:
                 self._gemm(L.KIND_BF16, L.EPI_GELU_QUANT, NV, c.vis_hidden,
                            [self._linear_seg(f"{p}.mlp.fc1", self.v_fc1_in, self.v_fc2_in)])
                 self._tap([f"{p}.mlp.fc2"], self.v_fc2_in)
-            self._gemm(self._kind(f"{p}.mlp.fc2"), L.EPI_RESID, NV, c.vis_mlp,
+            self._gemm(self._kind(f"{p}.mlp.fc2", NV), L.EPI_RESID, NV, c.vis_mlp,
                        [self._linear_seg(f"{p}.mlp.fc2", self.v_fc2_in, self.vh)], resid=self.vh, ldr=c.vis_hidden)
         # post LayerNorm + pixel shuffle + connector quantisation
         self._norm(self.vh, w.t[f"{VISION}.post_layernorm.weight"], c.vis_eps, bias=w.t[f"{VISION}.post_layernorm.bias"],
@@ -347,7 +362,7 @@ class SmolVLARunner:
                    tap=[CONNECTOR])
         # connector -> prefix rows (b, cam, token) -> b*Lp + cam*n_img + token, x bf16(sqrt(H)) in bf16
         img_scale = float(torch.tensor(H ** 0.5, dtype=torch.bfloat16))
-        self._gemm(self._kind(CONNECTOR), L.EPI_BF16, NI * c.n_img_tokens, self.conn_in.shape[1],
+        self._gemm(self._kind(CONNECTOR, NI * c.n_img_tokens), L.EPI_BF16, NI * c.n_img_tokens, self.conn_in.shape[1],
                    [self._linear_seg(CONNECTOR, self.conn_in, self.h)], post_scale=img_scale,
                    rows_per_group=c.n_cams * c.n_img_tokens, group_stride=Lp)
         # language tokens x sqrt(H) and the state token
@@ -366,7 +381,7 @@ class SmolVLARunner:
             self._norm(self.h, w.t[f"{p}.input_layernorm.weight"], c.rms_eps, quant_mods=mods, outs=self.t_in, tap=mods)
             a_in = self.t_in if q_mode else [self.t_in[0]] * 3
             outs = [self.t_q, self.kcache[i], self.vcache[i]]
-            self._gemm(self._kind(mods[0]), L.EPI_ROPE, B * Lp, H,
+            self._gemm(self._kind(mods[0], B * Lp), L.EPI_ROPE, B * Lp, H,
                        [self._linear_seg(m, a, o, rope=r) for m, a, o, r in zip(mods, a_in, outs, (1, 1, 0))],
                        rope_cs=self.rope_cs, pos=self.prefix_pos, max_pos=self.max_pos)
             last = i == c.text_layers - 1
@@ -374,15 +389,15 @@ class SmolVLARunner:
                 break
             self._attn(self.t_q, self.kcache[i], self.vcache[i], Lp, c.heads, c.kv_heads, mask=self.prefix_mask,
                        out_mod=f"{p}.self_attn.o_proj", out=self.t_ctx, tap=[f"{p}.self_attn.o_proj"])
-            self._gemm(self._kind(f"{p}.self_attn.o_proj"), L.EPI_RESID, B * Lp, c.q_dim,
+            self._gemm(self._kind(f"{p}.self_attn.o_proj", B * Lp), L.EPI_RESID, B * Lp, c.q_dim,
                        [self._linear_seg(f"{p}.self_attn.o_proj", self.t_ctx, self.h)], resid=self.h, ldr=H)
             mods = [f"{p}.mlp.gate_proj", f"{p}.mlp.up_proj"]
             self._norm(self.h, w.t[f"{p}.post_attention_layernorm.weight"], c.rms_eps, quant_mods=mods,
                        outs=self.t_mlp_in, tap=mods)
             a_in = self.t_mlp_in if q_mode else [self.t_mlp_in[0]] * 2
-            self._gemm(self._kind(mods[0]), L.EPI_SILU_MUL, B * Lp, H,
+            self._gemm(self._kind(mods[0], B * Lp), L.EPI_SILU_MUL, B * Lp, H,
                        [self._linear_seg(m, a, self.t_mlp) for m, a in zip(mods, a_in)], pair=True)
-            self._gemm(self._kind(f"{p}.mlp.down_proj"), L.EPI_RESID, B * Lp, c.mlp,
+            self._gemm(self._kind(f"{p}.mlp.down_proj", B * Lp), L.EPI_RESID, B * Lp, c.mlp,
                        [self._linear_seg(f"{p}.mlp.down_proj", self.t_mlp, self.h)], resid=self.h, ldr=H)
         if self.debug:
             self._norm(self.h, w.t[f"{TEXT}.norm.weight"], c.rms_eps, y=self.prefix_out)
@@ -390,7 +405,7 @@ class SmolVLARunner:
         # ---------------- cross-attention K/V of the cached prefix (step-invariant)
         for i in self.ck:
             p = f"{EXPERT}.layers.{i}.self_attn"
-            self._gemm(self._kind(f"{p}.k_proj"), L.EPI_BF16, B * Lp, c.kv_dim,
+            self._gemm(self._kind(f"{p}.k_proj", B * Lp), L.EPI_BF16, B * Lp, c.kv_dim,
                        [self._linear_seg(f"{p}.k_proj", self.kcache[i], self.ck[i]),
                         self._linear_seg(f"{p}.v_proj", self.vcache[i], self.cv[i])])
         # ---------------- flow matching
@@ -408,7 +423,7 @@ class SmolVLARunner:
             for i in range(c.expert_layers):
                 p = f"{EXPERT}.layers.{i}"
                 self._norm(self.eh, w.t[f"{p}.input_layernorm.weight"], c.rms_eps, y=self.ey)
-                kq = self._kind(f"{p}.self_attn.q_proj")
+                kq = self._kind(f"{p}.self_attn.q_proj", B * S)
                 if c.is_cross_layer(i):
                     self._gemm(kq, L.EPI_ROPE, B * S, E, [self._linear_seg(f"{p}.self_attn.q_proj", self.ey, self.eq, rope=1)],
                                rope_cs=self.rope_cs, pos=self.cross_pos, max_pos=self.max_pos)
@@ -421,13 +436,13 @@ class SmolVLARunner:
                                max_pos=self.max_pos)
                     self._attn(self.eq, self.kcache[i], self.vcache[i], S, c.heads, c.kv_heads, mask=self.self_mask,
                                k2=self.ek, v2=self.ev, out=self.ectx)
-                self._gemm(self._kind(f"{p}.self_attn.o_proj"), L.EPI_RESID, B * S, c.q_dim,
+                self._gemm(self._kind(f"{p}.self_attn.o_proj", B * S), L.EPI_RESID, B * S, c.q_dim,
                            [self._linear_seg(f"{p}.self_attn.o_proj", self.ectx, self.eh)], resid=self.eh, ldr=E)
                 self._norm(self.eh, w.t[f"{p}.post_attention_layernorm.weight"], c.rms_eps, y=self.ey)
-                self._gemm(self._kind(f"{p}.mlp.gate_proj"), L.EPI_SILU_MUL, B * S, E,
+                self._gemm(self._kind(f"{p}.mlp.gate_proj", B * S), L.EPI_SILU_MUL, B * S, E,
                            [self._linear_seg(f"{p}.mlp.gate_proj", self.ey, self.emlp),
                             self._linear_seg(f"{p}.mlp.up_proj", self.ey, self.emlp)], pair=True)
-                self._gemm(self._kind(f"{p}.mlp.down_proj"), L.EPI_RESID, B * S, c.expert_mlp,
+                self._gemm(self._kind(f"{p}.mlp.down_proj", B * S), L.EPI_RESID, B * S, c.expert_mlp,
                            [self._linear_seg(f"{p}.mlp.down_proj", self.emlp, self.eh)], resid=self.eh, ldr=E)
             self._norm(self.eh, w.t[f"{EXPERT}.norm.weight"], c.rms_eps, y=self.ey)
             self._gemm(L.KIND_BF16, L.EPI_EULER, B * S, E,

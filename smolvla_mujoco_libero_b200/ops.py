@@ -48,6 +48,16 @@ def pack_weight_i8(weight: torch.Tensor, smooth: torch.Tensor | None = None) -> 
     return q, ws
 
 
+def dequant_weight_bf16(q: torch.Tensor, ws: torch.Tensor) -> torch.Tensor:
+    """bf16(q * ws[:, None]): the weight W8A16Linear multiplies by (deploy/linear_only_quant.py:122-124)."""
+    _need(q, torch.int8, "q")
+    _need(ws, torch.float32, "ws")
+    n, k = q.shape
+    out = torch.empty(n, k, dtype=torch.bfloat16, device=q.device)
+    check(lib().svla_dequant_weight_bf16(_p(q), _p(ws), n, k, _p(out), _stream()), "dequant_weight_bf16")
+    return out
+
+
 def reciprocal(x: torch.Tensor) -> torch.Tensor:
     """Correctly rounded 1 / x (fp32) on the device -- the reciprocal smooth vectors the quantisers accept."""
     _need(x, torch.float32, "x")

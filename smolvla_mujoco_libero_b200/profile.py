@@ -4,6 +4,7 @@ time one operator on random inputs.
     python -m smolvla_mujoco_libero_b200.profile --batch 1 --iters 3 [--graph]
     python -m smolvla_mujoco_libero_b200.profile --op gemm --kind i8 --epi gelu_quant --m 16384 --n 3072 --k 768
     python -m smolvla_mujoco_libero_b200.profile --op attn --batch 16 --lq 1024 --lk 1024 --heads 12 --kv-heads 12
+    python -m smolvla_mujoco_libero_b200.profile --op attn --batch 64 --lq 50 --lk 227 --heads 15 --kv-heads 5 --mask --mask-ld 240
 
 Each call is wrapped in the NVTX range "sample_actions", so a profiler can capture exactly those launches
 (e.g. ``ncu --nvtx --nvtx-include "sample_actions/" --metrics gpu__time_duration.sum ...``).  Prints the
@@ -96,10 +97,17 @@ def op_attn(a) -> dict:
     q = torch.randn(a.batch, a.lq, a.heads * 64, generator=g).to(torch.bfloat16).to(dev)
     k = torch.randn(a.batch, a.lk, a.kv_heads * 64, generator=g).to(torch.bfloat16).to(dev)
     v = torch.randn(a.batch, a.lk, a.kv_heads * 64, generator=g).to(torch.bfloat16).to(dev)
-    ms = time_op(lambda: ops.attention(q, k, v, a.heads, a.kv_heads), a.iters)
+    mask = None
+    if a.mask:
+        # key padding (last 10% of keys masked) with the mask rows stored at a stride of `mask_ld` bytes
+        ld = max(a.mask_ld, a.lk)
+        full = torch.zeros(a.batch, a.lq, ld, dtype=torch.uint8)
+        full[:, :, : a.lk - a.lk // 10] = 1
+        mask = full.to(dev)[:, :, : a.lk]
+    ms = time_op(lambda: ops.attention(q, k, v, a.heads, a.kv_heads, mask=mask), a.iters)
     flops = 4.0 * a.batch * a.heads * a.lq * a.lk * 64
-    return {"op": "attn", "batch": a.batch, "lq": a.lq, "lk": a.lk, "ms": ms,
-            "tflops_best": flops / (min(ms) / 1e3) / 1e12}
+    return {"op": "attn", "batch": a.batch, "lq": a.lq, "lk": a.lk, "heads": a.heads, "kv_heads": a.kv_heads,
+            "mask": a.mask, "mask_ld": a.mask_ld, "ms": ms, "tflops_best": flops / (min(ms) / 1e3) / 1e12}
 
 
 def main() -> None:
@@ -119,6 +127,8 @@ def main() -> None:
     ap.add_argument("--lk", type=int, default=1024)
     ap.add_argument("--heads", type=int, default=12)
     ap.add_argument("--kv-heads", type=int, default=12)
+    ap.add_argument("--mask", action="store_true")
+    ap.add_argument("--mask-ld", type=int, default=0)
     a = ap.parse_args()
     if a.op == "gemm":
         print(json.dumps(op_gemm(a)))

@@ -491,3 +491,43 @@ def test_w8a16_rope_qkv(m):
     ops.gemm(ops.gemm_desc(L.KIND_W8A16, L.EPI_ROPE, m, k, segs, rope_cs=cs, pos=pos.to(DEV), max_pos=256))
     for s_, (ref, y, rope) in zip(segs, refs):
         rope_close(s_.out, ref, y, rope)
+
+
+# ----------------------------------------------------------------------------- W8A16 as a bf16 GEMM
+
+@pytest.mark.parametrize("n,k", [(720, 2048), (960, 720), (16, 8)])
+def test_dequant_weight_bit_exact(n, k):
+    g = synthetic.generator(n + k + 7)
+    w = (torch.randn(n, k, generator=g) * 0.03).to(torch.bfloat16)
+    lin = Q.W8A16Linear(w, None)
+    qw, ws = ops.pack_weight_i8(w.to(DEV))
+    assert torch.equal(ops.dequant_weight_bf16(qw, ws).cpu(), lin.weight)
+
+
+@pytest.mark.parametrize("epi,m,n,k", [("resid", 640, 720, 2048), ("silu_mul", 640, 2048, 720),
+                                       ("rope", 640, 960, 720), ("bf16", 700, 320, 960)])
+def test_w8a16_equals_bf16_gemm_on_dequantized_weight(epi, m, n, k):
+    """The large-M form of a W8A16 linear (a bf16 GEMM on bf16(q * wscale)) gives the same bits as the
+    int8-operand kernel: both feed identical bf16 operands to the same MMA sequence."""
+    g = synthetic.generator(m + n + k + 11)
+    x = torch.randn(m, k, generator=g).to(DEV, torch.bfloat16)
+    ws_, bs_ = [], []
+    for _ in range(2 if epi == "silu_mul" else 1):
+        qw, sc = ops.pack_weight_i8((torch.randn(n, k, generator=g) * 0.02).to(DEV, torch.bfloat16))
+        ws_.append((qw, sc, ops.dequant_weight_bf16(qw, sc)))
+        bs_.append((torch.randn(n, generator=g) * 0.02).to(DEV, torch.bfloat16))
+    res = torch.randn(m, n, generator=g).to(DEV, torch.bfloat16)
+    pos = (177 + torch.arange(m) % 50).to(DEV, torch.int32)
+    cs = ops.rope_table(256, 10000.0, DEV)
+    e = {"resid": L.EPI_RESID, "silu_mul": L.EPI_SILU_MUL, "rope": L.EPI_ROPE, "bf16": L.EPI_BF16}[epi]
+    outs = []
+    for kind in (L.KIND_W8A16, L.KIND_BF16):
+        out = res.clone()
+        segs = [ops.Seg(a=x, b=qw if kind == L.KIND_W8A16 else deq, out=out, n=n,
+                        wscale=sc if kind == L.KIND_W8A16 else None, bias=b, rope=1 if epi == "rope" else 0)
+                for (qw, sc, deq), b in zip(ws_, bs_)]
+        extra = {"resid": dict(resid=out, ldr=n), "silu_mul": dict(pair=True),
+                 "rope": dict(rope_cs=cs, pos=pos, max_pos=256), "bf16": {}}[epi]
+        ops.gemm(ops.gemm_desc(kind, e, m, k, segs, **extra))
+        outs.append(out.cpu())
+    assert torch.equal(outs[0], outs[1])
