@@ -12,9 +12,12 @@
 // The reference rounds the already-normalised probabilities instead; both roundings are 2^-9 relative
 // per term (bf16), well inside the stated tolerance.
 //
-// CTA: 8 warps x 16 query rows = 128 queries of one (batch, head).  Keys stream in tiles of 64 through a
-// two-stage cp.async pipeline; keys may come from two sources (the cached prefix followed by the current
-// suffix).  Tensor-core work is mma.sync m16n8k16 with ldmatrix fragments; exponentials are ex2.approx.
+// CTA: one (row tile, kv head, batch).  The rows of a kv head are its G = Hq / Hkv query heads' queries
+// packed head-major (row r = query head kh*G + r / Lq, query r % Lq), so every key/value tile is loaded
+// once for the whole group and short query lengths fill the tiles; a tile is 16 x warps rows, up to 128.
+// Keys stream in tiles of 64 through a two-stage cp.async pipeline; keys may come from two sources (the
+// cached prefix followed by the current suffix).  Tensor-core work is mma.sync m16n8k16 with ldmatrix
+// fragments; exponentials are ex2.approx.
 //
 // Optional fused output quantisation (the o_proj input of a W8A8 layer):
 //   qo[m, h*64 + d] = round((o / s[h*64+d]) / a).clamp(-128, 127).
@@ -34,11 +37,12 @@ struct AttnArgs {
   const float* qo_smooth;  const float* qo_rsmooth;  float qo_act;
   int Lq, Hq, Hkv;
   float scale;
+  int rows;  // packed rows per CTA: 16 x warps, at most 128
 };
 
 namespace attn_detail {
 constexpr int kD = 64;
-constexpr int kRows = 128;    // queries per CTA
+constexpr int kRows = 128;    // most packed rows per CTA
 constexpr int kWarps = kRows / 16;
 constexpr int kKeys = 64;     // keys per tile
 constexpr int kPad = 72;      // smem row (bf16): 144 bytes -> conflict-free ldmatrix
@@ -119,12 +123,12 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st
     // the scores of keys past Lk are forced to -inf and rows past Lq are never stored.  A 16-key run is
     // one 16-byte copy when it is aligned and lies inside the row's storage (the row stride covers Lk
     // rounded up to 16: then even the last, partial run stays in bounds); runs past Lk are zero-filled.
-    const int q0 = blockIdx.x * kRows;
+    const int r0 = blockIdx.x * a.rows, R = a.Lq * (a.Hq / a.Hkv);
     const bool padded_rows = a.mask_rs >= ((Lk + 15) & ~15);
-    for (int idx = threadIdx.x; idx < kRows * 4; idx += blockDim.x) {
+    for (int idx = threadIdx.x; idx < a.rows * 4; idx += blockDim.x) {
       const int r = idx >> 2, c = (idx & 3) * 16;
-      const int row = q0 + r, key = key0 + c;
-      const uint8_t* src = a.mask + static_cast<size_t>(b) * a.mask_bs + static_cast<size_t>(row < a.Lq ? row : 0) * a.mask_rs;
+      const int query = (r0 + r < R) ? (r0 + r) % a.Lq : 0, key = key0 + c;
+      const uint8_t* src = a.mask + static_cast<size_t>(b) * a.mask_bs + static_cast<size_t>(query) * a.mask_rs;
       uint8_t* dst = &sm.m[st][r * kKeys + c];
       if (key >= Lk) {
         cp_async16(dst, src, 0);
@@ -146,19 +150,21 @@ __global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int kh = h / (a.Hq / a.Hkv);
-  const int q0 = blockIdx.x * kRows;
+  const int kh = blockIdx.y, b = blockIdx.z;
+  const int G = a.Hq / a.Hkv, R = G * a.Lq;  // packed rows of this kv head
+  const int r0 = blockIdx.x * a.rows;
   const int Lk = a.L1 + a.L2;
   const int n_tiles = (Lk + kKeys - 1) / kKeys;
 
-  // Q tile -> smem (zero rows beyond Lq), first K/V tile in flight
+  // Q tile -> smem (zero rows beyond the packed rows), first K/V tile in flight
   {
-    const __nv_bfloat16* qb = a.q + static_cast<size_t>(b) * a.q_bs + h * kD;
-    for (int idx = threadIdx.x; idx < kRows * 8; idx += blockDim.x) {
+    const __nv_bfloat16* qb = a.q + static_cast<size_t>(b) * a.q_bs + kh * G * kD;
+    for (int idx = threadIdx.x; idx < a.rows * 8; idx += blockDim.x) {
       const int r = idx >> 3, c = (idx & 7) * 8;
-      const int row = q0 + r;
-      cp_async16(&sm.q[r * kPad + c], qb + static_cast<size_t>(row < a.Lq ? row : 0) * a.q_rs + c, row < a.Lq ? 16 : 0);
+      const int pr = r0 + r;
+      const bool in = pr < R;
+      const int hg = in ? pr / a.Lq : 0, query = in ? pr % a.Lq : 0;
+      cp_async16(&sm.q[r * kPad + c], qb + static_cast<size_t>(query) * a.q_rs + hg * kD + c, in ? 16 : 0);
     }
   }
   load_kv_tile(a, sm, 0, b, kh, 0);
@@ -284,8 +290,9 @@ __global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const
   const float ra = (a.qo && a.qo_rsmooth) ? __frcp_rn(a.qo_act) : 0.f;
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
-    const int row = q0 + wr + g + hr * 8;
-    if (row >= a.Lq) continue;
+    const int pr = r0 + wr + g + hr * 8;
+    if (pr >= R) continue;
+    const int h = kh * G + pr / a.Lq, row = pr % a.Lq;
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       const int d = n * 8 + 2 * t;

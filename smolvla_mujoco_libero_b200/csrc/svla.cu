@@ -520,8 +520,13 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
     if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  dim3 grid((d->lq + attn_detail::kRows - 1) / attn_detail::kRows, d->hq, d->batch);
-  return launch(attention_kernel, dim3(grid), dim3(attn_detail::kRows * 2), smem, cs(stream), "attention_kernel", a);
+  // packed rows of one kv head (its query heads' queries) split into equal tiles of 16 x warps rows
+  const long long rows = static_cast<long long>(d->hq / d->hkv) * d->lq;
+  const long long tiles = (rows + attn_detail::kRows - 1) / attn_detail::kRows;
+  if (tiles > 65535) return fail(SVLA_ERR_ARG, "svla_attention: too many query rows");
+  a.rows = static_cast<int>(((rows + tiles - 1) / tiles + 15) / 16 * 16);
+  dim3 grid(static_cast<unsigned>(tiles), d->hkv, d->batch);
+  return launch(attention_kernel, dim3(grid), dim3(a.rows * 2), smem, cs(stream), "attention_kernel", a);
 }
 
 int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* pos, void* q_out, void* k_out,
