@@ -190,6 +190,8 @@ int32_t svla_norm_quant(const svla_norm_desc* desc, svla_stream_t stream);
  * Attention; replaces the fused RoPE attention plugins (deploy/cuda/fused_rope_layout.h:44-50,
  * fused_rope_layout.cu:271-543) for post-RoPE q/k (RoPE is fused into the QKV GEMM epilogue).
  * Masked GQA, head_dim 64; keys from one or two sources (cached prefix, then current suffix).
+ * Unmasked single-source calls with at least 128 queries run on the tcgen05 kernel (S and O in tensor
+ * memory); the rest on an mma.sync kernel that packs each kv head's query heads into its row tiles.
  * ------------------------------------------------------------------------------------------------*/
 typedef struct svla_attn_desc {
   const void* q; int64_t q_bs; int32_t q_rs;
@@ -201,7 +203,11 @@ typedef struct svla_attn_desc {
   const float* qo_smooth; const float* qo_rsmooth; float qo_act; /* qo_rsmooth optional, as in svla_norm_desc */
   int32_t batch, lq, hq, hkv;
   float scale;                                           /* 0 = head_dim^-1/2 */
+  int32_t impl; /* SVLA_ATTN_AUTO, or force SVLA_ATTN_MMA_SYNC / SVLA_ATTN_TCGEN05 (the latter only for
+                   unmasked single-source calls with lq >= 128, aligned strides) */
 } svla_attn_desc;
+
+enum { SVLA_ATTN_AUTO = 0, SVLA_ATTN_MMA_SYNC = 1, SVLA_ATTN_TCGEN05 = 2 };
 
 int32_t svla_attention(const svla_attn_desc* desc, svla_stream_t stream);
 

@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libsvla.so"
 
 KIND_I8, KIND_BF16, KIND_W8A16 = 0, 1, 2
 EPI_BF16, EPI_I32, EPI_ROPE, EPI_RESID, EPI_SILU_MUL, EPI_GELU_QUANT, EPI_EULER, EPI_SILU, EPI_F32 = range(9)
+ATTN_AUTO, ATTN_MMA_SYNC, ATTN_TCGEN05 = range(3)
 
 
 class GemmSeg(ctypes.Structure):
@@ -54,6 +55,7 @@ class AttnDesc(ctypes.Structure):
         ("qo", c_void_p), ("qo_bs", c_int64), ("qo_rs", c_int32),
         ("qo_smooth", c_void_p), ("qo_rsmooth", c_void_p), ("qo_act", c_float),
         ("batch", c_int32), ("lq", c_int32), ("hq", c_int32), ("hkv", c_int32), ("scale", c_float),
+        ("impl", c_int32),
     ]
 
 

@@ -1,0 +1,315 @@
+// Unmasked attention on the 5th-generation tensor cores (tcgen05), head_dim 64, bf16 in / bf16 out:
+// the SigLIP encoder's self-attention (deploy/export_6f_layer0_attention_tensors.py:100-119 semantics,
+// without a mask):  o = bf16(softmax((q . k) * scale) @ v), fp32 scores, softmax and accumulation.
+//
+// CTA: two 128-query tiles of one (batch, head), 384 threads.
+//   warp 0       TMA: both Q tiles once, then K and V tiles of 128 keys through a 4-stage ring
+//   warp 1       TMEM owner (512 columns) and MMA issuer (one lane):
+//                  S_i = Q_i K_j^T   (M 128, N 128, K 64; both operands from shared memory, K-major)
+//                  O_i += P_i V_j    (M 128, N 64, K 128; P_i from tensor memory, V_j MN-major in smem)
+//   warps 4-7    softmax of query tile 0, warps 8-11 of tile 1: thread t owns TMEM lane t = query row t,
+//                so the row max and row sum need no shuffles.
+// TMEM columns: S_0 [0,128)  S_1 [128,256)  O_0 [256,320)  O_1 [320,384).  P_i (bf16 pairs) is written over
+// the first 64 columns of S_i.  The two query tiles alternate on the tensor core: while one softmax
+// warpgroup works on its S, the MMAs of the other tile run.
+//
+// Online softmax with a lazily updated running max (the rescale of O and l happens only when the row max
+// grows by more than 8 in log2 units; otherwise the stale max stays and the probabilities, at most 2^8,
+// are still exact in bf16's exponent range).  The final O / l uses the same max for both, so the result
+// is the softmax regardless.  Probabilities exp2(s * scale * log2 e - m) are rounded to bf16 for the
+// P.V product, as in the mma.sync kernel; the row sum uses the unrounded values.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace svla {
+
+struct AttnTcArgs {
+  CUtensorMap tq, tk, tv;  // 3-D maps (column, row, batch), box 64 x 128 x 1, 128-byte swizzle
+  __nv_bfloat16* o;        long long o_bs; int o_rs;
+  int8_t* qo;              long long qo_bs; int qo_rs;
+  const float* qo_smooth;  const float* qo_rsmooth;  float qo_act;
+  int Lq, Lk, Hq, Hkv;
+  float scale_log2;  // scale * log2(e)
+  int* err;
+};
+
+namespace atc {
+constexpr int kStages = 4;
+constexpr int kTileBytes = 128 * 128;  // 128 rows x 64 bf16
+constexpr int kQ0 = 0, kQ1 = kTileBytes, kK = 2 * kTileBytes, kV = kK + kStages * kTileBytes;
+constexpr int kBar = kV + kStages * kTileBytes;
+constexpr int kSmemBytes = kBar + 256 + 1024;  // + barriers + alignment slack
+constexpr int kThreads = 384;
+constexpr uint32_t kS0 = 0, kS1 = 128, kO0 = 256, kO1 = 320, kTmemCols = 512;
+}  // namespace atc
+
+__global__ void __launch_bounds__(atc::kThreads, 1) attention_tc_kernel(const __grid_constant__ AttnTcArgs a) {
+  using namespace atc;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + kBar);
+  uint64_t* k_full = q_full + 1;
+  uint64_t* v_full = k_full + kStages;
+  uint64_t* kv_empty = v_full + kStages;
+  uint64_t* s_full = kv_empty + kStages;  // [2]
+  uint64_t* p_full = s_full + 2;          // [2]
+  uint64_t* o_full = p_full + 2;          // [2]
+  uint64_t* mma_done = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kh = h / (a.Hq / a.Hkv);
+  const int q0 = blockIdx.x * 256;
+  const bool two = q0 + 128 < a.Lq;  // the second query tile has rows
+  const int n_kv = (a.Lk + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);  // one arrive per softmax warp
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // q, k, v are written by the previous kernel
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&a.tq);
+      prefetch_tmap(&a.tk);
+      prefetch_tmap(&a.tv);
+      mbar_arrive_expect_tx(q_full, (two ? 2 : 1) * kTileBytes);
+      tma_load_3d(smem + kQ0, &a.tq, q_full, h * 64, q0, b);
+      if (two) tma_load_3d(smem + kQ1, &a.tq, q_full, h * 64, q0 + 128, b);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % kStages;
+        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, a.err)) break;
+        mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+        tma_load_3d(smem + kK + s * kTileBytes, &a.tk, &k_full[s], kh * 64, j * 128, b);
+        mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+        tma_load_3d(smem + kV + s * kTileBytes, &a.tv, &v_full[s], kh * 64, j * 128, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_qk = idesc_bf16(128, 128);
+      const uint32_t id_pv = idesc_bf16(128, 64) | (1u << 16);  // B (V) MN-major
+      bool issued = false;
+      auto qk = [&](int i, int j) -> bool {
+        const int s = j % kStages;
+        if (!mbar_wait(&k_full[s], (j / kStages) & 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(smem + (i ? kQ1 : kQ0)), ka = smem_u32(smem + kK + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // 16 head dims (32 bytes) per MMA
+          mma_bf16(tmem + (i ? kS1 : kS0), smem_desc_sw128(qa + kk * 32), smem_desc_sw128(ka + kk * 32), id_qk,
+                   kk > 0 ? 1u : 0u);
+        mma_commit(&s_full[i]);
+        issued = true;
+        return true;
+      };
+      auto pv = [&](int i, int j) -> bool {
+        const int s = j % kStages;
+        if (!mbar_wait(&v_full[s], (j / kStages) & 1, a.err)) return false;
+        if (!mbar_wait(&p_full[i], j & 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t va = smem_u32(smem + kV + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 16 keys per MMA: 8 TMEM columns of P, 16 rows (2048 bytes) of V
+          mma_bf16_tmem_a(tmem + (i ? kO1 : kO0), tmem + (i ? kS1 : kS0) + kk * 8, smem_desc_sw128(va + kk * 2048),
+                          id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, a.err);
+      ok = ok && qk(0, 0) && (!two || qk(1, 0));
+      for (int j = 0; j < n_kv && ok; ++j) {
+        ok = pv(0, j);
+        if (ok && j + 1 < n_kv) ok = qk(0, j + 1);
+        if (ok && two) ok = pv(1, j);
+        if (ok) mma_commit(&kv_empty[j % kStages]);
+        if (ok && two && j + 1 < n_kv) ok = qk(1, j + 1);
+      }
+      if (ok) {
+        mma_commit(&o_full[0]);
+        if (two) mma_commit(&o_full[1]);
+      }
+      // every issued MMA completes before the TMEM is released
+      if (issued) {
+        mma_commit(mma_done);
+        mbar_wait(mma_done, 0, a.err);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax warpgroups
+    const int i = (warp - 4) >> 2;  // query tile
+    const int wq = warp & 3;        // TMEM lane quarter
+    const int row = q0 + i * 128 + wq * 32 + lane;
+    const uint32_t lanes = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lanes + (i ? kS1 : kS0);
+    const uint32_t tO = tmem + lanes + (i ? kO1 : kO0);
+    const float c = a.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    bool ok = (i == 0) || two;
+    const bool active = ok;
+    for (int j = 0; j < n_kv && ok; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[i], j & 1, a.err));
+      if (!ok) break;
+      tc_fence_after();
+      const int kvalid = a.Lk - j * 128;  // keys of this tile inside Lk
+      // pass 1: row max of the raw scores
+      float mx = -INFINITY;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(tS + ch * 32, r);
+        tmem_ld_wait();
+        if (kvalid >= 128) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = (ch * 32 + e < kvalid) ? fmaxf(mx, __uint_as_float(r[e])) : mx;
+        }
+      }
+      const float m_new = fmaxf(m, __fmul_rn(mx, c));  // max of s * c (rounding is monotonic)
+      if (j == 0) {
+        m = m_new;  // the first P.V overwrites O
+      } else {
+        const bool grow = m_new > m + 8.0f;
+        if (__any_sync(0xffffffffu, grow)) {
+          const float alpha = grow ? ex2_approx(m - m_new) : 1.0f;
+          l *= alpha;
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tO + ch * 32, r);
+            tmem_ld_wait();
+            uint32_t w0[16], w1[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              w0[e] = __float_as_uint(__fmul_rn(__uint_as_float(r[e]), alpha));
+              w1[e] = __float_as_uint(__fmul_rn(__uint_as_float(r[16 + e]), alpha));
+            }
+            tmem_st16(tO + ch * 32, w0);
+            tmem_st16(tO + ch * 32 + 16, w1);
+          }
+          if (grow) m = m_new;
+        }
+      }
+      // pass 2: probabilities, row sum, bf16 P over the first 64 columns of S (chunk ch writes columns
+      // 16ch .. 16ch+15, all read by chunks before it)
+      float ls = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(tS + ch * 32, r);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[e]), c, -m));
+          float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[e + 1]), c, -m));
+          if (kvalid < 128) {
+            p0 = (ch * 32 + e < kvalid) ? p0 : 0.f;
+            p1 = (ch * 32 + e + 1 < kvalid) ? p1 : 0.f;
+          }
+          ls += p0 + p1;
+          pk[e / 2] = pack_bf16_rn(p0, p1);
+        }
+        tmem_st16(tS + ch * 16, pk);
+      }
+      l += ls;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[i]);
+    }
+    // epilogue: O / l -> bf16 (and the int8 input of the next W8A8 linear)
+    if (active && ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&o_full[i], 0, a.err));
+      tc_fence_after();
+      if (ok) {
+        const float inv = __frcp_rn(l);
+        const float ra = (a.qo && a.qo_rsmooth) ? __frcp_rn(a.qo_act) : 0.f;
+        const bool in = row < a.Lq;
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          uint32_t r[32];
+          tmem_ld32(tO + ch * 32, r);
+          tmem_ld_wait();
+          if (!in) continue;
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            v[e] = __fmul_rn(__uint_as_float(r[e]), inv);
+            v[e + 1] = __fmul_rn(__uint_as_float(r[e + 1]), inv);
+            bf16_round2(v[e], v[e + 1]);
+          }
+          const int col = h * 64 + ch * 32;
+          if (a.o) {
+            __nv_bfloat16* op = a.o + static_cast<size_t>(b) * a.o_bs + static_cast<size_t>(row) * a.o_rs + col;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              *reinterpret_cast<int4*>(op + u * 8) =
+                  make_int4(pack_bf16_rn(v[8 * u], v[8 * u + 1]), pack_bf16_rn(v[8 * u + 2], v[8 * u + 3]),
+                            pack_bf16_rn(v[8 * u + 4], v[8 * u + 5]), pack_bf16_rn(v[8 * u + 6], v[8 * u + 7]));
+          }
+          if (a.qo) {
+            uint32_t w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+            uint32_t slow = a.qo_rsmooth ? 0u : 0xFFFFFFFFu;
+            if (a.qo_rsmooth) {
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                uint32_t sk = 0u;
+                w[k] = smooth_quant4_fast(&v[4 * k], *reinterpret_cast<const float4*>(a.qo_rsmooth + col + 4 * k), ra,
+                                          sk, 0);
+                slow |= sk << (4 * k);
+              }
+            }
+            if (slow != 0u) {  // rare: values near a rounding boundary take the two-divide path one by one
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                if (slow & (1u << e)) {
+                  const uint32_t q8 = static_cast<uint32_t>(smooth_quant_slow(v[e], a.qo_smooth[col + e], a.qo_act) & 0xFF);
+                  w[e / 4] = (w[e / 4] & ~(0xFFu << (8 * (e % 4)))) | (q8 << (8 * (e % 4)));
+                }
+              }
+            }
+            int8_t* qp = a.qo + static_cast<size_t>(b) * a.qo_bs + static_cast<size_t>(row) * a.qo_rs + col;
+            *reinterpret_cast<int4*>(qp) = make_int4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<int4*>(qp + 16) = make_int4(w[4], w[5], w[6], w[7]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace svla

@@ -15,6 +15,7 @@
 
 #include "../../include/svla.h"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "gemm.cuh"
 #include "misc.cuh"
 #include "norm.cuh"
@@ -470,6 +471,61 @@ int32_t svla_norm_quant(const svla_norm_desc* d, svla_stream_t stream) {
   return fail(SVLA_ERR_ARG, "svla_norm_quant: k=%d too large (max 3072)", d->k);
 }
 
+// 3-D bf16 tensor map (column, row, batch) with a 64 x 128 x 1 box and the 128-byte swizzle; rows past
+// `rows` (of each batch) read as zeros
+static int32_t make_tmap_bhd(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t batch,
+                             uint64_t rs, uint64_t bs) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SVLA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {cols, rows, batch};
+  cuuint64_t strides[2] = {rs * 2, bs * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SVLA_ERR_ARG, "cuTensorMapEncodeTiled (3-D) failed (%d)", static_cast<int>(r));
+  return SVLA_OK;
+}
+
+static int32_t run_attention_tc(const svla_attn_desc* d, float scale, cudaStream_t stream) {
+  AttnTcArgs a;
+  std::memset(&a, 0, sizeof(a));
+  int32_t rc = make_tmap_bhd(&a.tq, d->q, static_cast<uint64_t>(d->hq) * 64, d->lq, d->batch, d->q_rs, d->q_bs);
+  if (rc) return rc;
+  rc = make_tmap_bhd(&a.tk, d->k1, static_cast<uint64_t>(d->hkv) * 64, d->l1, d->batch, d->kv1_rs, d->kv1_bs);
+  if (rc) return rc;
+  rc = make_tmap_bhd(&a.tv, d->v1, static_cast<uint64_t>(d->hkv) * 64, d->l1, d->batch, d->kv1_rs, d->kv1_bs);
+  if (rc) return rc;
+  a.o = static_cast<__nv_bfloat16*>(d->o);
+  a.o_bs = d->o_bs;
+  a.o_rs = d->o_rs;
+  a.qo = d->qo;
+  a.qo_bs = d->qo_bs;
+  a.qo_rs = d->qo_rs;
+  a.qo_smooth = d->qo_smooth;
+  a.qo_rsmooth = d->qo_rsmooth;
+  a.qo_act = d->qo_act;
+  a.Lq = d->lq;
+  a.Lk = d->l1;
+  a.Hq = d->hq;
+  a.Hkv = d->hkv;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.err = device_error_ptr();
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         atc::kSmemBytes);
+    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((d->lq + 255) / 256), d->hq, d->batch);
+  return launch(attention_tc_kernel, grid, dim3(atc::kThreads), atc::kSmemBytes, stream, "attention_tc_kernel", a);
+}
+
 int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
   if (!d || !d->q || !d->k1 || !d->v1 || d->batch <= 0 || d->lq <= 0 || d->l1 <= 0 || d->hq <= 0 || d->hkv <= 0)
     return fail(SVLA_ERR_ARG, "svla_attention: bad args");
@@ -510,6 +566,17 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
   a.Hq = d->hq;
   a.Hkv = d->hkv;
   a.scale = d->scale > 0.f ? d->scale : 0.125f;
+  const bool a16 = [&] {
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return al(d->q) && al(d->k1) && al(d->v1) && (!d->o || (al(d->o) && d->o_rs % 8 == 0 && d->o_bs % 8 == 0)) &&
+           (!d->qo || (al(d->qo) && d->qo_rs % 16 == 0 && d->qo_bs % 16 == 0)) && d->q_bs % 8 == 0 &&
+           d->kv1_bs % 8 == 0 && (!d->qo_rsmooth || al(d->qo_rsmooth));
+  }();
+  const bool tc_ok = !d->mask && d->l2 <= 0 && d->lq >= 128 && a16;
+  if (d->impl == SVLA_ATTN_TCGEN05 && !tc_ok)
+    return fail(SVLA_ERR_ARG, "svla_attention: the tcgen05 kernel needs an unmasked single-source call, lq >= 128 "
+                              "and 16-byte aligned operands");
+  if (tc_ok && d->impl != SVLA_ATTN_MMA_SYNC) return run_attention_tc(d, a.scale, cs(stream));
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);

@@ -192,7 +192,7 @@ def attention_desc(q: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor, batch: i
                    mask: torch.Tensor | None = None, k2: torch.Tensor | None = None, v2: torch.Tensor | None = None,
                    o: torch.Tensor | None = None, qo: torch.Tensor | None = None,
                    qo_smooth: torch.Tensor | None = None, qo_act: float = 0.0, scale: float = 0.0,
-                   qo_rsmooth: torch.Tensor | None = None) -> L.AttnDesc:
+                   qo_rsmooth: torch.Tensor | None = None, impl: int = L.ATTN_AUTO) -> L.AttnDesc:
     """q [B, Lq, >=hq*64] (row stride = stride(1)), k/v [B, L, >=hkv*64], mask [B, Lq, L1+L2] (uint8/bool)."""
     d = L.AttnDesc()
     d.q, d.q_bs, d.q_rs = q.data_ptr(), q.stride(0), q.stride(1)
@@ -209,7 +209,7 @@ def attention_desc(q: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor, batch: i
         d.qo, d.qo_bs, d.qo_rs = qo.data_ptr(), qo.stride(0), qo.stride(1)
         d.qo_smooth, d.qo_act = qo_smooth.data_ptr(), float(qo_act)
         d.qo_rsmooth = _p(qo_rsmooth)
-    d.batch, d.lq, d.hq, d.hkv, d.scale = batch, lq, hq, hkv, float(scale)
+    d.batch, d.lq, d.hq, d.hkv, d.scale, d.impl = batch, lq, hq, hkv, float(scale), impl
     return d
 
 
@@ -218,7 +218,7 @@ def attention_run(desc: L.AttnDesc) -> None:
 
 
 def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smooth=None, qo_act=0.0,
-              qo_rsmooth=None):
+              qo_rsmooth=None, impl: int = L.ATTN_AUTO):
     """bf16 context [B, Lq, hq*64] (and the int8 context when qo_smooth is given)."""
     b, lq = q.shape[0], q.shape[1]
     o = torch.empty(b, lq, hq * 64, dtype=torch.bfloat16, device=q.device)
@@ -226,7 +226,7 @@ def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smoo
     if mask is not None and mask.dtype == torch.bool:
         mask = mask.view(torch.uint8)
     attention_run(attention_desc(q, k1, v1, b, lq, hq, hkv, mask=mask, k2=k2, v2=v2, o=o, qo=qo,
-                                 qo_smooth=qo_smooth, qo_act=qo_act, qo_rsmooth=qo_rsmooth))
+                                 qo_smooth=qo_smooth, qo_act=qo_act, qo_rsmooth=qo_rsmooth, impl=impl))
     return (o, qo) if qo is not None else o
 
 

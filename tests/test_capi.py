@@ -39,20 +39,19 @@ def test_version_and_error_string_without_gpu():
     assert isinstance(lib.svla_last_error(), bytes)
 
 
-def _c_sizeof(struct: str) -> int:
+def _c_sizeof(struct: str, tmp_path: Path) -> int:
     src = f'#include "{HEADER}"\n#include <stdio.h>\nint main(){{printf("%zu", sizeof({struct}));return 0;}}\n'
-    tmp = REPO / "_work" / "sizeof_probe"
-    tmp.parent.mkdir(exist_ok=True)
-    (tmp.with_suffix(".c")).write_text(src)
-    subprocess.run(["gcc", "-o", str(tmp), str(tmp.with_suffix(".c"))], check=True)
-    return int(subprocess.run([str(tmp)], capture_output=True, text=True).stdout)
+    probe = tmp_path / "sizeof_probe"
+    probe.with_suffix(".c").write_text(src)
+    subprocess.run(["gcc", "-o", str(probe), str(probe.with_suffix(".c"))], check=True)
+    return int(subprocess.run([str(probe)], capture_output=True, text=True).stdout)
 
 
 @pytest.mark.parametrize("cname,pyname", [("svla_gemm_desc", "GemmDesc"), ("svla_gemm_seg", "GemmSeg"),
                                           ("svla_norm_desc", "NormDesc"), ("svla_attn_desc", "AttnDesc")])
-def test_struct_layouts_match(cname, pyname):
+def test_struct_layouts_match(cname, pyname, tmp_path):
     import ctypes
-    assert ctypes.sizeof(getattr(_lib, pyname)) == _c_sizeof(cname)
+    assert ctypes.sizeof(getattr(_lib, pyname)) == _c_sizeof(cname, tmp_path)
 
 
 def test_argument_errors_are_reported_without_a_gpu():

@@ -375,6 +375,38 @@ def test_attention_single_source(b, lq, lk, hq, hkv, masked):
     assert float((o.cpu().float() - ref.float()).abs().max()) <= 2e-2
 
 
+@pytest.mark.parametrize("b,lq,lk,hq,hkv", [(2, 1024, 1024, 12, 12), (1, 300, 200, 4, 4), (2, 130, 77, 15, 5),
+                                             (1, 256, 128, 2, 1), (1, 129, 1, 2, 2)])
+def test_attention_tcgen05_kernel(b, lq, lk, hq, hkv):
+    """The tcgen05 kernel (unmasked, single source) against the reference and the mma.sync kernel, with
+    query tails (a second query tile partly or wholly empty) and key tails (a last key tile of 1..127)."""
+    g = synthetic.generator(b * 7 + lq * 3 + lk)
+    q = torch.randn(b, lq, hq * 64, generator=g).to(torch.bfloat16)
+    k = torch.randn(b, lk, hkv * 64, generator=g).to(torch.bfloat16)
+    v = torch.randn(b, lk, hkv * 64, generator=g).to(torch.bfloat16)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    o_tc = ops.attention(qd, kd, vd, hq, hkv, impl=L.ATTN_TCGEN05)
+    o_ms = ops.attention(qd, kd, vd, hq, hkv, impl=L.ATTN_MMA_SYNC)
+    ref = _attn_ref(q, k, v, None, hq, hkv)
+    assert cosine(o_tc, ref) >= 0.9999
+    assert float((o_tc.cpu().float() - ref.float()).abs().max()) <= 2e-2
+    assert float((o_tc.cpu().float() - o_ms.cpu().float()).abs().max()) <= 2e-2
+    # fused int8 output (the out_proj input): the quantisation of the kernel's own bf16 context
+    smooth = torch.rand(hq * 64, generator=g) + 0.5
+    o2, qo = ops.attention(qd, kd, vd, hq, hkv, qo_smooth=smooth.to(DEV), qo_act=0.01,
+                           qo_rsmooth=ops.reciprocal(smooth.to(DEV)), impl=L.ATTN_TCGEN05)
+    assert torch.equal(o2.cpu(), o_tc.cpu())
+    qo_ref = Q.smooth_quantize_activation(o2.cpu().reshape(-1, hq * 64), smooth, 0.01).reshape(b, lq, -1)
+    assert torch.equal(qo.cpu(), qo_ref)
+
+
+def test_attention_tcgen05_rejects_masked_calls():
+    q = torch.zeros(1, 128, 64, dtype=torch.bfloat16, device=DEV)
+    mask = torch.ones(1, 128, 128, dtype=torch.bool, device=DEV)
+    with pytest.raises(L.SvlaError):
+        ops.attention(q, q, q, 1, 1, mask=mask, impl=L.ATTN_TCGEN05)
+
+
 def test_attention_two_sources_and_quant_out():
     g = synthetic.generator(31)
     b, lq, l1, l2, hq, hkv = 2, 50, 177, 50, 15, 5
