@@ -205,6 +205,7 @@ typedef struct svla_attn_desc {
   float scale;                                           /* 0 = head_dim^-1/2 */
   int32_t impl; /* SVLA_ATTN_AUTO, or force SVLA_ATTN_MMA_SYNC / SVLA_ATTN_TCGEN05 (the latter only for
                    unmasked single-source calls with lq >= 128, aligned strides) */
+  void* debug_clock; /* profiling: uint64 [96] phase clock stamps of one CTA of the tcgen05 kernel, or NULL */
 } svla_attn_desc;
 
 enum { SVLA_ATTN_AUTO = 0, SVLA_ATTN_MMA_SYNC = 1, SVLA_ATTN_TCGEN05 = 2 };

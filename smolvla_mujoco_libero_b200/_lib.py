@@ -55,7 +55,7 @@ class AttnDesc(ctypes.Structure):
         ("qo", c_void_p), ("qo_bs", c_int64), ("qo_rs", c_int32),
         ("qo_smooth", c_void_p), ("qo_rsmooth", c_void_p), ("qo_act", c_float),
         ("batch", c_int32), ("lq", c_int32), ("hq", c_int32), ("hkv", c_int32), ("scale", c_float),
-        ("impl", c_int32),
+        ("impl", c_int32), ("debug_clock", c_void_p),
     ]
 
 

@@ -2,16 +2,18 @@
 // the SigLIP encoder's self-attention (deploy/export_6f_layer0_attention_tensors.py:100-119 semantics,
 // without a mask):  o = bf16(softmax((q . k) * scale) @ v), fp32 scores, softmax and accumulation.
 //
-// CTA: two 128-query tiles of one (batch, head), 384 threads.
+// CTA: two 128-query tiles of one (batch, head), 320 threads.
 //   warp 0       TMA: both Q tiles once, then K and V tiles of 128 keys through a 4-stage ring
 //   warp 1       TMEM owner (512 columns) and MMA issuer (one lane):
 //                  S_i = Q_i K_j^T   (M 128, N 128, K 64; both operands from shared memory, K-major)
 //                  O_i += P_i V_j    (M 128, N 64, K 128; P_i from tensor memory, V_j MN-major in smem)
-//   warps 4-7    softmax of query tile 0, warps 8-11 of tile 1: thread t owns TMEM lane t = query row t,
-//                so the row max and row sum need no shuffles.
+//   warps 2-5    softmax of query tile 0, warps 6-9 of tile 1 (warp w reads TMEM lanes 32*(w%4)..+31):
+//                thread t owns TMEM lane t = query row t, so the row max and row sum need no shuffles; the
+//                row's 128 scores of a key tile are held in registers (one TMEM read per tile).
 // TMEM columns: S_0 [0,128)  S_1 [128,256)  O_0 [256,320)  O_1 [320,384).  P_i (bf16 pairs) is written over
-// the first 64 columns of S_i.  The two query tiles alternate on the tensor core: while one softmax
-// warpgroup works on its S, the MMAs of the other tile run.
+// the first 64 columns of S_i.  The MMA issue order (P.V of tile 0, next Q.K^T of tile 0, P.V of tile 1,
+// next Q.K^T of tile 1) lets the two softmax warpgroups settle half a period apart, so the MMAs of one
+// query tile run while the other's softmax computes.
 //
 // Online softmax with a lazily updated running max (the rescale of O and l happens only when the row max
 // grows by more than 8 in log2 units; otherwise the stale max stays and the probabilities, at most 2^8,
@@ -31,6 +33,7 @@ struct AttnTcArgs {
   const float* qo_smooth;  const float* qo_rsmooth;  float qo_act;
   int Lq, Lk, Hq, Hkv;
   float scale_log2;  // scale * log2(e)
+  unsigned long long* dbg;  // optional phase clock stamps of the CTA (0, 0, batch / 2) (profiling)
   int* err;
 };
 
@@ -40,7 +43,7 @@ constexpr int kTileBytes = 128 * 128;  // 128 rows x 64 bf16
 constexpr int kQ0 = 0, kQ1 = kTileBytes, kK = 2 * kTileBytes, kV = kK + kStages * kTileBytes;
 constexpr int kBar = kV + kStages * kTileBytes;
 constexpr int kSmemBytes = kBar + 256 + 1024;  // + barriers + alignment slack
-constexpr int kThreads = 384;
+constexpr int kThreads = 320;
 constexpr uint32_t kS0 = 0, kS1 = 128, kO0 = 256, kO1 = 320, kTmemCols = 512;
 }  // namespace atc
 
@@ -64,6 +67,11 @@ __global__ void __launch_bounds__(atc::kThreads, 1) attention_tc_kernel(const __
   const int q0 = blockIdx.x * 256;
   const bool two = q0 + 128 < a.Lq;  // the second query tile has rows
   const int n_kv = (a.Lk + 127) / 128;
+  unsigned long long* dbg = (a.dbg && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == gridDim.z / 2) ? a.dbg : nullptr;
+  auto stamp = [&](int slot) {
+    if (dbg) dbg[slot] = clock64();
+  };
+  if (threadIdx.x == 0) stamp(0);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -90,6 +98,7 @@ __global__ void __launch_bounds__(atc::kThreads, 1) attention_tc_kernel(const __
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // q, k, v are written by the previous kernel
   pdl_trigger();
+  if (threadIdx.x == 0) stamp(1);
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -132,6 +141,7 @@ __global__ void __launch_bounds__(atc::kThreads, 1) attention_tc_kernel(const __
         const int s = j % kStages;
         if (!mbar_wait(&v_full[s], (j / kStages) & 1, a.err)) return false;
         if (!mbar_wait(&p_full[i], j & 1, a.err)) return false;
+        if (i == 0 && j < 8) stamp(8 + j);
         tc_fence_after();
         const uint32_t va = smem_u32(smem + kV + s * kTileBytes);
 #pragma unroll
@@ -141,11 +151,14 @@ __global__ void __launch_bounds__(atc::kThreads, 1) attention_tc_kernel(const __
         return true;
       };
       bool ok = mbar_wait(q_full, 0, a.err);
+      stamp(2);
       ok = ok && qk(0, 0) && (!two || qk(1, 0));
       for (int j = 0; j < n_kv && ok; ++j) {
         ok = pv(0, j);
+        if (j < 8) stamp(16 + j);
         if (ok && j + 1 < n_kv) ok = qk(0, j + 1);
         if (ok && two) ok = pv(1, j);
+        if (j < 8) stamp(24 + j);
         if (ok) mma_commit(&kv_empty[j % kStages]);
         if (ok && two && j + 1 < n_kv) ok = qk(1, j + 1);
       }
@@ -159,9 +172,9 @@ __global__ void __launch_bounds__(atc::kThreads, 1) attention_tc_kernel(const __
         mbar_wait(mma_done, 0, a.err);
       }
     }
-  } else if (warp >= 4) {
+  } else {
     // ---------------- softmax warpgroups
-    const int i = (warp - 4) >> 2;  // query tile
+    const int i = (warp - 2) >> 2;  // query tile
     const int wq = warp & 3;        // TMEM lane quarter
     const int row = q0 + i * 128 + wq * 32 + lane;
     const uint32_t lanes = static_cast<uint32_t>(wq * 32) << 16;
@@ -174,80 +187,89 @@ __global__ void __launch_bounds__(atc::kThreads, 1) attention_tc_kernel(const __
     for (int j = 0; j < n_kv && ok; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[i], j & 1, a.err));
       if (!ok) break;
+      const bool st0 = (wq == 0 && lane == 0 && j < 8);
+      if (st0) stamp(i ? 56 + j : 32 + j);
       tc_fence_after();
       const int kvalid = a.Lk - j * 128;  // keys of this tile inside Lk
-      // pass 1: row max of the raw scores
-      float mx = -INFINITY;
+      uint32_t r[128];
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t r[32];
-        tmem_ld32(tS + ch * 32, r);
-        tmem_ld_wait();
-        if (kvalid >= 128) {
+      for (int ch = 0; ch < 4; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[ch * 32]));
+      tmem_ld_wait();
+      // row max with 8 independent partial maxima (short dependency chains)
+      float mp[8];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
-        } else {
+      for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
+      if (kvalid >= 128) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = (ch * 32 + e < kvalid) ? fmaxf(mx, __uint_as_float(r[e])) : mx;
-        }
+        for (int e = 0; e < 128; ++e) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(r[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 128; ++e) mp[e & 7] = (e < kvalid) ? fmaxf(mp[e & 7], __uint_as_float(r[e])) : mp[e & 7];
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       const float m_new = fmaxf(m, __fmul_rn(mx, c));  // max of s * c (rounding is monotonic)
+      float alpha = 1.0f;
+      bool grow = false;
       if (j == 0) {
         m = m_new;  // the first P.V overwrites O
-      } else {
-        const bool grow = m_new > m + 8.0f;
-        if (__any_sync(0xffffffffu, grow)) {
-          const float alpha = grow ? ex2_approx(m - m_new) : 1.0f;
-          l *= alpha;
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) {
-            uint32_t r[32];
-            tmem_ld32(tO + ch * 32, r);
-            tmem_ld_wait();
-            uint32_t w0[16], w1[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              w0[e] = __float_as_uint(__fmul_rn(__uint_as_float(r[e]), alpha));
-              w1[e] = __float_as_uint(__fmul_rn(__uint_as_float(r[16 + e]), alpha));
-            }
-            tmem_st16(tO + ch * 32, w0);
-            tmem_st16(tO + ch * 32 + 16, w1);
-          }
-          if (grow) m = m_new;
-        }
+      } else if (m_new > m + 8.0f) {
+        grow = true;
+        alpha = ex2_approx(m - m_new);
+        m = m_new;
       }
-      // pass 2: probabilities, row sum, bf16 P over the first 64 columns of S (chunk ch writes columns
-      // 16ch .. 16ch+15, all read by chunks before it)
-      float ls = 0.f;
+      // probabilities and row sum; bf16 P over the first 64 columns of S (all of S is in registers)
+      float lp[8];  // 8 partial row sums
+#pragma unroll
+      for (int u = 0; u < 8; ++u) lp[u] = 0.f;
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
-        uint32_t r[32];
-        tmem_ld32(tS + ch * 32, r);
-        tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[e]), c, -m));
-          float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[e + 1]), c, -m));
+          const int k0 = ch * 32 + e;
+          float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[k0]), c, -m));
+          float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[k0 + 1]), c, -m));
           if (kvalid < 128) {
-            p0 = (ch * 32 + e < kvalid) ? p0 : 0.f;
-            p1 = (ch * 32 + e + 1 < kvalid) ? p1 : 0.f;
+            p0 = (k0 < kvalid) ? p0 : 0.f;
+            p1 = (k0 + 1 < kvalid) ? p1 : 0.f;
           }
-          ls += p0 + p1;
+          lp[(e / 2) & 7] += p0 + p1;
           pk[e / 2] = pack_bf16_rn(p0, p1);
         }
         tmem_st16(tS + ch * 16, pk);
       }
-      l += ls;
+      const float ls = ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
+      l = __fmaf_rn(l, alpha, ls);
+      // O rescale (rare after the first tiles): the previous P.V has completed -- its commit preceded the
+      // S of this tile -- and the next one waits for this warpgroup's arrival below
+      if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          uint32_t o32[32];
+          tmem_ld32(tO + ch * 32, o32);
+          tmem_ld_wait();
+          uint32_t w0[16], w1[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            w0[e] = __float_as_uint(__fmul_rn(__uint_as_float(o32[e]), alpha));
+            w1[e] = __float_as_uint(__fmul_rn(__uint_as_float(o32[16 + e]), alpha));
+          }
+          tmem_st16(tO + ch * 32, w0);
+          tmem_st16(tO + ch * 32 + 16, w1);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[i]);
+      if (st0) stamp(i ? 64 + j : 48 + j);
+      if (lane == 0 && j < 2) stamp((i ? 72 : 40) + 4 * j + wq);
     }
     // epilogue: O / l -> bf16 (and the int8 input of the next W8A8 linear)
     if (active && ok) {
       ok = __all_sync(0xffffffffu, mbar_wait(&o_full[i], 0, a.err));
       tc_fence_after();
+      if (wq == 0 && lane == 0) stamp(90 + 2 * i);
       if (ok) {
         const float inv = __frcp_rn(l);
         const float ra = (a.qo && a.qo_rsmooth) ? __frcp_rn(a.qo_act) : 0.f;
@@ -306,6 +328,7 @@ __global__ void __launch_bounds__(atc::kThreads, 1) attention_tc_kernel(const __
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) stamp(95);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

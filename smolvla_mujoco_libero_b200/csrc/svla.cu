@@ -511,6 +511,7 @@ static int32_t run_attention_tc(const svla_attn_desc* d, float scale, cudaStream
   a.Hq = d->hq;
   a.Hkv = d->hkv;
   a.scale_log2 = scale * 1.4426950408889634f;
+  a.dbg = static_cast<unsigned long long*>(d->debug_clock);
   a.err = device_error_ptr();
   static bool configured[64] = {false};
   int dev = 0;

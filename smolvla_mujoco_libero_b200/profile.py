@@ -106,8 +106,19 @@ def op_attn(a) -> dict:
         mask = full.to(dev)[:, :, : a.lk]
     ms = time_op(lambda: ops.attention(q, k, v, a.heads, a.kv_heads, mask=mask), a.iters)
     flops = 4.0 * a.batch * a.heads * a.lq * a.lk * 64
+    # phase clock stamps of one CTA of the tcgen05 kernel (when that kernel runs)
+    from . import _lib as L
+    dbg = torch.zeros(96, dtype=torch.int64, device=dev)
+    o = torch.empty(a.batch, a.lq, a.heads * 64, dtype=torch.bfloat16, device=dev)
+    d = ops.attention_desc(q, k, v, a.batch, a.lq, a.heads, a.kv_heads, mask=mask, o=o)
+    d.debug_clock = dbg.data_ptr()
+    ops.attention_run(d)
+    torch.cuda.synchronize()
+    c = dbg.cpu().tolist()
+    phases = {i: c[i] - c[0] for i in range(96) if c[i]} if c[0] else {}
     return {"op": "attn", "batch": a.batch, "lq": a.lq, "lk": a.lk, "heads": a.heads, "kv_heads": a.kv_heads,
-            "mask": a.mask, "mask_ld": a.mask_ld, "ms": ms, "tflops_best": flops / (min(ms) / 1e3) / 1e12}
+            "mask": a.mask, "mask_ld": a.mask_ld, "ms": ms, "tflops_best": flops / (min(ms) / 1e3) / 1e12,
+            "cta_cycles": phases}
 
 
 def main() -> None:
