@@ -157,7 +157,19 @@ typedef struct svla_gemm_desc {
   uint64_t* debug_clock;  /* optional [16]: SM clock stamps of the first CTA's phases (profiling), else NULL */
   int32_t weights_resident; /* 1: every B operand was written before the previously launched kernel started
                                (packed weights), so its first tiles are fetched before waiting for that kernel */
+  /* Split-K for GEMMs with few output tiles: split_k 0 = automatic (when a workspace is given and the
+   * output tiles fill at most half of the SMs), 1 = off, n > 1 = n splits.  Each split stores its raw
+   * accumulators in the workspace; the last one of a tile adds them in split order (int32 sums are exact,
+   * so I8 results do not change) and runs the epilogue.  The workspace (256-byte aligned) starts with
+   * SVLA_SPLITK_COUNTER_BYTES of tile counters that must be zero before its first use; every completed
+   * launch leaves them zero.  Launches that share a workspace must be stream-ordered.  Split-K runs with
+   * 64-column tiles (block_n 0 picks them for few-tile GEMMs; other block_n values cannot split). */
+  int32_t split_k;
+  void* workspace;
+  size_t workspace_bytes;
 } svla_gemm_desc;
+
+#define SVLA_SPLITK_COUNTER_BYTES 65536
 
 int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream);
 
@@ -206,6 +218,10 @@ typedef struct svla_attn_desc {
   int32_t impl; /* SVLA_ATTN_AUTO, or force SVLA_ATTN_MMA_SYNC / SVLA_ATTN_TCGEN05 (the latter only for
                    unmasked single-source calls with lq >= 128, aligned strides) */
   void* debug_clock; /* profiling: uint64 [96] phase clock stamps of one CTA of the tcgen05 kernel, or NULL */
+  /* Structured mask, instead of `mask` (same result as the equivalent byte mask, far less mask traffic):
+   * query i may see key k iff k < mask_keys ? key_mask[b*key_mask_bs + k] != 0 : k - mask_keys <= i
+   * (key padding over the first mask_keys keys, causal order over the rest: the action expert's masks). */
+  const uint8_t* key_mask; int64_t key_mask_bs; int32_t mask_keys;
 } svla_attn_desc;
 
 enum { SVLA_ATTN_AUTO = 0, SVLA_ATTN_MMA_SYNC = 1, SVLA_ATTN_TCGEN05 = 2 };

@@ -33,7 +33,11 @@ class GemmDesc(ctypes.Structure):
         ("resid_rows", c_int32), ("rope_cs", c_void_p), ("pos", c_void_p), ("max_pos", c_int32),
         ("q_smooth", c_void_p), ("q_rsmooth", c_void_p), ("q_act", c_float), ("qout", c_void_p), ("ldq", c_int32), ("dt", c_float),
         ("xt", c_void_p), ("xt_bf16", c_void_p), ("debug_clock", c_void_p), ("weights_resident", c_int32),
+        ("split_k", c_int32), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
+
+
+SPLITK_COUNTER_BYTES = 65536  # SVLA_SPLITK_COUNTER_BYTES
 
 
 class NormDesc(ctypes.Structure):
@@ -56,6 +60,7 @@ class AttnDesc(ctypes.Structure):
         ("qo_smooth", c_void_p), ("qo_rsmooth", c_void_p), ("qo_act", c_float),
         ("batch", c_int32), ("lq", c_int32), ("hq", c_int32), ("hkv", c_int32), ("scale", c_float),
         ("impl", c_int32), ("debug_clock", c_void_p),
+        ("key_mask", c_void_p), ("key_mask_bs", c_int64), ("mask_keys", c_int32),
     ]
 
 

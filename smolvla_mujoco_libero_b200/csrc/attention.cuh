@@ -32,6 +32,8 @@ struct AttnArgs {
   const __nv_bfloat16* k1; const __nv_bfloat16* v1; long long kv1_bs; int kv1_rs; int L1;
   const __nv_bfloat16* k2; const __nv_bfloat16* v2; long long kv2_bs; int kv2_rs; int L2;
   const uint8_t* mask;     long long mask_bs; int mask_rs;  // mask[b*mask_bs + i*mask_rs + key] or nullptr
+  // structured mask (instead of `mask`): key < mask_keys ? key_mask[b*key_mask_bs + key] : key - mask_keys <= i
+  const uint8_t* key_mask; long long key_mask_bs; int mask_keys;
   __nv_bfloat16* o;        long long o_bs; int o_rs;        // optional bf16 output
   int8_t* qo;              long long qo_bs; int qo_rs;      // optional int8 output
   const float* qo_smooth;  const float* qo_rsmooth;  float qo_act;
@@ -118,7 +120,20 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st
     cp_async16(&sm.k[st][r * kPad + c], kp, bytes);
     cp_async16(&sm.v[st][r * kPad + c], vp, bytes);
   }
-  if (a.mask) {
+  if (a.key_mask) {
+    // structured mask: one row of key flags (keys below mask_keys) for every query of the tile
+    if (threadIdx.x < 4) {
+      const int c = threadIdx.x * 16, key = key0 + c;
+      const int kend = a.mask_keys < Lk ? a.mask_keys : Lk;
+      const uint8_t* src = a.key_mask + static_cast<size_t>(b) * a.key_mask_bs;
+      uint8_t* dst = &sm.m[st][c];
+      if (key + 16 <= kend && ((reinterpret_cast<uintptr_t>(src + key) & 15) == 0)) {
+        cp_async16(dst, src + key, 16);
+      } else {
+        for (int j = 0; j < 16; ++j) dst[j] = (key + j < kend) ? src[key + j] : 0;
+      }
+    }
+  } else if (a.mask) {
     // mask bytes [128 rows x 64 keys]; rows past Lq and keys past Lk are left as whatever they read:
     // the scores of keys past Lk are forced to -inf and rows past Lq are never stored.  A 16-key run is
     // one 16-byte copy when it is aligned and lies inside the row's storage (the row stride covers Lk
@@ -172,6 +187,12 @@ __global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const
 
   uint32_t qa[4][4];
   float o[8][4];
+  int query[2];  // query index of this thread's two rows (structured mask)
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int pr = r0 + warp * 16 + g + hr * 8;
+    query[hr] = pr < R ? pr % a.Lq : 0;
+  }
 #pragma unroll
   for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float mx[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
@@ -224,6 +245,9 @@ __global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const
         float v = __fmul_rn(s[n][e], a.scale);
         if (key >= Lk) {
           v = -INFINITY;  // not a key at all
+        } else if (a.key_mask) {
+          const bool allowed = (key < a.mask_keys) ? (sm.m[st][kc] != 0) : (key - a.mask_keys <= query[e >> 1]);
+          if (!allowed) v = kMaskedScore;
         } else if (a.mask && sm.m[st][rl * kKeys + kc] == 0) {
           v = kMaskedScore;
         }

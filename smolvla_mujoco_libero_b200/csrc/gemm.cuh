@@ -74,6 +74,12 @@ struct GemmArgs {
   __nv_bfloat16* xt_bf16;           // Euler: bf16 copy
   unsigned long long* dbg;          // optional phase clock stamps of CTA 0 (profiling)
   int weights_resident;             // B operands were written before the previous kernel started
+  // split-K: work item t is split t % splits (k-tiles [split * kt_per_split, +kt_per_split)) of output
+  // tile t / splits.  Every split stores its raw 32-bit accumulators to `partial`; the last to arrive on
+  // the tile's counter adds them in split order into its own accumulator and runs the epilogue.
+  int splits, kt_per_split;
+  uint32_t* partial;                // [tiles][splits][P][128][BN]
+  int* counters;                    // [tiles], zero between launches (the last split resets it)
   int* err;
 };
 
@@ -144,6 +150,7 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 
 template <int BN, int P>
 __device__ __forceinline__ void tile_coord(const GemmArgs& a, int t, int& si, int& m0, int& n0) {
+  if (a.splits > 1) t /= a.splits;
   const int nt = t % a.tiles_n, mt = t / a.tiles_n;
   si = 0;
   if constexpr (P == 1) {
@@ -153,6 +160,17 @@ __device__ __forceinline__ void tile_coord(const GemmArgs& a, int t, int& si, in
   }
   m0 = mt * 128;
   n0 = (nt - a.seg[si].tile_begin) * BN;
+}
+
+// k-tile range [kb, ke) of work item t
+__device__ __forceinline__ void k_range(const GemmArgs& a, int t, int k_tiles, int& kb, int& ke) {
+  if (a.splits > 1) {
+    kb = (t % a.splits) * a.kt_per_split;
+    ke = kb + a.kt_per_split < k_tiles ? kb + a.kt_per_split : k_tiles;
+  } else {
+    kb = 0;
+    ke = k_tiles;
+  }
 }
 
 // Epilogue of one output tile for the calling warp's 32 TMEM lanes (rows row = 32*(warp%4) + lane) and
@@ -407,6 +425,105 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
   return ok;
 }
 
+// Split-K step of one output tile, run by all epilogue warps (each on its TMEM lane quarter and half of
+// the columns): store this split's raw accumulators; count the arrival; the tile's last split adds all
+// partials in split order (int32 exactly, fp32 in a fixed order) into its own accumulator.  Returns
+// whether this CTA runs the tile's epilogue.
+template <Kind KIND, int BN, int P, typename WaitAcc>
+__device__ __forceinline__ bool splitk_reduce(const GemmArgs& args, int t, int m0, int row, int half, int etid,
+                                              uint32_t t_row, bool ok, volatile int* split_last, WaitAcc&& wait_acc) {
+  constexpr int kEpiThreads = 32 * kEpiWarps;
+  const int tile = t / args.splits, sp = t % args.splits;
+  const bool aok = ok && wait_acc();
+  const bool row_in = m0 + row < args.M;
+  uint32_t* tile_part = args.partial + static_cast<size_t>(tile) * args.splits * (P * 128 * BN);
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+#pragma unroll
+    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
+      uint32_t r[16];
+      if (aok) {
+        tmem_ld16(t_row + p * BN + c, r);
+        tmem_ld_wait();
+      }
+      if (aok && row_in) {
+        uint32_t* dst = tile_part + (static_cast<size_t>(sp) * P + p) * (128 * BN) + row * BN + c;
+#pragma unroll
+        for (int u = 0; u < 16; u += 4) *reinterpret_cast<int4*>(dst + u) = make_int4(r[u], r[u + 1], r[u + 2], r[u + 3]);
+      }
+    }
+  }
+  // The CTA barrier orders every warp's partial stores before thread 0's gpu-scope release fence (fences
+  // are cumulative), which orders them before its counter increment; its acquire fence after the
+  // increment orders the other splits' stores before this CTA's reads.
+  if (etid == 0 && t == static_cast<int>(blockIdx.x)) stamp(args.dbg, 11);
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+  if (etid == 0 && t == static_cast<int>(blockIdx.x)) stamp(args.dbg, 12);
+  if (etid == 0) {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    *split_last = (atomicAdd(&args.counters[tile], 1) == args.splits - 1) ? 1 : 0;
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  }
+  if (etid == 0 && t == static_cast<int>(blockIdx.x)) stamp(args.dbg, 13);
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+  if (etid == 0 && t == static_cast<int>(blockIdx.x)) stamp(args.dbg, *split_last ? 14 : 15);
+  if (*split_last == 0) return false;
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+#pragma unroll
+    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
+      uint32_t acc[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) acc[u] = 0u;
+      if (aok && row_in) {
+        // eight columns at a time with four splits' loads in flight, added in split order
+#pragma unroll
+        for (int h8 = 0; h8 < 16; h8 += 8) {
+          for (int k0 = 0; k0 < args.splits; k0 += 4) {
+            int4 v[4][2];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              if (k0 + kk < args.splits) {
+                const uint32_t* src = tile_part + (static_cast<size_t>(k0 + kk) * P + p) * (128 * BN) + row * BN + c + h8;
+                v[kk][0] = __ldcg(reinterpret_cast<const int4*>(src));
+                v[kk][1] = __ldcg(reinterpret_cast<const int4*>(src + 4));
+              }
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              if (k0 + kk < args.splits) {
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const uint32_t w[4] = {static_cast<uint32_t>(v[kk][u].x), static_cast<uint32_t>(v[kk][u].y),
+                                         static_cast<uint32_t>(v[kk][u].z), static_cast<uint32_t>(v[kk][u].w)};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    uint32_t& a = acc[h8 + 4 * u + e];
+                    if (k0 + kk == 0)
+                      a = w[e];
+                    else if constexpr (KIND == Kind::I8)
+                      a = static_cast<uint32_t>(static_cast<int>(a) + static_cast<int>(w[e]));
+                    else
+                      a = __float_as_uint(__fadd_rn(__uint_as_float(a), __uint_as_float(w[e])));
+                  }
+                }
+              }
+            }
+          }
+        }
+      }
+      if (aok) tmem_st16(t_row + p * BN + c, acc);
+    }
+  }
+  tmem_st_wait();
+  // the epilogue may read columns another warp of this lane quarter summed (RoPE takes whole heads)
+  tc_fence_before();
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+  tc_fence_after();
+  if (etid == 0) args.counters[tile] = 0;  // ready for the next launch
+  return true;
+}
+
 template <Kind KIND, int BN, int P, int STAGES, Epi EPI>
 __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(const __grid_constant__ GemmArgs args) {
   using T = KindTraits<KIND>;
@@ -420,11 +537,12 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
   uint64_t* tempty = tfull + 2;             // [2] epilogue has drained the accumulator buffer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* split_last = abort_flag + 1;  // split-K: this CTA was the tile's last split
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int k_tiles = (args.K + T::kBK - 1) / T::kBK;
-  const int n_tiles_total = args.tiles_m * args.tiles_n;
+  const int n_tiles_total = args.tiles_m * args.tiles_n * (args.splits > 1 ? args.splits : 1);
 
   if (threadIdx.x == 0) stamp(args.dbg, 0);
   if (threadIdx.x == 0) {
@@ -459,7 +577,6 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
     *abort_flag = 1;
     return false;
   };
-
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
@@ -475,15 +592,16 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
       // tile's first STAGES weight tiles are requested before waiting, so they stream in while it finishes.
       int pre = 0;
       if (args.weights_resident && blockIdx.x < n_tiles_total) {
-        int si, m0, n0;
+        int si, m0, n0, kb, ke;
         tile_coord<BN, P>(args, blockIdx.x, si, m0, n0);
-        pre = k_tiles < STAGES ? k_tiles : STAGES;
-        for (int kt = 0; kt < pre; ++kt) {
-          uint8_t* st = smem + kt * S::kStage;
-          mbar_arrive_expect_tx(&full[kt], P * (S::kATile + kBBytes));
+        k_range(args, blockIdx.x, k_tiles, kb, ke);
+        pre = ke - kb < STAGES ? ke - kb : STAGES;
+        for (int i = 0; i < pre; ++i) {
+          uint8_t* st = smem + i * S::kStage;
+          mbar_arrive_expect_tx(&full[i], P * (S::kATile + kBBytes));
 #pragma unroll
           for (int p = 0; p < P; ++p)
-            tma_load_2d(b_dst(st, p), &args.tb[(P == 1) ? si : p], &full[kt], kt * T::kBK, n0);
+            tma_load_2d(b_dst(st, p), &args.tb[(P == 1) ? si : p], &full[i], (kb + i) * T::kBK, n0);
         }
       }
       pdl_wait();
@@ -491,9 +609,10 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x) {
-        int si, m0, n0;
+        int si, m0, n0, kb, ke;
         tile_coord<BN, P>(args, t, si, m0, n0);
-        for (int kt = 0; kt < k_tiles; ++kt, ++g) {
+        k_range(args, t, k_tiles, kb, ke);
+        for (int kt = kb; kt < ke; ++kt, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
           uint8_t* st = smem + s * S::kStage;
@@ -526,7 +645,9 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
         if (!(ok = bounded_wait(&tempty[ab], (use & 1) ^ 1))) break;
         tc_fence_after();
         const uint32_t d_base = tmem_base + ab * S::kAccCols;
-        for (int kt = 0; kt < k_tiles; ++kt, ++g) {
+        int kb, ke;
+        k_range(args, t, k_tiles, kb, ke);
+        for (int kt = kb; kt < ke; ++kt, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
           ok = bounded_wait(&full[s], ph);
@@ -545,7 +666,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
             for (int kk = 0; kk < 128 / 32; ++kk) {  // 4 MMAs of 32 bytes of K each
               const uint64_t ad = smem_desc_sw128(a_addr + kk * 32);
               const uint64_t bd = smem_desc_sw128(b_addr + kk * 32);
-              const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+              const uint32_t acc = (kt > kb || kk > 0) ? 1u : 0u;
               if constexpr (KIND == Kind::I8)
                 mma_i8(d_tmem, ad, bd, idesc, acc);
               else
@@ -594,14 +715,22 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
       }
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
       if (lt == 0 && etid == 0) stamp(args.dbg, 6);
+      bool acc_waited = false, acc_ok = true;
       auto wait_acc = [&]() -> bool {
-        const bool w = __all_sync(0xffffffffu, bounded_wait(&tfull[ab], use & 1));
+        if (acc_waited) return acc_ok;
+        acc_ok = __all_sync(0xffffffffu, bounded_wait(&tfull[ab], use & 1));
         tc_fence_after();
+        acc_waited = true;
         if (lt == 0 && etid == 0) stamp(args.dbg, 7);
-        return w;
+        return acc_ok;
       };
       const uint32_t t_row = tmem_base + ab * S::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      const bool ok_t = epilogue_tile<KIND, BN, P, EPI>(args, si, m0, n0, t_row, row, half, ok, cst, wait_acc);
+      bool run_epi = true;
+      if constexpr (BN == 64) {  // split-K is compiled for the narrow tile only (the one few-tile GEMMs use)
+        if (args.splits > 1) run_epi = splitk_reduce<KIND, BN, P>(args, t, m0, row, half, etid, t_row, ok, split_last, wait_acc);
+      }
+      const bool ok_t = run_epi ? epilogue_tile<KIND, BN, P, EPI>(args, si, m0, n0, t_row, row, half, ok, cst, wait_acc)
+                                : (ok && acc_ok);
       if (lt == 0 && etid == 0) stamp(args.dbg, 8);
       tc_fence_before();
       __syncwarp();
@@ -630,7 +759,9 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
           wsr[p][i] = (sp.wscale != nullptr && gn < sp.n) ? sp.wscale[gn] : 1.0f;
         }
       }
-      for (int kt = 0; kt < k_tiles; ++kt, ++g) {
+      int kb, ke;
+      k_range(args, t, k_tiles, kb, ke);
+      for (int kt = kb; kt < ke; ++kt, ++g) {
         const int s = g % STAGES;
         const uint32_t ph = (g / STAGES) & 1;
         ok = __all_sync(0xffffffffu, bounded_wait(&full[s], ph));

@@ -99,6 +99,10 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) 
     qcol0 = ((hh % s) * s + (ww % s)) * a.K;
   }
 
+  float ra[3];  // 1 / act_i, for the multiply form of the quantiser
+#pragma unroll
+  for (int qi = 0; qi < 3; ++qi) ra[qi] = (qi < a.nq && a.rsmooth[qi]) ? __frcp_rn(a.act[qi]) : 0.f;
+
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int k = (i * 32 + lane) * 8;
@@ -111,12 +115,19 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) 
       const __nv_bfloat16* bh = reinterpret_cast<const __nv_bfloat16*>(&br);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        y[j] = bf16_round(__fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i][j], mean), rstd), __bfloat162float(wh[j])),
-                                    __bfloat162float(bh[j])));
+        y[j] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i][j], mean), rstd), __bfloat162float(wh[j])),
+                         __bfloat162float(bh[j]));
     } else {
+      float h[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = bf16_round(__fmul_rn(__bfloat162float(wh[j]), bf16_round(__fmul_rn(v[i][j], rstd))));
+      for (int j = 0; j < 8; ++j) h[j] = __fmul_rn(v[i][j], rstd);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) bf16_round2(h[j], h[j + 1]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__bfloat162float(wh[j]), h[j]);
     }
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) bf16_round2(y[j], y[j + 1]);
     if (a.y) {
       uint32_t pk[4];
 #pragma unroll
@@ -124,24 +135,27 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) 
       *reinterpret_cast<int4*>(a.y + static_cast<size_t>(qrow) * a.ldy + qcol0 + k) =
           make_int4(pk[0], pk[1], pk[2], pk[3]);
     }
-    for (int qi = 0; qi < a.nq; ++qi) {
+#pragma unroll
+    for (int qi = 0; qi < 3; ++qi) {
+      if (qi >= a.nq) break;
       const int col = qcol0 + k;
-      const float4 s0 = *reinterpret_cast<const float4*>(a.smooth[qi] + col);
-      const float4 s1 = *reinterpret_cast<const float4*>(a.smooth[qi] + col + 4);
-      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-      int8_t qv[8];
+      uint32_t w[2] = {0u, 0u};
+      uint32_t slow = 0xFFu;  // every element exact without a reciprocal smooth vector
       if (a.rsmooth[qi]) {
-        const float4 r0 = *reinterpret_cast<const float4*>(a.rsmooth[qi] + col);
-        const float4 r1 = *reinterpret_cast<const float4*>(a.rsmooth[qi] + col + 4);
-        const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-        const float ra = __frcp_rn(a.act[qi]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) qv[j] = smooth_quant_fast(y[j], sv[j], rv[j], a.act[qi], ra);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) qv[j] = smooth_quant(y[j], sv[j], a.act[qi]);
+        slow = 0u;
+        w[0] = smooth_quant4_fast(&y[0], *reinterpret_cast<const float4*>(a.rsmooth[qi] + col), ra[qi], slow, 0);
+        w[1] = smooth_quant4_fast(&y[4], *reinterpret_cast<const float4*>(a.rsmooth[qi] + col + 4), ra[qi], slow, 4);
       }
-      *reinterpret_cast<int2*>(a.q[qi] + static_cast<size_t>(qrow) * a.ldq + col) = *reinterpret_cast<int2*>(qv);
+      if (slow != 0u) {  // rare: values near a rounding boundary take the two-divide path one by one
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (slow & (1u << j)) {
+            const uint32_t q8 = static_cast<uint32_t>(smooth_quant_slow(y[j], a.smooth[qi][col + j], a.act[qi]) & 0xFF);
+            w[j / 4] = (w[j / 4] & ~(0xFFu << (8 * (j % 4)))) | (q8 << (8 * (j % 4)));
+          }
+        }
+      }
+      *reinterpret_cast<int2*>(a.q[qi] + static_cast<size_t>(qrow) * a.ldq + col) = make_int2(w[0], w[1]);
     }
   }
 }

@@ -305,7 +305,47 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
     return fail(SVLA_ERR_ARG, "GELU_QUANT with qout needs q_smooth and q_act > 0");
   if (epi == Epi::GeluQuant && !d->qout && !d->seg[0].out) return fail(SVLA_ERR_ARG, "GELU_QUANT needs qout or out");
   if (epi == Epi::Euler && (!d->xt || !d->xt_bf16)) return fail(SVLA_ERR_ARG, "EULER needs xt/xt_bf16");
-  const long long total_tiles = static_cast<long long>(args.tiles_m) * args.tiles_n;
+  // split-K (see svla_gemm_desc): only with a workspace, 64-column tiles and few output tiles
+  const long long out_tiles = static_cast<long long>(args.tiles_m) * args.tiles_n;
+  const int kstage = kind == Kind::I8 ? 128 : 64;  // K elements per pipeline stage
+  const int k_tiles = (d->k + kstage - 1) / kstage;
+  args.splits = 1;
+  args.kt_per_split = k_tiles;
+  if (d->split_k < 0) return fail(SVLA_ERR_ARG, "split_k must be >= 0");
+  if (d->split_k > 1 && !d->workspace) return fail(SVLA_ERR_ARG, "split_k needs a workspace");
+  if (d->split_k > 1 && bn != 64) return fail(SVLA_ERR_ARG, "split_k needs block_n 64 (got %d)", bn);
+  if (d->workspace && d->split_k != 1 && bn == 64) {
+    if (reinterpret_cast<uintptr_t>(d->workspace) % 256 != 0) return fail(SVLA_ERR_ARG, "workspace not 256-byte aligned");
+    // automatic: up to 4 splits (the last split reads every split's partial: more splits cost more than
+    // the shorter K loop saves), at least 4 k-tiles each, within the SMs the output tiles leave free
+    long long want = 1;
+    if (d->split_k > 1) {
+      want = d->split_k;
+    } else if (out_tiles * 2 <= sms) {
+      want = k_tiles / 4;
+      if (want > 4) want = 4;
+      if (want > sms / out_tiles) want = sms / out_tiles;
+      if (want < 1) want = 1;
+    }
+    if (want > k_tiles) want = k_tiles;
+    if (want > 32) want = 32;
+    const long long per_split = static_cast<long long>(d->pair ? 2 : 1) * 128 * bn * 4;
+    const long long room = static_cast<long long>(d->workspace_bytes) - SVLA_SPLITK_COUNTER_BYTES;
+    if (want > 1 && (out_tiles > SVLA_SPLITK_COUNTER_BYTES / 4 || room < out_tiles * per_split * want)) {
+      if (d->split_k > 1)
+        return fail(SVLA_ERR_ARG, "split_k=%d does not fit the workspace (%zu bytes)", d->split_k, d->workspace_bytes);
+      want = (out_tiles <= SVLA_SPLITK_COUNTER_BYTES / 4 && room > 0) ? room / (out_tiles * per_split) : 1;
+      if (want < 1) want = 1;
+    }
+    if (want > 1) {
+      const int kps = static_cast<int>((k_tiles + want - 1) / want);
+      args.splits = (k_tiles + kps - 1) / kps;  // every split has at least one k-tile
+      args.kt_per_split = kps;
+      args.counters = static_cast<int*>(d->workspace);
+      args.partial = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(d->workspace) + SVLA_SPLITK_COUNTER_BYTES);
+    }
+  }
+  const long long total_tiles = out_tiles * args.splits;
   dim3 grid(static_cast<unsigned>(total_tiles < sms ? total_tiles : sms));
   switch (kind) {
     case Kind::I8: return dispatch_bn<Kind::I8>(bn, d->pair, epi, args, grid, stream);
@@ -554,6 +594,12 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
   a.mask = d->mask;
   a.mask_bs = d->mask_bs;
   a.mask_rs = d->mask_rs;
+  if (d->key_mask && d->mask) return fail(SVLA_ERR_ARG, "svla_attention: give mask or key_mask, not both");
+  if (d->key_mask && (d->mask_keys <= 0 || d->mask_keys > d->l1 + (d->l2 > 0 ? d->l2 : 0)))
+    return fail(SVLA_ERR_ARG, "svla_attention: mask_keys must be in 1..l1+l2");
+  a.key_mask = d->key_mask;
+  a.key_mask_bs = d->key_mask_bs;
+  a.mask_keys = d->mask_keys;
   a.o = static_cast<__nv_bfloat16*>(d->o);
   a.o_bs = d->o_bs;
   a.o_rs = d->o_rs;
@@ -573,7 +619,7 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
            (!d->qo || (al(d->qo) && d->qo_rs % 16 == 0 && d->qo_bs % 16 == 0)) && d->q_bs % 8 == 0 &&
            d->kv1_bs % 8 == 0 && (!d->qo_rsmooth || al(d->qo_rsmooth));
   }();
-  const bool tc_ok = !d->mask && d->l2 <= 0 && d->lq >= 128 && a16;
+  const bool tc_ok = !d->mask && !d->key_mask && d->l2 <= 0 && d->lq >= 128 && a16;
   if (d->impl == SVLA_ATTN_TCGEN05 && !tc_ok)
     return fail(SVLA_ERR_ARG, "svla_attention: the tcgen05 kernel needs an unmasked single-source call, lq >= 128 "
                               "and 16-byte aligned operands");

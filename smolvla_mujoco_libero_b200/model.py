@@ -130,9 +130,12 @@ class DeviceWeights:
 class SmolVLARunner:
     """Static buffers + launch list for one batch size."""
 
-    W8A16_BF16_ROWS = 512  # M from which W8A16 linears run as bf16 GEMMs on the dequantized weight
+    W8A16_BF16_ROWS = 1  # M from which W8A16 linears run as bf16 GEMMs on the dequantized weight (all M:
+    # measured faster than converting the int8 weight inside every tile, at M = 50 as at M = 3200)
+    SPLITK_BYTES = 32 << 20  # split-K workspace shared by the runner's GEMMs (stream-ordered)
 
-    def __init__(self, weights: DeviceWeights, batch: int, mode: str = "quant", debug_taps: bool = False):
+    def __init__(self, weights: DeviceWeights, batch: int, mode: str = "quant", debug_taps: bool = False,
+                 split_k: bool = True):
         if weights.cfg.expert_layers != weights.cfg.text_layers:
             raise ValueError("the expert must have one layer per text layer (each expert layer reads that layer's KV)")
         if mode == "quant" and not weights.quantized:
@@ -142,6 +145,9 @@ class SmolVLARunner:
                 if p.weight_bf16 is None:
                     raise ValueError("bf16 mode needs DeviceWeights(..., keep_bf16=True)")
         self.w, self.cfg, self.B, self.mode, self.debug = weights, weights.cfg, batch, mode, debug_taps
+        # split-K changes the fp32 summation order of the small-M bf16 GEMMs with the batch size; without it
+        # every batch row's result is bit-identical at any batch size
+        self.split_k = split_k
         self.dev = weights.device
         self.graph: torch.cuda.CUDAGraph | None = None
         self.taps: dict[str, list] = {}
@@ -158,6 +164,7 @@ class SmolVLARunner:
         NI = B * c.n_cams
         NV = NI * c.n_patches
         z = lambda *s, dt=bf: torch.zeros(*s, dtype=dt, device=d)  # noqa: E731
+        self.splitk_ws = ops.splitk_workspace(self.SPLITK_BYTES, d)
         self.in_img = z(B, c.n_cams, c.channels, c.image_size, c.image_size, dt=f32)
         self.in_img_mask = z(c.n_cams, B, dt=torch.uint8)
         self.in_tokens = torch.zeros(B, c.n_lang, dtype=torch.int64, device=d)
@@ -170,6 +177,10 @@ class SmolVLARunner:
         self.prefix_mask = z(B, Lp, ld(Lp), dt=torch.uint8)[:, :, :Lp]
         self.self_mask = z(B, S, ld(Lp + S), dt=torch.uint8)[:, :, :Lp + S]
         self.cross_mask = z(B, S, ld(Lp), dt=torch.uint8)[:, :, :Lp]
+        # the prefix key padding (a row of the cross mask): the expert's self and cross attention use it in
+        # the structured form (key padding over the prefix, causal over the chunk), the same masks as
+        # self_mask / cross_mask with one row of flags per sample instead of one per query
+        self.key_pad = self.cross_mask[:, 0, :]
         self.prefix_pos = z(B * Lp, dt=torch.int32)
         self.suffix_pos = z(B * S, dt=torch.int32)
         self.cross_pos = z(B * S, dt=torch.int32)
@@ -232,16 +243,18 @@ class SmolVLARunner:
         self.launches.append((_TAP, (list(mods), buf)))
 
     def _gemm(self, kind, epi, m, k, segs, **kw):
-        # every B operand here is a packed weight, written when the model was built
-        d = ops.gemm_desc(kind, epi, m, k, segs, weights_resident=1, **kw)
+        # every B operand here is a packed weight, written when the model was built; GEMMs with few output
+        # tiles split K over the SMs through the runner's split-K workspace
+        ws = dict(workspace=self.splitk_ws, workspace_bytes=self.splitk_ws.numel()) if self.split_k else {}
+        d = ops.gemm_desc(kind, epi, m, k, segs, weights_resident=1, **ws, **kw)
         self._keep.append(segs)
         self._add(L.lib().svla_gemm, d)
 
     def _deq_rows(self, p: PackedLinear, m: int) -> bool:
         """W8A16 linears with at least W8A16_BF16_ROWS rows multiply by the stored bf16(q * wscale) weight
         (a plain bf16 GEMM; the reference's W8A16Linear keeps exactly that buffer) instead of converting
-        the int8 weight inside every output tile: the same operands, so the same results, and at large M
-        the per-tile conversion would cost more than the weight bytes it saves."""
+        the int8 weight inside every output tile: the same operands, so the same results, and the per-tile
+        conversion costs more than the weight bytes it saves."""
         return p.kind == "w8a16" and m >= self.W8A16_BF16_ROWS
 
     def _linear_seg(self, name: str, a: torch.Tensor, out, rope=0, n=None):
@@ -284,7 +297,8 @@ class SmolVLARunner:
         if tap is not None and not (self.mode == "quant" and quant_mods):
             self._tap(tap, target)
 
-    def _attn(self, q, k1, v1, lq, hq, hkv, mask=None, k2=None, v2=None, out_mod=None, out=None, tap=None):
+    def _attn(self, q, k1, v1, lq, hq, hkv, mask=None, k2=None, v2=None, out_mod=None, out=None, tap=None,
+              key_mask=None, mask_keys=0):
         """attention; in quant mode with out_mod the context is quantised for that W8A8 linear.
         The batch is the number of sequences in q (images for the vision tower, samples otherwise)."""
         B = q.shape[0] // lq
@@ -299,9 +313,11 @@ class SmolVLARunner:
         if self.mode == "quant" and out_mod is not None:
             p = self.w.lin[out_mod]
             d = ops.attention_desc(qv, k1v, v1v, B, lq, hq, hkv, mask=mask, k2=k2v, v2=v2v, qo=ov,
-                                   qo_smooth=p.smooth, qo_act=p.act_scale, qo_rsmooth=p.rsmooth)
+                                   qo_smooth=p.smooth, qo_act=p.act_scale, qo_rsmooth=p.rsmooth,
+                                   key_mask=key_mask, mask_keys=mask_keys)
         else:
-            d = ops.attention_desc(qv, k1v, v1v, B, lq, hq, hkv, mask=mask, k2=k2v, v2=v2v, o=ov)
+            d = ops.attention_desc(qv, k1v, v1v, B, lq, hq, hkv, mask=mask, k2=k2v, v2=v2v, o=ov,
+                                   key_mask=key_mask, mask_keys=mask_keys)
         self._add(L.lib().svla_attention, d)
         if tap is not None and not (self.mode == "quant" and out_mod is not None):
             self._tap(tap, out)
@@ -427,14 +443,15 @@ class SmolVLARunner:
                 if c.is_cross_layer(i):
                     self._gemm(kq, L.EPI_ROPE, B * S, E, [self._linear_seg(f"{p}.self_attn.q_proj", self.ey, self.eq, rope=1)],
                                rope_cs=self.rope_cs, pos=self.cross_pos, max_pos=self.max_pos)
-                    self._attn(self.eq, self.ck[i], self.cv[i], S, c.heads, c.kv_heads, mask=self.cross_mask, out=self.ectx)
+                    self._attn(self.eq, self.ck[i], self.cv[i], S, c.heads, c.kv_heads, out=self.ectx,
+                               key_mask=self.key_pad, mask_keys=Lp)
                 else:
                     segs = [self._linear_seg(f"{p}.self_attn.q_proj", self.ey, self.eq, rope=1),
                             self._linear_seg(f"{p}.self_attn.k_proj", self.ey, self.ek, rope=1),
                             self._linear_seg(f"{p}.self_attn.v_proj", self.ey, self.ev, rope=0)]
                     self._gemm(kq, L.EPI_ROPE, B * S, E, segs, rope_cs=self.rope_cs, pos=self.suffix_pos,
                                max_pos=self.max_pos)
-                    self._attn(self.eq, self.kcache[i], self.vcache[i], S, c.heads, c.kv_heads, mask=self.self_mask,
+                    self._attn(self.eq, self.kcache[i], self.vcache[i], S, c.heads, c.kv_heads, key_mask=self.key_pad, mask_keys=Lp,
                                k2=self.ek, v2=self.ev, out=self.ectx)
                 self._gemm(self._kind(f"{p}.self_attn.o_proj", B * S), L.EPI_RESID, B * S, c.q_dim,
                            [self._linear_seg(f"{p}.self_attn.o_proj", self.ectx, self.eh)], resid=self.eh, ldr=E)

@@ -149,6 +149,11 @@ def gemm_desc(kind: int, epi: int, m: int, k: int, segs: list[Seg], pair: bool =
     return d
 
 
+def splitk_workspace(nbytes: int, device) -> torch.Tensor:
+    """A zeroed split-K workspace for svla_gemm (its leading tile counters must start at zero)."""
+    return torch.zeros(max(int(nbytes), L.SPLITK_COUNTER_BYTES + 4096), dtype=torch.uint8, device=device)
+
+
 def gemm(desc: L.GemmDesc) -> None:
     check(lib().svla_gemm(ctypes.byref(desc), _stream()), "svla_gemm")
 
@@ -192,7 +197,8 @@ def attention_desc(q: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor, batch: i
                    mask: torch.Tensor | None = None, k2: torch.Tensor | None = None, v2: torch.Tensor | None = None,
                    o: torch.Tensor | None = None, qo: torch.Tensor | None = None,
                    qo_smooth: torch.Tensor | None = None, qo_act: float = 0.0, scale: float = 0.0,
-                   qo_rsmooth: torch.Tensor | None = None, impl: int = L.ATTN_AUTO) -> L.AttnDesc:
+                   qo_rsmooth: torch.Tensor | None = None, impl: int = L.ATTN_AUTO,
+                   key_mask: torch.Tensor | None = None, mask_keys: int = 0) -> L.AttnDesc:
     """q [B, Lq, >=hq*64] (row stride = stride(1)), k/v [B, L, >=hkv*64], mask [B, Lq, L1+L2] (uint8/bool)."""
     d = L.AttnDesc()
     d.q, d.q_bs, d.q_rs = q.data_ptr(), q.stride(0), q.stride(1)
@@ -203,6 +209,8 @@ def attention_desc(q: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor, batch: i
         d.k2, d.v2, d.kv2_bs, d.kv2_rs, d.l2 = k2.data_ptr(), v2.data_ptr(), k2.stride(0), k2.stride(1), k2.shape[1]
     if mask is not None:
         d.mask, d.mask_bs, d.mask_rs = mask.data_ptr(), mask.stride(0), mask.stride(1)
+    if key_mask is not None:  # [B, >= mask_keys] key flags; keys from mask_keys on are causal
+        d.key_mask, d.key_mask_bs, d.mask_keys = key_mask.data_ptr(), key_mask.stride(0), int(mask_keys)
     if o is not None:
         d.o, d.o_bs, d.o_rs = o.data_ptr(), o.stride(0), o.stride(1)
     if qo is not None:
@@ -218,7 +226,7 @@ def attention_run(desc: L.AttnDesc) -> None:
 
 
 def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smooth=None, qo_act=0.0,
-              qo_rsmooth=None, impl: int = L.ATTN_AUTO):
+              qo_rsmooth=None, impl: int = L.ATTN_AUTO, key_mask=None, mask_keys: int = 0):
     """bf16 context [B, Lq, hq*64] (and the int8 context when qo_smooth is given)."""
     b, lq = q.shape[0], q.shape[1]
     o = torch.empty(b, lq, hq * 64, dtype=torch.bfloat16, device=q.device)
@@ -226,7 +234,8 @@ def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smoo
     if mask is not None and mask.dtype == torch.bool:
         mask = mask.view(torch.uint8)
     attention_run(attention_desc(q, k1, v1, b, lq, hq, hkv, mask=mask, k2=k2, v2=v2, o=o, qo=qo,
-                                 qo_smooth=qo_smooth, qo_act=qo_act, qo_rsmooth=qo_rsmooth, impl=impl))
+                                 qo_smooth=qo_smooth, qo_act=qo_act, qo_rsmooth=qo_rsmooth, impl=impl,
+                                 key_mask=key_mask, mask_keys=mask_keys))
     return (o, qo) if qo is not None else o
 
 

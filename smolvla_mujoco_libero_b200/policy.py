@@ -25,10 +25,10 @@ from .model import DeviceWeights, SmolVLARunner
 
 class SampleActions:
     def __init__(self, cfg: SmolVLAConfig, weights: DeviceWeights, use_cuda_graph: bool = True,
-                 action_dim: int | None = None):
+                 action_dim: int | None = None, split_k: bool = True):
         if not weights.quantized:
             raise ValueError("SampleActions needs weights packed with a scale table")
-        self.cfg, self.weights, self.use_cuda_graph = cfg, weights, use_cuda_graph
+        self.cfg, self.weights, self.use_cuda_graph, self.split_k = cfg, weights, use_cuda_graph, split_k
         self.action_dim = cfg.action_dim if action_dim is None else action_dim
         self.runners: dict[int, SmolVLARunner] = {}
         self.stats: dict[str, Any] = {"cuda_graph_failed": False}
@@ -36,7 +36,7 @@ class SampleActions:
     def runner(self, batch: int) -> SmolVLARunner:
         r = self.runners.get(batch)
         if r is None:
-            r = SmolVLARunner(self.weights, batch)
+            r = SmolVLARunner(self.weights, batch, split_k=self.split_k)
             if self.use_cuda_graph:
                 try:
                     r.capture()

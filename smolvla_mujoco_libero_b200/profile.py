@@ -18,7 +18,7 @@ import json
 
 import torch
 
-from . import synthetic
+from . import ops, synthetic
 from .calibrate import calibrate, load_scale_json
 from .config import BENCH
 from .model import DeviceWeights, SmolVLARunner
@@ -73,6 +73,9 @@ def op_gemm(a) -> dict:
     elif epi == 4:
         segs.append(ops.Seg(a=A, b=B, out=out, n=a.n, wscale=ws, act_scale=0.01))
         extra = dict(pair=True)
+    if a.split_k != 1:
+        ws = ops.splitk_workspace(64 << 20, dev)
+        extra.update(split_k=a.split_k, workspace=ws, workspace_bytes=ws.numel())
     d = ops.gemm_desc(kind, epi, a.m, a.k, segs, block_n=a.block_n, **extra)
     ms = time_op(lambda: ops.gemm(d), a.iters)
     # phase clock stamps of CTA 0 from one more launch
@@ -82,12 +85,34 @@ def op_gemm(a) -> dict:
     torch.cuda.synchronize()
     c = dbg.cpu().tolist()
     d.debug_clock = None
-    names = ["entry", "setup", "tma0", "full0", "conv0", "commit0", "epi_consts", "epi_acc", "epi_done", "sync_end", "dealloc"]
+    names = ["entry", "setup", "tma0", "full0", "conv0", "commit0", "epi_consts", "epi_acc", "epi_done", "sync_end", "dealloc",
+             "sk_stored", "sk_bar", "sk_counted", "sk_last", "sk_notlast"]
     phases = {names[i]: (c[i] - c[0]) if c[i] else None for i in range(len(names))}
     ops_count = 2.0 * a.m * a.n * a.k * (2 if epi == 4 else 1)
     best = min(ms)
-    return {"op": "gemm", "kind": a.kind, "epi": a.epi, "m": a.m, "n": a.n, "k": a.k, "ms": ms,
+    return {"op": "gemm", "kind": a.kind, "epi": a.epi, "m": a.m, "n": a.n, "k": a.k, "split_k": a.split_k, "ms": ms,
             "tflops_best": ops_count / (best / 1e3) / 1e12, "cta0_cycles": phases}
+
+
+def op_norm(a) -> dict:
+    """LayerNorm (or RMSNorm with --rms) fused with three SmoothQuant int8 outputs: the SigLIP q/k/v input."""
+    from . import _lib as L
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    x = torch.randn(a.m, a.k, generator=g).to(dev, torch.bfloat16)
+    w = (torch.rand(a.k, generator=g) + 0.5).to(dev, torch.bfloat16)
+    b = None if a.rms else (torch.randn(a.k, generator=g) * 0.1).to(dev, torch.bfloat16)
+    qs = [torch.empty(a.m, a.k, dtype=torch.int8, device=dev) for _ in range(3)]
+    sm = [(torch.rand(a.k, generator=g) + 0.5).to(dev) for _ in range(3)]
+    rs = [ops.reciprocal(t) for t in sm]
+    d = L.NormDesc()
+    d.x, d.ldx, d.weight, d.bias, d.eps = x.data_ptr(), a.k, w.data_ptr(), (b.data_ptr() if b is not None else None), 1e-6
+    d.layernorm, d.m, d.k, d.nq, d.ldq = int(b is not None), a.m, a.k, 3, a.k
+    for i in range(3):
+        d.q[i], d.smooth[i], d.rsmooth[i], d.act[i] = qs[i].data_ptr(), sm[i].data_ptr(), rs[i].data_ptr(), 0.05
+    ms = time_op(lambda: L.check(L.lib().svla_norm_quant(d, ops._stream()), "norm"), a.iters)
+    nbytes = a.m * a.k * (2 + 3)
+    return {"op": "norm", "m": a.m, "k": a.k, "ms": ms, "GBps_best": nbytes / (min(ms) / 1e3) / 1e9}
 
 
 def op_attn(a) -> dict:
@@ -121,9 +146,40 @@ def op_attn(a) -> dict:
             "cta_cycles": phases}
 
 
+def summarize_launches(csv_path: str, top: int = 30) -> str:
+    """Per-kernel launches, total device time and share from an ncu launch list
+    (``--metrics gpu__time_duration.sum --csv``): the summary format of the committed profiles."""
+    import csv
+    import re
+    rows = list(csv.reader(open(csv_path)))
+    hi = next(i for i, r in enumerate(rows) if "Kernel Name" in r)
+    h = rows[hi]
+    ki, vi, ui = h.index("Kernel Name"), h.index("Metric Value"), h.index("Metric Unit")
+    tot: dict[str, list] = {}
+    for r in rows[hi + 1:]:
+        if len(r) <= vi or r[vi] == "":
+            continue
+        v = float(r[vi].replace(",", ""))
+        v = v / 1e3 if r[ui] in ("nsecond", "ns") else (v * 1e3 if r[ui] in ("msecond", "ms") else v)  # -> us
+        name = re.sub(r"\(svla::[A-Za-z]+\)", "", r[ki]).replace("svla::", "")
+        name = re.sub(r"\(GemmArgs\)|\(AttnTcArgs\)|\(AttnArgs\)|\(NormQuantArgs\)|\(MaskArgs\)", "", name)
+        name = re.sub(r"\(.*\)$", "", name.replace("void ", ""))
+        e = tot.setdefault(name, [0, 0.0])
+        e[0] += 1
+        e[1] += v
+    total = sum(e[1] for e in tot.values())
+    n = sum(e[0] for e in tot.values())
+    out = [f"launches {n} total {total / 1e3:.3f} ms"]
+    for name, (cnt, us) in sorted(tot.items(), key=lambda kv: -kv[1][1])[:top]:
+        out.append(f"{name[:52]:52s} launches {cnt:5d} total {us / 1e3:9.3f} ms share {100 * us / total:5.1f}% "
+                   f"avg {us / cnt:9.2f} us")
+    return "\n".join(out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="sample_actions", choices=["sample_actions", "gemm", "attn"])
+    ap.add_argument("--op", default="sample_actions", choices=["sample_actions", "gemm", "attn", "norm"])
+    ap.add_argument("--rms", action="store_true", help="--op norm: RMSNorm instead of LayerNorm")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--graph", action="store_true")
@@ -134,15 +190,23 @@ def main() -> None:
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=768)
     ap.add_argument("--block-n", type=int, default=0)
+    ap.add_argument("--split-k", type=int, default=1, help="GEMM split-K: 1 off, 0 automatic, n splits")
     ap.add_argument("--lq", type=int, default=1024)
     ap.add_argument("--lk", type=int, default=1024)
     ap.add_argument("--heads", type=int, default=12)
     ap.add_argument("--kv-heads", type=int, default=12)
     ap.add_argument("--mask", action="store_true")
     ap.add_argument("--mask-ld", type=int, default=0)
+    ap.add_argument("--summarize", default=None, help="print the per-kernel summary of an ncu launch-list CSV")
     a = ap.parse_args()
+    if a.summarize:
+        print(summarize_launches(a.summarize))
+        return
     if a.op == "gemm":
         print(json.dumps(op_gemm(a)))
+        return
+    if a.op == "norm":
+        print(json.dumps(op_norm(a)))
         return
     if a.op == "attn":
         print(json.dumps(op_attn(a)))

@@ -563,3 +563,102 @@ def test_w8a16_equals_bf16_gemm_on_dequantized_weight(epi, m, n, k):
         ops.gemm(ops.gemm_desc(kind, e, m, k, segs, **extra))
         outs.append(out.cpu())
     assert torch.equal(outs[0], outs[1])
+
+
+# ----------------------------------------------------------------------------- split-K
+
+@pytest.mark.parametrize("m,n,k,splits", [(50, 720, 2048, 0), (50, 960, 768, 3), (177, 320, 1024, 4), (7, 64, 384, 2)])
+def test_split_k_i8_is_bit_exact(m, n, k, splits):
+    """int32 partial sums are exact: split-K int8 GEMMs equal the single-pass kernel bit for bit, and the
+    workspace counters are back at zero after every launch."""
+    g = synthetic.generator(m * 3 + n + k + splits)
+    a, w = _rand_i8((m, k), g).to(DEV), _rand_i8((n, k), g).to(DEV)
+    ws = ops.splitk_workspace(8 << 20, DEV)
+    outs = []
+    for sk, wsp in ((1, None), (splits, ws)):
+        acc = torch.empty(m, n, dtype=torch.int32, device=DEV)
+        extra = dict(split_k=sk) if wsp is None else dict(split_k=sk, workspace=wsp, workspace_bytes=wsp.numel())
+        ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_I32, m, k, [ops.Seg(a=a, b=w, out=acc, n=n)], **extra))
+        outs.append(acc.cpu())
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(outs[0], Q.int_gemm(a.cpu(), w.cpu()))
+    assert int(ws[:L.SPLITK_COUNTER_BYTES].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("kind,epi,m,n,k", [(L.KIND_W8A16, "resid", 50, 720, 2048), (L.KIND_BF16, "silu_mul", 50, 2048, 720),
+                                            (L.KIND_BF16, "rope", 50, 960, 720), (L.KIND_BF16, "resid", 100, 720, 960),
+                                            (L.KIND_I8, "gelu_quant", 64, 1024, 2048)])
+def test_split_k_epilogues_match_single_pass(kind, epi, m, n, k):
+    """Split-K sums the fp32 partials in another order than one K loop: the bf16 outputs agree with the
+    single-pass kernel to bf16 rounding (bounded by |y| where a residual or a rotation cancels); int8
+    accumulators are exact, so I8 results agree bit for bit."""
+    g = synthetic.generator(m + n + k + kind)
+    if kind == L.KIND_I8:
+        x = _rand_i8((m, k), g).to(DEV)
+    else:
+        x = torch.randn(m, k, generator=g).to(DEV, torch.bfloat16)
+    wts = []
+    for _ in range(2 if epi == "silu_mul" else 1):
+        w = (torch.randn(n, k, generator=g) * 0.02).to(DEV, torch.bfloat16)
+        wts.append((w, None) if kind == L.KIND_BF16 else ops.pack_weight_i8(w))
+    res = torch.randn(m, n, generator=g).to(DEV, torch.bfloat16)
+    pos = (177 + torch.arange(m) % 50).to(DEV, torch.int32)
+    cs = ops.rope_table(256, 10000.0, DEV)
+    smooth = (torch.rand(n, generator=g) + 0.5).to(DEV)
+    ws = ops.splitk_workspace(16 << 20, DEV)
+    e = {"resid": L.EPI_RESID, "silu_mul": L.EPI_SILU_MUL, "rope": L.EPI_ROPE, "gelu_quant": L.EPI_GELU_QUANT}[epi]
+    outs = []
+    for split in (1, 0):
+        out = res.clone()
+        qout = torch.zeros(m, n, dtype=torch.int8, device=DEV)
+        segs = [ops.Seg(a=x, b=b, out=None if epi == "gelu_quant" else out, n=n, wscale=sc, act_scale=0.02,
+                        rope=1 if epi == "rope" else 0) for b, sc in wts]
+        extra = {"resid": dict(resid=out, ldr=n), "silu_mul": dict(pair=True),
+                 "rope": dict(rope_cs=cs, pos=pos, max_pos=256),
+                 "gelu_quant": dict(q_smooth=smooth, q_rsmooth=ops.reciprocal(smooth), q_act=0.05, qout=qout, ldq=n)}[epi]
+        ops.gemm(ops.gemm_desc(kind, e, m, k, segs, split_k=split, workspace=ws, workspace_bytes=ws.numel(), **extra))
+        outs.append((out.cpu(), qout.cpu()))
+    assert int(ws[:L.SPLITK_COUNTER_BYTES].count_nonzero()) == 0
+    a0, a1 = outs[0][0].float(), outs[1][0].float()
+    if kind == L.KIND_I8:
+        assert torch.equal(outs[0][1], outs[1][1])
+    elif epi == "resid":
+        # a one-ulp flip of bf16(y) survives cancellation against the residual: bound it by |y|
+        r = res.cpu().float()
+        tol = ((a0 - r).abs() + a0.abs()) * 2.0 ** -7 + 1e-5 * float(a0.abs().max())
+        assert bool(((a1 - a0).abs() <= tol).all()), float(((a1 - a0).abs() > tol).float().mean())
+    elif epi == "rope":
+        # x1 cos - x2 sin cancels: bound the difference by the (rotation-invariant) norm of each pair
+        a0v, a1v = a0.view(m, n // 64, 2, 32), a1.view(m, n // 64, 2, 32)
+        pn = (a0v[:, :, 0] ** 2 + a0v[:, :, 1] ** 2).sqrt().unsqueeze(2)
+        tol = pn * 2.0 ** -7 + 1e-5 * float(a0.abs().max())
+        assert bool(((a1v - a0v).abs() <= tol).all()), float(((a1v - a0v).abs() > tol).float().mean())
+    else:
+        ok, frac = bf16_ulp_close(outs[1][0], outs[0][0], ulps=2.0, atol=1e-5)
+        assert ok, frac
+
+
+@pytest.mark.parametrize("two_sources", [True, False])
+def test_structured_mask_equals_byte_mask(two_sources):
+    """Key padding over the prefix keys plus causal order over the chunk keys, given as one row of key flags
+    per sample, gives the same bits as the equivalent [B, Lq, Lk] byte mask (the action expert's masks)."""
+    g = synthetic.generator(77 + int(two_sources))
+    b, lq, l1, hq, hkv = 3, 50, 177, 15, 5
+    l2 = lq if two_sources else 0
+    q = torch.randn(b, lq, hq * 64, generator=g).to(DEV, torch.bfloat16)
+    k1 = torch.randn(b, l1, hkv * 64, generator=g).to(DEV, torch.bfloat16)
+    v1 = torch.randn(b, l1, hkv * 64, generator=g).to(DEV, torch.bfloat16)
+    k2 = torch.randn(b, max(l2, 1), hkv * 64, generator=g).to(DEV, torch.bfloat16)[:, :l2]
+    v2 = torch.randn(b, max(l2, 1), hkv * 64, generator=g).to(DEV, torch.bfloat16)[:, :l2]
+    pad = torch.rand(b, l1, generator=g) > 0.25
+    pad[:, -1] = True
+    full = torch.zeros(b, lq, l1 + l2, dtype=torch.bool)
+    full[:, :, :l1] = pad[:, None, :]
+    if two_sources:
+        full[:, :, l1:] = torch.tril(torch.ones(lq, l2, dtype=torch.bool))
+    srcs = dict(k2=k2, v2=v2) if two_sources else {}
+    o_byte = ops.attention(q, k1, v1, hq, hkv, mask=full.to(DEV), **srcs)
+    key_rows = torch.zeros(b, 192, dtype=torch.uint8)
+    key_rows[:, :l1] = pad.to(torch.uint8)
+    o_key = ops.attention(q, k1, v1, hq, hkv, key_mask=key_rows.to(DEV)[:, :l1], mask_keys=l1, **srcs)
+    assert torch.equal(o_byte.cpu(), o_key.cpu())

@@ -62,16 +62,22 @@ def test_tiny_sample_actions_matches_oracle(tiny):
     assert L.device_error() == 0
 
 
-def test_batch_rows_are_independent(tiny):
+@pytest.mark.parametrize("split_k", [False, True])
+def test_batch_rows_are_independent(tiny, split_k):
+    """Without split-K each batch row is bit-identical at any batch size; with it (the default) the small-M
+    GEMMs of a single row sum their fp32 partials in another order, so rows agree within the tolerance."""
     w, js = tiny
-    sa = SampleActions(TINY, DeviceWeights(TINY, w, load_scale_json(js)))
+    sa = SampleActions(TINY, DeviceWeights(TINY, w, load_scale_json(js)), split_k=split_k)
     o = _obs(TINY, 3, 21)
     full = _run(sa, o)
     for i in range(3):
         one = synthetic.Observation(images=[im[i:i + 1] for im in o.images], img_masks=[m[i:i + 1] for m in o.img_masks],
                                     lang_tokens=o.lang_tokens[i:i + 1], lang_masks=o.lang_masks[i:i + 1],
                                     state=o.state[i:i + 1], noise=o.noise[i:i + 1])
-        assert torch.equal(_run(sa, one), full[i:i + 1])
+        if split_k:
+            _close(_run(sa, one), full[i:i + 1], cos=0.9999, max_abs=2e-2)
+        else:
+            assert torch.equal(_run(sa, one), full[i:i + 1])
 
 
 def test_graph_replay_equals_direct_launches(tiny):
