@@ -38,22 +38,16 @@ struct NormQuantArgs {
   int ps_grid;             // tokens per side of the input grid (32)
 };
 
+// one row m, its bf16 input already in registers (raw[i] = columns (i*32 + lane)*8 .. +7)
 template <int NV, bool LAYERNORM>
-__global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) {
-  pdl_wait();
-  pdl_trigger();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= a.M) return;
-  const int m = warp;
-  const __nv_bfloat16* xr = a.x + static_cast<size_t>(m) * a.ldx;
+__device__ __forceinline__ void norm_quant_row(const NormQuantArgs& a, int m, int lane, const int4 (&raw_in)[NV]) {
   float v[NV][8];
   float ss = 0.f, sum = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int k = (i * 32 + lane) * 8;
     if (k < a.K) {
-      const int4 raw = *reinterpret_cast<const int4*>(xr + k);
+      const int4 raw = raw_in[i];
       const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -157,6 +151,34 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) 
       }
       *reinterpret_cast<int2*>(a.q[qi] + static_cast<size_t>(qrow) * a.ldq + col) = make_int2(w[0], w[1]);
     }
+  }
+}
+
+// Warps stream rows (grid-stride); the next row's input is requested before the current row is processed,
+// so each warp keeps two rows of loads in flight.
+template <int NV, bool LAYERNORM>
+__global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int warp0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  auto load_row = [&](int m, int4 (&r)[NV]) {
+    const __nv_bfloat16* xr = a.x + static_cast<size_t>(m) * a.ldx;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int k = (i * 32 + lane) * 8;
+      r[i] = (k < a.K) ? *reinterpret_cast<const int4*>(xr + k) : make_int4(0, 0, 0, 0);
+    }
+  };
+  int4 next[NV];
+  if (warp0 < a.M) load_row(warp0, next);
+  for (int m = warp0; m < a.M; m += nwarps) {
+    int4 cur[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) cur[i] = next[i];
+    if (m + nwarps < a.M) load_row(m + nwarps, next);
+    norm_quant_row<NV, LAYERNORM>(a, m, lane, cur);
   }
 }
 

@@ -202,7 +202,10 @@ int sm_count() {
   return counts[dev];
 }
 
-// Widest tile that still gives every SM at least one tile (pairs: at most 128 so two buffers fit TMEM).
+// Tile width.  A k-stage costs about the same time at 64, 128 and 256 columns (measured), so a GEMM takes
+// about (rounds of tiles over the SMs) x (k-stages): take the width with the fewest rounds, the wider one on
+// a tie (pairs: at most 128 so two accumulator buffers fit TMEM).  When even 64-column tiles leave half of
+// the SMs idle, take 64 columns: split-K (which runs on 64-column tiles) then spreads K over the rest.
 int choose_block_n(const svla_gemm_desc* d, int sms) {
   const int m_tiles = (d->m + 127) / 128;
   auto tiles = [&](int bn) {
@@ -211,9 +214,14 @@ int choose_block_n(const svla_gemm_desc* d, int sms) {
     for (int s = 0; s < d->nseg; ++s) t += (d->seg[s].n + bn - 1) / bn;
     return m_tiles * t;
   };
-  if (!d->pair && tiles(256) >= sms) return 256;
-  if (tiles(128) >= sms) return 128;
-  return 64;
+  if (tiles(64) * 2 <= sms) return 64;
+  auto rounds = [&](int bn) { return (tiles(bn) + sms - 1) / sms; };
+  int best = 64;
+  for (int bn : {128, 256}) {
+    if (d->pair && bn > 128) continue;
+    if (rounds(bn) <= rounds(best)) best = bn;
+  }
+  return best;
 }
 
 }  // namespace
@@ -497,7 +505,10 @@ int32_t svla_norm_quant(const svla_norm_desc* d, svla_stream_t stream) {
   a.pixel_shuffle = d->pixel_shuffle;
   a.ps_grid = d->ps_grid;
   const int nv = (d->k + 255) / 256;
-  const unsigned blocks = static_cast<unsigned>((d->m + 7) / 8);
+  // 8 rows per 256-thread block at most; at most 8 blocks per SM resident at once, each warp then
+  // streams several rows
+  const long long max_blocks = static_cast<long long>(sm_count()) * 8;
+  const unsigned blocks = static_cast<unsigned>(((d->m + 7) / 8) < max_blocks ? (d->m + 7) / 8 : max_blocks);
   cudaStream_t st = cs(stream);
 #define SVLA_NORM(NV)                                                                                     \
   if (nv <= NV) {                                                                                         \
