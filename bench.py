@@ -291,8 +291,10 @@ def main():
     p50 = lat[len(lat) // 2]
     p95 = lat[min(len(lat) - 1, int(round(0.95 * (len(lat) - 1))))]
 
-    # ---------------- roofline of the dominant kernel, timed live (same launch as in the graph)
-    roof = dominant_kernel_roofline(runner, peaks)
+    # ---------------- roofline of the dominant kernel (the SigLIP attention: the largest share of the batch-64
+    # launch list) and of the largest GEMM, each timed live on its own with the step's own arguments
+    roof = attention_roofline(runner, peaks)
+    roof_gemm = dominant_kernel_roofline(runner, peaks)
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -306,6 +308,7 @@ def main():
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "roofline": roof,
+        "roofline_gemm": roof_gemm,
         "clocks": clk,
     }
     if rank == 0 and not args.no_cpu_baseline:
@@ -330,8 +333,48 @@ def measure_int8_peak(dev) -> float | None:
         return None
 
 
+def profile_traffic(name: str) -> float | None:
+    """DRAM bytes per full-size launch from a committed ncu summary (profiles/<name>.md, line
+    `traffic_bytes_per_launch: N`), or None when that summary is absent."""
+    f = REPO / "profiles" / f"{name}.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip())
+    return None
+
+
+def attention_roofline(runner, peaks):
+    """The largest attention launch of the step (SigLIP self-attention, tcgen05 kernel) timed on its own with
+    CUDA events.  Algorithmic work: 4 * B * Hq * Lq * Lk * 64 flops (Q.K^T and P.V)."""
+    from smolvla_mujoco_libero_b200 import _lib as L
+    best = None
+    for fn, a in runner.launches:
+        if fn is L.lib().svla_attention:
+            d = a[0]
+            lk = d.l1 + max(d.l2, 0)
+            flops = 4.0 * d.batch * d.hq * d.lq * lk * 64
+            if best is None or flops > best[0]:
+                best = (flops, d)
+    flops, d = best
+    stream = torch.cuda.current_stream().cuda_stream
+    import ctypes
+    fn = L.lib().svla_attention
+    ms = time_kernel(lambda: fn(ctypes.byref(d), stream), iters=20)
+    achieved = flops / (ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    src = "MEASURED_PEAKS.json bf16_tflops (burst: the kernel is timed alone)" if "bf16_tflops" in peaks \
+        else "fallback 1.59 PFLOP/s"
+    traffic = profile_traffic("attention_tc_siglip_b128")
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": traffic, "kernel": f"attention_tc B={d.batch} Hq={d.hq} Lq={d.lq} Lk={d.l1} d=64",
+            "ms_per_launch": ms, "flops_per_launch": flops, "peak_source": src}
+
+
 def dominant_kernel_roofline(runner, peaks):
-    """Time the largest W8A8 GEMM launch of the step (SigLIP fc1 / fc2 class) on its own with CUDA events."""
+    """The largest W8A8 GEMM launch of the step (SigLIP fc1, GELU + int8 quant epilogue) timed on its own with
+    CUDA events.  Algorithmic work: 2 * M * N * K int8 ops."""
     from smolvla_mujoco_libero_b200 import _lib as L
     best = None
     for fn, a in runner.launches:
@@ -358,7 +401,8 @@ def dominant_kernel_roofline(runner, peaks):
     else:
         peak, src = bf16, "MEASURED_PEAKS.json bf16_tflops (burst)"
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": None, "kernel": f"gemm_sm100 kind={'i8' if int8 else d.kind} M={d.m} N={sum(d.seg[i].n for i in range(d.nseg))} K={d.k}",
+            "traffic": profile_traffic("gemm_i8_gelu_quant_fc1_b64"),
+            "kernel": f"gemm_sm100 kind={'i8' if int8 else d.kind} M={d.m} N={sum(d.seg[i].n for i in range(d.nseg))} K={d.k}",
             "ms_per_launch": ms, "peak_source": src}
 
 

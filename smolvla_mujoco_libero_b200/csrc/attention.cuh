@@ -127,7 +127,12 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st
       const int kend = a.mask_keys < Lk ? a.mask_keys : Lk;
       const uint8_t* src = a.key_mask + static_cast<size_t>(b) * a.key_mask_bs;
       uint8_t* dst = &sm.m[st][c];
-      if (key + 16 <= kend && ((reinterpret_cast<uintptr_t>(src + key) & 15) == 0)) {
+      // a whole aligned 16-key run is one async copy when it lies inside the flags or inside the row's storage
+      // (row stride covering the flags rounded up to 16); runs past the flags are zero-filled
+      const bool padded = a.key_mask_bs >= ((kend + 15) & ~15);
+      if (key >= kend) {
+        cp_async16(dst, src, 0);
+      } else if ((key + 16 <= kend || padded) && ((reinterpret_cast<uintptr_t>(src + key) & 15) == 0)) {
         cp_async16(dst, src + key, 16);
       } else {
         for (int j = 0; j < 16; ++j) dst[j] = (key + j < kend) ? src[key + j] : 0;

@@ -373,7 +373,9 @@ extern "C" {
 
 const char* svla_last_error(void) { return t_last_error.c_str(); }
 
-const char* svla_version(void) { return "svla 0.1 sm_100a (tcgen05 kind::i8 / kind::f16, TMA, mma.sync attention)"; }
+const char* svla_version(void) {
+  return "svla 0.2 sm_100a (tcgen05 kind::i8 / kind::f16 GEMMs with split-K, tcgen05 + mma.sync attention, TMA)";
+}
 
 int32_t svla_device_error(int32_t* code, int32_t reset) {
   int* p = device_error_ptr();
