@@ -9,9 +9,9 @@
 // Persistent: one CTA per SM walks output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... in N-fastest
 // order (the CTAs running at one time share A row-blocks; the weights stay L2-resident).  Accumulators
 // are double-buffered in TMEM (2 x P x BN columns) so the epilogue of one tile overlaps the MMAs of the next.
-// Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma (one lane), warps 2-9 run the
-// epilogue (two warps per TMEM lane quarter 32*(warp%4) .. +31, each on half the tile's columns), and for
-// W8A16 warps 10-13 convert the int8 weight stages to bf16.  Tile: 128 rows (M) x BN columns (N) x 128
+// Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma (one lane), the next 8 or 16 warps
+// run the epilogue (two or four per TMEM lane quarter 32*(warp%4) .. +31, each on its share of the tile's
+// columns; see epi_warps), and for W8A16 the last 4 warps convert the int8 weight stages to bf16.  Tile: 128 rows (M) x BN columns (N) x 128
 // bytes of K per pipeline stage.
 //
 // "Segments" let one launch cover several linears that share M and K but have their own A operand,
@@ -129,10 +129,15 @@ struct GemmSmem {
   static_assert(kBytes <= 232448, "dynamic shared memory above the 227 KB per-CTA limit");
 };
 
-constexpr int kEpiWarps = 8;  // epilogue warps 2..9: two per TMEM lane quarter, each on half the columns
+// Epilogue warps: 16 (four per TMEM lane quarter, each on a quarter of the tile's columns) for the GELU +
+// SmoothQuant epilogue, whose long per-element arithmetic chain needs the extra warps to hide its latency
+// (measured 884 -> 638 us on the SigLIP fc1); 8 (two per lane quarter, half the columns each) for the
+// others, which are bound by their row-wise stores and gain nothing from more warps but register pressure.
+template <Kind KIND, int P, Epi EPI>
+__host__ __device__ constexpr int epi_warps() { return (EPI == Epi::GeluQuant && P == 1 && !KindTraits<KIND>::kConvert) ? 16 : 8; }
 
-template <Kind KIND>
-constexpr int gemm_threads() { return 32 * (2 + kEpiWarps + (KindTraits<KIND>::kConvert ? 4 : 0)); }
+template <Kind KIND, int P, Epi EPI>
+__host__ __device__ constexpr int gemm_threads() { return 32 * (2 + epi_warps<KIND, P, EPI>() + (KindTraits<KIND>::kConvert ? 4 : 0)); }
 
 // SiLU x * sigmoid(x) and tanh-GELU 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi)(x + 0.044715 x^3),
 // both evaluated as x / (1 + 2^(-z log2 e)) with the hardware 2^x and reciprocal approximations: the results
@@ -174,11 +179,11 @@ __device__ __forceinline__ void k_range(const GemmArgs& a, int t, int k_tiles, i
 }
 
 // Epilogue of one output tile for the calling warp's 32 TMEM lanes (rows row = 32*(warp%4) + lane) and
-// its half of the columns (two warps share each lane quarter).  `ok` is warp-uniform; when false the
+// its share of the columns (kEpiParts warps share each lane quarter).  `ok` is warp-uniform; when false the
 // TMEM loads are skipped and nothing is written.
-template <Kind KIND, int BN, int P, Epi EPI, typename WaitAcc>
+template <Kind KIND, int BN, int P, Epi EPI, int kEpiParts, typename WaitAcc>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int m0, int n0, uint32_t t_row,
-                                              int row, int half, bool ok_in, const float* consts, WaitAcc&& wait_acc) {
+                                              int row, int part, bool ok_in, const float* consts, WaitAcc&& wait_acc) {
   const GemmSeg& sg = args.seg[si];
   const int m = m0 + row;
   bool ok = ok_in;
@@ -236,7 +241,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
     row_ok = ok && (m < args.M);
     // one 64-column head at a time (the two warps of a lane quarter take alternate heads), rotated in two
     // blocks of 16 pairs (columns j..j+15 with j+32..j+47) to bound register use
-    for (int c = half * 64; c < BN; c += 128) {
+    for (int c = part * 64; c < BN; c += 64 * kEpiParts) {  // kEpiParts warps take alternate heads
       const int nb = n0 + c;
       const bool do_head = row_ok && nb < sg.n;
       int p = 0;
@@ -280,12 +285,12 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
       }
     }
   } else {
-    constexpr int kHalf = BN / 2;
-    constexpr int kChunk = kHalf >= 32 ? 32 : 16;  // columns per TMEM round trip
-    constexpr int kNC = kHalf / kChunk;            // chunks per warp and tile
+    constexpr int kPart = BN / kEpiParts;          // columns of this warp
+    constexpr int kChunk = kPart >= 32 ? 32 : 16;  // columns per TMEM round trip
+    constexpr int kNC = kPart / kChunk;            // chunks per warp and tile
     constexpr int kRes = (EPI == Epi::Resid) ? kChunk / 8 : 1;
     const float ra = (EPI == Epi::GeluQuant && args.qout) ? __frcp_rn(args.q_act) : 0.0f;
-    const int c0 = half * kHalf;
+    const int c0 = part * kPart;
     const int rrow = (EPI == Epi::Resid && args.resid_rows > 0) ? (m % args.resid_rows) : orow;
     // residual rows do not depend on the accumulator: fetch them ahead of it
     auto load_res = [&](int4 (&res)[kRes], int cb) {
@@ -425,14 +430,14 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
   return ok;
 }
 
-// Split-K step of one output tile, run by all epilogue warps (each on its TMEM lane quarter and half of
+// Split-K step of one output tile, run by all epilogue warps (each on its TMEM lane quarter and share of
 // the columns): store this split's raw accumulators; count the arrival; the tile's last split adds all
 // partials in split order (int32 exactly, fp32 in a fixed order) into its own accumulator.  Returns
 // whether this CTA runs the tile's epilogue.
-template <Kind KIND, int BN, int P, typename WaitAcc>
-__device__ __forceinline__ bool splitk_reduce(const GemmArgs& args, int t, int m0, int row, int half, int etid,
+template <Kind KIND, int BN, int P, int kEpiParts, typename WaitAcc>
+__device__ __forceinline__ bool splitk_reduce(const GemmArgs& args, int t, int m0, int row, int part, int etid,
                                               uint32_t t_row, bool ok, volatile int* split_last, WaitAcc&& wait_acc) {
-  constexpr int kEpiThreads = 32 * kEpiWarps;
+  constexpr int kEpiThreads = 32 * 4 * kEpiParts;
   const int tile = t / args.splits, sp = t % args.splits;
   const bool aok = ok && wait_acc();
   const bool row_in = m0 + row < args.M;
@@ -440,7 +445,7 @@ __device__ __forceinline__ bool splitk_reduce(const GemmArgs& args, int t, int m
 #pragma unroll
   for (int p = 0; p < P; ++p) {
 #pragma unroll
-    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
+    for (int c = part * (BN / kEpiParts); c < (part + 1) * (BN / kEpiParts); c += 16) {
       uint32_t r[16];
       if (aok) {
         tmem_ld16(t_row + p * BN + c, r);
@@ -471,7 +476,7 @@ __device__ __forceinline__ bool splitk_reduce(const GemmArgs& args, int t, int m
 #pragma unroll
   for (int p = 0; p < P; ++p) {
 #pragma unroll
-    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
+    for (int c = part * (BN / kEpiParts); c < (part + 1) * (BN / kEpiParts); c += 16) {
       uint32_t acc[16];
 #pragma unroll
       for (int u = 0; u < 16; ++u) acc[u] = 0u;
@@ -525,7 +530,8 @@ __device__ __forceinline__ bool splitk_reduce(const GemmArgs& args, int t, int m
 }
 
 template <Kind KIND, int BN, int P, int STAGES, Epi EPI>
-__global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(const __grid_constant__ GemmArgs args) {
+__global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_kernel(const __grid_constant__ GemmArgs args) {
+  constexpr int kEpiWarps = epi_warps<KIND, P, EPI>();
   using T = KindTraits<KIND>;
   using S = GemmSmem<KIND, BN, P, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -683,7 +689,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
     // ---------------- epilogue warps 2..9
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
-    const int half = (warp - 2) / 4;
+    const int part = (warp - 2) / 4;  // which share of the tile's columns (kEpiWarps / 4 shares)
     const int etid = threadIdx.x - 64;  // 0 .. 32*kEpiWarps-1
     float* const_base = reinterpret_cast<float*>(smem + S::kConstOff);
     uint32_t lt = 0;
@@ -727,9 +733,9 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1) gemm_sm100_kernel(con
       const uint32_t t_row = tmem_base + ab * S::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
       bool run_epi = true;
       if constexpr (BN == 64) {  // split-K is compiled for the narrow tile only (the one few-tile GEMMs use)
-        if (args.splits > 1) run_epi = splitk_reduce<KIND, BN, P>(args, t, m0, row, half, etid, t_row, ok, split_last, wait_acc);
+        if (args.splits > 1) run_epi = splitk_reduce<KIND, BN, P, kEpiWarps / 4>(args, t, m0, row, part, etid, t_row, ok, split_last, wait_acc);
       }
-      const bool ok_t = run_epi ? epilogue_tile<KIND, BN, P, EPI>(args, si, m0, n0, t_row, row, half, ok, cst, wait_acc)
+      const bool ok_t = run_epi ? epilogue_tile<KIND, BN, P, EPI, kEpiWarps / 4>(args, si, m0, n0, t_row, row, part, ok, cst, wait_acc)
                                 : (ok && acc_ok);
       if (lt == 0 && etid == 0) stamp(args.dbg, 8);
       tc_fence_before();

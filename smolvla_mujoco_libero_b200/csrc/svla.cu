@@ -147,7 +147,7 @@ int32_t launch_gemm_inst(const GemmArgs& args, dim3 grid, cudaStream_t stream) {
     if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  return launch(kern, grid, dim3(gemm_threads<K>()), S::kBytes, stream, "gemm_sm100_kernel", args);
+  return launch(kern, grid, dim3(gemm_threads<K, P, E>()), S::kBytes, stream, "gemm_sm100_kernel", args);
 }
 
 template <Kind K, int BN, int P>
