@@ -135,7 +135,7 @@ class SmolVLARunner:
     SPLITK_BYTES = 32 << 20  # split-K workspace shared by the runner's GEMMs (stream-ordered)
 
     def __init__(self, weights: DeviceWeights, batch: int, mode: str = "quant", debug_taps: bool = False,
-                 split_k: bool = True):
+                 split_k: bool = True, prefix_only: bool = False):
         if weights.cfg.expert_layers != weights.cfg.text_layers:
             raise ValueError("the expert must have one layer per text layer (each expert layer reads that layer's KV)")
         if mode == "quant" and not weights.quantized:
@@ -145,6 +145,9 @@ class SmolVLARunner:
                 if p.weight_bf16 is None:
                     raise ValueError("bf16 mode needs DeviceWeights(..., keep_bf16=True)")
         self.w, self.cfg, self.B, self.mode, self.debug = weights, weights.cfg, batch, mode, debug_taps
+        # prefix_only: stop after the prefix prefill, with the final-layer prefix hidden states in prefix_out
+        # (the RL-token features, smollvla_rltoken/rlt/rl_token.py:50-88) and the KV cache filled
+        self.prefix_only = prefix_only
         # split-K changes the fp32 summation order of the small-M bf16 GEMMs with the batch size; without it
         # every batch row's result is bit-identical at any batch size
         self.split_k = split_k
@@ -216,7 +219,7 @@ class SmolVLARunner:
         self.ev = z(B * S, c.kv_dim)
         self.ectx = z(B * S, c.q_dim)
         self.emlp = z(B * S, c.expert_mlp)
-        if self.debug:
+        if self.debug or self.prefix_only:
             self.prefix_out = z(B * Lp, H)
 
     def _constants(self):
@@ -401,7 +404,7 @@ class SmolVLARunner:
                        [self._linear_seg(m, a, o, rope=r) for m, a, o, r in zip(mods, a_in, outs, (1, 1, 0))],
                        rope_cs=self.rope_cs, pos=self.prefix_pos, max_pos=self.max_pos)
             last = i == c.text_layers - 1
-            if last and not self.debug and self.mode == "quant":
+            if last and not (self.debug or self.prefix_only) and self.mode == "quant":
                 break
             self._attn(self.t_q, self.kcache[i], self.vcache[i], Lp, c.heads, c.kv_heads, mask=self.prefix_mask,
                        out_mod=f"{p}.self_attn.o_proj", out=self.t_ctx, tap=[f"{p}.self_attn.o_proj"])
@@ -415,9 +418,12 @@ class SmolVLARunner:
                        [self._linear_seg(m, a, self.t_mlp) for m, a in zip(mods, a_in)], pair=True)
             self._gemm(self._kind(f"{p}.mlp.down_proj", B * Lp), L.EPI_RESID, B * Lp, c.mlp,
                        [self._linear_seg(f"{p}.mlp.down_proj", self.t_mlp, self.h)], resid=self.h, ldr=H)
-        if self.debug:
+        if self.debug or self.prefix_only:
             self._norm(self.h, w.t[f"{TEXT}.norm.weight"], c.rms_eps, y=self.prefix_out)
-            self._tap(["prefix_out"], self.prefix_out)
+            if self.debug:
+                self._tap(["prefix_out"], self.prefix_out)
+        if self.prefix_only:
+            return
         # ---------------- cross-attention K/V of the cached prefix (step-invariant)
         for i in self.ck:
             p = f"{EXPERT}.layers.{i}.self_attn"
@@ -509,7 +515,8 @@ class SmolVLARunner:
         if st.shape[1] != c.max_state_dim:
             st = torch.nn.functional.pad(st, (0, c.max_state_dim - st.shape[1]))
         self.in_state.copy_(st, non_blocking=True)
-        self.in_noise.copy_(noise.reshape(B, c.chunk, c.max_action_dim), non_blocking=True)
+        if noise is not None:  # the prefix-only runner has no flow loop
+            self.in_noise.copy_(noise.reshape(B, c.chunk, c.max_action_dim), non_blocking=True)
 
     def run(self, observer=None):
         """Launch the call on the current stream (graph replay when captured).  ``observer(mods, buf)`` is

@@ -59,6 +59,47 @@ class SampleActions:
         return out[:, :, : self.action_dim].clone()
 
 
+class PrefixFeatures:
+    """The RL-token consumer's features: the prefix prefill of ``sample_actions`` alone, keeping the
+    final-layer prefix hidden states (``RLTokenExtractor.extract``, smollvla_rltoken/rlt/rl_token.py:50-88).
+
+    ``extract`` returns ``z`` fp32 [B, Lp, hidden] (the final RMSNorm of the last text layer's output, as the
+    reference's ``outputs_embeds[0]``), ``pad_mask`` bool [B, Lp], ``n_img_tokens`` and ``kv_cache``: per text
+    layer the (K post-RoPE, V) bf16 tensors [B, Lp, kv_heads * 64] that the action expert reads.  The same
+    quantized kernels as ``SampleActions``; one CUDA graph per batch size."""
+
+    def __init__(self, cfg: SmolVLAConfig, weights: DeviceWeights, use_cuda_graph: bool = True):
+        if not weights.quantized:
+            raise ValueError("PrefixFeatures needs weights packed with a scale table")
+        self.cfg, self.weights, self.use_cuda_graph = cfg, weights, use_cuda_graph
+        self.runners: dict[int, SmolVLARunner] = {}
+
+    def runner(self, batch: int) -> SmolVLARunner:
+        r = self.runners.get(batch)
+        if r is None:
+            r = SmolVLARunner(self.weights, batch, prefix_only=True)
+            if self.use_cuda_graph:
+                r.capture()
+            self.runners[batch] = r
+        return r
+
+    @torch.no_grad()
+    def extract(self, images, img_masks, lang_tokens, lang_masks, state) -> dict[str, Any]:
+        c = self.cfg
+        B = state.shape[0]
+        r = self.runner(B)
+        r.load_inputs(images, img_masks, lang_tokens, lang_masks, state, None)
+        r.run()
+        Lp = c.prefix_len
+        return {
+            "z": r.prefix_out.view(B, Lp, c.hidden).float(),
+            "pad_mask": r.key_pad.bool().clone(),
+            "n_img_tokens": c.n_cams * c.n_img_tokens,
+            "kv_cache": [(r.kcache[i].view(B, Lp, -1).clone(), r.vcache[i].view(B, Lp, -1).clone())
+                         for i in range(c.text_layers)],
+        }
+
+
 def install_sample_actions(policy: Any, sample_actions: SampleActions) -> dict[str, Any]:
     """Replace ``policy.model.sample_actions`` (the reference installs its TensorRT runner the same way,
     deploy/trt_sample_actions_core_deploy.py:310)."""

@@ -114,3 +114,33 @@ def test_bench_architecture_batch1_matches_oracle():
     ref = OracleSmolVLA(BENCH, w, Q.load_activation_scales_by_module(js)).sample_actions(
         o.images, o.img_masks, o.lang_tokens, o.lang_masks, o.state, o.noise)[:, :, :BENCH.action_dim]
     _close(got, ref)
+
+
+def test_prefix_features_match_oracle(tiny):
+    """The RL-token features (prefix prefill only): final-layer prefix hidden states and the KV cache against
+    the oracle's prefix forward; the padding mask and image-token count as the reference extractor's."""
+    from smolvla_mujoco_libero_b200.policy import PrefixFeatures
+    w, js = tiny
+    pf = PrefixFeatures(TINY, DeviceWeights(TINY, w, load_scale_json(js)))
+    o = _obs(TINY, 2, 11, n_valid_tokens=9)
+    dev = "cuda"
+    feats = pf.extract([im.to(dev) for im in o.images], [m.to(dev) for m in o.img_masks], o.lang_tokens.to(dev),
+                       o.lang_masks.to(dev), o.state.to(dev))
+    taps = {}
+    OracleSmolVLA(TINY, w, Q.load_activation_scales_by_module(js)).sample_actions(
+        o.images, o.img_masks, o.lang_tokens, o.lang_masks, o.state, o.noise, taps=taps)
+    ref = taps["prefix_out"].float()
+    z = feats["z"].cpu()
+    assert z.shape == ref.shape
+    # relative bar: the prefix hidden states are O(1) after the final RMSNorm
+    c = float(F.cosine_similarity(z.flatten(), ref.flatten(), dim=0))
+    assert c >= 0.999, c
+    assert float((z - ref).abs().max()) <= 2e-2 * float(ref.abs().max()) + 2e-2
+    for (k, v), (rk, rv) in zip(feats["kv_cache"], taps["kv"]):
+        for got, want in ((k, rk), (v, rv)):
+            g, r = got.cpu().float().flatten(), want.float().reshape(got.shape).flatten()
+            assert float(F.cosine_similarity(g, r, dim=0)) >= 0.999
+    n_img = TINY.n_cams * TINY.n_img_tokens
+    assert feats["n_img_tokens"] == n_img
+    pad = feats["pad_mask"].cpu()
+    assert bool(pad[:, n_img + 9:n_img + TINY.n_lang].sum() == 0) and bool(pad[:, -1].all())
