@@ -239,6 +239,26 @@ int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* po
 /* -------------------------------------------------------------------------------------------------
  * sample_actions glue
  * ------------------------------------------------------------------------------------------------*/
+/* Policy-side processing around sample_actions (lerobot SmolVLA prepare_images / prepare_state and the
+ * action unnormalisation of predict_action_chunk; called at
+ * deploy/calibrate_smolvla_activation_channel_scales.py:138-139).
+ * Images: src fp32 [N, C, H, W] in [0, 1], or (src_u8_hwc) uint8 [N, H, W, C] read as value / 255; resized
+ * keeping the aspect ratio to (int(h / r), int(w / r)), r = max(w / out_w, h / out_h), by bilinear
+ * interpolation with half-pixel source indices (torch interpolate, align_corners=False), padded with
+ * pad_value on the top and left to out_h x out_w, then mapped to [-1, 1] (x * 2 - 1).  Output image i at
+ * out + i * out_image_stride (fp32 [C, out_h, out_w]). */
+int32_t svla_resize_pad_images(const void* src, int32_t src_u8_hwc, int32_t n, int32_t c, int32_t h, int32_t w,
+                               float* out, int64_t out_image_stride, int32_t out_h, int32_t out_w, float pad_value,
+                               svla_stream_t stream);
+/* state [B, dim] (row stride ld) -> [B, out_dim], zero-padded; mode 0 MEAN_STD (x - p0) / (p1 + 1e-8),
+ * mode 1 MIN_MAX ((x - p0) / (p1 - p0 + 1e-8)) * 2 - 1 (p0 = min, p1 = max). */
+int32_t svla_normalize_state(const float* state, int32_t batch, int32_t dim, int32_t ld, const float* p0,
+                             const float* p1, int32_t mode, int32_t out_dim, float* out, svla_stream_t stream);
+/* actions [rows, ld] -> [rows, action_dim]: mode 0 x * p1 + p0 (p0 = mean, p1 = std); mode 1
+ * (x + 1) / 2 * (p1 - p0) + p0 (p0 = min, p1 = max). */
+int32_t svla_unnormalize_actions(const float* actions, int32_t rows, int32_t ld, int32_t action_dim, const float* p0,
+                                 const float* p1, int32_t mode, float* out, svla_stream_t stream);
+
 /* cs[p][i] = (cos, sin)(p / max_wavelength^(2i/64)), p < max_pos, i < 32 */
 int32_t svla_rope_table(float* cs, int32_t max_pos, float max_wavelength, svla_stream_t stream);
 

@@ -86,6 +86,12 @@ SIGNATURES = {
     "svla_attention": (c_int32, [POINTER(AttnDesc), c_void_p]),
     "svla_rope_layout": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                    c_int32, c_float, c_void_p]),
+    "svla_resize_pad_images": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64,
+                                         c_int32, c_int32, c_float, c_void_p]),
+    "svla_normalize_state": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,
+                                       c_void_p, c_void_p]),
+    "svla_unnormalize_actions": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_void_p,
+                                           c_void_p]),
     "svla_rope_table": (c_int32, [c_void_p, c_int32, c_float, c_void_p]),
     "svla_build_masks": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p,
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),

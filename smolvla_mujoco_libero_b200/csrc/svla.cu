@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -19,6 +20,7 @@
 #include "gemm.cuh"
 #include "misc.cuh"
 #include "norm.cuh"
+#include "process.cuh"
 
 namespace svla {
 
@@ -667,6 +669,52 @@ int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* po
                 static_cast<const __nv_bfloat16*>(q_raw), static_cast<const __nv_bfloat16*>(k_raw), pos,
       static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out), batch, seq_len, q_heads, kv_heads,
       max_wavelength);
+}
+
+int32_t svla_resize_pad_images(const void* src, int32_t src_u8_hwc, int32_t n, int32_t c, int32_t h, int32_t w,
+                               float* out, int64_t out_image_stride, int32_t out_h, int32_t out_w, float pad_value,
+                               svla_stream_t stream) {
+  if (!src || !out || n <= 0 || c <= 0 || h <= 0 || w <= 0 || out_h <= 0 || out_w <= 0 ||
+      out_image_stride < static_cast<int64_t>(c) * out_h * out_w)
+    return fail(SVLA_ERR_ARG, "svla_resize_pad_images: bad args");
+  ResizeArgs a;
+  a.src = src;
+  a.u8_hwc = src_u8_hwc ? 1 : 0;
+  a.N = n;
+  a.C = c;
+  a.H = h;
+  a.W = w;
+  // the aspect-preserving size, in double precision like the Python reference (int() truncation)
+  const double ratio = std::max(static_cast<double>(w) / out_w, static_cast<double>(h) / out_h);
+  a.rh = static_cast<int>(h / ratio);
+  a.rw = static_cast<int>(w / ratio);
+  if (a.rh <= 0 || a.rw <= 0 || a.rh > out_h || a.rw > out_w) return fail(SVLA_ERR_ARG, "svla_resize_pad_images: degenerate size");
+  a.OH = out_h;
+  a.OW = out_w;
+  a.pad_value = pad_value;
+  a.out = out;
+  a.out_stride = out_image_stride;
+  const long long total = static_cast<long long>(n) * c * out_h * out_w;
+  return launch(resize_pad_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, cs(stream),
+                "resize_pad_kernel", a);
+}
+
+int32_t svla_normalize_state(const float* state, int32_t batch, int32_t dim, int32_t ld, const float* p0,
+                             const float* p1, int32_t mode, int32_t out_dim, float* out, svla_stream_t stream) {
+  if (!state || !p0 || !p1 || !out || batch <= 0 || dim <= 0 || ld < dim || out_dim < dim || (mode != 0 && mode != 1))
+    return fail(SVLA_ERR_ARG, "svla_normalize_state: bad args");
+  const int total = batch * out_dim;
+  return launch(normalize_state_kernel, dim3((total + 255) / 256), dim3(256), 0, cs(stream), "normalize_state_kernel",
+                state, batch, dim, ld, p0, p1, mode, out_dim, out);
+}
+
+int32_t svla_unnormalize_actions(const float* actions, int32_t rows, int32_t ld, int32_t action_dim, const float* p0,
+                                 const float* p1, int32_t mode, float* out, svla_stream_t stream) {
+  if (!actions || !p0 || !p1 || !out || rows <= 0 || action_dim <= 0 || ld < action_dim || (mode != 0 && mode != 1))
+    return fail(SVLA_ERR_ARG, "svla_unnormalize_actions: bad args");
+  const int total = rows * action_dim;
+  return launch(unnormalize_actions_kernel, dim3((total + 255) / 256), dim3(256), 0, cs(stream),
+                "unnormalize_actions_kernel", actions, rows, ld, action_dim, p0, p1, mode, out);
 }
 
 int32_t svla_rope_table(float* c, int32_t max_pos, float max_wavelength, svla_stream_t stream) {
