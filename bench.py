@@ -27,6 +27,7 @@ from datetime import timedelta
 from pathlib import Path
 
 import torch
+import torch.distributed as dist
 
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
@@ -55,6 +56,41 @@ def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return rank, world, local
+
+
+PG_TIMEOUT_S = 120  # ranks that wait for a missing peer end with an error instead of hanging
+
+
+def init_ranks(world: int, backend: str, device=None) -> None:
+    """One process per GPU (nccl) or per CPU rank (gloo, tests); rendezvous from the torchrun environment."""
+    if world > 1:
+        kw = {"device_id": device} if device is not None else {}
+        dist.init_process_group(backend, timeout=timedelta(seconds=PG_TIMEOUT_S), **kw)
+
+
+def max_over_ranks(value: float, world: int, device="cpu") -> float:
+    """The slowest rank's time: every rank takes this step (same collective, same order) after its timed
+    region."""
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def whole_job_rate(units_per_rank: int, world: int, steps: int, ms: float) -> float:
+    """Units per second of the whole job: every rank's units over the slowest rank's time."""
+    return units_per_rank * world * steps / (ms / 1e3)
+
+
+def arm_config(cfg, batch: int, world: int) -> dict:
+    """The `config` of the bench line, shared by both arms."""
+    return {"workload": f"sample_actions bs{batch} per GPU: SigLIP {cfg.vis_layers}x{cfg.vis_hidden} on "
+                        f"{batch * cfg.n_cams} images {cfg.image_size}px + connector, text {cfg.text_layers}x"
+                        f"{cfg.hidden} (L={cfg.prefix_len}), expert {cfg.expert_layers}x{cfg.expert_hidden} x "
+                        f"{cfg.num_steps} flow steps",
+            "global_batch": batch * world, "seq_len": cfg.prefix_len, "parallelism": f"dp{world} (replicas, no collectives)",
+            "l2": "inputs+activations > L2 (no flush needed)", "cuda_graph": True}
 
 
 class ClockSampler:
@@ -160,8 +196,7 @@ def run_reference(args, rank, world):
             "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8/bf16", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": "sample_actions, SmolVLA SigLIP-12x768 + text 16x960 + expert 16x720, "
-                                   "10 flow steps; each step one batch-1 observation on the host cores"},
+            "config": arm_config(cfg, args.batch, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                              "sample": "one batch-1 observation per step (bounded sample of the bs64 workload)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -185,8 +220,6 @@ def time_kernel(fn, iters=20, warm=3):
 def main():
     args = parse()
     rank, world, local = dist_env()
-    if world > 1:
-        import torch.distributed as dist
     if args.impl == "reference":
         return run_reference(args, rank, world)
 
@@ -198,8 +231,7 @@ def main():
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    init_ranks(world, "nccl", dev)
     cfg = BENCH
     B = args.batch
     peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
@@ -232,14 +264,10 @@ def main():
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world, dev)
     assert torch.isfinite(runner.actions()).all(), "non-finite actions"
     assert L.device_error() == 0, "device error word set"
-    value = B * world * args.steps / (ms / 1e3)
+    value = whole_job_rate(B, world, args.steps, ms)
     launches = runner.n_launches * args.steps
 
     # ---------------- end to end through the public call with host (pinned) buffers
@@ -265,12 +293,8 @@ def main():
         e2e_step()
     e1.record()
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = B * world * args.steps / (e2e_ms / 1e3)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    e2e_value = whole_job_rate(B, world, args.steps, e2e_ms)
 
     # ---------------- batch-1 latency (p50 over individually timed calls)
     r1 = SmolVLARunner(weights, 1)
@@ -300,10 +324,7 @@ def main():
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8/bf16", "data": "synthetic (seeded observations, random-init weights, GPU-calibrated SmoothQuant scales)",
-        "config": {"workload": f"sample_actions bs{B} per GPU: SigLIP 12x768 on {B * cfg.n_cams} images 512px + connector, "
-                               f"text 16x960 (L=177), expert 16x720 x 10 flow steps",
-                   "global_batch": B * world, "seq_len": cfg.prefix_len, "parallelism": f"dp{world} (replicas, no collectives)",
-                   "l2": "inputs+activations > L2 (no flush needed)", "cuda_graph": True},
+        "config": arm_config(cfg, B, world),
         "batch1_p50_ms": p50, "batch1_p95_ms": p95,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,

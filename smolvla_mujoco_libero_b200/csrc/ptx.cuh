@@ -1,4 +1,4 @@
-// Inline-PTX helpers for sm_100a: mbarriers, TMA (cp.async.bulk.tensor, no multicast),
+// Inline-PTX helpers for sm_100a: mbarriers, TMA (cp.async.bulk.tensor into this CTA's shared memory),
 // tcgen05 (TMEM alloc, MMA, commit, ld) and shared-memory matrix descriptors.
 //
 // Every wait on an mbarrier is bounded: after kSpinLimit polls it records an error

@@ -1,0 +1,55 @@
+"""The multi-rank path of bench.py on CPU: two gloo ranks (torchrun-style environment, 127.0.0.1) take the
+same collective steps; the slowest rank's time and the whole-job rate come out the same on every rank; the
+reference arm runs on rank 0 only."""
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import torch.multiprocessing as mp
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank: int, world: int, port: int, q) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    sys.path.insert(0, str(REPO))
+    import bench
+    import torch.distributed as dist
+    r, w, _ = bench.dist_env()
+    bench.init_ranks(w, "gloo")
+    ms = bench.max_over_ranks(10.0 + 5.0 * r, w)   # rank 1 is the slow one
+    rate = bench.whole_job_rate(64, w, 10, ms)
+    dist.barrier()
+    dist.destroy_process_group()
+    q.put((r, ms, rate))
+
+
+def test_two_gloo_ranks_agree_on_slowest_time_and_rate():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert [o[1] for o in out] == [15.0, 15.0]
+    assert all(abs(o[2] - 64 * 2 * 10 / 0.015) < 1e-6 for o in out)
+
+
+def test_reference_arm_runs_on_rank_zero_only(capsys):
+    sys.path.insert(0, str(REPO))
+    import bench
+    assert bench.run_reference(None, 1, 2) == 0
+    assert capsys.readouterr().out == ""
