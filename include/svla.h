@@ -286,6 +286,67 @@ int32_t svla_f32_to_bf16(const float* x, void* y, int64_t n, svla_stream_t strea
 int32_t svla_reciprocal(const float* x, float* y, int64_t n, svla_stream_t stream);
 int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n, svla_stream_t stream);
 
+/* -------------------------------------------------------------------------------------------------
+ * Whole-path engine: the quantized sample_actions call in native code.  Replaces the TensorRT core
+ * runner's engine load + execute (deploy/trt_sample_actions_core_deploy.py:108-237, called per chunk from
+ * deploy/eval_libero_trt_sample_actions_core.py) with one C call over the kernels above: masks, SigLIP,
+ * connector, the prefix prefill into the KV cache, the cross-layer K/V projections and the flow-matching
+ * loop of the action expert.
+ * The engine loads a packed-weights file (safetensors, metadata "svla_packed" = "1", "config" and
+ * "linears" JSON; tensors "lin/<module>/{weight,wscale,bias,smooth,rsmooth,weight_deq}" and "t/<name>",
+ * including "t/time_embedding" bf16 [num_steps, expert_hidden]), the file the Python package's save_packed
+ * writes.  It owns its device memory (weights, activation buffers for max_batch samples, a split-K
+ * workspace) and one launch list per batch size, recorded as a CUDA graph after its first run.
+ * ------------------------------------------------------------------------------------------------*/
+typedef struct svla_engine svla_engine;
+
+typedef struct svla_engine_info {
+  int32_t n_cams, channels, image_size;          /* images: n_cams x fp32 [B, channels, image_size, image_size] */
+  int32_t n_lang;                                /* language tokens per sample */
+  int32_t max_state_dim, max_action_dim, chunk, num_steps, action_dim;
+  int32_t prefix_len;
+  int32_t vis_layers, text_layers, expert_layers;
+  int32_t n_linears;                             /* linears in the file */
+  int32_t n_tensors;                             /* tensors in the file */
+  int32_t launches_per_call;                     /* kernel launches of one sample_actions call (0 = not built) */
+  int32_t max_batch;                             /* 0 for svla_engine_inspect */
+  int64_t weight_bytes;                          /* device bytes of the weights */
+  int64_t buffer_bytes;                          /* device bytes of activations, workspace and constants */
+} svla_engine_info;
+
+#define SVLA_ENGINE_NO_GRAPH 1    /* launch the kernels one by one on every call (no CUDA graph) */
+#define SVLA_ENGINE_NO_SPLIT_K 2  /* no split-K: every sample's result is bit-identical at any batch size */
+
+/* Parses and validates a packed-weights file without touching the GPU (info->max_batch = 0,
+ * launches_per_call = 0, buffer_bytes = 0). */
+int32_t svla_engine_inspect(const char* packed_path, svla_engine_info* info);
+/* Loads the file onto the current device and computes the call's constants on `stream` (synchronised
+ * before returning).  max_batch >= 1; flags: SVLA_ENGINE_* bits. */
+int32_t svla_engine_create(const char* packed_path, int32_t max_batch, int32_t flags, svla_stream_t stream,
+                           svla_engine** out);
+int32_t svla_engine_get_info(const svla_engine* engine, svla_engine_info* info);
+/* sample_actions(images, img_masks, lang_tokens, lang_masks, state, noise) for `batch` samples
+ * (lerobot VLAFlowMatching.sample_actions; the reference's core engine inputs,
+ * deploy/trt_sample_actions_core_deploy.py:240-299):
+ *   images[cam]    fp32 [batch, channels, image_size, image_size], cam < n_cams (already resized to the
+ *                  model's size and mapped to [-1, 1]: svla_resize_pad_images)
+ *   img_masks[cam] uint8 [batch] (0 = camera missing)
+ *   lang_tokens    int64 [batch, lang_len], lang_masks uint8 [batch, lang_len]; the first n_lang tokens are
+ *                  used, shorter rows are padded with masked-out zeros (match_static_shape,
+ *                  deploy/trt_sample_actions_core_deploy.py:276-286)
+ *   state          fp32 [batch, state_dim], state_dim <= max_state_dim (zero-padded)
+ *   noise          fp32 [batch, chunk, max_action_dim]
+ *   actions        fp32 [batch, chunk, max_action_dim] (out)
+ * Every array may be host memory (pageable or pinned) or device memory; copies are stream-ordered on
+ * `stream`, as are the kernels.  Calls share the engine's buffers: issue them on one stream, or
+ * synchronise between calls on different streams. */
+int32_t svla_engine_sample_actions(svla_engine* engine, const float* const* images, const uint8_t* const* img_masks,
+                                   const int64_t* lang_tokens, const uint8_t* lang_masks, int32_t lang_len,
+                                   const float* state, int32_t state_dim, const float* noise, int32_t batch,
+                                   float* actions, svla_stream_t stream);
+/* Frees the engine's device memory and graphs (synchronises the device first).  NULL is a no-op. */
+int32_t svla_engine_destroy(svla_engine* engine);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,6 +64,18 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+class EngineInfo(ctypes.Structure):
+    _fields_ = [
+        ("n_cams", c_int32), ("channels", c_int32), ("image_size", c_int32), ("n_lang", c_int32),
+        ("max_state_dim", c_int32), ("max_action_dim", c_int32), ("chunk", c_int32), ("num_steps", c_int32),
+        ("action_dim", c_int32), ("prefix_len", c_int32), ("vis_layers", c_int32), ("text_layers", c_int32),
+        ("expert_layers", c_int32), ("n_linears", c_int32), ("n_tensors", c_int32), ("launches_per_call", c_int32),
+        ("max_batch", c_int32), ("weight_bytes", c_int64), ("buffer_bytes", c_int64),
+    ]
+
+
+ENGINE_NO_GRAPH, ENGINE_NO_SPLIT_K = 1, 2  # SVLA_ENGINE_* flags
+
 # name -> (restype, argtypes) for every symbol in include/svla.h
 SIGNATURES = {
     "svla_last_error": (c_char_p, []),
@@ -101,6 +113,12 @@ SIGNATURES = {
     "svla_f32_to_bf16": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
     "svla_euler_init": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "svla_reciprocal": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "svla_engine_inspect": (c_int32, [c_char_p, POINTER(EngineInfo)]),
+    "svla_engine_create": (c_int32, [c_char_p, c_int32, c_int32, c_void_p, POINTER(c_void_p)]),
+    "svla_engine_get_info": (c_int32, [c_void_p, POINTER(EngineInfo)]),
+    "svla_engine_sample_actions": (c_int32, [c_void_p, POINTER(c_void_p), POINTER(c_void_p), c_void_p, c_void_p,
+                                             c_int32, c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_void_p]),
+    "svla_engine_destroy": (c_int32, [c_void_p]),
 }
 
 

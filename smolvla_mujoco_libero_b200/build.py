@@ -27,27 +27,48 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+BUILD = PKG / "_build"
+HEADER = PKG.parent / "include" / "svla.h"
+FLAGS = [*ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC"]
+
+
+def units() -> list[tuple[Path, list[Path]]]:
+    """(source, the files its object depends on) for every translation unit of the library."""
+    kernels = [CSRC / "svla.cu", *sorted(CSRC.glob("*.cuh")), HEADER]
+    return [(CSRC / "svla.cu", kernels), (CSRC / "engine.cpp", [CSRC / "engine.cpp", HEADER])]
+
+
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [PKG.parent / "include" / "svla.h"]
+    return sorted({p for _, deps in units() for p in deps})
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in deps)
 
 
 def up_to_date() -> bool:
-    if not OUT.exists():
-        return False
-    t = OUT.stat().st_mtime
-    return all(p.stat().st_mtime <= t for p in sources())
+    return not _stale(OUT, sources())
 
 
 def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Path:
     if not force and not debug and up_to_date():
         return OUT
-    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           "-o", str(OUT), str(CSRC / "svla.cu")]
-    if debug:
-        cmd.insert(1, "-DSVLA_BOUNDS_CHECK")
-    if verbose:
-        cmd.append("-Xptxas=-v")
-    subprocess.run(cmd, check=True)
+    BUILD.mkdir(exist_ok=True)
+    objs = []
+    for src, deps in units():
+        obj = BUILD / (src.stem + (".debug.o" if debug else ".o"))
+        if force or debug or _stale(obj, deps):
+            cmd = [nvcc(), *FLAGS, "-c", "-o", str(obj), str(src)]
+            if debug:
+                cmd.insert(1, "-DSVLA_BOUNDS_CHECK")
+            if verbose:
+                cmd.append("-Xptxas=-v")
+            subprocess.run(cmd, check=True)
+        objs.append(str(obj))
+    subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(OUT), *objs], check=True)
     return OUT
 
 

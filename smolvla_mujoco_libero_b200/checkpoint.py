@@ -22,7 +22,7 @@ from pathlib import Path
 import torch
 
 from .config import BENCH, CONNECTOR, EXPERT, TEXT, VISION, SmolVLAConfig
-from .model import DeviceWeights, PackedLinear
+from .model import DeviceWeights, PackedLinear, time_embedding_bf16
 from .weights import linear_specs, other_specs
 
 
@@ -136,7 +136,10 @@ def save_packed(weights: DeviceWeights, path: str | Path) -> None:
             if t is not None:
                 tensors[f"lin/{name}/{f}"] = t.detach().cpu().contiguous()
     for key, t in weights.t.items():
-        tensors[f"t/{key}"] = t.detach().cpu().contiguous()
+        # a copy: some tensors are views of others (patch_w2d reshapes the patch-embedding weight)
+        tensors[f"t/{key}"] = t.detach().cpu().contiguous().clone()
+    # derived constant the native engine reads instead of recomputing it (float64 on the host)
+    tensors["t/time_embedding"] = time_embedding_bf16(weights.cfg).contiguous()
     save_file(tensors, str(path), metadata={"svla_packed": "1", "config": meta["config"],
                                             "linears": json.dumps(meta["linears"])})
 
@@ -161,7 +164,7 @@ def load_packed(path: str | Path, device="cuda") -> DeviceWeights:
                                    get("smooth"), get("rsmooth"), float(m["act_scale"]),
                                    weight_bf16=get("weight") if m["kind"] == "bf16" else None,
                                    weight_deq=get("weight_deq"))
-    w.t = {k[2:]: v.to(dev) for k, v in tensors.items() if k.startswith("t/")}
+    w.t = {k[2:]: v.to(dev) for k, v in tensors.items() if k.startswith("t/") and k != "t/time_embedding"}
     w.quantized = any(p.kind == "w8a8" for p in w.lin.values())
     torch.cuda.synchronize(dev)
     return w

@@ -228,6 +228,12 @@ int choose_block_n(const svla_gemm_desc* d, int sms) {
 
 }  // namespace
 
+// the last-error message of the calling thread, for the library's other translation units (engine.cpp)
+int32_t set_error(int32_t code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
 int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   if (!d) return fail(SVLA_ERR_ARG, "null gemm descriptor");
   if (d->kind < 0 || d->kind > 2) return fail(SVLA_ERR_ARG, "bad operand kind %d", d->kind);
