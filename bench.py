@@ -270,19 +270,26 @@ def main():
     value = whole_job_rate(B, world, args.steps, ms)
     launches = runner.n_launches * args.steps
 
-    # ---------------- end to end through the public call with host (pinned) buffers
+    # ---------------- end to end through the C ABI (svla_engine_sample_actions on the packed weights) with host
+    # (pinned) buffers: every step copies its observations in and its actions out inside the timed region
+    import tempfile
+
+    from smolvla_mujoco_libero_b200.checkpoint import save_packed
+    from smolvla_mujoco_libero_b200.engine import NativeSampleActions
+    with tempfile.TemporaryDirectory() as tmp:
+        packed = Path(tmp) / f"packed_rank{rank}.safetensors"
+        save_packed(weights, packed)
+        engine = NativeSampleActions(packed, max_batch=B, device=dev)
     host = ([im.pin_memory() for im in obs.images], [m.pin_memory() for m in obs.img_masks],
             obs.lang_tokens.pin_memory(), obs.lang_masks.pin_memory(), obs.state.pin_memory(), obs.noise.pin_memory())
-    out_host = torch.empty(B, cfg.chunk, cfg.action_dim, dtype=torch.float32).pin_memory()
+    out_host = torch.empty(B, cfg.chunk, cfg.max_action_dim, dtype=torch.float32).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in (*host[0], *host[1], *host[2:]))
     d2h = out_host.numel() * out_host.element_size()
 
     def e2e_step():
-        runner.load_inputs(*host)
-        runner.run()
-        out_host.copy_(runner.actions()[:, :, :cfg.action_dim], non_blocking=True)
+        engine.sample_actions(*host, out=out_host)
 
-    for _ in range(2):
+    for _ in range(max(2, args.warmup)):
         e2e_step()
     torch.cuda.synchronize()
     if world > 1:
@@ -295,10 +302,27 @@ def main():
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
     e2e_value = whole_job_rate(B, world, args.steps, e2e_ms)
+    assert torch.equal(out_host, runner.actions().cpu()), "engine and runner disagree"
 
-    # ---------------- batch-1 latency (p50 over individually timed calls)
-    r1 = SmolVLARunner(weights, 1)
+    # batch-1 end to end through the same call (one observation in from pinned host memory, its chunk out)
     o1 = make_observations(cfg, 1, 2_000_000 + rank)
+    host1 = ([im.pin_memory() for im in o1.images], [m.pin_memory() for m in o1.img_masks],
+             o1.lang_tokens.pin_memory(), o1.lang_masks.pin_memory(), o1.state.pin_memory(), o1.noise.pin_memory())
+    out1 = torch.empty(1, cfg.chunk, cfg.max_action_dim, dtype=torch.float32).pin_memory()
+    lat_e2e = []
+    for i in range(args.b1_iters + 5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        engine.sample_actions(*host1, out=out1)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 5:
+            lat_e2e.append(a.elapsed_time(b))
+    lat_e2e.sort()
+    engine.close()
+
+    # ---------------- batch-1 latency (p50 over individually timed calls, inputs resident)
+    r1 = SmolVLARunner(weights, 1)
     r1.load_inputs([im.to(dev) for im in o1.images], [m.to(dev) for m in o1.img_masks], o1.lang_tokens.to(dev),
                    o1.lang_masks.to(dev), o1.state.to(dev), o1.noise.to(dev))
     r1.capture()
@@ -325,8 +349,9 @@ def main():
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8/bf16", "data": "synthetic (seeded observations, random-init weights, GPU-calibrated SmoothQuant scales)",
         "config": arm_config(cfg, B, world),
-        "batch1_p50_ms": p50, "batch1_p95_ms": p95,
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "batch1_p50_ms": p50, "batch1_p95_ms": p95, "batch1_e2e_p50_ms": lat_e2e[len(lat_e2e) // 2],
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "call": "svla_engine_sample_actions (C ABI, pinned host buffers)"},
         "gpu_launches": launches,
         "roofline": roof,
         "roofline_gemm": roof_gemm,

@@ -287,6 +287,67 @@ int32_t svla_reciprocal(const float* x, float* y, int64_t n, svla_stream_t strea
 int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n, svla_stream_t stream);
 
 /* -------------------------------------------------------------------------------------------------
+ * Flow-matching loop as one persistent kernel, for calls with batch * chunk <= 64 action rows (batch-1
+ * latency).  Runs x_t = noise, then num_steps x [action_in_proj, time MLP, every expert layer, final
+ * RMSNorm, action_out_proj, x_t += dt * v] (lerobot VLAFlowMatching.sample_actions / denoise_step) in one
+ * cooperative launch (one CTA per SM, grid barriers between phases, every wait bounded).  Same arithmetic
+ * and rounding points as the per-layer launches (svla_gemm / svla_norm_quant / svla_attention with the
+ * structured expert masks); only the fp32 summation order inside dot products differs.  Expert linears
+ * are bf16 weights (the W8A16 linears' bf16(q * w_s) weights).  No counterpart launch in the reference,
+ * whose TensorRT engine runs the loop as separate layers (deploy/trt_sample_actions_core_deploy.py:108-237).
+ * ------------------------------------------------------------------------------------------------*/
+#define SVLA_FLOW_MAX_LAYERS 32
+#define SVLA_FLOW_MAX_ROWS 64
+
+typedef struct svla_flow_layer {
+  const void* input_norm;  /* bf16 [E] */
+  const void* post_norm;   /* bf16 [E] */
+  const void* wq;          /* bf16 [heads * 64, E] */
+  const void* wk;          /* bf16 [kv_heads * 64, E] (self-attention layers; NULL on cross-attention layers) */
+  const void* wv;
+  const void* wo;          /* bf16 [E, heads * 64] */
+  const void* wg;          /* bf16 [mlp, E] */
+  const void* wu;          /* bf16 [mlp, E] */
+  const void* wd;          /* bf16 [E, mlp] */
+  const void* keys;        /* bf16 [batch * prefix_len, kv_heads * 64]: the layer's prefix KV cache (self) or */
+  const void* values;      /*   its cross-attention K/V projections (cross) */
+  int32_t cross;
+} svla_flow_layer;
+
+typedef struct svla_flow_desc {
+  int32_t batch, chunk, prefix_len;
+  int32_t hidden;          /* E (multiple of 16, <= 1024) */
+  int32_t action_dim;      /* the padded action width A (multiple of 16) */
+  int32_t heads, kv_heads, mlp, n_layers, num_steps;
+  float eps;               /* RMSNorm epsilon */
+  const float* noise;      /* fp32 [batch * chunk, A] */
+  float* xt;               /* fp32 [batch * chunk, A]: the actions on return */
+  void* xt_bf16;           /* bf16 [batch * chunk, A] scratch */
+  const void* w_action_in; const void* b_action_in;       /* bf16 [E, A], [E] */
+  const void* w_time_in; int32_t ld_time_in;              /* bf16 [E, >= E]: the first E columns are used */
+  const float* time_in_const;                             /* fp32 [num_steps, E]: W[:, E:] . time_emb(t_k) + b */
+  const void* w_time_out; const void* b_time_out;         /* bf16 [E, E], [E] */
+  const void* final_norm;                                 /* bf16 [E] */
+  const void* w_action_out; const void* b_action_out;     /* bf16 [A, E], [A] */
+  const uint8_t* key_mask; int64_t key_mask_bs;           /* prefix key flags of sample b at key_mask + b * bs
+                                                             (16-byte aligned rows of >= prefix_len rounded up to
+                                                             16 bytes), or NULL */
+  const int32_t* suffix_pos; const int32_t* cross_pos;    /* [batch * chunk] RoPE positions */
+  const float* rope_cs; int32_t max_pos;                  /* svla_rope_table */
+  /* scratch (bf16): a_emb, a_t, eh [rows, E]; eq, ectx [rows, heads * 64]; ek, ev [rows, kv_heads * 64];
+   * emlp [rows, mlp] */
+  void* a_emb; void* a_t; void* eh; void* eq; void* ek; void* ev; void* ectx; void* emlp;
+  uint32_t* sync;          /* 8 bytes (8-byte aligned), zero before the first launch; every completed launch leaves
+                              it valid.  After a device error (svla_device_error) zero it again. */
+  uint64_t* debug_clock;   /* profiling, or NULL: 2 x 1024 (event, globaltimer ns) pairs of the first and last CTA
+                              (events 1/2 barrier enter/exit, 3 rows staged, 4 products done, 5 epilogue done,
+                              6 attention task done) */
+  svla_flow_layer layer[SVLA_FLOW_MAX_LAYERS];
+} svla_flow_desc;
+
+int32_t svla_flow(const svla_flow_desc* desc, svla_stream_t stream);
+
+/* -------------------------------------------------------------------------------------------------
  * Whole-path engine: the quantized sample_actions call in native code.  Replaces the TensorRT core
  * runner's engine load + execute (deploy/trt_sample_actions_core_deploy.py:108-237, called per chunk from
  * deploy/eval_libero_trt_sample_actions_core.py) with one C call over the kernels above: masks, SigLIP,
@@ -316,6 +377,7 @@ typedef struct svla_engine_info {
 
 #define SVLA_ENGINE_NO_GRAPH 1    /* launch the kernels one by one on every call (no CUDA graph) */
 #define SVLA_ENGINE_NO_SPLIT_K 2  /* no split-K: every sample's result is bit-identical at any batch size */
+#define SVLA_ENGINE_NO_FLOW 4     /* run the flow loop as per-layer launches even when svla_flow applies */
 
 /* Parses and validates a packed-weights file without touching the GPU (info->max_batch = 0,
  * launches_per_call = 0, buffer_bytes = 0). */

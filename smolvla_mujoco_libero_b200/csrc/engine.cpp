@@ -582,6 +582,7 @@ struct Buffers {
   // constants
   void* splitk_ws;
   size_t splitk_bytes;
+  uint32_t* flow_sync;  // grid-barrier words of the persistent flow kernel
   float* rope_cs;
   float* c_step;
 };
@@ -820,6 +821,7 @@ uint64_t layout_buffers(const Cfg& c, int B, char* base, Buffers* b) {
   b->emlp = take(B * S * c.expert_mlp * 2);
   b->splitk_bytes = kSplitKBytes;
   b->splitk_ws = take(kSplitKBytes);
+  b->flow_sync = reinterpret_cast<uint32_t*>(take(8));
   const int max_pos = c.prefix_len() + c.chunk;
   b->rope_cs = reinterpret_cast<float*>(take(static_cast<uint64_t>(max_pos) * 32 * 2 * 4));
   b->c_step = reinterpret_cast<float*>(take(static_cast<uint64_t>(c.num_steps) * E * 4));
@@ -1001,6 +1003,10 @@ class Builder {
     }
     // ---------------- flow matching
     const int MS = B * S, A = c.max_action_dim;
+    if (use_flow()) {
+      flow(MS);
+      return;
+    }
     {
       const int64_t n = static_cast<int64_t>(MS) * A;
       const float* noise = b.in_noise;
@@ -1099,6 +1105,91 @@ class Builder {
   std::vector<Launch>* out_;
 
   static svla_stream_t st(cudaStream_t s) { return reinterpret_cast<svla_stream_t>(s); }
+
+  // the persistent flow kernel applies: few action rows and bf16 / W8A16 expert linears
+  bool use_flow() const {
+    if ((e_.flags & SVLA_ENGINE_NO_FLOW) || B_ * c_.chunk > SVLA_FLOW_MAX_ROWS || c_.expert_layers > SVLA_FLOW_MAX_LAYERS)
+      return false;
+    if (c_.expert_hidden % 16 || c_.expert_hidden > 1024 || c_.max_action_dim % 16 || c_.expert_mlp % 16) return false;
+    const std::string ep = std::string(kExpert) + ".";
+    for (const auto& kv : e_.lin)
+      if (kv.first.compare(0, ep.size(), ep) == 0 && kv.second.kind == "w8a8") return false;
+    return true;
+  }
+
+  const void* bf16_weight(const std::string& name) const {
+    const Lin& p = e_.lin.at(name);
+    return p.kind == "w8a16" ? p.weight_deq : p.weight;
+  }
+
+  void flow(int MS) {
+    const Cfg& c = c_;
+    const Buffers& b = b_;
+    svla_flow_desc d;
+    std::memset(&d, 0, sizeof(d));
+    d.batch = B_;
+    d.chunk = c.chunk;
+    d.prefix_len = c.prefix_len();
+    d.hidden = c.expert_hidden;
+    d.action_dim = c.max_action_dim;
+    d.heads = c.heads;
+    d.kv_heads = c.kv_heads;
+    d.mlp = c.expert_mlp;
+    d.n_layers = c.expert_layers;
+    d.num_steps = c.num_steps;
+    d.eps = static_cast<float>(c.rms_eps);
+    d.noise = b.in_noise;
+    d.xt = b.xt;
+    d.xt_bf16 = b.xt_bf;
+    d.w_action_in = bf16_weight("model.action_in_proj");
+    d.b_action_in = e_.lin.at("model.action_in_proj").bias;
+    d.w_time_in = e_.lin.at("model.action_time_mlp_in").weight;
+    d.ld_time_in = 2 * c.expert_hidden;
+    d.time_in_const = b.c_step;
+    d.w_time_out = bf16_weight("model.action_time_mlp_out");
+    d.b_time_out = e_.lin.at("model.action_time_mlp_out").bias;
+    d.final_norm = tensor(std::string(kExpert) + ".norm.weight");
+    d.w_action_out = bf16_weight("model.action_out_proj");
+    d.b_action_out = e_.lin.at("model.action_out_proj").bias;
+    d.key_mask = b.cross_mask;
+    d.key_mask_bs = static_cast<int64_t>(c.chunk) * ld16(c.prefix_len());
+    d.suffix_pos = b.suffix_pos;
+    d.cross_pos = b.cross_pos;
+    d.rope_cs = b.rope_cs;
+    d.max_pos = c.prefix_len() + c.chunk;
+    d.a_emb = b.a_emb;
+    d.a_t = b.a_t;
+    d.eh = b.eh;
+    d.eq = b.eq;
+    d.ek = b.ek;
+    d.ev = b.ev;
+    d.ectx = b.ectx;
+    d.emlp = b.emlp;
+    d.sync = b.flow_sync;
+    for (int i = 0; i < c.expert_layers; ++i) {
+      const std::string p = std::string(kExpert) + ".layers." + std::to_string(i);
+      svla_flow_layer& l = d.layer[i];
+      l.input_norm = tensor(p + ".input_layernorm.weight");
+      l.post_norm = tensor(p + ".post_attention_layernorm.weight");
+      l.wq = bf16_weight(p + ".self_attn.q_proj");
+      l.wo = bf16_weight(p + ".self_attn.o_proj");
+      l.wg = bf16_weight(p + ".mlp.gate_proj");
+      l.wu = bf16_weight(p + ".mlp.up_proj");
+      l.wd = bf16_weight(p + ".mlp.down_proj");
+      l.cross = c.is_cross(i) ? 1 : 0;
+      if (l.cross) {
+        l.keys = b.ck[i];
+        l.values = b.cv[i];
+      } else {
+        l.wk = bf16_weight(p + ".self_attn.k_proj");
+        l.wv = bf16_weight(p + ".self_attn.v_proj");
+        l.keys = b.kcache[i];
+        l.values = b.vcache[i];
+      }
+    }
+    (void)MS;
+    add([d](cudaStream_t s) { return svla_flow(&d, st(s)); });
+  }
   void add(Launch f) { out_->push_back(std::move(f)); }
 
   const void* tensor(const std::string& name) const {
@@ -1409,7 +1500,7 @@ int32_t svla_engine_create(const char* packed_path, int32_t max_batch, int32_t f
   if (!out) return set_error(SVLA_ERR_ARG, "svla_engine_create: null out");
   *out = nullptr;
   if (max_batch < 1 || max_batch > 4096) return set_error(SVLA_ERR_ARG, "svla_engine_create: max_batch must be 1..4096");
-  if (flags & ~(SVLA_ENGINE_NO_GRAPH | SVLA_ENGINE_NO_SPLIT_K))
+  if (flags & ~(SVLA_ENGINE_NO_GRAPH | SVLA_ENGINE_NO_SPLIT_K | SVLA_ENGINE_NO_FLOW))
     return set_error(SVLA_ERR_ARG, fmt("svla_engine_create: unknown flags 0x%x", flags));
   std::unique_ptr<svla_engine, void (*)(svla_engine*)> e(new svla_engine(), release);
   std::string err;

@@ -1,0 +1,913 @@
+// The action expert's flow-matching loop as ONE persistent kernel, for calls with at most 64 action rows
+// (batch x chunk; batch 1 at chunk 50).  lerobot VLAFlowMatching.sample_actions / denoise_step:
+//   x_t = noise;  for step: v = expert(x_t, t_step, prefix KV);  x_t += dt * v      (dt = -1 / num_steps)
+// with, per step, action_in_proj, the time MLP (SiLU), 16 expert layers (RMSNorm, q/k/v + RoPE, attention
+// over the cached prefix K/V [+ the chunk's own K/V on self-attention layers], o_proj + residual, RMSNorm,
+// SiLU-gated MLP, down_proj + residual), the final RMSNorm and action_out_proj.
+//
+// At these sizes every launch of the per-layer kernels is latency-bound (a few CTAs, short K loops); here
+// the ~84 phases of one step run back to back inside one cooperative grid (one CTA per SM), separated by
+// grid barriers, so a phase costs a barrier instead of a kernel launch with its prologue and drain.
+//
+// Phases are GEMMs of the rows against 16-column slices of a weight (tasks spread over the CTAs; the 8 warps
+// of a CTA split K and add their partial tiles in a fixed order), mma.sync m16n8k16 bf16 with fp32
+// accumulators, the A rows staged in shared memory (RMSNorm applied while staging, by the same row routine
+// as the stand-alone norm kernel), weights read straight from global memory.  Epilogues round exactly where
+// the GEMM kernel's epilogues do (bias, SiLU, RoPE, residual, SiLU-gate, Euler update), so the only
+// difference from the per-layer launch list is the fp32 summation order inside each dot product.
+// Attention: one CTA per (sample, query head, 16-query tile); the 8 warps take consecutive key ranges with
+// an online softmax each and their partial (max, sum, O) are merged in a fixed order.
+//
+// Grid barrier: a monotonic 64-bit arrival counter in a caller-provided 8-byte buffer (zero before first use;
+// every completed launch leaves it at a multiple of the grid size).  Every wait is bounded: a barrier that
+// does not open within kSpinLimit polls records kErrFlowBarrier in the device error word; the other CTAs see
+// the error word at their next wait and return, so the kernel always ends (and later launches refuse to run
+// while the error word is set).  A rows are staged with bulk copies completing on an mbarrier, also waited
+// for with a bound.
+#pragma once
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "norm.cuh"
+#include "ptx.cuh"
+
+namespace svla {
+
+constexpr int kFlowMaxLayers = 32;
+constexpr int kFlowThreads = 256;
+constexpr int kFlowWarps = kFlowThreads / 32;
+constexpr int kFlowRows = 64;             // most action rows per call (four m16 tiles)
+constexpr int kFlowMT = kFlowRows / 16;
+constexpr int kFlowKC = 1024;             // A columns staged in shared memory at a time
+constexpr int kFlowLda = kFlowKC + 16;    // largest staged row stride (elements)
+constexpr int kFlowRedStride = 40;        // fp32 row stride of the per-warp partial tiles (conflict-free)
+constexpr int kFlowAttnStride = 72;       // fp32 row stride of the per-warp attention partials
+constexpr int kErrFlowBarrier = 103;
+
+struct FlowLayer {
+  const __nv_bfloat16* ln1;  // input RMSNorm weight [E]
+  const __nv_bfloat16* ln2;  // post-attention RMSNorm weight [E]
+  const __nv_bfloat16* wq;   // [q_dim, E]
+  const __nv_bfloat16* wk;   // [kv_dim, E] (self-attention layers)
+  const __nv_bfloat16* wv;
+  const __nv_bfloat16* wo;   // [E, q_dim]
+  const __nv_bfloat16* wg;   // [mlp, E]
+  const __nv_bfloat16* wu;
+  const __nv_bfloat16* wd;   // [E, mlp]
+  const __nv_bfloat16* k1;   // prefix keys [B * Lp, kv_dim]: the KV cache (self) or its cross projection
+  const __nv_bfloat16* v1;
+  int cross;
+};
+
+struct FlowArgs {
+  int B, S, Lp, E, A, Hq, Hkv, mlp, n_layers, n_steps;
+  float eps, dt, scale;
+  const float* noise;
+  float* xt;
+  __nv_bfloat16* xt_bf;
+  const __nv_bfloat16* w_in;   // action_in_proj [E, A] + bias [E]
+  const __nv_bfloat16* b_in;
+  const __nv_bfloat16* w_tin;  // action_time_mlp_in, its first E columns (row stride ld_tin)
+  int ld_tin;
+  const float* c_step;         // [n_steps, E]: W_tin[:, E:] . time_emb(t_step) + b_tin
+  const __nv_bfloat16* w_tout;  // action_time_mlp_out [E, E] + bias
+  const __nv_bfloat16* b_tout;
+  const __nv_bfloat16* ln_f;   // final RMSNorm [E]
+  const __nv_bfloat16* w_out;  // action_out_proj [A, E] + bias [A]
+  const __nv_bfloat16* b_out;
+  const uint8_t* key_mask;     // prefix key flags, row b at key_mask + b * key_mask_bs
+  long long key_mask_bs;
+  const int* suffix_pos;       // [B * S] RoPE positions (self- / cross-attention layers)
+  const int* cross_pos;
+  const float* rope_cs;        // [max_pos][32] (cos, sin)
+  int max_pos;
+  __nv_bfloat16 *a_emb, *a_t, *eh, *eq, *ek, *ev, *ectx, *emlp;  // scratch rows
+  unsigned long long* sync;    // monotonic arrival counter (a multiple of gridDim.x between launches)
+  int* err;
+  unsigned long long* dbg;     // profiling: (event, globaltimer ns) pairs of CTA 0 and the last CTA, or nullptr
+  FlowLayer layer[kFlowMaxLayers];
+};
+
+// profiling events (FlowArgs::dbg): kFlowDbgEvents (code, ns) pairs for CTA 0, then as many for the last CTA
+constexpr int kFlowDbgEvents = 1024;
+enum FlowEvent : int {
+  kEvBarrierIn = 1, kEvBarrierOut = 2, kEvStaged = 3, kEvMma = 4, kEvEpilogue = 5, kEvAttn = 6,
+  kEvCopied = 7,     // A rows landed in shared memory (before the row norm)
+  kEvKeys = 8,       // attention: warp 0's first keys / values landed
+  kEvAttnDone = 9,   // attention: warp 0's partial done (before the merge)
+};
+
+struct FlowSmem {
+  uint64_t bar;                                          // completion of the bulk copies that stage A
+  uint64_t pad_;
+  __nv_bfloat16 a[kFlowRows * kFlowLda];                 // A rows (bf16)
+  float red[kFlowWarps * kFlowRows * kFlowRedStride];    // per-warp partial tiles / attention partials
+  float ml[kFlowWarps * 32];                             // attention: per-warp row max (16) and sum (16)
+  uint8_t kf[kFlowWarps * 32];                           // attention: the staged keys' padding flags
+  int ok;
+  int n_ev;                                              // profiling events recorded by this CTA
+};
+
+namespace flow_detail {
+
+using attn_detail::cp_async16;
+using attn_detail::cp_async_commit;
+using attn_detail::cp_async_wait;
+using attn_detail::ex2;
+using attn_detail::ldmatrix_x4_trans;
+using attn_detail::kLog2e;
+using attn_detail::kMaskedScore;
+using attn_detail::ldmatrix_x4;
+using attn_detail::mma16816;
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// bulk copy (no tensor map, no multicast) of `bytes` from global memory into this CTA's shared memory,
+// completing on `bar`; 16-byte aligned addresses, bytes a multiple of 16
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ uint32_t ldcg_u32(const __nv_bfloat16* p) {
+  return __ldcg(reinterpret_cast<const unsigned int*>(p));
+}
+__device__ __forceinline__ uint32_t ldcg_u16(const __nv_bfloat16* p) {
+  return __ldcg(reinterpret_cast<const unsigned short*>(p));
+}
+__device__ __forceinline__ float bf(const __nv_bfloat16* p, int i) { return __bfloat162float(p[i]); }
+__device__ __forceinline__ void store2(__nv_bfloat16* p, float x, float y) {
+  *reinterpret_cast<uint32_t*>(p) = pack_bf16_rn(x, y);
+}
+
+// profiling: thread 0 of CTA 0 and of the last CTA append (event, globaltimer) while there is room
+__device__ __forceinline__ void event(const FlowArgs& a, FlowSmem& sm, int code) {
+  if (a.dbg == nullptr || threadIdx.x != 0) return;
+  const int sel = blockIdx.x == 0 ? 0 : (blockIdx.x == gridDim.x - 1 ? 1 : -1);
+  if (sel < 0 || sm.n_ev >= kFlowDbgEvents) return;
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  unsigned long long* d = a.dbg + (static_cast<size_t>(sel) * kFlowDbgEvents + sm.n_ev) * 2;
+  d[0] = static_cast<unsigned long long>(code);
+  d[1] = t;
+  ++sm.n_ev;
+}
+
+// Grid barrier on a monotonic 64-bit arrival counter: barrier k of a launch opens when the counter reaches
+// the next multiple of gridDim.x above this CTA's arrival.  False when it timed out or another CTA recorded an
+// error (then the caller returns).
+__device__ bool grid_sync(const FlowArgs& a, FlowSmem& sm) {
+  __syncthreads();
+  event(a, sm, kEvBarrierIn);
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");  // this CTA's writes (ordered by the CTA barrier) first
+    const unsigned long long n = gridDim.x;
+    const unsigned long long old = atomicAdd(a.sync, 1ull);
+    const unsigned long long target = (old / n + 1ull) * n;
+    uint32_t spins = 0;
+    while (ld_acquire_u64(a.sync) < target) {
+      if (++spins >= kSpinLimit) {
+        record_error(a.err, kErrFlowBarrier);
+        ok = 0;
+        break;
+      }
+      if ((spins & 63u) == 0 && *reinterpret_cast<volatile int*>(a.err) != 0) {
+        ok = 0;
+        break;
+      }
+      __nanosleep(32);
+    }
+    sm.ok = ok;
+  }
+  __syncthreads();
+  event(a, sm, kEvBarrierOut);
+  return sm.ok != 0;
+}
+
+// row stride (elements) of a staged chunk of kc columns: 16-byte rows whose 8-row ldmatrix groups hit
+// distinct bank groups ((stride / 8) odd)
+__device__ __forceinline__ int staged_ld(int kc) {
+  int s = kc + 8;
+  if (((s / 8) & 1) == 0) s += 8;
+  return s;
+}
+
+// rows [0, M) x columns [k0, k0 + kc) of A (row stride lda) into shared memory: one bulk copy per row, all in
+// flight at once, completing on the CTA's mbarrier (stage_wait: bounded; a timeout records an error that ends
+// the kernel at its next grid barrier).  Rows M..63 are left as they are: they only feed output rows that are
+// not stored.
+__device__ void stage_issue(FlowSmem& sm, const __nv_bfloat16* A, int lda, int M, int k0, int kc, int ldsa) {
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(&sm.bar, static_cast<uint32_t>(M * kc * 2));
+  __syncthreads();
+  if (static_cast<int>(threadIdx.x) < M) {
+    // order other CTAs' earlier (generic) writes of A and this CTA's earlier reads of the buffer before the copy
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    bulk_g2s(&sm.a[threadIdx.x * ldsa], A + static_cast<size_t>(threadIdx.x) * lda + k0, static_cast<uint32_t>(kc * 2),
+             &sm.bar);
+  }
+}
+__device__ __forceinline__ void stage_wait(FlowSmem& sm, uint32_t& parity, int* err) {
+  mbar_wait(&sm.bar, parity, err);
+  parity ^= 1u;
+}
+
+// L2 prefetch of `rows` rows of K bf16 (row stride ld) starting at p, spread over the CTA's threads
+__device__ __forceinline__ void prefetch_rows(const __nv_bfloat16* p, int rows, int K, int ld) {
+  const int lines = (K * 2 + 127) / 128;
+  for (int idx = threadIdx.x; idx < rows * lines; idx += kFlowThreads) {
+    const int r = idx / lines, l = idx % lines;
+    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p + static_cast<size_t>(r) * ld + l * 64));
+  }
+}
+
+// RMSNorm of the staged rows [0, M) (K <= 256 * NV) in place, one warp per row, with the arithmetic of the
+// stand-alone norm kernel's RMSNorm rows (norm_quant_row) in the same order, so the same bf16 results:
+//   ss = sum_k x^2 (fma, lane elements in order, then a butterfly over the lanes); rstd = 1 / sqrt(ss / K + eps)
+//   y = bf16(w * bf16(x * rstd)).  The weight stays in registers across rows.
+template <int NV>
+__device__ void norm_staged_rows(FlowSmem& sm, int K, const __nv_bfloat16* w, float eps, int M, int ldsa) {
+  constexpr int R = 2;  // rows per warp in flight (rows warp + 8 r)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __nv_bfloat162 w2[NV][4];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int k = (i * 32 + lane) * 8;
+    const int4 wr = k < K ? *reinterpret_cast<const int4*>(w + k) : make_int4(0, 0, 0, 0);
+    const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wr);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w2[i][j] = wh[j];
+  }
+  for (int m0 = warp; m0 < M; m0 += R * kFlowWarps) {
+    float2 v[R][NV][4];
+    float ss[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int m = m0 + r * kFlowWarps;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int k = (i * 32 + lane) * 8;
+        const int4 raw = (m < M && k < K) ? *reinterpret_cast<const int4*>(&sm.a[m * ldsa + k]) : make_int4(0, 0, 0, 0);
+        const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[r][i][j] = __bfloat1622float2(hx[j]);
+      }
+      ss[r] = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if ((i * 32 + lane) * 8 < K) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            ss[r] = fmaf(v[r][i][j].x, v[r][i][j].x, ss[r]);
+            ss[r] = fmaf(v[r][i][j].y, v[r][i][j].y, ss[r]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], o);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int m = m0 + r * kFlowWarps;
+      if (m >= M) continue;
+      const float var = __fdiv_rn(ss[r], static_cast<float>(K));
+      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+      const float2 rs = make_float2(rstd, rstd);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int k = (i * 32 + lane) * 8;
+        if (k >= K) continue;
+        uint32_t out[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // h = bf16(x * rstd); y = bf16(w * h): the product of two bf16 values is exact in fp32, so one bf16x2
+          // multiply rounds it exactly as bf16(fp32(w) * fp32(h)) does
+          const __nv_bfloat162 h = __float22bfloat162_rn(__fmul2_rn(v[r][i][j], rs));
+          const __nv_bfloat162 y = __hmul2(w2[i][j], h);
+          out[j] = *reinterpret_cast<const uint32_t*>(&y);
+        }
+        *reinterpret_cast<int4*>(&sm.a[m * ldsa + k]) = make_int4(out[0], out[1], out[2], out[3]);
+      }
+    }
+  }
+}
+
+// finish staging A (optionally RMSNorm-ed; K <= 1024 then) for a phase whose K fits one chunk
+__device__ void stage_single_finish(const FlowArgs& fa, FlowSmem& sm, int K, const __nv_bfloat16* norm_w, float eps,
+                                    int M, int ldsa, uint32_t& parity) {
+  stage_wait(sm, parity, fa.err);
+  event(fa, sm, kEvCopied);
+  if (norm_w != nullptr) {
+    if (K <= 256) norm_staged_rows<1>(sm, K, norm_w, eps, M, ldsa);
+    else if (K <= 512) norm_staged_rows<2>(sm, K, norm_w, eps, M, ldsa);
+    else if (K <= 768) norm_staged_rows<3>(sm, K, norm_w, eps, M, ldsa);
+    else norm_staged_rows<4>(sm, K, norm_w, eps, M, ldsa);
+    __syncthreads();
+  }
+}
+
+// this warp's weight fragments of one chunk (k16 steps w, w + 8, ..., at most 8), loaded before they are
+// needed so that their latency overlaps the staging of A
+template <int G>
+__device__ __forceinline__ void load_w(const __nv_bfloat16* const (&wrow)[G], int ldw, int k0, int kc,
+                                       uint32_t (&b)[8][G][2][2]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int steps = kc / 16;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int s = warp + u * kFlowWarps;
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        if (s < steps) {
+          const __nv_bfloat16* p = wrow[gi] + static_cast<size_t>(nt * 8 + g) * ldw + k0 + s * 16 + 2 * t;
+          b[u][gi][nt][0] = __ldg(reinterpret_cast<const unsigned int*>(p));
+          b[u][gi][nt][1] = __ldg(reinterpret_cast<const unsigned int*>(p + 8));
+        } else {
+          b[u][gi][nt][0] = b[u][gi][nt][1] = 0u;
+        }
+      }
+    }
+  }
+}
+
+// this warp's partial products over its k16 steps of the staged chunk
+template <int G>
+__device__ __forceinline__ void mma_w(const FlowSmem& sm, int ldsa, int kc, const uint32_t (&b)[8][G][2][2],
+                                      float (&acc)[G][2][kFlowMT][4]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int steps = kc / 16;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int s = warp + u * kFlowWarps;
+    if (s >= steps) break;
+#pragma unroll
+    for (int mt = 0; mt < kFlowMT; ++mt) {
+      uint32_t af[4];
+      ldmatrix_x4(af, &sm.a[(mt * 16 + (lane & 15)) * ldsa + s * 16 + (lane >> 4) * 8]);
+#pragma unroll
+      for (int gi = 0; gi < G; ++gi) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) mma16816(acc[gi][nt][mt], af, b[u][gi][nt][0], b[u][gi][nt][1]);
+      }
+    }
+  }
+}
+
+// adds the 8 warps' partial tiles (warp order) and hands each (row, column pair) to the epilogue together
+// with the four words pre(m, j) fetched for it before the partial tiles were exchanged (residuals, biases:
+// their load latency overlaps the exchange)
+template <int G, typename Pre, typename Epi>
+__device__ __forceinline__ void reduce_tiles(FlowSmem& sm, int M, const float (&acc)[G][2][kFlowMT][4], Pre&& pre,
+                                             Epi&& epi) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  constexpr int kItems = kFlowRows * 8 / kFlowThreads;  // (row, column pair) items per thread at most
+  uint4 pv[kItems];
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const int idx = threadIdx.x + u * kFlowThreads;
+    pv[u] = idx < M * 8 ? pre(idx >> 3, (idx & 7) * 2) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float* red = sm.red + warp * kFlowRows * kFlowRedStride;
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int mt = 0; mt < kFlowMT; ++mt) {
+        const int col = gi * 16 + nt * 8 + 2 * t, r0 = mt * 16 + g;
+        *reinterpret_cast<float2*>(&red[r0 * kFlowRedStride + col]) =
+            make_float2(acc[gi][nt][mt][0], acc[gi][nt][mt][1]);
+        *reinterpret_cast<float2*>(&red[(r0 + 8) * kFlowRedStride + col]) =
+            make_float2(acc[gi][nt][mt][2], acc[gi][nt][mt][3]);
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const int idx = threadIdx.x + u * kFlowThreads;
+    if (idx >= M * 8) break;
+    const int m = idx >> 3, j = (idx & 7) * 2;
+    float v[G][2];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      v[gi][0] = v[gi][1] = 0.f;
+#pragma unroll
+      for (int w = 0; w < kFlowWarps; ++w) {
+        const float2 p = *reinterpret_cast<const float2*>(
+            &sm.red[(w * kFlowRows + m) * kFlowRedStride + gi * 16 + j]);
+        v[gi][0] = __fadd_rn(v[gi][0], p.x);
+        v[gi][1] = __fadd_rn(v[gi][1], p.y);
+      }
+    }
+    epi(m, j, v, pv[u]);
+  }
+  __syncthreads();
+}
+
+// One GEMM phase: out[:, slice] = epi(A[:M, :K] . W[slice, :K]^T) for n_tasks slices of G x 16 columns;
+// wrows(task, w) gives each group's first weight row.  norm_w: RMSNorm the A rows while staging (K <= 1024).
+template <int G, typename WFn, typename PreFn, typename EpiFn>
+__device__ void gemm_phase(const FlowArgs& fa, FlowSmem& sm, uint32_t& parity, int M, const __nv_bfloat16* A, int K,
+                           const __nv_bfloat16* norm_w, float eps, int n_tasks, int ldw, WFn&& wrows, PreFn&& pre,
+                           EpiFn&& epi) {
+  if (static_cast<int>(blockIdx.x) >= n_tasks) return;
+  const bool single = K <= kFlowKC;
+  const int ldsa = staged_ld(single ? K : kFlowKC);
+  uint32_t b[8][G][2][2];
+  for (int task = blockIdx.x; task < n_tasks; task += gridDim.x) {
+    const __nv_bfloat16* wr[G];
+    wrows(task, wr);
+    float acc[G][2][kFlowMT][4];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int mt = 0; mt < kFlowMT; ++mt) acc[gi][nt][mt][0] = acc[gi][nt][mt][1] = acc[gi][nt][mt][2] = acc[gi][nt][mt][3] = 0.f;
+    for (int k0 = 0; k0 < K; k0 += kFlowKC) {
+      const int kc = (K - k0) < kFlowKC ? (K - k0) : kFlowKC;
+      // the rows are requested before the weights, whose loads would otherwise queue ahead of them
+      const bool stage = !single || task == static_cast<int>(blockIdx.x);
+      if (stage) {
+        if (!single) __syncthreads();  // every warp is done with the previous chunk
+        stage_issue(sm, A, K, M, k0, kc, ldsa);
+      }
+      load_w<G>(wr, ldw, k0, kc, b);
+      if (stage) {
+        if (single) {
+          stage_single_finish(fa, sm, K, norm_w, eps, M, ldsa, parity);
+          event(fa, sm, kEvStaged);
+        } else {
+          stage_wait(sm, parity, fa.err);
+        }
+      }
+      mma_w<G>(sm, ldsa, kc, b, acc);
+    }
+    event(fa, sm, kEvMma);
+    reduce_tiles<G>(
+        sm, M, acc, [&](int m, int j) { return pre(task, m, j); },
+        [&](int m, int j, float (&v)[G][2], const uint4& p) { epi(task, m, j, v, p); });
+    event(fa, sm, kEvEpilogue);
+  }
+}
+
+// attention of one expert layer; o -> ectx (bf16).  Each warp stages its keys / values 32 at a time in its
+// own slice of shared memory (asynchronous copies, all in flight at once) and reads MMA fragments with
+// ldmatrix; keys past the warp's range or past the last key are zero-filled and masked.
+__device__ void attention_phase(FlowSmem& sm, const FlowArgs& a, const FlowLayer& L) {
+  constexpr int kSub = 32, kRs = 72;  // keys staged at a time; bf16 row stride (conflict-free ldmatrix)
+  const int qd = a.Hq * 64, kvd = a.Hkv * 64, grp = a.Hq / a.Hkv;
+  const int qtiles = (a.S + 15) / 16;
+  const int n_tasks = a.B * a.Hq * qtiles;
+  const int L1 = a.Lp, Lk = L1 + (L.cross ? 0 : a.S);
+  const int ks = ((Lk + kFlowWarps - 1) / kFlowWarps + 15) / 16 * 16;  // keys per warp
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  __nv_bfloat16* sk = sm.a + warp * (2 * kSub * kRs);
+  __nv_bfloat16* sv = sk + kSub * kRs;
+  for (int task = blockIdx.x; task < n_tasks; task += gridDim.x) {
+    const int qt = task % qtiles, h = (task / qtiles) % a.Hq, b = task / (qtiles * a.Hq);
+    const int kh = h / grp;
+    const int s0 = qt * 16 + g, s1 = s0 + 8;
+    auto krow = [&](int key) -> const __nv_bfloat16* {
+      return key < L1 ? L.k1 + (static_cast<size_t>(b) * a.Lp + key) * kvd + kh * 64
+                      : a.ek + (static_cast<size_t>(b) * a.S + (key - L1)) * kvd + kh * 64;
+    };
+    auto vrow = [&](int key) -> const __nv_bfloat16* {
+      return key < L1 ? L.v1 + (static_cast<size_t>(b) * a.Lp + key) * kvd + kh * 64
+                      : a.ev + (static_cast<size_t>(b) * a.S + (key - L1)) * kvd + kh * 64;
+    };
+    const int kbeg = warp * ks, kend = (kbeg + ks) < Lk ? (kbeg + ks) : Lk;
+    const uint8_t* kflags = a.key_mask ? a.key_mask + static_cast<size_t>(b) * a.key_mask_bs : nullptr;
+    uint8_t* kf = sm.kf + warp * kSub;
+    auto stage = [&](int sub0) {
+      for (int idx = lane; idx < kSub * 8; idx += 32) {
+        const int r = idx >> 3, c = (idx & 7) * 8;
+        const int key = sub0 + r;
+        const bool in = key < kend;
+        cp_async16(&sk[r * kRs + c], in ? krow(key) + c : L.k1, in ? 16 : 0);
+        cp_async16(&sv[r * kRs + c], in ? vrow(key) + c : L.v1, in ? 16 : 0);
+      }
+      // padding flags of the prefix keys among them (16-byte runs; runs at or past the prefix read as 0)
+      if (lane < kSub / 16) {
+        const int key = sub0 + lane * 16;
+        const bool in = kflags != nullptr && key < a.Lp;
+        cp_async16(kf + lane * 16, in ? static_cast<const void*>(kflags + key) : static_cast<const void*>(L.k1),
+                   in ? 16 : 0);
+      }
+      cp_async_commit();
+    };
+    if (kbeg < kend) stage(kbeg);  // in flight while the queries load
+    uint32_t qa[4][4];
+    {
+      const __nv_bfloat16* q0 = a.eq + static_cast<size_t>(b * a.S + s0) * qd + h * 64;
+      const __nv_bfloat16* q1 = a.eq + static_cast<size_t>(b * a.S + s1) * qd + h * 64;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        qa[kk][0] = s0 < a.S ? ldcg_u32(q0 + kk * 16 + 2 * t) : 0u;
+        qa[kk][1] = s1 < a.S ? ldcg_u32(q1 + kk * 16 + 2 * t) : 0u;
+        qa[kk][2] = s0 < a.S ? ldcg_u32(q0 + kk * 16 + 8 + 2 * t) : 0u;
+        qa[kk][3] = s1 < a.S ? ldcg_u32(q1 + kk * 16 + 8 + 2 * t) : 0u;
+      }
+    }
+    float o[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float mx[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    for (int sub0 = kbeg; sub0 < kend; sub0 += kSub) {
+      if (sub0 != kbeg) {
+        __syncwarp();  // the previous keys' fragments have been read
+        stage(sub0);
+      }
+      cp_async_wait<0>();
+      __syncwarp();
+      if (sub0 == kbeg) event(a, sm, kEvKeys);
+      const int sub_end = (sub0 + kSub) < kend ? (sub0 + kSub) : kend;
+      for (int key0 = sub0; key0 < sub_end; key0 += 16) {
+        const int rb = key0 - sub0;
+        float s[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          // B fragments of the two 8-key n-tiles: keys rb + 0..7 | 8..15, head dims kk*16 + 0..7 | 8..15
+          uint32_t kb[4];
+          ldmatrix_x4(kb, &sk[(rb + (lane & 7) + ((lane >> 4) << 3)) * kRs + kk * 16 + ((lane >> 3) & 1) * 8]);
+          mma16816(s[0], qa[kk], kb[0], kb[1]);
+          mma16816(s[1], qa[kk], kb[2], kb[3]);
+        }
+        // scale, mask (key padding over the prefix, causal order over the chunk), online softmax
+        float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = key0 + nt * 8 + 2 * t + (e & 1);
+            const int query = (e >> 1) ? s1 : s0;
+            float v = __fmul_rn(s[nt][e], a.scale);
+            if (key >= Lk) {
+              v = -INFINITY;
+            } else if (key < a.Lp) {
+              if (kflags != nullptr && kf[key - sub0] == 0) v = kMaskedScore;
+            } else if (key - a.Lp > query) {
+              v = kMaskedScore;
+            }
+            s[nt][e] = v;
+            tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
+          }
+        }
+        float alpha[2];
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          tmax[hr] = fmaxf(tmax[hr], __shfl_xor_sync(0xffffffffu, tmax[hr], 1));
+          tmax[hr] = fmaxf(tmax[hr], __shfl_xor_sync(0xffffffffu, tmax[hr], 2));
+          const float nm = fmaxf(mx[hr], tmax[hr]);
+          alpha[hr] = (mx[hr] == -INFINITY) ? 0.f : ex2((mx[hr] - nm) * kLog2e);
+          mx[hr] = nm;
+          l[hr] *= alpha[hr];
+        }
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          o[n][0] *= alpha[0];
+          o[n][1] *= alpha[0];
+          o[n][2] *= alpha[1];
+          o[n][3] *= alpha[1];
+        }
+        uint32_t pa[4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float p0 = ex2((s[nt][0] - mx[0]) * kLog2e), p1 = ex2((s[nt][1] - mx[0]) * kLog2e);
+          const float p2 = ex2((s[nt][2] - mx[1]) * kLog2e), p3 = ex2((s[nt][3] - mx[1]) * kLog2e);
+          l[0] += p0 + p1;
+          l[1] += p2 + p3;
+          pa[2 * nt] = pack_bf16_rn(p0, p1);
+          pa[2 * nt + 1] = pack_bf16_rn(p2, p3);
+        }
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          // V^T fragments: keys rb + 0..15, head dims np*16 + 0..7 | 8..15
+          uint32_t vb[4];
+          ldmatrix_x4_trans(vb, &sv[(rb + (lane & 15)) * kRs + np * 16 + ((lane >> 4) << 3)]);
+          mma16816(o[2 * np], pa, vb[0], vb[1]);
+          mma16816(o[2 * np + 1], pa, vb[2], vb[3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      l[hr] += __shfl_xor_sync(0xffffffffu, l[hr], 1);
+      l[hr] += __shfl_xor_sync(0xffffffffu, l[hr], 2);
+    }
+    event(a, sm, kEvAttnDone);
+    // this warp's partial (max, sum, unnormalised O) -> shared memory; merged in warp order
+    float* po = sm.red + warp * 16 * kFlowAttnStride;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+      const int d = nd * 8 + 2 * t;
+      *reinterpret_cast<float2*>(&po[g * kFlowAttnStride + d]) = make_float2(o[nd][0], o[nd][1]);
+      *reinterpret_cast<float2*>(&po[(g + 8) * kFlowAttnStride + d]) = make_float2(o[nd][2], o[nd][3]);
+    }
+    if (t == 0) {
+      sm.ml[warp * 32 + g] = mx[0];
+      sm.ml[warp * 32 + g + 8] = mx[1];
+      sm.ml[warp * 32 + 16 + g] = l[0];
+      sm.ml[warp * 32 + 16 + g + 8] = l[1];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < 16 * 32; idx += kFlowThreads) {
+      const int r = idx >> 5, d = (idx & 31) * 2;
+      const int s = qt * 16 + r;
+      if (s >= a.S) continue;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kFlowWarps; ++w) M = fmaxf(M, sm.ml[w * 32 + r]);
+      float Ls = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < kFlowWarps; ++w) {
+        const float mw = sm.ml[w * 32 + r];
+        if (mw == -INFINITY) continue;  // a warp without keys
+        const float f = ex2((mw - M) * kLog2e);
+        const float2 ow = *reinterpret_cast<const float2*>(&sm.red[(w * 16 + r) * kFlowAttnStride + d]);
+        Ls = __fmaf_rn(sm.ml[w * 32 + 16 + r], f, Ls);
+        o0 = __fmaf_rn(ow.x, f, o0);
+        o1 = __fmaf_rn(ow.y, f, o1);
+      }
+      const float inv = __frcp_rn(Ls);
+      store2(a.ectx + static_cast<size_t>(b * a.S + s) * qd + h * 64 + d, bf16_round(o0 * inv), bf16_round(o1 * inv));
+    }
+    __syncthreads();
+    event(a, sm, kEvAttn);
+  }
+}
+
+}  // namespace flow_detail
+
+__global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a) {
+  using namespace flow_detail;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  FlowSmem& sm = *reinterpret_cast<FlowSmem*>(smem_raw);
+  uint32_t parity = 0;  // phase parity of the staging mbarrier
+  if (threadIdx.x == 0) {
+    sm.n_ev = 0;
+    mbar_init(&sm.bar, 1);
+    fence_mbar_init();
+    // a device error left by an earlier launch may have left the barrier counter between multiples: do not run
+    sm.ok = *reinterpret_cast<volatile int*>(a.err) == 0;
+  }
+  __syncthreads();
+  if (!sm.ok) return;
+  const int M = a.B * a.S, E = a.E, Ad = a.A, qd = a.Hq * 64, kvd = a.Hkv * 64;
+
+  // x_t = noise
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < M * Ad; i += gridDim.x * blockDim.x) {
+    const float x = a.noise[i];
+    a.xt[i] = x;
+    a.xt_bf[i] = __float2bfloat16_rn(x);
+  }
+
+  // Before each grid barrier, the next phase's weight rows of this CTA's first task (and, ahead of attention,
+  // its prefix keys / values) are prefetched into L2: they do not depend on the barrier.
+  enum { kPhIn, kPhTimeIn, kPhTimeOut, kPhQkv, kPhAttn, kPhO, kPhGateUp, kPhDown, kPhOut };
+  auto prefetch_phase = [&](int ph, int li) {
+    const int task = blockIdx.x;
+    const FlowLayer& L = a.layer[li < a.n_layers ? li : 0];
+    switch (ph) {
+      case kPhIn:
+        if (task < E / 16) prefetch_rows(a.w_in + static_cast<size_t>(task) * 16 * Ad, 16, Ad, Ad);
+        break;
+      case kPhTimeIn:
+        if (task < E / 16) prefetch_rows(a.w_tin + static_cast<size_t>(task) * 16 * a.ld_tin, 16, E, a.ld_tin);
+        break;
+      case kPhTimeOut:
+        if (task < E / 16) prefetch_rows(a.w_tout + static_cast<size_t>(task) * 16 * E, 16, E, E);
+        break;
+      case kPhQkv: {
+        const int q_tasks = 2 * a.Hq, kv_tasks = L.cross ? 0 : 2 * a.Hkv;
+        if (task >= q_tasks + 2 * kv_tasks) break;
+        const int seg = task < q_tasks ? 0 : (task < q_tasks + kv_tasks ? 1 : 2);
+        const int tt = seg == 0 ? task : (seg == 1 ? task - q_tasks : task - q_tasks - kv_tasks);
+        const int c0 = (tt >> 1) * 64 + (tt & 1) * 16;
+        const __nv_bfloat16* W = seg == 0 ? L.wq : (seg == 1 ? L.wk : L.wv);
+        prefetch_rows(W + static_cast<size_t>(c0) * E, 16, E, E);
+        prefetch_rows(W + static_cast<size_t>(c0 + 32) * E, 16, E, E);
+        break;
+      }
+      case kPhAttn: {
+        const int qtiles = (a.S + 15) / 16;
+        if (task >= a.B * a.Hq * qtiles) break;
+        const int h = (task / qtiles) % a.Hq, b = task / (qtiles * a.Hq), kh = h / (a.Hq / a.Hkv);
+        const size_t off = static_cast<size_t>(b) * a.Lp * kvd + kh * 64;
+        prefetch_rows(L.k1 + off, a.Lp, 64, kvd);
+        prefetch_rows(L.v1 + off, a.Lp, 64, kvd);
+        break;
+      }
+      case kPhO:
+        if (task < E / 16) prefetch_rows(L.wo + static_cast<size_t>(task) * 16 * qd, 16, qd, qd);
+        break;
+      case kPhGateUp:
+        if (task < a.mlp / 16) {
+          prefetch_rows(L.wg + static_cast<size_t>(task) * 16 * E, 16, E, E);
+          prefetch_rows(L.wu + static_cast<size_t>(task) * 16 * E, 16, E, E);
+        }
+        break;
+      case kPhDown:
+        if (task < E / 16) prefetch_rows(L.wd + static_cast<size_t>(task) * 16 * a.mlp, 16, a.mlp, a.mlp);
+        break;
+      default:
+        if (task < Ad / 16) prefetch_rows(a.w_out + static_cast<size_t>(task) * 16 * E, 16, E, E);
+        break;
+    }
+  };
+  auto no_pre = [](int, int, int) { return make_uint4(0u, 0u, 0u, 0u); };
+  // two bf16 biases of columns c, c + 1 (one word)
+  auto bias_pre = [](const __nv_bfloat16* bias, int c) {
+    return make_uint4(__ldg(reinterpret_cast<const unsigned int*>(bias + c)), 0u, 0u, 0u);
+  };
+  auto lo = [](uint32_t w) { return __uint_as_float(w << 16); };          // bf16 in the low half
+  auto hi = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };  // bf16 in the high half
+  // residual epilogue: p.x holds eh[m, c..c+1]
+  auto resid_store = [&](int c, int m, const float (&v)[1][2], const uint4& p) {
+    store2(a.eh + static_cast<size_t>(m) * E + c, __fadd_rn(bf16_round(v[0][0]), lo(p.x)),
+           __fadd_rn(bf16_round(v[0][1]), hi(p.x)));
+  };
+
+  prefetch_phase(kPhIn, 0);
+  if (!grid_sync(a, sm)) return;
+
+  for (int step = 0; step < a.n_steps; ++step) {
+    // action_in_proj: a_emb = bf16(x_t . W_in^T + b)
+    gemm_phase<1>(
+        a, sm, parity, M, a.xt_bf, Ad, nullptr, 0.f, E / 16, Ad,
+        [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_in + static_cast<size_t>(task) * 16 * Ad; },
+        [&](int task, int, int j) { return bias_pre(a.b_in, task * 16 + j); },
+        [&](int task, int m, int j, float (&v)[1][2], const uint4& p) {
+          store2(a.a_emb + static_cast<size_t>(m) * E + task * 16 + j, __fadd_rn(v[0][0], lo(p.x)),
+                 __fadd_rn(v[0][1], hi(p.x)));
+        });
+    prefetch_phase(kPhTimeIn, 0);
+    if (!grid_sync(a, sm)) return;
+    // time MLP in: a_t = bf16(silu(bf16(a_emb . W_tin[:, :E]^T + c_step)))
+    const float* cst = a.c_step + static_cast<size_t>(step) * E;
+    gemm_phase<1>(
+        a, sm, parity, M, a.a_emb, E, nullptr, 0.f, E / 16, a.ld_tin,
+        [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_tin + static_cast<size_t>(task) * 16 * a.ld_tin; },
+        [&](int task, int, int j) {
+          const float2 c2 = __ldg(reinterpret_cast<const float2*>(cst + task * 16 + j));
+          return make_uint4(__float_as_uint(c2.x), __float_as_uint(c2.y), 0u, 0u);
+        },
+        [&](int task, int m, int j, float (&v)[1][2], const uint4& p) {
+          const float x0 = bf16_round(__fadd_rn(v[0][0], __uint_as_float(p.x)));
+          const float x1 = bf16_round(__fadd_rn(v[0][1], __uint_as_float(p.y)));
+          store2(a.a_t + static_cast<size_t>(m) * E + task * 16 + j, silu_f(x0), silu_f(x1));
+        });
+    prefetch_phase(kPhTimeOut, 0);
+    if (!grid_sync(a, sm)) return;
+    // time MLP out: eh = bf16(a_t . W_tout^T + b)
+    gemm_phase<1>(
+        a, sm, parity, M, a.a_t, E, nullptr, 0.f, E / 16, E,
+        [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_tout + static_cast<size_t>(task) * 16 * E; },
+        [&](int task, int, int j) { return bias_pre(a.b_tout, task * 16 + j); },
+        [&](int task, int m, int j, float (&v)[1][2], const uint4& p) {
+          store2(a.eh + static_cast<size_t>(m) * E + task * 16 + j, __fadd_rn(v[0][0], lo(p.x)),
+                 __fadd_rn(v[0][1], hi(p.x)));
+        });
+    prefetch_phase(kPhQkv, 0);
+    if (!grid_sync(a, sm)) return;
+
+    for (int li = 0; li < a.n_layers; ++li) {
+      const FlowLayer& L = a.layer[li];
+      // q (and k, v on self-attention layers) with RoPE; a task is the column pairs (c, c + 32) of 16
+      // consecutive rotation pairs of one head: c0 = head * 64 + half * 16
+      const int q_tasks = 2 * a.Hq, kv_tasks = L.cross ? 0 : 2 * a.Hkv;
+      const int* pos = L.cross ? a.cross_pos : a.suffix_pos;
+      auto seg_of = [&](int task, int& seg, int& c0) {
+        if (task < q_tasks) {
+          seg = 0;
+          c0 = (task >> 1) * 64 + (task & 1) * 16;
+        } else if (task < q_tasks + kv_tasks) {
+          seg = 1;
+          const int tk = task - q_tasks;
+          c0 = (tk >> 1) * 64 + (tk & 1) * 16;
+        } else {
+          seg = 2;
+          const int tv = task - q_tasks - kv_tasks;
+          c0 = (tv >> 1) * 64 + (tv & 1) * 16;
+        }
+      };
+      gemm_phase<2>(
+          a, sm, parity, M, a.eh, E, L.ln1, a.eps, q_tasks + 2 * kv_tasks, E,
+          [&](int task, const __nv_bfloat16* (&w)[2]) {
+            int seg, c0;
+            seg_of(task, seg, c0);
+            const __nv_bfloat16* W = seg == 0 ? L.wq : (seg == 1 ? L.wk : L.wv);
+            w[0] = W + static_cast<size_t>(c0) * E;
+            w[1] = W + static_cast<size_t>(c0 + 32) * E;
+          },
+          [&](int task, int m, int j) {
+            // (cos, sin) of rotation pairs i0, i0 + 1 at this row's position
+            int seg, c0;
+            seg_of(task, seg, c0);
+            if (seg == 2) return make_uint4(0u, 0u, 0u, 0u);
+            int ps = pos[m];
+            ps = ps < 0 ? 0 : (ps >= a.max_pos ? a.max_pos - 1 : ps);
+            const int i0 = (c0 & 63) + j;
+            const float4 cs = __ldg(reinterpret_cast<const float4*>(a.rope_cs + (static_cast<size_t>(ps) * 32 + i0) * 2));
+            return make_uint4(__float_as_uint(cs.x), __float_as_uint(cs.y), __float_as_uint(cs.z), __float_as_uint(cs.w));
+          },
+          [&](int task, int m, int j, float (&v)[2][2], const uint4& p) {
+            int seg, c0;
+            seg_of(task, seg, c0);
+            __nv_bfloat16* out = seg == 0 ? a.eq : (seg == 1 ? a.ek : a.ev);
+            const int ld = seg == 0 ? qd : kvd;
+            float x1a = bf16_round(v[0][0]), x1b = bf16_round(v[0][1]);
+            float x2a = bf16_round(v[1][0]), x2b = bf16_round(v[1][1]);
+            if (seg < 2) {
+              const float ca = __uint_as_float(p.x), sa = __uint_as_float(p.y);
+              const float cb = __uint_as_float(p.z), sb = __uint_as_float(p.w);
+              const float y1a = __fsub_rn(__fmul_rn(x1a, ca), __fmul_rn(x2a, sa));
+              const float y2a = __fadd_rn(__fmul_rn(x2a, ca), __fmul_rn(x1a, sa));
+              const float y1b = __fsub_rn(__fmul_rn(x1b, cb), __fmul_rn(x2b, sb));
+              const float y2b = __fadd_rn(__fmul_rn(x2b, cb), __fmul_rn(x1b, sb));
+              x1a = y1a;
+              x2a = y2a;
+              x1b = y1b;
+              x2b = y2b;
+            }
+            store2(out + static_cast<size_t>(m) * ld + c0 + j, x1a, x1b);
+            store2(out + static_cast<size_t>(m) * ld + c0 + 32 + j, x2a, x2b);
+          });
+      prefetch_phase(kPhAttn, li);
+      if (!grid_sync(a, sm)) return;
+      attention_phase(sm, a, L);
+      prefetch_phase(kPhO, li);
+      if (!grid_sync(a, sm)) return;
+      // o_proj + residual: eh = bf16(bf16(ectx . W_o^T) + eh)
+      gemm_phase<1>(
+          a, sm, parity, M, a.ectx, qd, nullptr, 0.f, E / 16, qd,
+          [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = L.wo + static_cast<size_t>(task) * 16 * qd; },
+          [&](int task, int m, int j) {
+            return make_uint4(ldcg_u32(a.eh + static_cast<size_t>(m) * E + task * 16 + j), 0u, 0u, 0u);
+          },
+          [&](int task, int m, int j, float (&v)[1][2], const uint4& p) { resid_store(task * 16 + j, m, v, p); });
+      prefetch_phase(kPhGateUp, li);
+      if (!grid_sync(a, sm)) return;
+      // gate / up + SiLU gate: emlp = bf16(bf16(silu(bf16(gate))) * bf16(up))
+      gemm_phase<2>(
+          a, sm, parity, M, a.eh, E, L.ln2, a.eps, a.mlp / 16, E,
+          [&](int task, const __nv_bfloat16* (&w)[2]) {
+            w[0] = L.wg + static_cast<size_t>(task) * 16 * E;
+            w[1] = L.wu + static_cast<size_t>(task) * 16 * E;
+          },
+          no_pre,
+          [&](int task, int m, int j, float (&v)[2][2], const uint4&) {
+            const float g0 = bf16_round(silu_f(bf16_round(v[0][0])));
+            const float g1 = bf16_round(silu_f(bf16_round(v[0][1])));
+            store2(a.emlp + static_cast<size_t>(m) * a.mlp + task * 16 + j, __fmul_rn(g0, bf16_round(v[1][0])),
+                   __fmul_rn(g1, bf16_round(v[1][1])));
+          });
+      prefetch_phase(kPhDown, li);
+      if (!grid_sync(a, sm)) return;
+      // down_proj + residual
+      gemm_phase<1>(
+          a, sm, parity, M, a.emlp, a.mlp, nullptr, 0.f, E / 16, a.mlp,
+          [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = L.wd + static_cast<size_t>(task) * 16 * a.mlp; },
+          [&](int task, int m, int j) {
+            return make_uint4(ldcg_u32(a.eh + static_cast<size_t>(m) * E + task * 16 + j), 0u, 0u, 0u);
+          },
+          [&](int task, int m, int j, float (&v)[1][2], const uint4& p) { resid_store(task * 16 + j, m, v, p); });
+      prefetch_phase(li + 1 < a.n_layers ? kPhQkv : kPhOut, li + 1);
+      if (!grid_sync(a, sm)) return;
+    }
+    // final RMSNorm + action_out_proj + Euler: x_t += dt * (y . W_out^T + b), x_t_bf16 = bf16(x_t)
+    gemm_phase<1>(
+        a, sm, parity, M, a.eh, E, a.ln_f, a.eps, Ad / 16, E,
+        [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_out + static_cast<size_t>(task) * 16 * E; },
+        [&](int task, int m, int j) {
+          const int c = task * 16 + j;
+          const float2 x = __ldcg(reinterpret_cast<const float2*>(a.xt + static_cast<size_t>(m) * Ad + c));
+          return make_uint4(__float_as_uint(x.x), __float_as_uint(x.y),
+                            __ldg(reinterpret_cast<const unsigned int*>(a.b_out + c)), 0u);
+        },
+        [&](int task, int m, int j, float (&v)[1][2], const uint4& p) {
+          const size_t i = static_cast<size_t>(m) * Ad + task * 16 + j;
+          const float x0 = __fadd_rn(__uint_as_float(p.x), __fmul_rn(a.dt, __fadd_rn(v[0][0], lo(p.z))));
+          const float x1 = __fadd_rn(__uint_as_float(p.y), __fmul_rn(a.dt, __fadd_rn(v[0][1], hi(p.z))));
+          *reinterpret_cast<float2*>(a.xt + i) = make_float2(x0, x1);
+          store2(a.xt_bf + i, x0, x1);
+        });
+    prefetch_phase(kPhIn, 0);
+    if (!grid_sync(a, sm)) return;
+  }
+}
+
+}  // namespace svla

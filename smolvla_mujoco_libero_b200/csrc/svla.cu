@@ -20,6 +20,7 @@
 #include "gemm.cuh"
 #include "misc.cuh"
 #include "norm.cuh"
+#include "flow.cuh"
 #include "process.cuh"
 
 namespace svla {
@@ -778,6 +779,99 @@ int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n,
   return launch(euler_init_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, cs(stream), "euler_init_kernel",
                 noise, xt,
                                                                                     static_cast<__nv_bfloat16*>(xt_bf16), n);
+}
+
+int32_t svla_flow(const svla_flow_desc* d, svla_stream_t stream) {
+  if (!d) return fail(SVLA_ERR_ARG, "svla_flow: null descriptor");
+  const int rows = d->batch * d->chunk;
+  if (d->batch < 1 || d->chunk < 1 || rows > SVLA_FLOW_MAX_ROWS)
+    return fail(SVLA_ERR_ARG, "svla_flow: batch * chunk = %d outside 1..%d", rows, SVLA_FLOW_MAX_ROWS);
+  if (d->hidden < 16 || d->hidden % 16 != 0 || d->hidden > kFlowKC)
+    return fail(SVLA_ERR_ARG, "svla_flow: hidden %d must be a multiple of 16 in 16..%d", d->hidden, kFlowKC);
+  if (d->action_dim < 16 || d->action_dim % 16 != 0 || d->mlp < 16 || d->mlp % 16 != 0)
+    return fail(SVLA_ERR_ARG, "svla_flow: action_dim %d and mlp %d must be multiples of 16", d->action_dim, d->mlp);
+  if (d->heads < 1 || d->kv_heads < 1 || d->heads % d->kv_heads != 0)
+    return fail(SVLA_ERR_ARG, "svla_flow: heads %d not a multiple of kv_heads %d", d->heads, d->kv_heads);
+  if (d->n_layers < 1 || d->n_layers > SVLA_FLOW_MAX_LAYERS || d->num_steps < 1 || d->prefix_len < 1)
+    return fail(SVLA_ERR_ARG, "svla_flow: n_layers %d (1..%d), num_steps %d, prefix_len %d", d->n_layers,
+                SVLA_FLOW_MAX_LAYERS, d->num_steps, d->prefix_len);
+  if (d->ld_time_in < d->hidden || d->ld_time_in % 8 != 0 || d->max_pos < 1)
+    return fail(SVLA_ERR_ARG, "svla_flow: ld_time_in %d / max_pos %d", d->ld_time_in, d->max_pos);
+  const void* need[] = {d->noise, d->xt, d->xt_bf16, d->w_action_in, d->b_action_in, d->w_time_in, d->time_in_const,
+                        d->w_time_out, d->b_time_out, d->final_norm, d->w_action_out, d->b_action_out, d->suffix_pos,
+                        d->cross_pos, d->rope_cs, d->a_emb, d->a_t, d->eh, d->eq, d->ek, d->ev, d->ectx, d->emlp,
+                        d->sync};
+  for (const void* p : need)
+    if (!p) return fail(SVLA_ERR_ARG, "svla_flow: null pointer argument");
+  // 16-byte rows for the staged A loads and the packed stores
+  const void* aligned[] = {d->xt_bf16, d->a_emb, d->a_t, d->eh, d->eq, d->ek, d->ev, d->ectx, d->emlp, d->rope_cs};
+  for (const void* p : aligned)
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return fail(SVLA_ERR_ARG, "svla_flow: buffers must be 16-byte aligned");
+  FlowArgs a{};
+  a.B = d->batch; a.S = d->chunk; a.Lp = d->prefix_len; a.E = d->hidden; a.A = d->action_dim;
+  a.Hq = d->heads; a.Hkv = d->kv_heads; a.mlp = d->mlp; a.n_layers = d->n_layers; a.n_steps = d->num_steps;
+  a.eps = d->eps;
+  a.dt = static_cast<float>(-1.0 / d->num_steps);
+  a.scale = 0.125f;  // head_dim^-1/2
+  a.noise = d->noise; a.xt = d->xt; a.xt_bf = static_cast<__nv_bfloat16*>(d->xt_bf16);
+  auto bfp = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  a.w_in = bfp(d->w_action_in); a.b_in = bfp(d->b_action_in);
+  a.w_tin = bfp(d->w_time_in); a.ld_tin = d->ld_time_in; a.c_step = d->time_in_const;
+  a.w_tout = bfp(d->w_time_out); a.b_tout = bfp(d->b_time_out);
+  a.ln_f = bfp(d->final_norm); a.w_out = bfp(d->w_action_out); a.b_out = bfp(d->b_action_out);
+  a.key_mask = d->key_mask; a.key_mask_bs = d->key_mask_bs;
+  a.suffix_pos = d->suffix_pos; a.cross_pos = d->cross_pos; a.rope_cs = d->rope_cs; a.max_pos = d->max_pos;
+  auto bfw = [](void* p) { return static_cast<__nv_bfloat16*>(p); };
+  a.a_emb = bfw(d->a_emb); a.a_t = bfw(d->a_t); a.eh = bfw(d->eh); a.eq = bfw(d->eq); a.ek = bfw(d->ek);
+  a.ev = bfw(d->ev); a.ectx = bfw(d->ectx); a.emlp = bfw(d->emlp);
+  if (reinterpret_cast<uintptr_t>(d->sync) % 8 != 0) return fail(SVLA_ERR_ARG, "svla_flow: sync must be 8-byte aligned");
+  if (d->key_mask && (reinterpret_cast<uintptr_t>(d->key_mask) % 16 != 0 || d->key_mask_bs % 16 != 0 ||
+                      d->key_mask_bs < (d->prefix_len + 15) / 16 * 16))
+    return fail(SVLA_ERR_ARG, "svla_flow: key flag rows must be 16-byte aligned and hold prefix_len rounded up to 16");
+  a.sync = reinterpret_cast<unsigned long long*>(d->sync);
+  a.dbg = reinterpret_cast<unsigned long long*>(d->debug_clock);
+  a.err = device_error_ptr();
+  if (!a.err) return fail(SVLA_ERR_CUDA, "svla_flow: device error word unavailable");
+  for (int i = 0; i < d->n_layers; ++i) {
+    const svla_flow_layer& s = d->layer[i];
+    if (!s.input_norm || !s.post_norm || !s.wq || !s.wo || !s.wg || !s.wu || !s.wd || !s.keys || !s.values ||
+        (!s.cross && (!s.wk || !s.wv)))
+      return fail(SVLA_ERR_ARG, "svla_flow: layer %d lacks a weight or its keys / values", i);
+    FlowLayer& L = a.layer[i];
+    L.ln1 = bfp(s.input_norm); L.ln2 = bfp(s.post_norm); L.wq = bfp(s.wq); L.wk = bfp(s.wk); L.wv = bfp(s.wv);
+    L.wo = bfp(s.wo); L.wg = bfp(s.wg); L.wu = bfp(s.wu); L.wd = bfp(s.wd); L.k1 = bfp(s.keys); L.v1 = bfp(s.values);
+    L.cross = s.cross ? 1 : 0;
+  }
+  // one CTA per SM, all resident at once (a cooperative launch refuses a grid that cannot be)
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return fail(SVLA_ERR_CUDA, "svla_flow: cannot read the SM count");
+  const size_t smem = sizeof(FlowSmem);
+  static bool configured[64] = {false};  // the attribute is per function and per device
+  if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(flow_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "svla_flow: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, flow_kernel, kFlowThreads, smem) != cudaSuccess ||
+      per_sm < 1)
+    return fail(SVLA_ERR_CUDA, "svla_flow: the kernel does not fit on an SM");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(sms));
+  cfg.blockDim = dim3(kFlowThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = cs(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, flow_kernel, a);
+  if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "flow_kernel: %s", cudaGetErrorString(e));
+  return check_launch("flow_kernel");
 }
 
 }  // extern "C"

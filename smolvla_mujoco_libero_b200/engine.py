@@ -42,11 +42,13 @@ class NativeSampleActions:
     engine, for up to ``max_batch`` samples per call."""
 
     def __init__(self, packed_path: str | Path, max_batch: int = 1, use_cuda_graph: bool = True,
-                 split_k: bool = True, device: str | torch.device = "cuda", action_dim: int | None = None):
+                 split_k: bool = True, device: str | torch.device = "cuda", action_dim: int | None = None,
+                 flow: bool = True):
         self.device = torch.device(device)
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
-        flags = (0 if use_cuda_graph else L.ENGINE_NO_GRAPH) | (0 if split_k else L.ENGINE_NO_SPLIT_K)
+        flags = (0 if use_cuda_graph else L.ENGINE_NO_GRAPH) | (0 if split_k else L.ENGINE_NO_SPLIT_K) | \
+            (0 if flow else L.ENGINE_NO_FLOW)
         handle = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             check(lib().svla_engine_create(str(packed_path).encode(), int(max_batch), flags, _stream(self.device),

@@ -135,7 +135,7 @@ class SmolVLARunner:
     SPLITK_BYTES = 32 << 20  # split-K workspace shared by the runner's GEMMs (stream-ordered)
 
     def __init__(self, weights: DeviceWeights, batch: int, mode: str = "quant", debug_taps: bool = False,
-                 split_k: bool = True, prefix_only: bool = False):
+                 split_k: bool = True, prefix_only: bool = False, flow: bool | None = None):
         if weights.cfg.expert_layers != weights.cfg.text_layers:
             raise ValueError("the expert must have one layer per text layer (each expert layer reads that layer's KV)")
         if mode == "quant" and not weights.quantized:
@@ -151,6 +151,13 @@ class SmolVLARunner:
         # split-K changes the fp32 summation order of the small-M bf16 GEMMs with the batch size; without it
         # every batch row's result is bit-identical at any batch size
         self.split_k = split_k
+        # flow: the flow-matching loop as one persistent kernel (svla_flow) instead of ~117 launches per step;
+        # None = when it applies (quant mode, batch * chunk <= 64 rows, no taps)
+        can_flow = self._flow_supported(weights.cfg, batch, mode, debug_taps)
+        if flow and not can_flow:
+            raise ValueError("the persistent flow kernel needs quant mode, batch * chunk <= 64, no taps and "
+                             "bf16 / W8A16 expert linears")
+        self.flow = can_flow if flow is None else bool(flow)
         self.dev = weights.device
         self.graph: torch.cuda.CUDAGraph | None = None
         self.taps: dict[str, list] = {}
@@ -158,6 +165,14 @@ class SmolVLARunner:
         self._constants()
         self.launches: list = []
         self._build()
+
+    def _flow_supported(self, c: SmolVLAConfig, batch: int, mode: str, debug: bool) -> bool:
+        if mode != "quant" or debug or batch * c.chunk > L.FLOW_MAX_ROWS or c.expert_layers > L.FLOW_MAX_LAYERS:
+            return False
+        if c.expert_hidden % 16 or c.expert_hidden > 1024 or c.max_action_dim % 16 or c.expert_mlp % 16:
+            return False
+        expert = [p for n, p in self.w.lin.items() if n.startswith(EXPERT + ".")]
+        return all(p.kind == "bf16" or (p.kind == "w8a16" and p.weight_deq is not None) for p in expert)
 
     # ------------------------------------------------------------------ buffers
     def _alloc(self):
@@ -431,6 +446,9 @@ class SmolVLARunner:
                        [self._linear_seg(f"{p}.k_proj", self.kcache[i], self.ck[i]),
                         self._linear_seg(f"{p}.v_proj", self.vcache[i], self.cv[i])])
         # ---------------- flow matching
+        if self.flow:
+            self._add(lib.svla_flow, self._flow_desc())
+            return
         self._add(lib.svla_euler_init, self.in_noise.data_ptr(), self.xt.data_ptr(), self.xt_bf.data_ptr(),
                   self.xt.numel())
         dt = -1.0 / c.num_steps
@@ -471,6 +489,48 @@ class SmolVLARunner:
             self._gemm(L.KIND_BF16, L.EPI_EULER, B * S, E,
                        [self._linear_seg("model.action_out_proj", self.ey, None)], dt=dt, xt=self.xt,
                        xt_bf16=self.xt_bf)
+
+    def _flow_desc(self) -> L.FlowDesc:
+        """Descriptor of the persistent flow kernel over this runner's buffers."""
+        c, B, w = self.cfg, self.B, self.w
+        E = c.expert_hidden
+
+        def wt(name):  # the bf16 weight a linear multiplies by
+            p = w.lin[name]
+            return (p.weight if p.kind == "bf16" else p.weight_deq).data_ptr()
+
+        d = L.FlowDesc()
+        d.batch, d.chunk, d.prefix_len, d.hidden, d.action_dim = B, c.chunk, c.prefix_len, E, c.max_action_dim
+        d.heads, d.kv_heads, d.mlp, d.n_layers, d.num_steps = c.heads, c.kv_heads, c.expert_mlp, c.expert_layers, c.num_steps
+        d.eps = float(c.rms_eps)
+        d.noise, d.xt, d.xt_bf16 = self.in_noise.data_ptr(), self.xt.data_ptr(), self.xt_bf.data_ptr()
+        d.w_action_in, d.b_action_in = wt("model.action_in_proj"), w.lin["model.action_in_proj"].bias.data_ptr()
+        mi = w.lin["model.action_time_mlp_in"]
+        d.w_time_in, d.ld_time_in, d.time_in_const = mi.weight.data_ptr(), mi.weight.stride(0), self.c_step.data_ptr()
+        d.w_time_out, d.b_time_out = wt("model.action_time_mlp_out"), w.lin["model.action_time_mlp_out"].bias.data_ptr()
+        d.final_norm = w.t[f"{EXPERT}.norm.weight"].data_ptr()
+        d.w_action_out, d.b_action_out = wt("model.action_out_proj"), w.lin["model.action_out_proj"].bias.data_ptr()
+        d.key_mask, d.key_mask_bs = self.key_pad.data_ptr(), self.key_pad.stride(0)
+        d.suffix_pos, d.cross_pos = self.suffix_pos.data_ptr(), self.cross_pos.data_ptr()
+        d.rope_cs, d.max_pos = self.rope_cs.data_ptr(), self.max_pos
+        d.a_emb, d.a_t, d.eh, d.eq = self.a_emb.data_ptr(), self.a_t.data_ptr(), self.eh.data_ptr(), self.eq.data_ptr()
+        d.ek, d.ev, d.ectx, d.emlp = self.ek.data_ptr(), self.ev.data_ptr(), self.ectx.data_ptr(), self.emlp.data_ptr()
+        self.flow_sync = torch.zeros(2, dtype=torch.int32, device=self.dev)
+        d.sync = self.flow_sync.data_ptr()
+        for i in range(c.expert_layers):
+            p = f"{EXPERT}.layers.{i}"
+            ly = d.layer[i]
+            ly.input_norm = w.t[f"{p}.input_layernorm.weight"].data_ptr()
+            ly.post_norm = w.t[f"{p}.post_attention_layernorm.weight"].data_ptr()
+            ly.wq, ly.wo = wt(f"{p}.self_attn.q_proj"), wt(f"{p}.self_attn.o_proj")
+            ly.wg, ly.wu, ly.wd = wt(f"{p}.mlp.gate_proj"), wt(f"{p}.mlp.up_proj"), wt(f"{p}.mlp.down_proj")
+            ly.cross = int(c.is_cross_layer(i))
+            if ly.cross:
+                ly.keys, ly.values = self.ck[i].data_ptr(), self.cv[i].data_ptr()
+            else:
+                ly.wk, ly.wv = wt(f"{p}.self_attn.k_proj"), wt(f"{p}.self_attn.v_proj")
+                ly.keys, ly.values = self.kcache[i].data_ptr(), self.vcache[i].data_ptr()
+        return d
 
     # ------------------------------------------------------------------ execution
     @property
@@ -551,6 +611,6 @@ class SmolVLARunner:
 
 import ctypes as _ct  # noqa: E402
 
-ctypes_structs = (L.GemmDesc, L.NormDesc, L.AttnDesc)
+ctypes_structs = (L.GemmDesc, L.NormDesc, L.AttnDesc, L.FlowDesc)
 _TAP = object()  # marker of a tap entry in the launch list
 ctypes_byref = _ct.byref
