@@ -25,10 +25,12 @@ from .model import DeviceWeights, SmolVLARunner
 
 class SampleActions:
     def __init__(self, cfg: SmolVLAConfig, weights: DeviceWeights, use_cuda_graph: bool = True,
-                 action_dim: int | None = None, split_k: bool = True):
+                 action_dim: int | None = None, split_k: bool = True, flow: bool | None = None):
         if not weights.quantized:
             raise ValueError("SampleActions needs weights packed with a scale table")
         self.cfg, self.weights, self.use_cuda_graph, self.split_k = cfg, weights, use_cuda_graph, split_k
+        # flow: the persistent flow-matching kernel for batch * chunk <= 64 rows (None = wherever it applies)
+        self.flow = flow
         self.action_dim = cfg.action_dim if action_dim is None else action_dim
         self.runners: dict[int, SmolVLARunner] = {}
         self.stats: dict[str, Any] = {"cuda_graph_failed": False}
@@ -36,7 +38,8 @@ class SampleActions:
     def runner(self, batch: int) -> SmolVLARunner:
         r = self.runners.get(batch)
         if r is None:
-            r = SmolVLARunner(self.weights, batch, split_k=self.split_k)
+            # flow=True asks for the kernel wherever it applies (large batches keep the per-layer launches)
+            r = SmolVLARunner(self.weights, batch, split_k=self.split_k, flow=False if self.flow is False else None)
             if self.use_cuda_graph:
                 try:
                     r.capture()

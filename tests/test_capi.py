@@ -49,7 +49,8 @@ def _c_sizeof(struct: str, tmp_path: Path) -> int:
 
 @pytest.mark.parametrize("cname,pyname", [("svla_gemm_desc", "GemmDesc"), ("svla_gemm_seg", "GemmSeg"),
                                           ("svla_norm_desc", "NormDesc"), ("svla_attn_desc", "AttnDesc"),
-                                          ("svla_engine_info", "EngineInfo")])
+                                          ("svla_engine_info", "EngineInfo"), ("svla_flow_desc", "FlowDesc"),
+                                          ("svla_flow_layer", "FlowLayer")])
 def test_struct_layouts_match(cname, pyname, tmp_path):
     import ctypes
     assert ctypes.sizeof(getattr(_lib, pyname)) == _c_sizeof(cname, tmp_path)

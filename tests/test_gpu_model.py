@@ -64,10 +64,12 @@ def test_tiny_sample_actions_matches_oracle(tiny):
 
 @pytest.mark.parametrize("split_k", [False, True])
 def test_batch_rows_are_independent(tiny, split_k):
-    """Without split-K each batch row is bit-identical at any batch size; with it (the default) the small-M
-    GEMMs of a single row sum their fp32 partials in another order, so rows agree within the tolerance."""
+    """Without split-K (and on one path: the batch-1 call would otherwise take the persistent flow kernel) each
+    batch row is bit-identical at any batch size; with split-K and the flow kernel (the defaults) a single row
+    sums its fp32 partials in another order, so rows agree within the tolerance."""
     w, js = tiny
-    sa = SampleActions(TINY, DeviceWeights(TINY, w, load_scale_json(js)), split_k=split_k)
+    sa = SampleActions(TINY, DeviceWeights(TINY, w, load_scale_json(js)), split_k=split_k,
+                       flow=None if split_k else False)
     o = _obs(TINY, 3, 21)
     full = _run(sa, o)
     for i in range(3):
