@@ -217,14 +217,6 @@ __device__ __forceinline__ void stage_wait(FlowSmem& sm, uint32_t& parity, int* 
   parity ^= 1u;
 }
 
-// L2 prefetch of `rows` rows of K bf16 (row stride ld) starting at p, spread over the CTA's threads
-__device__ __forceinline__ void prefetch_rows(const __nv_bfloat16* p, int rows, int K, int ld) {
-  const int lines = (K * 2 + 127) / 128;
-  for (int idx = threadIdx.x; idx < rows * lines; idx += kFlowThreads) {
-    const int r = idx / lines, l = idx % lines;
-    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p + static_cast<size_t>(r) * ld + l * 64));
-  }
-}
 
 // RMSNorm of the staged rows [0, M) (K <= 256 * NV) in place, one warp per row, with the arithmetic of the
 // stand-alone norm kernel's RMSNorm rows (norm_quant_row) in the same order, so the same bf16 results:
@@ -314,15 +306,15 @@ __device__ void stage_single_finish(const FlowArgs& fa, FlowSmem& sm, int K, con
   }
 }
 
-// this warp's weight fragments of one chunk (k16 steps w, w + 8, ..., at most 8), loaded before they are
+// this warp's weight fragments of one chunk (k16 steps w, w + 8, ..., at most U), loaded before they are
 // needed so that their latency overlaps the staging of A
-template <int G>
+template <int G, int U>
 __device__ __forceinline__ void load_w(const __nv_bfloat16* const (&wrow)[G], int ldw, int k0, int kc,
-                                       uint32_t (&b)[8][G][2][2]) {
+                                       uint32_t (&b)[U][G][2][2]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int steps = kc / 16;
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int s = warp + u * kFlowWarps;
 #pragma unroll
     for (int gi = 0; gi < G; ++gi) {
@@ -341,17 +333,17 @@ __device__ __forceinline__ void load_w(const __nv_bfloat16* const (&wrow)[G], in
 }
 
 // this warp's partial products over its k16 steps of the staged chunk
-template <int G>
-__device__ __forceinline__ void mma_w(const FlowSmem& sm, int ldsa, int kc, const uint32_t (&b)[8][G][2][2],
-                                      float (&acc)[G][2][kFlowMT][4]) {
+template <int G, int MT, int U>
+__device__ __forceinline__ void mma_w(const FlowSmem& sm, int ldsa, int kc, const uint32_t (&b)[U][G][2][2],
+                                      float (&acc)[G][2][MT][4]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int steps = kc / 16;
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int s = warp + u * kFlowWarps;
     if (s >= steps) break;
 #pragma unroll
-    for (int mt = 0; mt < kFlowMT; ++mt) {
+    for (int mt = 0; mt < MT; ++mt) {
       uint32_t af[4];
       ldmatrix_x4(af, &sm.a[(mt * 16 + (lane & 15)) * ldsa + s * 16 + (lane >> 4) * 8]);
 #pragma unroll
@@ -366,11 +358,11 @@ __device__ __forceinline__ void mma_w(const FlowSmem& sm, int ldsa, int kc, cons
 // adds the 8 warps' partial tiles (warp order) and hands each (row, column pair) to the epilogue together
 // with the four words pre(m, j) fetched for it before the partial tiles were exchanged (residuals, biases:
 // their load latency overlaps the exchange)
-template <int G, typename Pre, typename Epi>
-__device__ __forceinline__ void reduce_tiles(FlowSmem& sm, int M, const float (&acc)[G][2][kFlowMT][4], Pre&& pre,
+template <int G, int MT, typename Pre, typename Epi>
+__device__ __forceinline__ void reduce_tiles(FlowSmem& sm, int M, const float (&acc)[G][2][MT][4], Pre&& pre,
                                              Epi&& epi) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  constexpr int kItems = kFlowRows * 8 / kFlowThreads;  // (row, column pair) items per thread at most
+  constexpr int kItems = (MT * 16 * 8 + kFlowThreads - 1) / kFlowThreads;  // (row, column pair) items per thread
   uint4 pv[kItems];
 #pragma unroll
   for (int u = 0; u < kItems; ++u) {
@@ -383,7 +375,7 @@ __device__ __forceinline__ void reduce_tiles(FlowSmem& sm, int M, const float (&
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-      for (int mt = 0; mt < kFlowMT; ++mt) {
+      for (int mt = 0; mt < MT; ++mt) {
         const int col = gi * 16 + nt * 8 + 2 * t, r0 = mt * 16 + g;
         *reinterpret_cast<float2*>(&red[r0 * kFlowRedStride + col]) =
             make_float2(acc[gi][nt][mt][0], acc[gi][nt][mt][1]);
@@ -415,99 +407,151 @@ __device__ __forceinline__ void reduce_tiles(FlowSmem& sm, int M, const float (&
   __syncthreads();
 }
 
-// One GEMM phase: out[:, slice] = epi(A[:M, :K] . W[slice, :K]^T) for n_tasks slices of G x 16 columns;
-// wrows(task, w) gives each group's first weight row.  norm_w: RMSNorm the A rows while staging (K <= 1024).
-template <int G, typename WFn, typename PreFn, typename EpiFn>
+// One GEMM phase: out[rows, slice] = epi(A[rows, :K] . W[slice, :K]^T) for n_col slices of G x 16 columns,
+// each split into blocks of MT * 16 rows (a task = a slice x a row block: with MT = 2 a CTA stages, normalises
+// and multiplies half of the rows, at twice the tasks); wrows(slice, w) gives each group's first weight row.
+// norm_w: RMSNorm the A rows while staging (K <= 1024).
+template <int G, int MT, typename WFn, typename PreFn, typename EpiFn>
 __device__ void gemm_phase(const FlowArgs& fa, FlowSmem& sm, uint32_t& parity, int M, const __nv_bfloat16* A, int K,
-                           const __nv_bfloat16* norm_w, float eps, int n_tasks, int ldw, WFn&& wrows, PreFn&& pre,
+                           const __nv_bfloat16* norm_w, float eps, int n_col, int ldw, WFn&& wrows, PreFn&& pre,
                            EpiFn&& epi) {
+  constexpr int kRowsT = MT * 16;
+  // columns staged per chunk: as many as the A buffer holds for kRowsT rows, at most U k16 steps per warp
+  constexpr int U = G == 1 ? 16 : 8;
+  constexpr int KC0 = U * 16 * kFlowWarps, KC1 = (kFlowRows * kFlowLda) / kRowsT - 16;
+  constexpr int KC = KC0 < KC1 ? KC0 : KC1;
+  static_assert(KC % 16 == 0 && KC >= 1024, "chunk width");
+  const int blocks = (M + kRowsT - 1) / kRowsT;
+  const int n_tasks = n_col * blocks;
   if (static_cast<int>(blockIdx.x) >= n_tasks) return;
-  const bool single = K <= kFlowKC;
-  const int ldsa = staged_ld(single ? K : kFlowKC);
-  uint32_t b[8][G][2][2];
+  const bool single = K <= KC;
+  const int ldsa = staged_ld(single ? K : KC);
+  int staged = -1;  // row block in shared memory (single-chunk phases)
+  uint32_t b[U][G][2][2];
   for (int task = blockIdx.x; task < n_tasks; task += gridDim.x) {
+    const int ct = task / blocks, rb = task % blocks;
+    const int row0 = rb * kRowsT, rows = (M - row0) < kRowsT ? (M - row0) : kRowsT;
+    const __nv_bfloat16* Ab = A + static_cast<size_t>(row0) * K;
     const __nv_bfloat16* wr[G];
-    wrows(task, wr);
-    float acc[G][2][kFlowMT][4];
+    wrows(ct, wr);
+    float acc[G][2][MT][4];
 #pragma unroll
     for (int gi = 0; gi < G; ++gi)
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int mt = 0; mt < kFlowMT; ++mt) acc[gi][nt][mt][0] = acc[gi][nt][mt][1] = acc[gi][nt][mt][2] = acc[gi][nt][mt][3] = 0.f;
-    for (int k0 = 0; k0 < K; k0 += kFlowKC) {
-      const int kc = (K - k0) < kFlowKC ? (K - k0) : kFlowKC;
+        for (int mt = 0; mt < MT; ++mt) acc[gi][nt][mt][0] = acc[gi][nt][mt][1] = acc[gi][nt][mt][2] = acc[gi][nt][mt][3] = 0.f;
+    for (int k0 = 0; k0 < K; k0 += KC) {
+      const int kc = (K - k0) < KC ? (K - k0) : KC;
       // the rows are requested before the weights, whose loads would otherwise queue ahead of them
-      const bool stage = !single || task == static_cast<int>(blockIdx.x);
+      const bool stage = !single || staged != rb;
       if (stage) {
         if (!single) __syncthreads();  // every warp is done with the previous chunk
-        stage_issue(sm, A, K, M, k0, kc, ldsa);
+        stage_issue(sm, Ab, K, rows, k0, kc, ldsa);
       }
-      load_w<G>(wr, ldw, k0, kc, b);
+      load_w<G, U>(wr, ldw, k0, kc, b);
       if (stage) {
         if (single) {
-          stage_single_finish(fa, sm, K, norm_w, eps, M, ldsa, parity);
+          stage_single_finish(fa, sm, K, norm_w, eps, rows, ldsa, parity);
+          staged = rb;
           event(fa, sm, kEvStaged);
         } else {
           stage_wait(sm, parity, fa.err);
         }
       }
-      mma_w<G>(sm, ldsa, kc, b, acc);
+      mma_w<G, MT, U>(sm, ldsa, kc, b, acc);
     }
     event(fa, sm, kEvMma);
-    reduce_tiles<G>(
-        sm, M, acc, [&](int m, int j) { return pre(task, m, j); },
-        [&](int m, int j, float (&v)[G][2], const uint4& p) { epi(task, m, j, v, p); });
+    reduce_tiles<G, MT>(
+        sm, rows, acc, [&](int m, int j) { return pre(ct, row0 + m, j); },
+        [&](int m, int j, float (&v)[G][2], const uint4& p) { epi(ct, row0 + m, j, v, p); });
     event(fa, sm, kEvEpilogue);
   }
+}
+
+constexpr int kAttnSub = 32;  // keys a warp stages at a time
+constexpr int kAttnRs = 72;   // bf16 row stride of the staged keys / values (conflict-free ldmatrix)
+enum { kKeysAll = 0, kKeysPrefix = 1, kKeysSuffix = 2 };
+
+// Warp-level asynchronous copies of keys [sub0, sub0 + 32) of kv head kh of sample b (and their padding flags)
+// into this warp's slice of shared memory; keys at or past kend are zero-filled.  part: all keys, or only those
+// of the prefix (keys < Lp: the KV cache / cross projections, final before the flow kernel starts) with the
+// flags, or only the chunk's own keys (written by the QKV phase).
+__device__ void stage_keys(FlowSmem& sm, const FlowArgs& a, const FlowLayer& L, int b, int kh, int sub0, int kend,
+                           int part) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, kvd = a.Hkv * 64, L1 = a.Lp;
+  __nv_bfloat16* sk = sm.a + warp * (2 * kAttnSub * kAttnRs);
+  __nv_bfloat16* sv = sk + kAttnSub * kAttnRs;
+  for (int idx = lane; idx < kAttnSub * 8; idx += 32) {
+    const int r = idx >> 3, c = (idx & 7) * 8;
+    const int key = sub0 + r;
+    if ((part == kKeysPrefix && key >= L1) || (part == kKeysSuffix && key < L1)) continue;
+    const bool in = key < kend;
+    const __nv_bfloat16* kp = L.k1;
+    const __nv_bfloat16* vp = L.v1;
+    if (in) {
+      if (key < L1) {
+        const size_t off = (static_cast<size_t>(b) * a.Lp + key) * kvd + kh * 64 + c;
+        kp = L.k1 + off;
+        vp = L.v1 + off;
+      } else {
+        const size_t off = (static_cast<size_t>(b) * a.S + (key - L1)) * kvd + kh * 64 + c;
+        kp = a.ek + off;
+        vp = a.ev + off;
+      }
+    }
+    cp_async16(&sk[r * kAttnRs + c], kp, in ? 16 : 0);
+    cp_async16(&sv[r * kAttnRs + c], vp, in ? 16 : 0);
+  }
+  // padding flags of the prefix keys among them (16-byte runs; runs at or past the prefix read as 0)
+  if (part != kKeysSuffix && lane < kAttnSub / 16) {
+    const int key = sub0 + lane * 16;
+    const bool in = a.key_mask != nullptr && key < a.Lp;
+    const void* src = in ? static_cast<const void*>(a.key_mask + static_cast<size_t>(b) * a.key_mask_bs + key)
+                         : static_cast<const void*>(L.k1);
+    cp_async16(sm.kf + warp * kAttnSub + lane * 16, src, in ? 16 : 0);
+  }
+  cp_async_commit();
+}
+
+// Before the grid barrier that precedes attention: the prefix part of every warp's first keys of this CTA's
+// first attention task (the same decomposition as attention_phase)
+__device__ void attention_prestage(FlowSmem& sm, const FlowArgs& a, const FlowLayer& L) {
+  const int qtiles = (a.S + 15) / 16;
+  const int task = blockIdx.x;
+  if (task >= a.B * a.Hq * qtiles) return;
+  const int Lk = a.Lp + (L.cross ? 0 : a.S);
+  const int ks = ((Lk + kFlowWarps - 1) / kFlowWarps + 15) / 16 * 16;
+  const int warp = threadIdx.x >> 5;
+  const int h = (task / qtiles) % a.Hq, b = task / (qtiles * a.Hq), kh = h / (a.Hq / a.Hkv);
+  const int kbeg = warp * ks, kend = (kbeg + ks) < Lk ? (kbeg + ks) : Lk;
+  if (kbeg < kend) stage_keys(sm, a, L, b, kh, kbeg, kend, kKeysPrefix);
 }
 
 // attention of one expert layer; o -> ectx (bf16).  Each warp stages its keys / values 32 at a time in its
 // own slice of shared memory (asynchronous copies, all in flight at once) and reads MMA fragments with
 // ldmatrix; keys past the warp's range or past the last key are zero-filled and masked.
 __device__ void attention_phase(FlowSmem& sm, const FlowArgs& a, const FlowLayer& L) {
-  constexpr int kSub = 32, kRs = 72;  // keys staged at a time; bf16 row stride (conflict-free ldmatrix)
-  const int qd = a.Hq * 64, kvd = a.Hkv * 64, grp = a.Hq / a.Hkv;
+  constexpr int kSub = kAttnSub, kRs = kAttnRs;
+  const int qd = a.Hq * 64, grp = a.Hq / a.Hkv;
   const int qtiles = (a.S + 15) / 16;
   const int n_tasks = a.B * a.Hq * qtiles;
   const int L1 = a.Lp, Lk = L1 + (L.cross ? 0 : a.S);
   const int ks = ((Lk + kFlowWarps - 1) / kFlowWarps + 15) / 16 * 16;  // keys per warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  __nv_bfloat16* sk = sm.a + warp * (2 * kSub * kRs);
-  __nv_bfloat16* sv = sk + kSub * kRs;
+  const __nv_bfloat16* sk = sm.a + warp * (2 * kSub * kRs);
+  const __nv_bfloat16* sv = sk + kSub * kRs;
   for (int task = blockIdx.x; task < n_tasks; task += gridDim.x) {
     const int qt = task % qtiles, h = (task / qtiles) % a.Hq, b = task / (qtiles * a.Hq);
     const int kh = h / grp;
     const int s0 = qt * 16 + g, s1 = s0 + 8;
-    auto krow = [&](int key) -> const __nv_bfloat16* {
-      return key < L1 ? L.k1 + (static_cast<size_t>(b) * a.Lp + key) * kvd + kh * 64
-                      : a.ek + (static_cast<size_t>(b) * a.S + (key - L1)) * kvd + kh * 64;
-    };
-    auto vrow = [&](int key) -> const __nv_bfloat16* {
-      return key < L1 ? L.v1 + (static_cast<size_t>(b) * a.Lp + key) * kvd + kh * 64
-                      : a.ev + (static_cast<size_t>(b) * a.S + (key - L1)) * kvd + kh * 64;
-    };
     const int kbeg = warp * ks, kend = (kbeg + ks) < Lk ? (kbeg + ks) : Lk;
-    const uint8_t* kflags = a.key_mask ? a.key_mask + static_cast<size_t>(b) * a.key_mask_bs : nullptr;
-    uint8_t* kf = sm.kf + warp * kSub;
-    auto stage = [&](int sub0) {
-      for (int idx = lane; idx < kSub * 8; idx += 32) {
-        const int r = idx >> 3, c = (idx & 7) * 8;
-        const int key = sub0 + r;
-        const bool in = key < kend;
-        cp_async16(&sk[r * kRs + c], in ? krow(key) + c : L.k1, in ? 16 : 0);
-        cp_async16(&sv[r * kRs + c], in ? vrow(key) + c : L.v1, in ? 16 : 0);
-      }
-      // padding flags of the prefix keys among them (16-byte runs; runs at or past the prefix read as 0)
-      if (lane < kSub / 16) {
-        const int key = sub0 + lane * 16;
-        const bool in = kflags != nullptr && key < a.Lp;
-        cp_async16(kf + lane * 16, in ? static_cast<const void*>(kflags + key) : static_cast<const void*>(L.k1),
-                   in ? 16 : 0);
-      }
-      cp_async_commit();
-    };
-    if (kbeg < kend) stage(kbeg);  // in flight while the queries load
+    const uint8_t* kflags = a.key_mask;
+    const uint8_t* kf = sm.kf + warp * kSub;
+    // the first keys of the CTA's first task had their prefix part (and flags) staged before the grid barrier
+    // (attention_prestage): only the chunk's own keys are left
+    const bool prestaged = task == static_cast<int>(blockIdx.x);
+    if (kbeg < kend) stage_keys(sm, a, L, b, kh, kbeg, kend, prestaged ? kKeysSuffix : kKeysAll);
     uint32_t qa[4][4];
     {
       const __nv_bfloat16* q0 = a.eq + static_cast<size_t>(b * a.S + s0) * qd + h * 64;
@@ -527,7 +571,7 @@ __device__ void attention_phase(FlowSmem& sm, const FlowArgs& a, const FlowLayer
     for (int sub0 = kbeg; sub0 < kend; sub0 += kSub) {
       if (sub0 != kbeg) {
         __syncwarp();  // the previous keys' fragments have been read
-        stage(sub0);
+        stage_keys(sm, a, L, b, kh, sub0, kend, kKeysAll);
       }
       cp_async_wait<0>();
       __syncwarp();
@@ -675,59 +719,6 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
     a.xt_bf[i] = __float2bfloat16_rn(x);
   }
 
-  // Before each grid barrier, the next phase's weight rows of this CTA's first task (and, ahead of attention,
-  // its prefix keys / values) are prefetched into L2: they do not depend on the barrier.
-  enum { kPhIn, kPhTimeIn, kPhTimeOut, kPhQkv, kPhAttn, kPhO, kPhGateUp, kPhDown, kPhOut };
-  auto prefetch_phase = [&](int ph, int li) {
-    const int task = blockIdx.x;
-    const FlowLayer& L = a.layer[li < a.n_layers ? li : 0];
-    switch (ph) {
-      case kPhIn:
-        if (task < E / 16) prefetch_rows(a.w_in + static_cast<size_t>(task) * 16 * Ad, 16, Ad, Ad);
-        break;
-      case kPhTimeIn:
-        if (task < E / 16) prefetch_rows(a.w_tin + static_cast<size_t>(task) * 16 * a.ld_tin, 16, E, a.ld_tin);
-        break;
-      case kPhTimeOut:
-        if (task < E / 16) prefetch_rows(a.w_tout + static_cast<size_t>(task) * 16 * E, 16, E, E);
-        break;
-      case kPhQkv: {
-        const int q_tasks = 2 * a.Hq, kv_tasks = L.cross ? 0 : 2 * a.Hkv;
-        if (task >= q_tasks + 2 * kv_tasks) break;
-        const int seg = task < q_tasks ? 0 : (task < q_tasks + kv_tasks ? 1 : 2);
-        const int tt = seg == 0 ? task : (seg == 1 ? task - q_tasks : task - q_tasks - kv_tasks);
-        const int c0 = (tt >> 1) * 64 + (tt & 1) * 16;
-        const __nv_bfloat16* W = seg == 0 ? L.wq : (seg == 1 ? L.wk : L.wv);
-        prefetch_rows(W + static_cast<size_t>(c0) * E, 16, E, E);
-        prefetch_rows(W + static_cast<size_t>(c0 + 32) * E, 16, E, E);
-        break;
-      }
-      case kPhAttn: {
-        const int qtiles = (a.S + 15) / 16;
-        if (task >= a.B * a.Hq * qtiles) break;
-        const int h = (task / qtiles) % a.Hq, b = task / (qtiles * a.Hq), kh = h / (a.Hq / a.Hkv);
-        const size_t off = static_cast<size_t>(b) * a.Lp * kvd + kh * 64;
-        prefetch_rows(L.k1 + off, a.Lp, 64, kvd);
-        prefetch_rows(L.v1 + off, a.Lp, 64, kvd);
-        break;
-      }
-      case kPhO:
-        if (task < E / 16) prefetch_rows(L.wo + static_cast<size_t>(task) * 16 * qd, 16, qd, qd);
-        break;
-      case kPhGateUp:
-        if (task < a.mlp / 16) {
-          prefetch_rows(L.wg + static_cast<size_t>(task) * 16 * E, 16, E, E);
-          prefetch_rows(L.wu + static_cast<size_t>(task) * 16 * E, 16, E, E);
-        }
-        break;
-      case kPhDown:
-        if (task < E / 16) prefetch_rows(L.wd + static_cast<size_t>(task) * 16 * a.mlp, 16, a.mlp, a.mlp);
-        break;
-      default:
-        if (task < Ad / 16) prefetch_rows(a.w_out + static_cast<size_t>(task) * 16 * E, 16, E, E);
-        break;
-    }
-  };
   auto no_pre = [](int, int, int) { return make_uint4(0u, 0u, 0u, 0u); };
   // two bf16 biases of columns c, c + 1 (one word)
   auto bias_pre = [](const __nv_bfloat16* bias, int c) {
@@ -741,12 +732,11 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
            __fadd_rn(bf16_round(v[0][1]), hi(p.x)));
   };
 
-  prefetch_phase(kPhIn, 0);
   if (!grid_sync(a, sm)) return;
 
   for (int step = 0; step < a.n_steps; ++step) {
     // action_in_proj: a_emb = bf16(x_t . W_in^T + b)
-    gemm_phase<1>(
+    gemm_phase<1, 2>(
         a, sm, parity, M, a.xt_bf, Ad, nullptr, 0.f, E / 16, Ad,
         [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_in + static_cast<size_t>(task) * 16 * Ad; },
         [&](int task, int, int j) { return bias_pre(a.b_in, task * 16 + j); },
@@ -754,11 +744,10 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
           store2(a.a_emb + static_cast<size_t>(m) * E + task * 16 + j, __fadd_rn(v[0][0], lo(p.x)),
                  __fadd_rn(v[0][1], hi(p.x)));
         });
-    prefetch_phase(kPhTimeIn, 0);
     if (!grid_sync(a, sm)) return;
     // time MLP in: a_t = bf16(silu(bf16(a_emb . W_tin[:, :E]^T + c_step)))
     const float* cst = a.c_step + static_cast<size_t>(step) * E;
-    gemm_phase<1>(
+    gemm_phase<1, 2>(
         a, sm, parity, M, a.a_emb, E, nullptr, 0.f, E / 16, a.ld_tin,
         [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_tin + static_cast<size_t>(task) * 16 * a.ld_tin; },
         [&](int task, int, int j) {
@@ -770,10 +759,9 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
           const float x1 = bf16_round(__fadd_rn(v[0][1], __uint_as_float(p.y)));
           store2(a.a_t + static_cast<size_t>(m) * E + task * 16 + j, silu_f(x0), silu_f(x1));
         });
-    prefetch_phase(kPhTimeOut, 0);
     if (!grid_sync(a, sm)) return;
     // time MLP out: eh = bf16(a_t . W_tout^T + b)
-    gemm_phase<1>(
+    gemm_phase<1, 2>(
         a, sm, parity, M, a.a_t, E, nullptr, 0.f, E / 16, E,
         [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_tout + static_cast<size_t>(task) * 16 * E; },
         [&](int task, int, int j) { return bias_pre(a.b_tout, task * 16 + j); },
@@ -781,7 +769,6 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
           store2(a.eh + static_cast<size_t>(m) * E + task * 16 + j, __fadd_rn(v[0][0], lo(p.x)),
                  __fadd_rn(v[0][1], hi(p.x)));
         });
-    prefetch_phase(kPhQkv, 0);
     if (!grid_sync(a, sm)) return;
 
     for (int li = 0; li < a.n_layers; ++li) {
@@ -804,7 +791,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
           c0 = (tv >> 1) * 64 + (tv & 1) * 16;
         }
       };
-      gemm_phase<2>(
+      gemm_phase<2, 2>(
           a, sm, parity, M, a.eh, E, L.ln1, a.eps, q_tasks + 2 * kv_tasks, E,
           [&](int task, const __nv_bfloat16* (&w)[2]) {
             int seg, c0;
@@ -846,23 +833,21 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
             store2(out + static_cast<size_t>(m) * ld + c0 + j, x1a, x1b);
             store2(out + static_cast<size_t>(m) * ld + c0 + 32 + j, x2a, x2b);
           });
-      prefetch_phase(kPhAttn, li);
+      attention_prestage(sm, a, L);  // prefix keys / values do not depend on this phase
       if (!grid_sync(a, sm)) return;
       attention_phase(sm, a, L);
-      prefetch_phase(kPhO, li);
       if (!grid_sync(a, sm)) return;
       // o_proj + residual: eh = bf16(bf16(ectx . W_o^T) + eh)
-      gemm_phase<1>(
+      gemm_phase<1, 2>(
           a, sm, parity, M, a.ectx, qd, nullptr, 0.f, E / 16, qd,
           [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = L.wo + static_cast<size_t>(task) * 16 * qd; },
           [&](int task, int m, int j) {
             return make_uint4(ldcg_u32(a.eh + static_cast<size_t>(m) * E + task * 16 + j), 0u, 0u, 0u);
           },
           [&](int task, int m, int j, float (&v)[1][2], const uint4& p) { resid_store(task * 16 + j, m, v, p); });
-      prefetch_phase(kPhGateUp, li);
       if (!grid_sync(a, sm)) return;
       // gate / up + SiLU gate: emlp = bf16(bf16(silu(bf16(gate))) * bf16(up))
-      gemm_phase<2>(
+      gemm_phase<2, 4>(
           a, sm, parity, M, a.eh, E, L.ln2, a.eps, a.mlp / 16, E,
           [&](int task, const __nv_bfloat16* (&w)[2]) {
             w[0] = L.wg + static_cast<size_t>(task) * 16 * E;
@@ -875,21 +860,19 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
             store2(a.emlp + static_cast<size_t>(m) * a.mlp + task * 16 + j, __fmul_rn(g0, bf16_round(v[1][0])),
                    __fmul_rn(g1, bf16_round(v[1][1])));
           });
-      prefetch_phase(kPhDown, li);
       if (!grid_sync(a, sm)) return;
       // down_proj + residual
-      gemm_phase<1>(
+      gemm_phase<1, 2>(
           a, sm, parity, M, a.emlp, a.mlp, nullptr, 0.f, E / 16, a.mlp,
           [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = L.wd + static_cast<size_t>(task) * 16 * a.mlp; },
           [&](int task, int m, int j) {
             return make_uint4(ldcg_u32(a.eh + static_cast<size_t>(m) * E + task * 16 + j), 0u, 0u, 0u);
           },
           [&](int task, int m, int j, float (&v)[1][2], const uint4& p) { resid_store(task * 16 + j, m, v, p); });
-      prefetch_phase(li + 1 < a.n_layers ? kPhQkv : kPhOut, li + 1);
       if (!grid_sync(a, sm)) return;
     }
     // final RMSNorm + action_out_proj + Euler: x_t += dt * (y . W_out^T + b), x_t_bf16 = bf16(x_t)
-    gemm_phase<1>(
+    gemm_phase<1, 2>(
         a, sm, parity, M, a.eh, E, a.ln_f, a.eps, Ad / 16, E,
         [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_out + static_cast<size_t>(task) * 16 * E; },
         [&](int task, int m, int j) {
@@ -905,7 +888,6 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
           *reinterpret_cast<float2*>(a.xt + i) = make_float2(x0, x1);
           store2(a.xt_bf + i, x0, x1);
         });
-    prefetch_phase(kPhIn, 0);
     if (!grid_sync(a, sm)) return;
   }
 }
