@@ -66,3 +66,34 @@ def test_argument_errors_are_reported_without_a_gpu():
     assert lib.svla_quantize_smooth(None, 8, None, 1.0, None, 8, 1, 8, None) == 1
     assert lib.svla_sq_linear_w8a8(None, None, 1.0, None, None, None, 4, 16, 16, None, None, 0, None) == 1
     assert b"workspace" in lib.svla_last_error()
+
+
+def test_flow_arguments_are_checked_before_any_launch():
+    """svla_flow rejects what the persistent kernel cannot take (more than 64 action rows, widths that are not
+    multiples of 16, too many layers, missing pointers) with status 1, without touching the GPU."""
+    import ctypes
+    lib = _lib.lib()
+    assert lib.svla_flow(None, None) == 1
+
+    def desc(**kw):
+        d = _lib.FlowDesc()
+        d.batch, d.chunk, d.prefix_len, d.hidden, d.action_dim = 1, 50, 177, 720, 32
+        d.heads, d.kv_heads, d.mlp, d.n_layers, d.num_steps = 15, 5, 2048, 16, 10
+        d.ld_time_in, d.max_pos, d.eps = 1440, 227, 1e-5
+        for k, v in kw.items():
+            setattr(d, k, v)
+        return d
+
+    cases = [
+        (dict(batch=2), "batch * chunk"),          # 100 rows
+        (dict(hidden=712), "hidden"),              # not a multiple of 16
+        (dict(mlp=2040), "multiples of 16"),
+        (dict(kv_heads=4), "kv_heads"),            # 15 heads over 4 kv heads
+        (dict(n_layers=33), "n_layers"),
+        (dict(ld_time_in=700), "ld_time_in"),
+        (dict(), "null pointer"),                  # no buffers at all
+    ]
+    for kw, word in cases:
+        d = desc(**kw)
+        assert lib.svla_flow(ctypes.byref(d), None) == 1, kw
+        assert word.encode() in lib.svla_last_error(), (kw, lib.svla_last_error())
