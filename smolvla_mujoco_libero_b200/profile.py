@@ -129,7 +129,15 @@ def op_attn(a) -> dict:
         full = torch.zeros(a.batch, a.lq, ld, dtype=torch.uint8)
         full[:, :, : a.lk - a.lk // 10] = 1
         mask = full.to(dev)[:, :, : a.lk]
-    ms = time_op(lambda: ops.attention(q, k, v, a.heads, a.kv_heads, mask=mask), a.iters)
+    key_mask = None
+    if a.prefix > 0:
+        # the action expert's structured mask: padding flags over the first `prefix` keys (last 10% off),
+        # causal order over the rest
+        kf = torch.zeros(a.batch, (a.prefix + 15) // 16 * 16, dtype=torch.uint8)
+        kf[:, : a.prefix - a.prefix // 10] = 1
+        key_mask = kf.to(dev)
+    ms = time_op(lambda: ops.attention(q, k, v, a.heads, a.kv_heads, mask=mask, key_mask=key_mask,
+                                       mask_keys=a.prefix), a.iters)
     flops = 4.0 * a.batch * a.heads * a.lq * a.lk * 64
     # phase clock stamps of one CTA of the tcgen05 kernel (when that kernel runs)
     from . import _lib as L
@@ -142,7 +150,7 @@ def op_attn(a) -> dict:
     c = dbg.cpu().tolist()
     phases = {i: c[i] - c[0] for i in range(96) if c[i]} if c[0] else {}
     return {"op": "attn", "batch": a.batch, "lq": a.lq, "lk": a.lk, "heads": a.heads, "kv_heads": a.kv_heads,
-            "mask": a.mask, "mask_ld": a.mask_ld, "ms": ms, "tflops_best": flops / (min(ms) / 1e3) / 1e12,
+            "mask": a.mask, "mask_ld": a.mask_ld, "prefix": a.prefix, "ms": ms, "tflops_best": flops / (min(ms) / 1e3) / 1e12,
             "cta_cycles": phases}
 
 
@@ -197,6 +205,8 @@ def main() -> None:
     ap.add_argument("--kv-heads", type=int, default=12)
     ap.add_argument("--mask", action="store_true")
     ap.add_argument("--mask-ld", type=int, default=0)
+    ap.add_argument("--prefix", type=int, default=0, help="--op attn: structured mask, key padding over this many "
+                    "prefix keys and causal order over the rest")
     ap.add_argument("--summarize", default=None, help="print the per-kernel summary of an ncu launch-list CSV")
     a = ap.parse_args()
     if a.summarize:
