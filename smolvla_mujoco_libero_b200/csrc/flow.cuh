@@ -9,14 +9,17 @@
 // the ~84 phases of one step run back to back inside one cooperative grid (one CTA per SM), separated by
 // grid barriers, so a phase costs a barrier instead of a kernel launch with its prologue and drain.
 //
-// Phases are GEMMs of the rows against 16-column slices of a weight (tasks spread over the CTAs; the 8 warps
-// of a CTA split K and add their partial tiles in a fixed order), mma.sync m16n8k16 bf16 with fp32
-// accumulators, the A rows staged in shared memory (RMSNorm applied while staging, by the same row routine
-// as the stand-alone norm kernel), weights read straight from global memory.  Epilogues round exactly where
-// the GEMM kernel's epilogues do (bias, SiLU, RoPE, residual, SiLU-gate, Euler update), so the only
-// difference from the per-layer launch list is the fp32 summation order inside each dot product.
+// Phases are GEMMs of row blocks (32 rows; 64 for gate/up) against 16-column slices of a weight (a task = a
+// slice x a row block, tasks spread over the CTAs; the 8 warps of a CTA split K and add their partial tiles in
+// a fixed order), mma.sync m16n8k16 bf16 with fp32 accumulators, the A rows staged in shared memory by bulk
+// copies (RMSNorm applied there with the stand-alone norm kernel's arithmetic and operation order), weights
+// read straight from global memory.  Epilogues round exactly where the GEMM kernel's epilogues do (bias, SiLU,
+// RoPE, residual, SiLU-gate, Euler update), so the only difference from the per-layer launch list is the
+// fp32 summation order inside each dot product.
 // Attention: one CTA per (sample, query head, 16-query tile); the 8 warps take consecutive key ranges with
-// an online softmax each and their partial (max, sum, O) are merged in a fixed order.
+// an online softmax each and their partial (max, sum, O) are merged in a fixed order.  The prefix keys /
+// values of a CTA's first task are copied into shared memory before the grid barrier that precedes the
+// phase (they are final before the kernel starts).
 //
 // Grid barrier: a monotonic 64-bit arrival counter in a caller-provided 8-byte buffer (zero before first use;
 // every completed launch leaves it at a multiple of the grid size).  Every wait is bounded: a barrier that
@@ -37,9 +40,8 @@ constexpr int kFlowMaxLayers = 32;
 constexpr int kFlowThreads = 256;
 constexpr int kFlowWarps = kFlowThreads / 32;
 constexpr int kFlowRows = 64;             // most action rows per call (four m16 tiles)
-constexpr int kFlowMT = kFlowRows / 16;
-constexpr int kFlowKC = 1024;             // A columns staged in shared memory at a time
-constexpr int kFlowLda = kFlowKC + 16;    // largest staged row stride (elements)
+constexpr int kFlowKC = 1024;             // A columns staged for 64 rows (twice as many for 32-row blocks)
+constexpr int kFlowLda = kFlowKC + 16;    // largest staged row stride (elements) of 64 rows
 constexpr int kFlowRedStride = 40;        // fp32 row stride of the per-warp partial tiles (conflict-free)
 constexpr int kFlowAttnStride = 72;       // fp32 row stride of the per-warp attention partials
 constexpr int kErrFlowBarrier = 103;
@@ -136,10 +138,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ uint32_t ldcg_u32(const __nv_bfloat16* p) {
   return __ldcg(reinterpret_cast<const unsigned int*>(p));
 }
-__device__ __forceinline__ uint32_t ldcg_u16(const __nv_bfloat16* p) {
-  return __ldcg(reinterpret_cast<const unsigned short*>(p));
-}
-__device__ __forceinline__ float bf(const __nv_bfloat16* p, int i) { return __bfloat162float(p[i]); }
 __device__ __forceinline__ void store2(__nv_bfloat16* p, float x, float y) {
   *reinterpret_cast<uint32_t*>(p) = pack_bf16_rn(x, y);
 }
