@@ -342,6 +342,7 @@ def main():
     # ---------------- roofline of the dominant kernel (the SigLIP attention: the largest share of the batch-64
     # launch list) and of the largest GEMM, each timed live on its own with the step's own arguments
     roof = attention_roofline(runner, peaks)
+    roof_b1 = flow_roofline(r1, peaks)
     roof_gemm = dominant_kernel_roofline(runner, peaks)
 
     line = {
@@ -355,6 +356,7 @@ def main():
         "gpu_launches": launches,
         "roofline": roof,
         "roofline_gemm": roof_gemm,
+        "roofline_batch1": roof_b1,
         "clocks": clk,
     }
     if rank == 0 and not args.no_cpu_baseline:
@@ -416,6 +418,39 @@ def attention_roofline(runner, peaks):
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": traffic, "kernel": f"attention_tc B={d.batch} Hq={d.hq} Lq={d.lq} Lk={d.l1} d=64",
             "ms_per_launch": ms, "flops_per_launch": flops, "peak_source": src}
+
+
+def flow_roofline(runner, peaks):
+    """The batch-1 call's dominant kernel (svla_flow: the whole flow-matching loop, 64% of the batch-1 launch
+    list) timed on its own with CUDA events on the launch stream.  Algorithmic bytes: the expert's bf16 weights
+    read once per flow step (they exceed L2) plus the prefix K/V once."""
+    import ctypes
+
+    from smolvla_mujoco_libero_b200 import _lib as L
+    from smolvla_mujoco_libero_b200.config import EXPERT
+    flows = [a[0] for fn, a in runner.launches if fn is L.lib().svla_flow]
+    if not flows:
+        return None
+    d, c, w = flows[0], runner.cfg, runner.w
+    E = c.expert_hidden
+    per_step = 0
+    for name, p in w.lin.items():
+        if name.startswith(EXPERT + ".layers."):
+            if c.is_cross_layer(int(name.split(".layers.")[1].split(".")[0])) and (".k_proj" in name or ".v_proj" in name):
+                continue  # cross layers read the precomputed K/V projections, not these weights
+            per_step += p.n * p.k * 2
+    per_step += (E * c.max_action_dim * 2) * 2 + E * E * 2 * 2  # action in / out, time MLP (in: first E columns)
+    kv = c.expert_layers * c.prefix_len * c.kv_dim * 2 * 2
+    nbytes = per_step * c.num_steps + kv
+    stream = torch.cuda.current_stream().cuda_stream
+    fn = L.lib().svla_flow
+    ms = time_kernel(lambda: fn(ctypes.byref(d), stream), iters=5)
+    achieved = nbytes / (ms / 1e3) / 1e9
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    src = "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6.65 TB/s"
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": profile_traffic("flow_kernel_b1"), "kernel": f"flow_kernel batch {d.batch} x {c.num_steps} steps",
+            "ms_per_launch": ms, "bytes_per_launch": nbytes, "peak_source": src}
 
 
 def dominant_kernel_roofline(runner, peaks):
