@@ -152,6 +152,20 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
   const float z = __fmul_rn(x, __fmaf_rn(c1, __fmul_rn(x, x), c0));
   return __fmul_rn(x, rcp_approx(__fadd_rn(1.0f, ex2_approx(z))));
 }
+// Two lanes of silu_f / gelu_tanh_f through the packed fp32 pipe: every packed lane rounds exactly as the
+// scalar op it replaces, so the results are bit-identical to the scalar forms above.
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 silu_f2(float2 x) {
+  const float2 z = __fmul2_rn(x, f2(-1.4426950408889634f));
+  const float2 d = __fadd2_rn(f2(1.0f), make_float2(ex2_approx(z.x), ex2_approx(z.y)));
+  return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+}
+__device__ __forceinline__ float2 gelu_tanh_f2(float2 x) {
+  constexpr float c0 = -2.302208198f, c1 = -0.1029432396f;
+  const float2 z = __fmul2_rn(x, __ffma2_rn(f2(c1), __fmul2_rn(x, x), f2(c0)));
+  const float2 d = __fadd2_rn(f2(1.0f), make_float2(ex2_approx(z.x), ex2_approx(z.y)));
+  return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+}
 
 template <int BN, int P>
 __device__ __forceinline__ void tile_coord(const GemmArgs& a, int t, int& si, int& m0, int& n0) {
@@ -211,22 +225,39 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
     float sc[16], bi[16];
     col_consts(set, nb, sc, bi);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float x;
+    for (int j = 0; j < 16; j += 2) {
+      float2 x;
       if constexpr (KIND == Kind::I8)
-        x = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(raw[j])), g.act_scale), sc[j]);
+        x = __fmul2_rn(__fmul2_rn(make_float2(static_cast<float>(static_cast<int>(raw[j])),
+                                              static_cast<float>(static_cast<int>(raw[j + 1]))),
+                                  f2(g.act_scale)),
+                       make_float2(sc[j], sc[j + 1]));
       else
-        x = __uint_as_float(raw[j]);
-      v[j] = __fadd_rn(x, bi[j]);
+        x = make_float2(__uint_as_float(raw[j]), __uint_as_float(raw[j + 1]));
+      const float2 y = __fadd2_rn(x, make_float2(bi[j], bi[j + 1]));
+      v[j] = y.x;
+      v[j + 1] = y.y;
     }
     if (g.bias_f32 != nullptr) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], g.bias_f32[nb + j]);
+      for (int j = 0; j < 16; j += 2) {
+        const float2 y = __fadd2_rn(make_float2(v[j], v[j + 1]), make_float2(g.bias_f32[nb + j], g.bias_f32[nb + j + 1]));
+        v[j] = y.x;
+        v[j + 1] = y.y;
+      }
     }
   };
   auto round16 = [](float (&v)[16]) {
 #pragma unroll
     for (int j = 0; j < 16; j += 2) bf16_round2(v[j], v[j + 1]);
+  };
+  auto map2 = [](float (&v)[16], auto fn) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const float2 y = fn(make_float2(v[j], v[j + 1]));
+      v[j] = y.x;
+      v[j + 1] = y.y;
+    }
   };
   auto store_bf16_16 = [](__nv_bfloat16* o, const float (&v)[16]) {
     uint32_t pk[8];
@@ -345,15 +376,17 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
             dequant16(args.seg[1], 1, &r2[u], nb, uv);
             round16(v);
             round16(uv);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = silu_f(v[j]);
+            map2(v, [](float2 x) { return silu_f2(x); });
             round16(v);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], uv[j]);
+            for (int j = 0; j < 16; j += 2) {
+              const float2 y = __fmul2_rn(make_float2(v[j], v[j + 1]), make_float2(uv[j], uv[j + 1]));
+              v[j] = y.x;
+              v[j + 1] = y.y;
+            }
           } else if constexpr (EPI == Epi::SiluBf16) {
             round16(v);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = silu_f(v[j]);
+            map2(v, [](float2 x) { return silu_f2(x); });
           } else if constexpr (EPI == Epi::Resid) {
             round16(v);
             const int4 ra4 = res[u / 8], rb4 = res[u / 8 + 1];
@@ -363,13 +396,14 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
                                     static_cast<uint32_t>(rb4.z), static_cast<uint32_t>(rb4.w)};
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              v[2 * j] = __fadd_rn(v[2 * j], __uint_as_float(rw[j] << 16));
-              v[2 * j + 1] = __fadd_rn(v[2 * j + 1], __uint_as_float(rw[j] & 0xFFFF0000u));
+              const float2 y = __fadd2_rn(make_float2(v[2 * j], v[2 * j + 1]),
+                                          make_float2(__uint_as_float(rw[j] << 16), __uint_as_float(rw[j] & 0xFFFF0000u)));
+              v[2 * j] = y.x;
+              v[2 * j + 1] = y.y;
             }
           } else if constexpr (EPI == Epi::GeluQuant) {
             round16(v);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_f(v[j]);
+            map2(v, [](float2 x) { return gelu_tanh_f2(x); });
             round16(v);
             if (args.qout != nullptr) {
               uint32_t w[4] = {0u, 0u, 0u, 0u};

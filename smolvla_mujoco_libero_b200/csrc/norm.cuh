@@ -107,18 +107,34 @@ __device__ __forceinline__ void norm_quant_row(const NormQuantArgs& a, int m, in
     if constexpr (LAYERNORM) {
       const int4 br = *reinterpret_cast<const int4*>(a.b + k);
       const __nv_bfloat16* bh = reinterpret_cast<const __nv_bfloat16*>(&br);
+      // pairs through the packed fp32 pipe, each lane rounded exactly as the scalar op (x - mean is
+      // x + (-mean), the same rounding)
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        y[j] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i][j], mean), rstd), __bfloat162float(wh[j])),
-                         __bfloat162float(bh[j]));
+      for (int j = 0; j < 8; j += 2) {
+        const float2 d = __fadd2_rn(make_float2(v[i][j], v[i][j + 1]), make_float2(-mean, -mean));
+        const float2 t = __fmul2_rn(__fmul2_rn(d, make_float2(rstd, rstd)),
+                                    make_float2(__bfloat162float(wh[j]), __bfloat162float(wh[j + 1])));
+        const float2 r = __fadd2_rn(t, make_float2(__bfloat162float(bh[j]), __bfloat162float(bh[j + 1])));
+        y[j] = r.x;
+        y[j + 1] = r.y;
+      }
     } else {
       float h[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = __fmul_rn(v[i][j], rstd);
+      for (int j = 0; j < 8; j += 2) {
+        const float2 t = __fmul2_rn(make_float2(v[i][j], v[i][j + 1]), make_float2(rstd, rstd));
+        h[j] = t.x;
+        h[j + 1] = t.y;
+      }
 #pragma unroll
       for (int j = 0; j < 8; j += 2) bf16_round2(h[j], h[j + 1]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__bfloat162float(wh[j]), h[j]);
+      for (int j = 0; j < 8; j += 2) {
+        const float2 t = __fmul2_rn(make_float2(__bfloat162float(wh[j]), __bfloat162float(wh[j + 1])),
+                                    make_float2(h[j], h[j + 1]));
+        y[j] = t.x;
+        y[j + 1] = t.y;
+      }
     }
 #pragma unroll
     for (int j = 0; j < 8; j += 2) bf16_round2(y[j], y[j + 1]);

@@ -295,14 +295,25 @@ __device__ __forceinline__ int8_t smooth_quant_fast(float x, float s, float rs, 
 // so only values within 2^-12 (5x that) of a .5 boundary can round differently: bit e of the returned
 // `slow` mask (bit 4k+e of the caller's group) marks those, and the caller recomputes them with smooth_quant.
 __device__ __forceinline__ uint32_t smooth_quant4_fast(const float* x, float4 rs, float ra, uint32_t& slow, int bit0) {
-  const float r4[4] = {rs.x, rs.y, rs.z, rs.w};
+  // Pairs through the packed fp32 pipe (FMUL2 / FADD2 / FFMA2): each lane of a packed op is the IEEE
+  // round-to-nearest result of the scalar op, so y, t and the fraction are bit-identical to the scalar form
+  // fmin(fmax((x * rs) * ra)), t = y + C, y - (t - C); t - C is written t + (-C) and y - r as fma(r, -1, y),
+  // both exactly the same roundings.
+  constexpr float kC = 12582912.0f;
+  const float2 ra2 = make_float2(ra, ra);
+  float2 y[2] = {__fmul2_rn(__fmul2_rn(make_float2(x[0], x[1]), make_float2(rs.x, rs.y)), ra2),
+                 __fmul2_rn(__fmul2_rn(make_float2(x[2], x[3]), make_float2(rs.z, rs.w)), ra2)};
   uint32_t b[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float y = fminf(fmaxf(__fmul_rn(__fmul_rn(x[e], r4[e]), ra), -128.0f), 127.0f);
-    const float t = __fadd_rn(y, 12582912.0f);
-    if (fabsf(__fsub_rn(y, __fsub_rn(t, 12582912.0f))) > 0.5f - 0.000244140625f) slow |= 1u << (bit0 + e);
-    b[e] = __float_as_uint(t);
+  for (int h = 0; h < 2; ++h) {
+    y[h].x = fminf(fmaxf(y[h].x, -128.0f), 127.0f);
+    y[h].y = fminf(fmaxf(y[h].y, -128.0f), 127.0f);
+    const float2 t = __fadd2_rn(y[h], make_float2(kC, kC));
+    const float2 f = __ffma2_rn(__fadd2_rn(t, make_float2(-kC, -kC)), make_float2(-1.0f, -1.0f), y[h]);
+    if (fabsf(f.x) > 0.5f - 0.000244140625f) slow |= 1u << (bit0 + 2 * h);
+    if (fabsf(f.y) > 0.5f - 0.000244140625f) slow |= 1u << (bit0 + 2 * h + 1);
+    b[2 * h] = __float_as_uint(t.x);
+    b[2 * h + 1] = __float_as_uint(t.y);
   }
   return __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
 }
