@@ -728,33 +728,61 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
     float* const_base = reinterpret_cast<float*>(smem + S::kConstOff);
     uint32_t lt = 0;
     bool ok = true;
+    // Per-tile column constants (weight scale and bias of each linear of the tile, and for GeluQuant the
+    // next linear's smooth vector and its reciprocal), one column per thread (BN <= epilogue threads):
+    // fetched from global memory into registers one tile ahead, so their latency hides behind the current
+    // tile's epilogue, and written into the constant buffer of the tile's parity.
+    static_assert(BN <= 32 * kEpiWarps, "one column of constants per epilogue thread");
+    float cpre[S::kConstArrays];
+    auto fetch_consts = [&](int t) {
+      if (t >= n_tiles_total || etid >= BN) return;
+      int si, m0, n0;
+      tile_coord<BN, P>(args, t, si, m0, n0);
+      const int n = n0 + etid;
+#pragma unroll
+      for (int set = 0; set < P; ++set) {
+        const GemmSeg& g = args.seg[P == 1 ? si : set];
+        const bool in = n < g.n;
+        cpre[2 * set] = (KIND == Kind::I8 && g.wscale && in) ? g.wscale[n] : 1.0f;
+        cpre[2 * set + 1] = (g.bias && in) ? __bfloat162float(g.bias[n]) : -0.0f;  // x + -0 == x for every x
+      }
+      if constexpr (EPI == Epi::GeluQuant) {
+        const bool in = args.qout && n < args.seg[si].n;
+        cpre[4] = in ? args.q_smooth[n] : 1.0f;
+        cpre[5] = (in && args.q_rsmooth) ? args.q_rsmooth[n] : 1.0f;
+      }
+    };
+    auto put_consts = [&](int t, uint32_t buf) {
+      if (t >= n_tiles_total || etid >= BN) return;
+      float* cst = const_base + buf * S::kConstArrays * BN;
+#pragma unroll
+      for (int set = 0; set < P; ++set) {
+        cst[(2 * set) * BN + etid] = cpre[2 * set];
+        cst[(2 * set + 1) * BN + etid] = cpre[2 * set + 1];
+      }
+      if constexpr (EPI == Epi::GeluQuant) {
+        cst[4 * BN + etid] = cpre[4];
+        cst[5 * BN + etid] = cpre[5];
+      }
+    };
+    // scales and biases are written with the weights: when those predate the previous kernel the first
+    // tile's constants are requested before waiting for it
+    if (args.weights_resident) fetch_consts(blockIdx.x);
     pdl_wait();  // residuals / outputs may be touched by the previous kernel
+    if (!args.weights_resident) fetch_consts(blockIdx.x);
+    put_consts(blockIdx.x, 0);
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+    if (etid == 0) stamp(args.dbg, 6);
     // Every epilogue warp runs every iteration (also after a failed wait) so that the named barrier
     // below is reached the same number of times by all of them.
     for (int t = blockIdx.x; t < n_tiles_total; t += gridDim.x, ++lt) {
       const uint32_t ab = lt & 1, use = lt >> 1;
       int si, m0, n0;
       tile_coord<BN, P>(args, t, si, m0, n0);
-      // stage this tile's column constants (double-buffered by tile parity)
-      float* cst = const_base + ab * S::kConstArrays * BN;
-      for (int c = etid; c < BN; c += 32 * kEpiWarps) {
-#pragma unroll
-        for (int set = 0; set < P; ++set) {
-          const GemmSeg& g = args.seg[P == 1 ? si : set];
-          const int n = n0 + c;
-          const bool in = n < g.n;
-          cst[(2 * set) * BN + c] = (KIND == Kind::I8 && g.wscale && in) ? g.wscale[n] : 1.0f;
-          cst[(2 * set + 1) * BN + c] = (g.bias && in) ? __bfloat162float(g.bias[n]) : -0.0f;  // x + -0 == x for every x
-        }
-        if constexpr (EPI == Epi::GeluQuant) {
-          const int n = n0 + c;
-          const bool in = args.qout && n < args.seg[si].n;
-          cst[4 * BN + c] = in ? args.q_smooth[n] : 1.0f;
-          cst[5 * BN + c] = (in && args.q_rsmooth) ? args.q_rsmooth[n] : 1.0f;
-        }
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
-      if (lt == 0 && etid == 0) stamp(args.dbg, 6);
+      // this tile's constants are in buffer ab (written before the barrier that ended the previous
+      // iteration); the next tile's are requested now
+      const float* cst = const_base + ab * S::kConstArrays * BN;
+      fetch_consts(t + gridDim.x);
       bool acc_waited = false, acc_ok = true;
       auto wait_acc = [&]() -> bool {
         if (acc_waited) return acc_ok;
@@ -776,6 +804,10 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);
       ok = ok_t;
+      // the other buffer was last read by the previous tile, which every warp finished before the barrier
+      // that ended the previous iteration
+      put_consts(t + gridDim.x, ab ^ 1u);
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
     }
   } else if constexpr (T::kConvert) {
     // ---------------- W8A16 weight conversion, warps 10..13, all four on every stage:
