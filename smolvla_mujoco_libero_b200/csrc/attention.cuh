@@ -95,7 +95,11 @@ struct Smem {
   uint8_t m[2][kRows * kKeys];
 };
 
+// Mask kinds, a template parameter of the kernel so that the per-score mask test is resolved at compile time
+enum MaskKind : int { kMaskNone = 0, kMaskBytes = 1, kMaskStructured = 2 };
+
 // issue the cp.async copies of key tile `tile` (keys key0 .. key0+63) of kv head kh into stage st
+template <int MK>
 __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st, int b, int kh, int key0) {
   const int Lk = a.L1 + a.L2;
   for (int idx = threadIdx.x; idx < kKeys * 8; idx += blockDim.x) {
@@ -120,7 +124,7 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st
     cp_async16(&sm.k[st][r * kPad + c], kp, bytes);
     cp_async16(&sm.v[st][r * kPad + c], vp, bytes);
   }
-  if (a.key_mask) {
+  if constexpr (MK == kMaskStructured) {
     // structured mask: one row of key flags (keys below mask_keys) for every query of the tile
     if (threadIdx.x < 4) {
       const int c = threadIdx.x * 16, key = key0 + c;
@@ -138,7 +142,7 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st
         for (int j = 0; j < 16; ++j) dst[j] = (key + j < kend) ? src[key + j] : 0;
       }
     }
-  } else if (a.mask) {
+  } else if constexpr (MK == kMaskBytes) {
     // mask bytes [128 rows x 64 keys]; rows past Lq and keys past Lk are left as whatever they read:
     // the scores of keys past Lk are forced to -inf and rows past Lq are never stored.  A 16-key run is
     // one 16-byte copy when it is aligned and lies inside the row's storage (the row stride covers Lk
@@ -162,7 +166,8 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& a, Smem& sm, int st
 }
 }  // namespace attn_detail
 
-__global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const AttnArgs a) {
+template <int MK>
+__global__ void __launch_bounds__(attn_detail::kRows * 2, 2) attention_kernel(const AttnArgs a) {
   pdl_wait();
   pdl_trigger();
   using namespace attn_detail;
@@ -187,7 +192,7 @@ __global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const
       cp_async16(&sm.q[r * kPad + c], qb + static_cast<size_t>(query) * a.q_rs + hg * kD + c, in ? 16 : 0);
     }
   }
-  load_kv_tile(a, sm, 0, b, kh, 0);
+  load_kv_tile<MK>(a, sm, 0, b, kh, 0);
   cp_async_commit();
 
   uint32_t qa[4][4];
@@ -206,7 +211,7 @@ __global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const
   for (int tile = 0; tile < n_tiles; ++tile) {
     const int st = tile & 1;
     if (tile + 1 < n_tiles) {
-      load_kv_tile(a, sm, st ^ 1, b, kh, (tile + 1) * kKeys);
+      load_kv_tile<MK>(a, sm, st ^ 1, b, kh, (tile + 1) * kKeys);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -240,22 +245,33 @@ __global__ void __launch_bounds__(attn_detail::kRows * 2) attention_kernel(const
     }
     // ---- scale, mask, online softmax (rows g and g + 8 of this warp)
     float tmax[2] = {-INFINITY, -INFINITY};
+    // structured mask: this thread's 16 key flags (keys n*8 + 2t and n*8 + 2t + 1, two per 16-bit load) as
+    // bits 2n and 2n + 1 of one word
+    uint32_t kf = 0u;
+    if constexpr (MK == kMaskStructured) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const uint32_t w = *reinterpret_cast<const uint16_t*>(&sm.m[st][n * 8 + 2 * t]);
+        kf |= ((w & 0xFFu) != 0u ? 1u : 0u) << (2 * n);
+        kf |= ((w >> 8) != 0u ? 1u : 0u) << (2 * n + 1);
+      }
+    }
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int kc = n * 8 + 2 * t + (e & 1);  // key inside the tile
         const int key = key0 + kc;
-        const int rl = wr + g + ((e >> 1) << 3);  // row inside the CTA tile
         float v = __fmul_rn(s[n][e], a.scale);
-        if (key >= Lk) {
-          v = -INFINITY;  // not a key at all
-        } else if (a.key_mask) {
-          const bool allowed = (key < a.mask_keys) ? (sm.m[st][kc] != 0) : (key - a.mask_keys <= query[e >> 1]);
-          if (!allowed) v = kMaskedScore;
-        } else if (a.mask && sm.m[st][rl * kKeys + kc] == 0) {
-          v = kMaskedScore;
+        bool allowed = true;
+        if constexpr (MK == kMaskStructured) {
+          allowed = (key < a.mask_keys) ? ((kf >> (2 * n + (e & 1))) & 1u) != 0u : (key - a.mask_keys <= query[e >> 1]);
+        } else if constexpr (MK == kMaskBytes) {
+          const int rl = wr + g + ((e >> 1) << 3);  // row inside the CTA tile
+          allowed = sm.m[st][rl * kKeys + kc] != 0;
         }
+        if (!allowed) v = kMaskedScore;
+        if (key >= Lk) v = -INFINITY;  // not a key at all
         s[n][e] = v;
         tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
       }

@@ -652,8 +652,11 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
   if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
   const int smem = static_cast<int>(sizeof(attn_detail::Smem));
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    for (auto kern : {attention_kernel<attn_detail::kMaskNone>, attention_kernel<attn_detail::kMaskBytes>,
+                      attention_kernel<attn_detail::kMaskStructured>}) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    }
     configured[dev] = true;
   }
   // packed rows of one kv head (its query heads' queries) split into equal tiles of 16 x warps rows
@@ -662,7 +665,14 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
   if (tiles > 65535) return fail(SVLA_ERR_ARG, "svla_attention: too many query rows");
   a.rows = static_cast<int>(((rows + tiles - 1) / tiles + 15) / 16 * 16);
   dim3 grid(static_cast<unsigned>(tiles), d->hkv, d->batch);
-  return launch(attention_kernel, dim3(grid), dim3(a.rows * 2), smem, cs(stream), "attention_kernel", a);
+  if (a.key_mask)
+    return launch(attention_kernel<attn_detail::kMaskStructured>, dim3(grid), dim3(a.rows * 2), smem, cs(stream),
+                  "attention_kernel", a);
+  if (a.mask)
+    return launch(attention_kernel<attn_detail::kMaskBytes>, dim3(grid), dim3(a.rows * 2), smem, cs(stream),
+                  "attention_kernel", a);
+  return launch(attention_kernel<attn_detail::kMaskNone>, dim3(grid), dim3(a.rows * 2), smem, cs(stream),
+                "attention_kernel", a);
 }
 
 int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* pos, void* q_out, void* k_out,
