@@ -579,14 +579,17 @@ static int32_t run_attention_tc(const svla_attn_desc* d, float scale, cudaStream
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
+  // one 128-query tile per CTA, two CTAs per SM: each CTA's softmax overlaps the other's MMAs, and one CTA's
+  // set-up and epilogue overlap the other's key loop
+  using C = atc::Cfg<false>;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         atc::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
     if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  dim3 grid(static_cast<unsigned>((d->lq + 255) / 256), d->hq, d->batch);
-  return launch(attention_tc_kernel, grid, dim3(atc::kThreads), atc::kSmemBytes, stream, "attention_tc_kernel", a);
+  dim3 grid(static_cast<unsigned>((d->lq + 127) / 128), d->hq, d->batch);
+  return launch(attention_tc_kernel<false>, grid, dim3(C::kThreads), C::kSmemBytes, stream, "attention_tc_kernel", a);
 }
 
 int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
