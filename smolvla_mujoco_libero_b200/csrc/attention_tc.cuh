@@ -43,6 +43,13 @@ struct AttnTcArgs {
   int* err;
 };
 
+// max of three floats in one instruction (the three-input form of max.f32, sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 namespace atc {
 constexpr int kTileBytes = 128 * 128;  // 128 rows x 64 bf16
 // PAIR: two 128-query tiles per CTA (320 threads, 4 K/V stages, 512 TMEM columns, one CTA per SM);
@@ -218,7 +225,7 @@ __global__ void __launch_bounds__(atc::Cfg<PAIR>::kThreads, PAIR ? 1 : 2)
       for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
       if (kvalid >= 128) {
 #pragma unroll
-        for (int e = 0; e < 128; ++e) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(r[e]));
+        for (int e = 0; e < 128; e += 2) mp[(e >> 1) & 7] = max3f(mp[(e >> 1) & 7], __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
       } else {
 #pragma unroll
         for (int e = 0; e < 128; ++e) mp[e & 7] = (e < kvalid) ? fmaxf(mp[e & 7], __uint_as_float(r[e])) : mp[e & 7];
@@ -234,28 +241,32 @@ __global__ void __launch_bounds__(atc::Cfg<PAIR>::kThreads, PAIR ? 1 : 2)
         alpha = ex2_approx(m - m_new);
         m = m_new;
       }
-      // probabilities and row sum; bf16 P over the first 64 columns of S (all of S is in registers)
-      float lp[8];  // 8 partial row sums
+      // probabilities and row sum; bf16 P over the first 64 columns of S (all of S is in registers).
+      // Pairs of scores go through the packed fp32 pipe (FFMA2 for the exponent arguments, FADD2 for the
+      // row sum, kept as 8 partial sums in 4 packed accumulators).
+      float2 lp[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) lp[u] = 0.f;
+      for (int u = 0; u < 4; ++u) lp[u] = make_float2(0.f, 0.f);
+      const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const int k0 = ch * 32 + e;
-          float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[k0]), c, -m));
-          float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[k0 + 1]), c, -m));
+          const float2 z = __ffma2_rn(make_float2(__uint_as_float(r[k0]), __uint_as_float(r[k0 + 1])), c2, nm2);
+          float p0 = ex2_approx(z.x);
+          float p1 = ex2_approx(z.y);
           if (kvalid < 128) {
             p0 = (k0 < kvalid) ? p0 : 0.f;
             p1 = (k0 + 1 < kvalid) ? p1 : 0.f;
           }
-          lp[(e / 2) & 7] += p0 + p1;
+          lp[(e / 2) & 3] = __fadd2_rn(lp[(e / 2) & 3], make_float2(p0, p1));
           pk[e / 2] = pack_bf16_rn(p0, p1);
         }
         tmem_st16(tS + ch * 16, pk);
       }
-      const float ls = ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
+      const float ls = ((lp[0].x + lp[0].y) + (lp[1].x + lp[1].y)) + ((lp[2].x + lp[2].y) + (lp[3].x + lp[3].y));
       l = __fmaf_rn(l, alpha, ls);
       // O rescale (rare after the first tiles): the previous P.V has completed -- its commit preceded the
       // S of this tile -- and the next one waits for this warpgroup's arrival below
