@@ -74,6 +74,7 @@ struct GemmArgs {
   __nv_bfloat16* xt_bf16;           // Euler: bf16 copy
   unsigned long long* dbg;          // optional phase clock stamps of CTA 0 (profiling)
   int weights_resident;             // B operands were written before the previous kernel started
+  int out_v8;                       // every bf16 output row start is 32-byte aligned: 256-bit stores
   // split-K: work item t is split t % splits (k-tiles [split * kt_per_split, +kt_per_split)) of output
   // tile t / splits.  Every split stores its raw 32-bit accumulators to `partial`; the last to arrive on
   // the tile's counter adds them in split order into its own accumulator and runs the epilogue.
@@ -259,12 +260,22 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
       v[j + 1] = y.y;
     }
   };
-  auto store_bf16_16 = [](__nv_bfloat16* o, const float (&v)[16]) {
+  // 16 bf16 (32 bytes) of one row: one 256-bit store when the outputs allow it (each thread writes its own
+  // row, so a warp's store touches 32 rows: half as many store instructions halve the L1 work), else two
+  // 128-bit stores
+  const bool out_v8 = args.out_v8 != 0;
+  auto store_bf16_16 = [out_v8](__nv_bfloat16* o, const float (&v)[16]) {
     uint32_t pk[8];
 #pragma unroll
     for (int q2 = 0; q2 < 8; ++q2) pk[q2] = pack_bf16_rn(v[2 * q2], v[2 * q2 + 1]);
-    *reinterpret_cast<int4*>(o) = make_int4(pk[0], pk[1], pk[2], pk[3]);
-    *reinterpret_cast<int4*>(o + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
+    if (out_v8) {
+      asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(o), "r"(pk[0]), "r"(pk[1]),
+                   "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]), "r"(pk[7])
+                   : "memory");
+    } else {
+      *reinterpret_cast<int4*>(o) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<int4*>(o + 8) = make_int4(pk[4], pk[5], pk[6], pk[7]);
+    }
   };
 
   if constexpr (EPI == Epi::Rope) {

@@ -316,6 +316,10 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   args.err = device_error_ptr();
   args.dbg = reinterpret_cast<unsigned long long*>(d->debug_clock);
   args.weights_resident = d->weights_resident;
+  // 256-bit bf16 output stores need every 16-column group of every row 32-byte aligned: base and row stride
+  args.out_v8 = 1;
+  for (int s = 0; s < d->nseg; ++s)
+    if (d->seg[s].out && (reinterpret_cast<uintptr_t>(d->seg[s].out) % 32 != 0 || d->seg[s].ldo % 16 != 0)) args.out_v8 = 0;
   if (epi == Epi::Resid && !d->resid) return fail(SVLA_ERR_ARG, "RESID needs a residual");
   if (epi == Epi::Rope && (!d->rope_cs || !d->pos || d->max_pos <= 0)) return fail(SVLA_ERR_ARG, "ROPE needs rope_cs/pos");
   if (epi == Epi::GeluQuant && d->qout && (!d->q_smooth || d->q_act <= 0.f))
