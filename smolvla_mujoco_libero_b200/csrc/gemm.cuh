@@ -75,6 +75,7 @@ struct GemmArgs {
   unsigned long long* dbg;          // optional phase clock stamps of CTA 0 (profiling)
   int weights_resident;             // B operands were written before the previous kernel started
   int out_v8;                       // every bf16 output row start is 32-byte aligned: 256-bit stores
+  int resid_v8;                     // every residual row start is 32-byte aligned: 256-bit loads
   // split-K: work item t is split t % splits (k-tiles [split * kt_per_split, +kt_per_split)) of output
   // tile t / splits.  Every split stores its raw 32-bit accumulators to `partial`; the last to arrive on
   // the tile's counter adds them in split order into its own accumulator and runs the epilogue.
@@ -339,9 +340,24 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& args, int si, int 
       if constexpr (EPI == Epi::Resid) {
         const bool in = ok && m < args.M;
         const __nv_bfloat16* rs = args.resid + static_cast<size_t>(rrow) * args.ldr + n0 + cb;
+        // 16 columns (32 bytes) per load: one 256-bit load when the residual rows allow it (segment widths
+        // are multiples of 16, so both halves of a 16-column group are inside or outside together)
 #pragma unroll
-        for (int u = 0; u < kRes; ++u)
-          res[u] = (in && n0 + cb + u * 8 < sg.n) ? *reinterpret_cast<const int4*>(rs + u * 8) : make_int4(0, 0, 0, 0);
+        for (int u = 0; u < kRes; u += 2) {
+          const bool col_in = in && n0 + cb + u * 8 < sg.n;
+          if (col_in && args.resid_v8) {
+            uint32_t w[8];
+            asm volatile("ld.global.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                         : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+                         : "l"(rs + u * 8)
+                         : "memory");
+            res[u] = make_int4(w[0], w[1], w[2], w[3]);
+            res[u + 1] = make_int4(w[4], w[5], w[6], w[7]);
+          } else {
+            res[u] = col_in ? *reinterpret_cast<const int4*>(rs + u * 8) : make_int4(0, 0, 0, 0);
+            res[u + 1] = col_in ? *reinterpret_cast<const int4*>(rs + u * 8 + 8) : make_int4(0, 0, 0, 0);
+          }
+        }
       }
     };
     auto tmem_load = [&](uint32_t (&r)[kChunk], uint32_t (&r2)[P == 2 ? kChunk : 1], int cb) {

@@ -320,6 +320,7 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   args.out_v8 = 1;
   for (int s = 0; s < d->nseg; ++s)
     if (d->seg[s].out && (reinterpret_cast<uintptr_t>(d->seg[s].out) % 32 != 0 || d->seg[s].ldo % 16 != 0)) args.out_v8 = 0;
+  args.resid_v8 = (d->resid && reinterpret_cast<uintptr_t>(d->resid) % 32 == 0 && d->ldr % 16 == 0) ? 1 : 0;
   if (epi == Epi::Resid && !d->resid) return fail(SVLA_ERR_ARG, "RESID needs a residual");
   if (epi == Epi::Rope && (!d->rope_cs || !d->pos || d->max_pos <= 0)) return fail(SVLA_ERR_ARG, "ROPE needs rope_cs/pos");
   if (epi == Epi::GeluQuant && d->qout && (!d->q_smooth || d->q_act <= 0.f))
