@@ -75,7 +75,8 @@ int32_t svla_dequant_weight_bf16(const int8_t* qweight, const float* wscale, int
 
 /* SmoothQuant activation quantisation; replaces smoothQuantActivationKernel
  * (deploy/cuda/smoothquant_linear_epilogue.cu:108-119) with bf16 input:
- * q[m,k] = round((x[m,k] / smooth[k]) / act_scale).clamp(-128, 127).  K % 8 == 0. */
+ * q[m,k] = round((x[m,k] / smooth[k]) / act_scale).clamp(-128, 127).  K, ldx, ldq multiples of 8 (>= K);
+ * x 16-byte aligned, q 8-byte aligned; smooth fp32 [K], or NULL for no smoothing. */
 int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, float act_scale, int8_t* q,
                              int32_t ldq, int32_t m, int32_t k, svla_stream_t stream);
 
@@ -171,6 +172,8 @@ typedef struct svla_gemm_desc {
 
 #define SVLA_SPLITK_COUNTER_BYTES 65536
 
+/* Alignment (checked, status 1 otherwise): A / B operands and every output 16-byte aligned with row strides that
+ * are multiples of 16 bytes and >= the segment's columns (ldo, ldr, ldq); I8 / W8A16 segments need wscale. */
 int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream);
 
 /* -------------------------------------------------------------------------------------------------

@@ -245,6 +245,37 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   if (d->pair && d->nseg != 2) return fail(SVLA_ERR_ARG, "a pair needs exactly 2 segments");
   if (epi == Epi::SiluMul && !d->pair) return fail(SVLA_ERR_ARG, "SILU_MUL needs pair = 1");
   if (epi == Epi::I32 && kind != Kind::I8) return fail(SVLA_ERR_ARG, "I32 epilogue needs kind I8");
+  if (d->epi < 0 || d->epi > static_cast<int>(Epi::F32)) return fail(SVLA_ERR_ARG, "bad epilogue %d", d->epi);
+  {
+    // The epilogue moves 16 columns per access (128- or 256-bit vectors): every row it touches must start on a
+    // 16-byte boundary, or the launch would fault instead of returning status 1.
+    auto al = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+    const int out_bytes = (epi == Epi::I32 || epi == Epi::F32) ? 4 : 2;
+    int max_n = 0;
+    for (int s = 0; s < d->nseg; ++s) {
+      const svla_gemm_seg& g = d->seg[s];
+      if (g.n > max_n) max_n = g.n;
+      if (kind != Kind::BF16 && !g.wscale) return fail(SVLA_ERR_ARG, "segment %d: null wscale", s);
+      if (epi == Epi::Euler) {
+        if (g.ldo < g.n) return fail(SVLA_ERR_ARG, "segment %d: EULER row stride %d below n=%d", s, g.ldo, g.n);
+        continue;
+      }
+      if (!g.out) continue;
+      if (!al(g.out, 16)) return fail(SVLA_ERR_ARG, "segment %d: output not 16-byte aligned", s);
+      if (g.ldo < g.n || (static_cast<long long>(g.ldo) * out_bytes) % 16 != 0)
+        return fail(SVLA_ERR_ARG, "segment %d: output row stride %d must be >= n=%d and a multiple of %d", s, g.ldo,
+                    g.n, 16 / out_bytes);
+    }
+    if (epi == Epi::Resid && d->resid &&
+        (!al(d->resid, 16) || d->ldr < max_n || d->ldr % 8 != 0))
+      return fail(SVLA_ERR_ARG, "RESID: residual must be 16-byte aligned with a row stride >= n and a multiple of 8");
+    if (epi == Epi::GeluQuant && d->qout && (!al(d->qout, 16) || d->ldq < max_n || d->ldq % 16 != 0))
+      return fail(SVLA_ERR_ARG, "GELU_QUANT: qout must be 16-byte aligned with a row stride >= n and a multiple of 16");
+    if (epi == Epi::Euler && d->xt && (!al(d->xt, 4) || !al(d->xt_bf16, 2)))
+      return fail(SVLA_ERR_ARG, "EULER: misaligned xt / xt_bf16");
+    if (epi == Epi::Rope && d->rope_cs && !al(d->rope_cs, 16))
+      return fail(SVLA_ERR_ARG, "ROPE: rope_cs must be 16-byte aligned");
+  }
   const int sms = sm_count();
   const int bn = d->block_n ? d->block_n : choose_block_n(d, sms);
   const int elem_a = (kind == Kind::I8) ? 1 : 2;
@@ -423,8 +454,11 @@ int32_t svla_dequant_weight_bf16(const int8_t* qweight, const float* wscale, int
 
 int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, float act_scale, int8_t* q, int32_t ldq,
                              int32_t m, int32_t k, svla_stream_t stream) {
-  if (!x || !q || m <= 0 || k <= 0 || k % 8 || ldx % 8 || ldq % 8 || act_scale <= 0.f)
-    return fail(SVLA_ERR_ARG, "svla_quantize_smooth: bad args (k, ldx, ldq must be multiples of 8)");
+  if (!x || !q || m <= 0 || k <= 0 || k % 8 || ldx % 8 || ldq % 8 || ldx < k || ldq < k || !(act_scale > 0.f))
+    return fail(SVLA_ERR_ARG, "svla_quantize_smooth: bad args (k, ldx >= k, ldq >= k must be multiples of 8)");
+  // each thread loads 8 bf16 values (16 bytes) and stores 8 int8 values (8 bytes)
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(q) % 8 != 0)
+    return fail(SVLA_ERR_ARG, "svla_quantize_smooth: x must be 16-byte and q 8-byte aligned");
   const long long total = static_cast<long long>(m) * (k / 8);
   return launch(smooth_quant_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, cs(stream), "smooth_quant_kernel",
                 static_cast<const __nv_bfloat16*>(x), ldx, smooth, act_scale, q, ldq, m, k);

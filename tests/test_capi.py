@@ -97,3 +97,52 @@ def test_flow_arguments_are_checked_before_any_launch():
         d = desc(**kw)
         assert lib.svla_flow(ctypes.byref(d), None) == 1, kw
         assert word.encode() in lib.svla_last_error(), (kw, lib.svla_last_error())
+
+
+def test_gemm_epilogue_pointers_are_checked_before_any_launch():
+    """Outputs, residuals and int8 outputs that the epilogue would touch with 16-byte vectors must be 16-byte
+    aligned with row strides that keep every row aligned; a bad one is status 1, not a GPU fault.  The fake
+    device addresses are never dereferenced: every case fails on the host."""
+    import ctypes
+    lib = _lib.lib()
+
+    def desc(epi=_lib.EPI_BF16, kind=_lib.KIND_I8, out=0x100000, ldo=64, **kw):
+        d = _lib.GemmDesc()
+        d.kind, d.epi, d.m, d.k, d.nseg = kind, epi, 128, 128, 1
+        g = d.seg[0]
+        g.a, g.lda, g.b, g.ldb, g.wscale = 0x200000, 128, 0x300000, 128, 0x400000
+        g.out, g.ldo, g.n, g.act_scale = out, ldo, 64, 1.0
+        for k, v in kw.items():
+            setattr(d, k, v)
+        return d
+
+    cases = [
+        (desc(out=0x100002), "16-byte"),                      # bf16 output 2 bytes off
+        (desc(ldo=60), "row stride"),                         # below n
+        (desc(ldo=68), "row stride"),                         # 136-byte rows
+        (desc(epi=_lib.EPI_I32, ldo=66), "row stride"),       # int32 rows not 16-byte multiples
+        (desc(epi=_lib.EPI_RESID, resid=0x500008, ldr=64), "RESID"),
+        (desc(epi=_lib.EPI_RESID, resid=0x500000, ldr=60), "RESID"),
+        (desc(epi=_lib.EPI_GELU_QUANT, out=None, qout=0x600004, ldq=64, q_smooth=0x700000, q_act=1.0), "qout"),
+        (desc(epi=_lib.EPI_GELU_QUANT, out=None, qout=0x600000, ldq=72, q_smooth=0x700000, q_act=1.0), "qout"),
+        (desc(epi=11), "epilogue"),
+    ]
+    for d, word in cases:
+        assert lib.svla_gemm(ctypes.byref(d), None) == 1, word
+        assert word.encode() in lib.svla_last_error(), (word, lib.svla_last_error())
+    d = desc()
+    d.seg[0].wscale = None
+    assert lib.svla_gemm(ctypes.byref(d), None) == 1
+    assert b"wscale" in lib.svla_last_error()
+
+
+def test_quantize_and_linear_alignment_is_checked_before_any_launch():
+    lib = _lib.lib()
+    # x 2 bytes off a 16-byte boundary, q 4 bytes off an 8-byte one
+    assert lib.svla_quantize_smooth(0x100002, 64, None, 1.0, 0x200000, 64, 4, 64, None) == 1
+    assert b"aligned" in lib.svla_last_error()
+    assert lib.svla_quantize_smooth(0x100000, 64, None, 1.0, 0x200004, 64, 4, 64, None) == 1
+    assert lib.svla_quantize_smooth(0x100000, 32, None, 1.0, 0x200000, 64, 4, 64, None) == 1  # ldx < k
+    assert lib.svla_sq_linear_w8a8(0x100002, None, 1.0, 0x300000, 0x400000, None, 4, 64, 64, 0x500000, 0x600000,
+                                   4096, None) == 1
+    assert b"aligned" in lib.svla_last_error()

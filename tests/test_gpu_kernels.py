@@ -311,6 +311,43 @@ def test_row_remap_and_post_scale():
     assert buf[128:177].abs().sum() == 0
 
 
+@pytest.mark.parametrize("layout", ["offset", "padded_rows"])
+def test_epilogues_on_16_byte_aligned_rows_equal_32_byte_aligned(layout):
+    """The bf16 output stores and residual loads use 256-bit accesses when every row starts on a 32-byte
+    boundary and 128-bit ones otherwise.  Outputs / residuals 16 bytes off (a +8 element slice, or rows of
+    n + 8 elements) take the 128-bit path; the results must equal the 32-byte aligned call bit for bit."""
+    g = synthetic.generator(31)
+    m, k, n = 300, 256, 320
+    qx, qw = _rand_i8((m, k), g).to(DEV), _rand_i8((n, k), g).to(DEV)
+    ws = (torch.rand(n, generator=g) * 1e-3).to(DEV)
+    bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16).to(DEV)
+
+    def seg(out, ldo=None):
+        return ops.Seg(a=qx, b=qw, out=out, n=n, wscale=ws, bias=bias, act_scale=0.02, ldo=ldo)
+
+    def buf():
+        if layout == "offset":  # base 16 bytes past a 32-byte boundary, rows of n elements
+            raw = torch.zeros(m * n + 16, dtype=torch.bfloat16, device=DEV)
+            return raw[8:8 + m * n].view(m, n), None
+        raw = torch.zeros(m, n + 8, dtype=torch.bfloat16, device=DEV)  # 656-byte rows
+        return raw[:, :n], n + 8
+
+    y_ref = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_BF16, m, k, [seg(y_ref)]))
+    y, ldo = buf()
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_BF16, m, k, [seg(y, ldo)]))
+    assert torch.equal(y, y_ref)
+    r_ref = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_RESID, m, k, [seg(r_ref)], resid=res, ldr=n))
+    r_in, ldr = buf()
+    r_in.copy_(res)
+    r_out, ldo = buf()
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_RESID, m, k, [seg(r_out, ldo)], resid=r_in, ldr=ldr or n))
+    assert torch.equal(r_out, r_ref)
+    assert torch.equal(r_ref.cpu(), (y_ref.float() + res.float()).to(torch.bfloat16).cpu())
+
+
 # ----------------------------------------------------------------------------- norms
 
 def test_rmsnorm_quant_three_outputs():

@@ -2,11 +2,13 @@
 
 It is for callers that cannot allocate device memory -- a fixed-rate control loop that must not allocate
 after start-up, or a binding that only holds the pointers it was given.  Its scratch is a fixed 4 MiB
-array inside the library instead of a caller workspace.  This file is collected last on purpose.
+array inside the library instead of a caller workspace.  The file name sorts last so that a run stopping at
+the first failure (pytest -x) has already run every other test when this one runs.
 
 Checked through the C ABI: two calls in a row, each on a different input, give exactly the output of
-svla_sq_linear_w8a8 (the workspace entry point) -- the same kernels run, so the tolerance is zero -- and a
-call whose int8 activations would not fit is refused with status 1 before any GPU work.
+svla_sq_linear_w8a8 (the workspace entry point) -- the same kernels run, so the tolerance is zero -- and
+leave the device's free memory unchanged (nothing is allocated per call); a call whose int8 activations would
+not fit is refused with status 1 before any GPU work.
 """
 
 import pytest
@@ -34,13 +36,22 @@ def test_static_scratch_entry_matches_workspace_entry_on_two_calls():
     smooth = (torch.rand(960, generator=synthetic.generator(9)) * 2 + 0.25).to(dev)
     qw, ws = ops.pack_weight_i8(case.weight.to(dev), smooth)
     bias = case.bias.to(dev)
-    for x_cpu, a in ((case.x, 0.011), (other.x, 0.017)):
-        x = x_cpu.to(dev)
-        ref = ops.sq_linear_w8a8(x, smooth, a, qw, ws, bias)
-        y = torch.full_like(ref, float("nan"))
+    inputs = [(case.x.to(dev), 0.011), (other.x.to(dev), 0.017)]
+    refs = [ops.sq_linear_w8a8(x, smooth, a, qw, ws, bias) for x, a in inputs]
+    outs = [torch.full_like(r, float("nan")) for r in refs]
+    # a first call looks up the array's device address; after it, calls must not change the free memory
+    assert _call(lib, inputs[0][0], smooth, inputs[0][1], qw, ws, bias, outs[0]) == 0, lib.svla_last_error()
+    torch.cuda.synchronize()
+    outs[0].fill_(float("nan"))
+    torch.cuda.synchronize()
+    free0, allocated0 = torch.cuda.mem_get_info()[0], torch.cuda.memory_allocated()
+    for (x, a), y in zip(inputs, outs):
         rc = _call(lib, x, smooth, a, qw, ws, bias, y)
         assert rc == 0, lib.svla_last_error()
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert torch.cuda.memory_allocated() == allocated0
+    for y, ref in zip(outs, refs):
         assert torch.equal(y, ref)
     assert _lib.device_error() == 0
 
