@@ -153,40 +153,69 @@ class OracleSmolVLA:
         return self.lin[name](x)
 
     # -- vision
-    def embed_image(self, image: torch.Tensor) -> torch.Tensor:
-        """SigLIP + pixel-shuffle connector: fp32 [B,3,S,S] -> bf16 [B, n_img_tokens, hidden]."""
-        from smolvla_mujoco_libero_b200.config import CONNECTOR, VISION
+    def vision_embeddings(self, image: torch.Tensor) -> torch.Tensor:
+        """Patch-16 conv (bf16) + learned position embedding: fp32 [B,3,S,S] -> bf16 [B, n_patches, vis_hidden]
+        (SmolVLMVisionEmbeddings with every patch valid, so the position ids are 0..n_patches-1)."""
+        from smolvla_mujoco_libero_b200.config import VISION
         c, w = self.cfg, self.w
         pe = f"{VISION}.embeddings"
         x = F.conv2d(image.to(torch.bfloat16), w[f"{pe}.patch_embedding.weight"], w[f"{pe}.patch_embedding.bias"],
                      stride=c.patch)
-        h = x.flatten(2).transpose(1, 2) + w[f"{pe}.position_embedding.weight"][None]
-        b = h.shape[0]
+        return x.flatten(2).transpose(1, 2) + w[f"{pe}.position_embedding.weight"][None]
+
+    def vision_attention(self, i: int, y: torch.Tensor) -> torch.Tensor:
+        """q/k/v projections, unmasked attention (scores and softmax in fp32, export_6f's restatement), out_proj."""
+        from smolvla_mujoco_libero_b200.config import VISION
+        c = self.cfg
+        p = f"{VISION}.encoder.layers.{i}"
+        q = self._linear(f"{p}.self_attn.q_proj", y)
+        k = self._linear(f"{p}.self_attn.k_proj", y)
+        v = self._linear(f"{p}.self_attn.v_proj", y)
+        ctx = eager_attention(q, k, v, None, c.vis_heads, c.vis_heads)
+        return self._linear(f"{p}.self_attn.out_proj", ctx)
+
+    def vision_mlp(self, i: int, y: torch.Tensor) -> torch.Tensor:
+        """fc1 -> GELU(tanh) -> fc2 (SmolVLMVisionMLP with gelu_pytorch_tanh)."""
+        from smolvla_mujoco_libero_b200.config import VISION
+        p = f"{VISION}.encoder.layers.{i}"
+        return self._linear(f"{p}.mlp.fc2", F.gelu(self._linear(f"{p}.mlp.fc1", y), approximate="tanh"))
+
+    def vision_layer(self, i: int, h: torch.Tensor) -> torch.Tensor:
+        """Pre-LN encoder layer (SmolVLMEncoderLayer): h + attn(LN1(h)), then + mlp(LN2(.))."""
+        from smolvla_mujoco_libero_b200.config import VISION
+        c, w = self.cfg, self.w
+        p = f"{VISION}.encoder.layers.{i}"
+        h = h + self.vision_attention(i, layer_norm(h, w[f"{p}.layer_norm1.weight"], w[f"{p}.layer_norm1.bias"],
+                                                    c.vis_eps))
+        return h + self.vision_mlp(i, layer_norm(h, w[f"{p}.layer_norm2.weight"], w[f"{p}.layer_norm2.bias"],
+                                                 c.vis_eps))
+
+    def connector(self, h: torch.Tensor) -> torch.Tensor:
+        """Post-LayerNorm output -> pixel shuffle -> modality projection (SmolVLMConnector)."""
+        from smolvla_mujoco_libero_b200.config import CONNECTOR
+        return self._linear(CONNECTOR, pixel_shuffle(h, self.cfg.scale_factor))
+
+    def embed_image(self, image: torch.Tensor) -> torch.Tensor:
+        """SigLIP + pixel-shuffle connector: fp32 [B,3,S,S] -> bf16 [B, n_img_tokens, hidden]."""
+        from smolvla_mujoco_libero_b200.config import VISION
+        c, w = self.cfg, self.w
+        h = self.vision_embeddings(image)
         for i in range(c.vis_layers):
-            p = f"{VISION}.encoder.layers.{i}"
-            r = h
-            y = layer_norm(h, w[f"{p}.layer_norm1.weight"], w[f"{p}.layer_norm1.bias"], c.vis_eps)
-            q = self._linear(f"{p}.self_attn.q_proj", y)
-            k = self._linear(f"{p}.self_attn.k_proj", y)
-            v = self._linear(f"{p}.self_attn.v_proj", y)
-            ctx = eager_attention(q, k, v, None, c.vis_heads, c.vis_heads)
-            h = r + self._linear(f"{p}.self_attn.out_proj", ctx)
-            r = h
-            y = layer_norm(h, w[f"{p}.layer_norm2.weight"], w[f"{p}.layer_norm2.bias"], c.vis_eps)
-            f1 = F.gelu(self._linear(f"{p}.mlp.fc1", y), approximate="tanh")
-            h = r + self._linear(f"{p}.mlp.fc2", f1)
+            h = self.vision_layer(i, h)
         h = layer_norm(h, w[f"{VISION}.post_layernorm.weight"], w[f"{VISION}.post_layernorm.bias"], c.vis_eps)
-        h = pixel_shuffle(h, c.scale_factor)
-        return self._linear(CONNECTOR, h)
+        return self.connector(h)
 
     # -- prefix
-    def embed_prefix(self, images, img_masks, lang_tokens, lang_masks, state):
-        """deploy/diagnose_3_4_numeric_baseline.py:72-115 (image embeddings from embed_image)."""
+    def embed_prefix(self, images, img_masks, lang_tokens, lang_masks, state, image_embs=None):
+        """deploy/diagnose_3_4_numeric_baseline.py:72-115.  The image embeddings come from embed_image, or, in
+        the embeds mode of the exported core (deploy/export_smolvla_sample_actions_onnx.py:64-115), are given
+        as ``image_embs`` (one bf16 [B, n_img_tokens, hidden] per camera) and ``images`` is ignored."""
         from smolvla_mujoco_libero_b200.config import TEXT
         c = self.cfg
         embs, pads, att = [], [], []
-        for img, m in zip(images, img_masks):
-            e = self.embed_image(img)
+        sources = image_embs if image_embs is not None else [self.embed_image(img) for img in images]
+        for e, m in zip(sources, img_masks):
+            e = e.to(torch.bfloat16)
             e = e * torch.tensor(e.shape[-1] ** 0.5, dtype=e.dtype)
             embs.append(e)
             pads.append(m[:, None].expand(e.shape[0], e.shape[1]))
@@ -209,28 +238,41 @@ class OracleSmolVLA:
         return self._linear(f"{p}.mlp.down_proj",
                             F.silu(self._linear(f"{p}.mlp.gate_proj", y)) * self._linear(f"{p}.mlp.up_proj", y))
 
+    def text_layer(self, i: int, h: torch.Tensor, mask: torch.Tensor, pos: torch.Tensor, taps: dict | None = None):
+        """One SmolVLM2 text decoder layer with KV fill (lerobot forward_attn_layer, fill_kv_cache=True):
+        RMSNorm -> q/k/v (W8A8) -> RoPE -> masked GQA attention -> o_proj (W8A8) + residual -> RMSNorm ->
+        SiLU(gate) * up (W8A8) -> down (W8A16) + residual.  Returns (h, (k post-RoPE, v)); ``taps`` (optional)
+        receives the layer's intermediate bf16 tensors by name."""
+        from smolvla_mujoco_libero_b200.config import TEXT
+        c, w = self.cfg, self.w
+        b, L, _ = h.shape
+        p = f"{TEXT}.layers.{i}"
+        y = rms_norm(h, w[f"{p}.input_layernorm.weight"], c.rms_eps)
+        q = self._linear(f"{p}.self_attn.q_proj", y).view(b, L, c.heads, c.head_dim)
+        k = self._linear(f"{p}.self_attn.k_proj", y).view(b, L, c.kv_heads, c.head_dim)
+        v = self._linear(f"{p}.self_attn.v_proj", y)
+        q = apply_rope(q, pos, c.rope_wavelength).reshape(b, L, -1)
+        k = apply_rope(k, pos, c.rope_wavelength).reshape(b, L, -1)
+        ctx = eager_attention(q, k, v, mask, c.heads, c.kv_heads)
+        h1 = h + self._linear(f"{p}.self_attn.o_proj", ctx)
+        y2 = rms_norm(h1, w[f"{p}.post_attention_layernorm.weight"], c.rms_eps)
+        act = F.silu(self._linear(f"{p}.mlp.gate_proj", y2)) * self._linear(f"{p}.mlp.up_proj", y2)
+        out = h1 + self._linear(f"{p}.mlp.down_proj", act)
+        if taps is not None:
+            taps.update(input_norm=y, q=q, k=k, v=v, ctx=ctx, attn_out=h1, post_norm=y2, mlp_act=act, out=out)
+        return out, (k, v)
+
     def prefix_forward(self, prefix, pad, att):
         """VLM layers with KV fill (lerobot forward_attn_layer, fill_kv_cache=True)."""
         from smolvla_mujoco_libero_b200.config import TEXT
         c, w = self.cfg, self.w
         mask = make_att_2d_masks(pad, att)
         pos = torch.cumsum(pad.to(torch.int64), dim=1) - 1
-        b, L, _ = prefix.shape
         h = prefix
         cache = []
         for i in range(c.text_layers):
-            p = f"{TEXT}.layers.{i}"
-            y = rms_norm(h, w[f"{p}.input_layernorm.weight"], c.rms_eps)
-            q = self._linear(f"{p}.self_attn.q_proj", y).view(b, L, c.heads, c.head_dim)
-            k = self._linear(f"{p}.self_attn.k_proj", y).view(b, L, c.kv_heads, c.head_dim)
-            v = self._linear(f"{p}.self_attn.v_proj", y)
-            q = apply_rope(q, pos, c.rope_wavelength).reshape(b, L, -1)
-            k = apply_rope(k, pos, c.rope_wavelength).reshape(b, L, -1)
-            cache.append((k, v))
-            ctx = eager_attention(q, k, v, mask, c.heads, c.kv_heads)
-            h = h + self._linear(f"{p}.self_attn.o_proj", ctx)
-            y = rms_norm(h, w[f"{p}.post_attention_layernorm.weight"], c.rms_eps)
-            h = h + self._mlp(p, y)
+            h, kv = self.text_layer(i, h, mask, pos)
+            cache.append(kv)
         prefix_out = rms_norm(h, w[f"{TEXT}.norm.weight"], c.rms_eps)
         return cache, prefix_out, mask, pos
 
@@ -276,13 +318,19 @@ class OracleSmolVLA:
             h = h + self._mlp(p, y)
         out = rms_norm(h, w[f"{EXPERT}.norm.weight"], c.rms_eps)
         wo = self.lin["model.action_out_proj"]
+        self.last_suffix_out = out
         return out.float() @ wo.weight.float().t() + wo.bias.float()
 
     @torch.no_grad()
-    def sample_actions(self, images, img_masks, lang_tokens, lang_masks, state, noise, taps: dict | None = None):
-        """Returns the fp32 chunk [B, chunk, max_action_dim] (callers slice the first action_dim)."""
+    def sample_actions(self, images, img_masks, lang_tokens, lang_masks, state, noise, taps: dict | None = None,
+                       image_embs=None):
+        """Returns the fp32 chunk [B, chunk, max_action_dim] (callers slice the first action_dim).
+
+        ``taps`` (optional) receives the debug outputs of deploy/diagnose_3_4_numeric_baseline.py:55-70 by the
+        same names -- prefix_embs, prefix_out, suffix_out_step_NN (the expert's final-norm output that
+        action_out_proj reads), v_t_step_NN, x_t_step_NN -- plus the prefix KV cache as ``kv``."""
         c = self.cfg
-        prefix, pad, att = self.embed_prefix(images, img_masks, lang_tokens, lang_masks, state)
+        prefix, pad, att = self.embed_prefix(images, img_masks, lang_tokens, lang_masks, state, image_embs)
         cache, prefix_out, _, _ = self.prefix_forward(prefix, pad, att)
         if taps is not None:
             taps["prefix_embs"] = prefix
@@ -295,6 +343,7 @@ class OracleSmolVLA:
             v_t = self.denoise_step(cache, pad, x_t, t)
             x_t = x_t + dt * v_t
             if taps is not None:
+                taps[f"suffix_out_step_{step:02d}"] = self.last_suffix_out
                 taps[f"v_t_step_{step:02d}"] = v_t
                 taps[f"x_t_step_{step:02d}"] = x_t
         return x_t

@@ -135,7 +135,8 @@ class SmolVLARunner:
     SPLITK_BYTES = 32 << 20  # split-K workspace shared by the runner's GEMMs (stream-ordered)
 
     def __init__(self, weights: DeviceWeights, batch: int, mode: str = "quant", debug_taps: bool = False,
-                 split_k: bool = True, prefix_only: bool = False, flow: bool | None = None):
+                 split_k: bool = True, prefix_only: bool = False, flow: bool | None = None,
+                 image_embeds: bool = False):
         if weights.cfg.expert_layers != weights.cfg.text_layers:
             raise ValueError("the expert must have one layer per text layer (each expert layer reads that layer's KV)")
         if mode == "quant" and not weights.quantized:
@@ -148,6 +149,10 @@ class SmolVLARunner:
         # prefix_only: stop after the prefix prefill, with the final-layer prefix hidden states in prefix_out
         # (the RL-token features, smollvla_rltoken/rlt/rl_token.py:50-88) and the KV cache filled
         self.prefix_only = prefix_only
+        # image_embeds: the embeds mode of the exported core (deploy/export_smolvla_sample_actions_onnx.py:64-164):
+        # the call takes one bf16 [B, n_img_tokens, hidden] image embedding per camera instead of the images,
+        # and the vision tower and connector are not run
+        self.image_embeds = image_embeds
         # split-K changes the fp32 summation order of the small-M bf16 GEMMs with the batch size; without it
         # every batch row's result is bit-identical at any batch size
         self.split_k = split_k
@@ -180,10 +185,17 @@ class SmolVLARunner:
         bf, i8, f32 = torch.bfloat16, torch.int8, torch.float32
         Lp, S = c.prefix_len, c.chunk
         NI = B * c.n_cams
-        NV = NI * c.n_patches
+        NV = 0 if self.image_embeds else NI * c.n_patches  # the vision tower's rows (none in embeds mode)
         z = lambda *s, dt=bf: torch.zeros(*s, dtype=dt, device=d)  # noqa: E731
         self.splitk_ws = ops.splitk_workspace(self.SPLITK_BYTES, d)
-        self.in_img = z(B, c.n_cams, c.channels, c.image_size, c.image_size, dt=f32)
+        if self.image_embeds:
+            n_emb = c.n_cams * c.n_img_tokens
+            self.in_emb = z(B, n_emb, c.hidden)
+            # row b * n_emb + j of in_emb, viewed as a table, is image token j of sample b
+            self.emb_rows = torch.arange(B * n_emb, dtype=torch.int64, device=d).view(B, n_emb)
+            self.in_img = z(1, dt=f32)
+        else:
+            self.in_img = z(B, c.n_cams, c.channels, c.image_size, c.image_size, dt=f32)
         self.in_img_mask = z(c.n_cams, B, dt=torch.uint8)
         self.in_tokens = torch.zeros(B, c.n_lang, dtype=torch.int64, device=d)
         self.in_lang_mask = z(B, c.n_lang, dt=torch.uint8)
@@ -203,15 +215,16 @@ class SmolVLARunner:
         self.suffix_pos = z(B * S, dt=torch.int32)
         self.cross_pos = z(B * S, dt=torch.int32)
         H, Hv = c.hidden, c.vis_hidden
-        self.patches = z(NV, c.channels * c.patch * c.patch)
-        self.vh = z(NV, Hv)
         q = self.mode == "quant"
-        self.v_in = [z(NV, Hv, dt=i8 if q else bf) for _ in range(3)]   # LN1 -> q/k/v inputs
-        self.v_qkv = [z(NV, Hv) for _ in range(3)]
-        self.v_ctx = z(NV, Hv, dt=i8 if q else bf)
-        self.v_fc1_in = z(NV, Hv, dt=i8 if q else bf)
-        self.v_fc2_in = z(NV, c.vis_mlp, dt=i8 if q else bf)
-        self.conn_in = z(NI * c.n_img_tokens, Hv * c.scale_factor ** 2, dt=i8 if q else bf)
+        if not self.image_embeds:
+            self.patches = z(NV, c.channels * c.patch * c.patch)
+            self.vh = z(NV, Hv)
+            self.v_in = [z(NV, Hv, dt=i8 if q else bf) for _ in range(3)]   # LN1 -> q/k/v inputs
+            self.v_qkv = [z(NV, Hv) for _ in range(3)]
+            self.v_ctx = z(NV, Hv, dt=i8 if q else bf)
+            self.v_fc1_in = z(NV, Hv, dt=i8 if q else bf)
+            self.v_fc2_in = z(NV, c.vis_mlp, dt=i8 if q else bf)
+            self.conn_in = z(NI * c.n_img_tokens, Hv * c.scale_factor ** 2, dt=i8 if q else bf)
         self.h = z(B * Lp, H)
         self.t_in = [z(B * Lp, H, dt=i8 if q else bf) for _ in range(3)]
         self.t_q = z(B * Lp, c.q_dim)
@@ -236,6 +249,13 @@ class SmolVLARunner:
         self.emlp = z(B * S, c.expert_mlp)
         if self.debug or self.prefix_only:
             self.prefix_out = z(B * Lp, H)
+        if self.debug:
+            # debug-only outputs that the deployed launches fuse away: the normalised rows in front of the
+            # quantisers, the bf16 attention context beside its int8 copy, and v_t before the Euler update
+            self.dbg_norm = z(max(NV, B * Lp, B * S), max(Hv, H, E))
+            self.dbg_ctx = z(max(NV, B * Lp), max(Hv, c.q_dim))
+            self.dbg_fc2 = z(NV, c.vis_mlp) if NV else None
+            self.v_t = z(B * S, c.max_action_dim, dt=f32)
 
     def _constants(self):
         c = self.cfg
@@ -300,20 +320,27 @@ class SmolVLARunner:
             (bias.data_ptr() if bias is not None else None), float(eps)
         d.layernorm, d.m, d.k = int(bias is not None), m, k
         d.pixel_shuffle, d.ps_grid = pixel_shuffle, ps_grid
-        if self.mode == "quant" and quant_mods:
+        quant = self.mode == "quant" and bool(quant_mods)
+        if quant:
             for i, (mod, q) in enumerate(zip(quant_mods, outs)):
                 p = self.w.lin[mod]
                 d.q[i], d.smooth[i], d.act[i] = q.data_ptr(), p.smooth.data_ptr(), p.act_scale
                 d.rsmooth[i] = p.rsmooth.data_ptr()
             d.nq, d.ldq = len(quant_mods), outs[0].stride(0)
+            if y is None and self.debug and not pixel_shuffle:
+                y = self.dbg_norm[:m, :k]  # debug: keep the bf16 rows the quantisers read
             if y is not None:
                 d.y, d.ldy = y.data_ptr(), y.stride(0)
+            target = y
         else:
             target = y if y is not None else outs[0]
             d.y, d.ldy = target.data_ptr(), target.stride(0)
         self._add(L.lib().svla_norm_quant, d)
-        if tap is not None and not (self.mode == "quant" and quant_mods):
+        if tap is not None and target is not None and (not quant or self.debug):
             self._tap(tap, target)
+        if quant and self.debug:
+            for mod, q in zip(quant_mods, outs):
+                self._tap([f"{mod}#int8"], q)
 
     def _attn(self, q, k1, v1, lq, hq, hkv, mask=None, k2=None, v2=None, out_mod=None, out=None, tap=None,
               key_mask=None, mask_keys=0):
@@ -328,33 +355,69 @@ class SmolVLARunner:
             l2 = k2.shape[0] // B
             k2v, v2v = k2.view(B, l2, -1), v2.view(B, l2, -1)
         ov = out.view(B, lq, -1)
-        if self.mode == "quant" and out_mod is not None:
+        quant = self.mode == "quant" and out_mod is not None
+        if quant:
             p = self.w.lin[out_mod]
+            # debug: the bf16 context beside the int8 one the next linear reads
+            dbg = self.dbg_ctx[:q.shape[0], :q.shape[1]] if self.debug else None
             d = ops.attention_desc(qv, k1v, v1v, B, lq, hq, hkv, mask=mask, k2=k2v, v2=v2v, qo=ov,
+                                   o=None if dbg is None else dbg.view(B, lq, -1),
                                    qo_smooth=p.smooth, qo_act=p.act_scale, qo_rsmooth=p.rsmooth,
                                    key_mask=key_mask, mask_keys=mask_keys)
         else:
             d = ops.attention_desc(qv, k1v, v1v, B, lq, hq, hkv, mask=mask, k2=k2v, v2=v2v, o=ov,
                                    key_mask=key_mask, mask_keys=mask_keys)
         self._add(L.lib().svla_attention, d)
-        if tap is not None and not (self.mode == "quant" and out_mod is not None):
+        if tap is not None and not quant:
             self._tap(tap, out)
+        elif tap is not None and self.debug:
+            self._tap(tap, dbg)
+            self._tap([f"{out_mod}#int8"], out)
 
     # ------------------------------------------------------------------ the call
     def _build(self):
         c, B, w = self.cfg, self.B, self.w
         lib = L.lib()
         self._keep = []
-        q_mode = self.mode == "quant"
-        Lp, S, H, E = c.prefix_len, c.chunk, c.hidden, c.expert_hidden
-        NI = B * c.n_cams
-        NV = NI * c.n_patches
+        Lp, S, H = c.prefix_len, c.chunk, c.hidden
         # masks and positions
         self._add(lib.svla_build_masks, self.in_img_mask[0].data_ptr(), self.in_img_mask[1].data_ptr()
                   if c.n_cams > 1 else self.in_img_mask[0].data_ptr(), self.in_lang_mask.data_ptr(), B,
                   c.n_img_tokens, c.n_lang, S, self.prefix_mask.data_ptr(), self.prefix_pos.data_ptr(),
                   self.self_mask.data_ptr(), self.cross_mask.data_ptr(), self.suffix_pos.data_ptr(),
                   self.cross_pos.data_ptr())
+        if self.image_embeds:
+            self._build_embeds_prefix()
+        else:
+            self._build_vision()
+        # language tokens x sqrt(H) and the state token
+        self._add(lib.svla_embed_tokens, self.in_tokens.data_ptr(), B, c.n_lang, w.t[f"{TEXT}.embed_tokens.weight"].data_ptr(),
+                  c.vocab, H, float(math.sqrt(H)), self.h.data_ptr(), Lp, c.n_cams * c.n_img_tokens)
+        self._add(lib.svla_f32_to_bf16, self.in_state.data_ptr(), self.state_bf.data_ptr(), self.in_state.numel())
+        self._gemm(L.KIND_BF16, L.EPI_BF16, B, c.max_state_dim,
+                   [self._linear_seg("model.state_proj", self.state_bf, self.h)], rows_per_group=1,
+                   group_stride=Lp, row_offset=Lp - 1)
+        if self.debug:
+            self._tap(["prefix_embs"], self.h)
+        self._build_text_and_expert()
+
+    def _build_embeds_prefix(self):
+        """Embeds mode: image token rows (b, cam, t) of the prefix = bf16(emb * bf16(sqrt(H))), the scaling of
+        embed_prefix_from_image_embeds (deploy/export_smolvla_sample_actions_onnx.py:87-94)."""
+        c, B = self.cfg, self.B
+        n_emb = c.n_cams * c.n_img_tokens
+        img_scale = float(torch.tensor(c.hidden ** 0.5, dtype=torch.bfloat16))
+        self._add(L.lib().svla_embed_tokens, self.emb_rows.data_ptr(), B, n_emb, self.in_emb.data_ptr(), B * n_emb,
+                  c.hidden, img_scale, self.h.data_ptr(), c.prefix_len, 0)
+
+    def _build_vision(self):
+        """SigLIP + post-LN + pixel shuffle + connector, writing the image token rows of the prefix."""
+        c, B, w = self.cfg, self.B, self.w
+        lib = L.lib()
+        q_mode = self.mode == "quant"
+        Lp, H = c.prefix_len, c.hidden
+        NI = B * c.n_cams
+        NV = NI * c.n_patches
         # ---------------- vision tower
         self._add(lib.svla_im2col, self.in_img.data_ptr(), NI, c.channels, c.image_size, c.patch,
                   self.patches.data_ptr())
@@ -380,10 +443,14 @@ class SmolVLARunner:
                        quant_mods=[f"{p}.mlp.fc1"], outs=[self.v_fc1_in], tap=[f"{p}.mlp.fc1"])
             fc2 = w.lin[f"{p}.mlp.fc2"]
             if q_mode:
+                gelu_bf16 = self.dbg_fc2 if self.debug else None  # debug: the bf16 GELU output beside the int8 one
                 self._gemm(L.KIND_I8, L.EPI_GELU_QUANT, NV, c.vis_hidden,
-                           [self._linear_seg(f"{p}.mlp.fc1", self.v_fc1_in, None)],
+                           [self._linear_seg(f"{p}.mlp.fc1", self.v_fc1_in, gelu_bf16)],
                            q_smooth=fc2.smooth, q_rsmooth=fc2.rsmooth, q_act=fc2.act_scale, qout=self.v_fc2_in,
                            ldq=c.vis_mlp)
+                if self.debug:
+                    self._tap([f"{p}.mlp.fc2"], gelu_bf16)
+                    self._tap([f"{p}.mlp.fc2#int8"], self.v_fc2_in)
             else:
                 self._gemm(L.KIND_BF16, L.EPI_GELU_QUANT, NV, c.vis_hidden,
                            [self._linear_seg(f"{p}.mlp.fc1", self.v_fc1_in, self.v_fc2_in)])
@@ -399,15 +466,12 @@ class SmolVLARunner:
         self._gemm(self._kind(CONNECTOR, NI * c.n_img_tokens), L.EPI_BF16, NI * c.n_img_tokens, self.conn_in.shape[1],
                    [self._linear_seg(CONNECTOR, self.conn_in, self.h)], post_scale=img_scale,
                    rows_per_group=c.n_cams * c.n_img_tokens, group_stride=Lp)
-        # language tokens x sqrt(H) and the state token
-        self._add(lib.svla_embed_tokens, self.in_tokens.data_ptr(), B, c.n_lang, w.t[f"{TEXT}.embed_tokens.weight"].data_ptr(),
-                  c.vocab, H, float(math.sqrt(H)), self.h.data_ptr(), Lp, c.n_cams * c.n_img_tokens)
-        self._add(lib.svla_f32_to_bf16, self.in_state.data_ptr(), self.state_bf.data_ptr(), self.in_state.numel())
-        self._gemm(L.KIND_BF16, L.EPI_BF16, B, c.max_state_dim,
-                   [self._linear_seg("model.state_proj", self.state_bf, self.h)], rows_per_group=1,
-                   group_stride=Lp, row_offset=Lp - 1)
-        if self.debug:
-            self._tap(["prefix_embs"], self.h)
+
+    def _build_text_and_expert(self):
+        c, B, w = self.cfg, self.B, self.w
+        lib = L.lib()
+        q_mode = self.mode == "quant"
+        Lp, S, H, E = c.prefix_len, c.chunk, c.hidden, c.expert_hidden
         # ---------------- text layers (KV fill)
         for i in range(c.text_layers):
             p = f"{TEXT}.layers.{i}"
@@ -418,6 +482,9 @@ class SmolVLARunner:
             self._gemm(self._kind(mods[0], B * Lp), L.EPI_ROPE, B * Lp, H,
                        [self._linear_seg(m, a, o, rope=r) for m, a, o, r in zip(mods, a_in, outs, (1, 1, 0))],
                        rope_cs=self.rope_cs, pos=self.prefix_pos, max_pos=self.max_pos)
+            if self.debug:  # post-RoPE q / k and v: k and v are also this layer's KV cache
+                for name, buf in zip(("q_rope", "k_rope", "v"), outs):
+                    self._tap([f"{p}.self_attn.{name}"], buf)
             last = i == c.text_layers - 1
             if last and not (self.debug or self.prefix_only) and self.mode == "quant":
                 break
@@ -425,14 +492,20 @@ class SmolVLARunner:
                        out_mod=f"{p}.self_attn.o_proj", out=self.t_ctx, tap=[f"{p}.self_attn.o_proj"])
             self._gemm(self._kind(f"{p}.self_attn.o_proj", B * Lp), L.EPI_RESID, B * Lp, c.q_dim,
                        [self._linear_seg(f"{p}.self_attn.o_proj", self.t_ctx, self.h)], resid=self.h, ldr=H)
+            if self.debug:
+                self._tap([f"{p}.attn_residual"], self.h)
             mods = [f"{p}.mlp.gate_proj", f"{p}.mlp.up_proj"]
             self._norm(self.h, w.t[f"{p}.post_attention_layernorm.weight"], c.rms_eps, quant_mods=mods,
                        outs=self.t_mlp_in, tap=mods)
             a_in = self.t_mlp_in if q_mode else [self.t_mlp_in[0]] * 2
             self._gemm(self._kind(mods[0], B * Lp), L.EPI_SILU_MUL, B * Lp, H,
                        [self._linear_seg(m, a, self.t_mlp) for m, a in zip(mods, a_in)], pair=True)
+            if self.debug:
+                self._tap([f"{p}.mlp.down_proj"], self.t_mlp)
             self._gemm(self._kind(f"{p}.mlp.down_proj", B * Lp), L.EPI_RESID, B * Lp, c.mlp,
                        [self._linear_seg(f"{p}.mlp.down_proj", self.t_mlp, self.h)], resid=self.h, ldr=H)
+            if self.debug:
+                self._tap([f"{p}.output"], self.h)
         if self.debug or self.prefix_only:
             self._norm(self.h, w.t[f"{TEXT}.norm.weight"], c.rms_eps, y=self.prefix_out)
             if self.debug:
@@ -486,9 +559,18 @@ class SmolVLARunner:
                 self._gemm(self._kind(f"{p}.mlp.down_proj", B * S), L.EPI_RESID, B * S, c.expert_mlp,
                            [self._linear_seg(f"{p}.mlp.down_proj", self.emlp, self.eh)], resid=self.eh, ldr=E)
             self._norm(self.eh, w.t[f"{EXPERT}.norm.weight"], c.rms_eps, y=self.ey)
+            if self.debug:
+                # the reference's debug outputs (deploy/diagnose_3_4_numeric_baseline.py:55-70): suffix_out
+                # (what action_out_proj reads), v_t from the same GEMM in fp32, x_t after the Euler update
+                self._tap([f"suffix_out_step_{step:02d}"], self.ey)
+                self._gemm(L.KIND_BF16, L.EPI_F32, B * S, E,
+                           [self._linear_seg("model.action_out_proj", self.ey, self.v_t)])
+                self._tap([f"v_t_step_{step:02d}"], self.v_t)
             self._gemm(L.KIND_BF16, L.EPI_EULER, B * S, E,
                        [self._linear_seg("model.action_out_proj", self.ey, None)], dt=dt, xt=self.xt,
                        xt_bf16=self.xt_bf)
+            if self.debug:
+                self._tap([f"x_t_step_{step:02d}"], self.xt)
 
     def _flow_desc(self) -> L.FlowDesc:
         """Descriptor of the persistent flow kernel over this runner's buffers."""
@@ -553,14 +635,22 @@ class SmolVLARunner:
                 L.check(rc, getattr(fn, "__name__", "svla"))
 
     def load_inputs(self, images, img_masks, lang_tokens, lang_masks, state, noise):
-        """Copy one call's inputs into the static buffers (stream-ordered, no host sync)."""
+        """Copy one call's inputs into the static buffers (stream-ordered, no host sync).  In embeds mode
+        ``images`` holds one bf16 [B, n_img_tokens, hidden] image embedding per camera."""
         c, B = self.cfg, self.B
         if state.shape[0] != B:
             raise ValueError(f"runner built for batch {B}, got {state.shape[0]}")
+        if len(images) != c.n_cams or len(img_masks) != c.n_cams:
+            raise ValueError(f"expected {c.n_cams} cameras")
         for cam in range(c.n_cams):
-            self.in_img[:, cam].copy_(images[cam], non_blocking=True)
-            self.in_img_mask[cam].copy_(img_masks[cam].to(torch.uint8) if not img_masks[cam].is_cuda
-                                        else img_masks[cam].to(torch.uint8), non_blocking=True)
+            if self.image_embeds:
+                if tuple(images[cam].shape) != (B, c.n_img_tokens, c.hidden):
+                    raise ValueError(f"image embedding {cam} must be [{B}, {c.n_img_tokens}, {c.hidden}]")
+                n = c.n_img_tokens
+                self.in_emb[:, cam * n:(cam + 1) * n].copy_(images[cam], non_blocking=True)
+            else:
+                self.in_img[:, cam].copy_(images[cam], non_blocking=True)
+            self.in_img_mask[cam].copy_(img_masks[cam].to(torch.uint8), non_blocking=True)
         toks = lang_tokens
         if toks.shape[1] != c.n_lang:  # pad / truncate like match_static_shape (trt_sample_actions_core_deploy.py:276-286)
             t = torch.zeros(B, c.n_lang, dtype=toks.dtype, device=toks.device)
