@@ -173,7 +173,7 @@ typedef struct svla_gemm_desc {
 #define SVLA_SPLITK_COUNTER_BYTES 65536
 
 /* Alignment (checked, status 1 otherwise): A / B operands and every output 16-byte aligned with row strides that
- * are multiples of 16 bytes and >= the segment's columns (ldo, ldr, ldq); I8 / W8A16 segments need wscale. */
+ * are multiples of 16 bytes and >= the segment's columns (ldo, ldr, ldq).  A NULL wscale reads as all ones. */
 int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream);
 
 /* -------------------------------------------------------------------------------------------------
@@ -231,13 +231,54 @@ enum { SVLA_ATTN_AUTO = 0, SVLA_ATTN_MMA_SYNC = 1, SVLA_ATTN_TCGEN05 = 2 };
 
 int32_t svla_attention(const svla_attn_desc* desc, svla_stream_t stream);
 
+/* -------------------------------------------------------------------------------------------------
+ * Plugin-semantics RoPE operators (the SmolVLAFusedRopeLayout / SmolVLAFusedRopeAttention TensorRT plugins).
+ * Data and position types use TensorRT's nvinfer1::DataType numbering, so a plugin's enqueue can pass its
+ * tensor descriptors' types straight through.
+ * ------------------------------------------------------------------------------------------------*/
+#define SVLA_DT_FLOAT 0
+#define SVLA_DT_HALF 1
+#define SVLA_DT_INT32 3
+#define SVLA_DT_BF16 7
+#define SVLA_DT_INT64 8
+
+/* FusedRopeLayoutParams (deploy/cuda/fused_rope_layout.h:24-30): defaults 15 / 5 / 64 / 10000. */
+typedef struct svla_rope_params {
+  int32_t q_heads, kv_heads, head_dim;
+  float max_wavelength;
+} svla_rope_params;
+
 /* RoPE + layout; replaces launchFusedRopeLayout (deploy/cuda/fused_rope_layout.h:32-34,
- * fused_rope_layout.cu:81-124) for bf16 tensors and int32 positions:
- * q_raw [B, L, Hq*64] -> q_out [B, Hq, L, 64]; k_raw [B, L, Hkv*64] -> k_out [B, Hq, 64, L]
- * (GQA-expanded and transposed), rotate-half with theta_i = pos / max_wavelength^(2i/64). */
+ * fused_rope_layout.cu:81-124, :545-571): q_raw [B, L, Hq*D] -> q_out [B, Hq, L, D];
+ * k_raw [B, L, Hkv*D] -> k_out [B, Hq, D, L] (GQA-expanded and transposed); rotate-half in fp32 with
+ * theta_i = pos / max_wavelength^(2i/D).  data_type FLOAT / HALF / BF16 (outputs in the same type),
+ * position_type INT32 / INT64 ([B, L]); head_dim even. */
+int32_t svla_fused_rope_layout(const void* q_raw, const void* k_raw, const void* position_ids, void* q_out,
+                               void* k_out, int32_t batch, int32_t seq_len, const svla_rope_params* params,
+                               int32_t data_type, int32_t position_type, svla_stream_t stream);
+
+/* The bf16 / int32-position / head_dim-64 case of svla_fused_rope_layout. */
 int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* pos, void* q_out, void* k_out,
                          int32_t batch, int32_t seq_len, int32_t q_heads, int32_t kv_heads,
                          float max_wavelength, svla_stream_t stream);
+
+/* Fused RoPE attention; replaces launchFusedRopeAttention (deploy/cuda/fused_rope_layout.h:44-46,
+ * fused_rope_layout.cu:271-431, :768-788; the plugin of deploy/cuda/fused_attention_v3_real.cpp:104-116):
+ * raw q [B, L, Hq*D], raw k / v [B, L, Hkv*D] (data_type), position_ids [B, L] (position_type), mask bool
+ * bytes [B, L, L] (nonzero = keep) -> context fp32 [B, Hq, L, D].  fp32 arithmetic throughout: rotated q / k,
+ * scores * D^-1/2 over kept keys, softmax, P.V; a query with every key masked gets the mean of V.
+ * head_dim a multiple of 32 up to 128. */
+int32_t svla_fused_rope_attention(const void* q_raw, const void* k_raw, const void* v_raw, const void* position_ids,
+                                  const void* mask, float* context, int32_t batch, int32_t seq_len,
+                                  const svla_rope_params* params, int32_t data_type, int32_t position_type,
+                                  svla_stream_t stream);
+
+/* The fp32 variant with implicit positions 0..L-1 and an fp32 mask (keep = value > 0.5); replaces
+ * launchFusedRopeAttentionFp32MaskImplicitPos (deploy/cuda/fused_rope_layout.h:48-50, .cu:433-543, :790-800). */
+int32_t svla_fused_rope_attention_f32_mask_implicit_pos(const float* q_raw, const float* k_raw, const float* v_raw,
+                                                        const float* mask, float* context, int32_t batch,
+                                                        int32_t seq_len, const svla_rope_params* params,
+                                                        svla_stream_t stream);
 
 /* -------------------------------------------------------------------------------------------------
  * sample_actions glue

@@ -93,6 +93,23 @@ def eager_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: tor
     return ctx.permute(0, 2, 1, 3).reshape(b, lq, hq * d)
 
 
+def fused_rope_attention(q_raw: torch.Tensor, k_raw: torch.Tensor, v_raw: torch.Tensor, positions: torch.Tensor,
+                         mask: torch.Tensor, hq: int, hkv: int, head_dim: int = 64,
+                         max_wavelength: float = 10_000.0) -> torch.Tensor:
+    """The SmolVLAFusedRopeAttention plugin's arithmetic (deploy/cuda/fused_rope_layout.cu:271-431), all fp32:
+    raw q [B, L, hq*D], k / v [B, L, hkv*D] (any float dtype, read as fp32), positions [B, L], keep-mask bool
+    [B, L, L] -> context fp32 [B, hq, L, D].  RoPE on the fp32 values (no rounding back to the input dtype),
+    masked scores at finfo.min (a query with no kept key gets the mean of V), fp32 softmax and P.V."""
+    b, L, _ = q_raw.shape
+    g = hq // hkv
+    q = apply_rope(q_raw.float().view(b, L, hq, head_dim), positions, max_wavelength)
+    k = apply_rope(k_raw.float().view(b, L, hkv, head_dim), positions, max_wavelength).repeat_interleave(g, dim=2)
+    v = v_raw.float().view(b, L, hkv, head_dim).repeat_interleave(g, dim=2)
+    scores = torch.einsum("bqhd,bkhd->bhqk", q, k) * (head_dim ** -0.5)
+    scores = torch.where(mask.bool()[:, None], scores, MASKED)
+    return torch.einsum("bhqk,bkhd->bhqd", torch.softmax(scores, dim=-1), v)
+
+
 def make_att_2d_masks(pad_masks: torch.Tensor, att_masks: torch.Tensor) -> torch.Tensor:
     """deploy/diagnose_3_4_numeric_baseline.py:42-46."""
     cumsum = torch.cumsum(att_masks.to(torch.int64), dim=1)

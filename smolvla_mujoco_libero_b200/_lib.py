@@ -102,6 +102,13 @@ class EngineInfo(ctypes.Structure):
 
 ENGINE_NO_GRAPH, ENGINE_NO_SPLIT_K, ENGINE_NO_FLOW = 1, 2, 4  # SVLA_ENGINE_* flags
 
+# SVLA_DT_*: TensorRT's nvinfer1::DataType numbering
+DT_FLOAT, DT_HALF, DT_INT32, DT_BF16, DT_INT64 = 0, 1, 3, 7, 8
+
+
+class RopeParams(ctypes.Structure):
+    _fields_ = [("q_heads", c_int32), ("kv_heads", c_int32), ("head_dim", c_int32), ("max_wavelength", c_float)]
+
 # name -> (restype, argtypes) for every symbol in include/svla.h
 SIGNATURES = {
     "svla_last_error": (c_char_p, []),
@@ -124,6 +131,12 @@ SIGNATURES = {
     "svla_attention": (c_int32, [POINTER(AttnDesc), c_void_p]),
     "svla_rope_layout": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                    c_int32, c_float, c_void_p]),
+    "svla_fused_rope_layout": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                                         POINTER(RopeParams), c_int32, c_int32, c_void_p]),
+    "svla_fused_rope_attention": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
+                                            c_int32, POINTER(RopeParams), c_int32, c_int32, c_void_p]),
+    "svla_fused_rope_attention_f32_mask_implicit_pos": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                                                  c_int32, c_int32, POINTER(RopeParams), c_void_p]),
     "svla_resize_pad_images": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64,
                                          c_int32, c_int32, c_float, c_void_p]),
     "svla_normalize_state": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,

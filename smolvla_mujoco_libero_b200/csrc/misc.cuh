@@ -188,47 +188,3 @@ __global__ void euler_init_kernel(const float* noise, float* xt, __nv_bfloat16* 
 }
 
 }  // namespace svla
-
-namespace svla {
-
-// Plugin-semantics RoPE + layout (deploy/cuda/fused_rope_layout.cu:81-124): q_raw [B, L, Hq*64] ->
-// q_out [B, Hq, L, 64]; k_raw [B, L, Hkv*64] -> k_out [B, Hq, 64, L] with kv head j expanded to query
-// heads j*g .. j*g+g-1 (g = Hq / Hkv).  One thread per rotation pair.
-__global__ void rope_layout_kernel(const __nv_bfloat16* q_raw, const __nv_bfloat16* k_raw, const int* pos,
-                                   __nv_bfloat16* q_out, __nv_bfloat16* k_out, int B, int L, int Hq, int Hkv,
-                                   float max_wavelength) {
-  pdl_wait();
-  pdl_trigger();
-  const long long nq = static_cast<long long>(B) * L * Hq * 32;
-  const long long nk = static_cast<long long>(B) * L * Hkv * 32;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= nq + nk) return;
-  const bool is_q = idx < nq;
-  long long r = is_q ? idx : idx - nq;
-  const int H = is_q ? Hq : Hkv;
-  const int i = static_cast<int>(r % 32); r /= 32;
-  const int h = static_cast<int>(r % H); r /= H;
-  const int l = static_cast<int>(r % L);
-  const int b = static_cast<int>(r / L);
-  const float freq = __fmul_rn(2.0f / 64.0f, static_cast<float>(i));
-  const float rad = __fdiv_rn(static_cast<float>(pos[b * L + l]), powf(max_wavelength, freq));
-  const float c = cosf(rad), s = sinf(rad);
-  const __nv_bfloat16* src = (is_q ? q_raw : k_raw) + (static_cast<size_t>(b) * L + l) * H * 64 + h * 64;
-  const float x1 = __bfloat162float(src[i]), x2 = __bfloat162float(src[i + 32]);
-  const __nv_bfloat16 o1 = __float2bfloat16_rn(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
-  const __nv_bfloat16 o2 = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
-  if (is_q) {
-    __nv_bfloat16* dst = q_out + ((static_cast<size_t>(b) * Hq + h) * L + l) * 64;
-    dst[i] = o1;
-    dst[i + 32] = o2;
-  } else {
-    const int gsz = Hq / Hkv;
-    for (int j = 0; j < gsz; ++j) {
-      __nv_bfloat16* dst = k_out + (static_cast<size_t>(b) * Hq + h * gsz + j) * 64 * L;
-      dst[static_cast<size_t>(i) * L + l] = o1;
-      dst[static_cast<size_t>(i + 32) * L + l] = o2;
-    }
-  }
-}
-
-}  // namespace svla

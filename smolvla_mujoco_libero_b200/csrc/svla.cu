@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -22,6 +23,7 @@
 #include "norm.cuh"
 #include "flow.cuh"
 #include "process.cuh"
+#include "rope.cuh"
 
 namespace svla {
 
@@ -255,7 +257,6 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
     for (int s = 0; s < d->nseg; ++s) {
       const svla_gemm_seg& g = d->seg[s];
       if (g.n > max_n) max_n = g.n;
-      if (kind != Kind::BF16 && !g.wscale) return fail(SVLA_ERR_ARG, "segment %d: null wscale", s);
       if (epi == Epi::Euler) {
         if (g.ldo < g.n) return fail(SVLA_ERR_ARG, "segment %d: EULER row stride %d below n=%d", s, g.ldo, g.n);
         continue;
@@ -720,14 +721,147 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
 int32_t svla_rope_layout(const void* q_raw, const void* k_raw, const int32_t* pos, void* q_out, void* k_out,
                          int32_t batch, int32_t seq_len, int32_t q_heads, int32_t kv_heads, float max_wavelength,
                          svla_stream_t stream) {
-  if (!q_raw || !k_raw || !pos || !q_out || !k_out || batch <= 0 || seq_len <= 0 || q_heads <= 0 || kv_heads <= 0 ||
-      q_heads % kv_heads || max_wavelength <= 0.f)
-    return fail(SVLA_ERR_ARG, "svla_rope_layout: bad args");
-  const long long total = static_cast<long long>(batch) * seq_len * (q_heads + kv_heads) * 32;
-  return launch(rope_layout_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, cs(stream), "rope_layout_kernel",
-                static_cast<const __nv_bfloat16*>(q_raw), static_cast<const __nv_bfloat16*>(k_raw), pos,
-      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out), batch, seq_len, q_heads, kv_heads,
-      max_wavelength);
+  const svla_rope_params p{q_heads, kv_heads, 64, max_wavelength};
+  return svla_fused_rope_layout(q_raw, k_raw, pos, q_out, k_out, batch, seq_len, &p, SVLA_DT_BF16, SVLA_DT_INT32,
+                                stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int32_t check_rope_params(const svla_rope_params* p, int32_t batch, int32_t seq_len, const char* who) {
+  if (!p) return fail(SVLA_ERR_ARG, "%s: null params", who);
+  if (batch <= 0 || seq_len <= 0 || p->q_heads <= 0 || p->kv_heads <= 0 || p->q_heads % p->kv_heads != 0 ||
+      p->head_dim <= 0 || p->head_dim % 2 != 0 || !(p->max_wavelength > 0.f))
+    return fail(SVLA_ERR_ARG, "%s: bad shape or params (batch %d, seq_len %d, heads %d/%d, head_dim %d)", who, batch,
+                seq_len, p->q_heads, p->kv_heads, p->head_dim);
+  return SVLA_OK;
+}
+
+template <typename T, typename PosT>
+int32_t launch_rope_layout_t(const void* q, const void* k, const void* pos, void* qo, void* ko, int32_t B, int32_t L,
+                             const svla_rope_params& p, cudaStream_t st) {
+  const long long total = static_cast<long long>(B) * L * (p.q_heads + p.kv_heads) * (p.head_dim / 2);
+  return launch(rope_layout_kernel<T, PosT>, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, st,
+                "rope_layout_kernel", static_cast<const T*>(q), static_cast<const T*>(k),
+                static_cast<const PosT*>(pos), static_cast<T*>(qo), static_cast<T*>(ko), static_cast<int>(B),
+                static_cast<int>(L), p.q_heads, p.kv_heads, p.head_dim, p.max_wavelength);
+}
+
+template <typename T>
+int32_t launch_rope_layout_pos(int32_t pos_type, const void* q, const void* k, const void* pos, void* qo, void* ko,
+                               int32_t B, int32_t L, const svla_rope_params& p, cudaStream_t st) {
+  if (pos_type == SVLA_DT_INT32) return launch_rope_layout_t<T, int32_t>(q, k, pos, qo, ko, B, L, p, st);
+  if (pos_type == SVLA_DT_INT64) return launch_rope_layout_t<T, long long>(q, k, pos, qo, ko, B, L, p, st);
+  return fail(SVLA_ERR_ARG, "svla_fused_rope_layout: position type %d (int32 %d or int64 %d)", pos_type,
+              SVLA_DT_INT32, SVLA_DT_INT64);
+}
+
+template <typename T, typename PosT>
+int32_t launch_rope_attention_t(const RopeAttnArgs& a, cudaStream_t st) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
+  auto kern = rope_attention_kernel<T, PosT>;
+  const size_t smem = rope_attention_smem();
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((a.L + a.qpc - 1) / a.qpc), a.Hkv, a.B);
+  return launch(kern, grid, dim3(kRopeAttnWarps * 32), smem, st, "rope_attention_kernel", a);
+}
+
+template <typename T>
+int32_t launch_rope_attention_pos(int32_t pos_type, const RopeAttnArgs& a, cudaStream_t st) {
+  if (a.pos == nullptr || pos_type == SVLA_DT_INT32) return launch_rope_attention_t<T, int32_t>(a, st);
+  if (pos_type == SVLA_DT_INT64) return launch_rope_attention_t<T, long long>(a, st);
+  return fail(SVLA_ERR_ARG, "svla_fused_rope_attention: position type %d (int32 %d or int64 %d)", pos_type,
+              SVLA_DT_INT32, SVLA_DT_INT64);
+}
+
+int32_t run_rope_attention(const void* q, const void* k, const void* v, const void* pos, const void* mask,
+                           int mask_f32, float* ctx, int32_t B, int32_t L, const svla_rope_params* p, int32_t data_type,
+                           int32_t pos_type, cudaStream_t st, const char* who) {
+  int32_t rc = check_rope_params(p, B, L, who);
+  if (rc) return rc;
+  if (!q || !k || !v || !ctx) return fail(SVLA_ERR_ARG, "%s: null q, k, v or context", who);
+  if (p->head_dim % 32 != 0 || p->head_dim > kRopeAttnMaxD)
+    return fail(SVLA_ERR_ARG, "%s: head_dim %d must be a multiple of 32 up to %d", who, p->head_dim, kRopeAttnMaxD);
+  const int g = p->q_heads / p->kv_heads;
+  if (g > kRopeAttnRows) return fail(SVLA_ERR_ARG, "%s: more than %d query heads per kv head", who, kRopeAttnRows);
+  RopeAttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.pos = pos;
+  a.mask = mask;
+  a.mask_f32 = mask_f32;
+  a.ctx = ctx;
+  a.B = B;
+  a.L = L;
+  a.Hq = p->q_heads;
+  a.Hkv = p->kv_heads;
+  a.D = p->head_dim;
+  a.qpc = kRopeAttnRows / g;
+  a.max_wavelength = p->max_wavelength;
+  a.scale = 1.0f / std::sqrt(static_cast<float>(p->head_dim));
+  switch (data_type) {
+    case SVLA_DT_FLOAT: return launch_rope_attention_pos<float>(pos_type, a, st);
+    case SVLA_DT_HALF: return launch_rope_attention_pos<__half>(pos_type, a, st);
+    case SVLA_DT_BF16: return launch_rope_attention_pos<__nv_bfloat16>(pos_type, a, st);
+    default: return fail(SVLA_ERR_ARG, "%s: data type %d (float %d, half %d or bf16 %d)", who, data_type,
+                         SVLA_DT_FLOAT, SVLA_DT_HALF, SVLA_DT_BF16);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t svla_fused_rope_layout(const void* q_raw, const void* k_raw, const void* position_ids, void* q_out,
+                               void* k_out, int32_t batch, int32_t seq_len, const svla_rope_params* params,
+                               int32_t data_type, int32_t position_type, svla_stream_t stream) {
+  int32_t rc = check_rope_params(params, batch, seq_len, "svla_fused_rope_layout");
+  if (rc) return rc;
+  if (!q_raw || !k_raw || !position_ids || !q_out || !k_out)
+    return fail(SVLA_ERR_ARG, "svla_fused_rope_layout: null pointer argument");
+  const svla_rope_params& p = *params;
+  switch (data_type) {
+    case SVLA_DT_FLOAT:
+      return launch_rope_layout_pos<float>(position_type, q_raw, k_raw, position_ids, q_out, k_out, batch, seq_len, p,
+                                           cs(stream));
+    case SVLA_DT_HALF:
+      return launch_rope_layout_pos<__half>(position_type, q_raw, k_raw, position_ids, q_out, k_out, batch, seq_len,
+                                            p, cs(stream));
+    case SVLA_DT_BF16:
+      return launch_rope_layout_pos<__nv_bfloat16>(position_type, q_raw, k_raw, position_ids, q_out, k_out, batch,
+                                                   seq_len, p, cs(stream));
+    default:
+      return fail(SVLA_ERR_ARG, "svla_fused_rope_layout: data type %d (float %d, half %d or bf16 %d)", data_type,
+                  SVLA_DT_FLOAT, SVLA_DT_HALF, SVLA_DT_BF16);
+  }
+}
+
+int32_t svla_fused_rope_attention(const void* q_raw, const void* k_raw, const void* v_raw, const void* position_ids,
+                                  const void* mask, float* context, int32_t batch, int32_t seq_len,
+                                  const svla_rope_params* params, int32_t data_type, int32_t position_type,
+                                  svla_stream_t stream) {
+  if (!position_ids || !mask) return fail(SVLA_ERR_ARG, "svla_fused_rope_attention: null positions or mask");
+  return run_rope_attention(q_raw, k_raw, v_raw, position_ids, mask, 0, context, batch, seq_len, params, data_type,
+                            position_type, cs(stream), "svla_fused_rope_attention");
+}
+
+int32_t svla_fused_rope_attention_f32_mask_implicit_pos(const float* q_raw, const float* k_raw, const float* v_raw,
+                                                        const float* mask, float* context, int32_t batch,
+                                                        int32_t seq_len, const svla_rope_params* params,
+                                                        svla_stream_t stream) {
+  if (!mask) return fail(SVLA_ERR_ARG, "svla_fused_rope_attention_f32_mask_implicit_pos: null mask");
+  return run_rope_attention(q_raw, k_raw, v_raw, nullptr, mask, 1, context, batch, seq_len, params, SVLA_DT_FLOAT,
+                            SVLA_DT_INT32, cs(stream), "svla_fused_rope_attention_f32_mask_implicit_pos");
 }
 
 int32_t svla_resize_pad_images(const void* src, int32_t src_u8_hwc, int32_t n, int32_t c, int32_t h, int32_t w,

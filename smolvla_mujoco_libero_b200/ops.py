@@ -239,18 +239,65 @@ def attention(q, k1, v1, hq: int, hkv: int, mask=None, k2=None, v2=None, qo_smoo
     return (o, qo) if qo is not None else o
 
 
+_DT = {torch.float32: L.DT_FLOAT, torch.float16: L.DT_HALF, torch.bfloat16: L.DT_BF16, torch.int32: L.DT_INT32,
+       torch.int64: L.DT_INT64}
+
+
+def _dtype_code(t: torch.Tensor, allowed: tuple, name: str) -> int:
+    code = _DT.get(t.dtype)
+    if code is None or code not in allowed:
+        raise ValueError(f"{name}: unsupported dtype {t.dtype}")
+    return code
+
+
 def rope_layout(q_raw: torch.Tensor, k_raw: torch.Tensor, pos: torch.Tensor, q_heads: int, kv_heads: int,
-                max_wavelength: float = 10000.0):
-    """Plugin semantics of SmolVLAFusedRopeLayout (deploy/cuda/fused_rope_layout.h:32-34)."""
-    _need(q_raw, torch.bfloat16, "q_raw")
-    _need(k_raw, torch.bfloat16, "k_raw")
-    _need(pos, torch.int32, "pos")
+                max_wavelength: float = 10000.0, head_dim: int = 64):
+    """Plugin semantics of SmolVLAFusedRopeLayout (deploy/cuda/fused_rope_layout.h:24-34): fp32 / fp16 / bf16
+    q_raw [B, L, Hq*D] and k_raw [B, L, Hkv*D], int32 / int64 positions [B, L] -> q [B, Hq, L, D] and
+    k [B, Hq, D, L] in the input dtype."""
+    for t, n in ((q_raw, "q_raw"), (k_raw, "k_raw"), (pos, "pos")):
+        _need(t, t.dtype, n)
+    if k_raw.dtype != q_raw.dtype:
+        raise ValueError("q_raw and k_raw must share a dtype")
+    dt = _dtype_code(q_raw, (L.DT_FLOAT, L.DT_HALF, L.DT_BF16), "q_raw")
+    pt = _dtype_code(pos, (L.DT_INT32, L.DT_INT64), "pos")
     b, l, _ = q_raw.shape
-    q_out = torch.empty(b, q_heads, l, 64, dtype=torch.bfloat16, device=q_raw.device)
-    k_out = torch.empty(b, q_heads, 64, l, dtype=torch.bfloat16, device=q_raw.device)
-    check(lib().svla_rope_layout(_p(q_raw), _p(k_raw), _p(pos), _p(q_out), _p(k_out), b, l, q_heads, kv_heads,
-                                 float(max_wavelength), _stream()), "rope_layout")
+    q_out = torch.empty(b, q_heads, l, head_dim, dtype=q_raw.dtype, device=q_raw.device)
+    k_out = torch.empty(b, q_heads, head_dim, l, dtype=q_raw.dtype, device=q_raw.device)
+    params = L.RopeParams(q_heads, kv_heads, head_dim, float(max_wavelength))
+    check(lib().svla_fused_rope_layout(_p(q_raw), _p(k_raw), _p(pos), _p(q_out), _p(k_out), b, l, ctypes.byref(params),
+                                       dt, pt, _stream()), "fused_rope_layout")
     return q_out, k_out
+
+
+def rope_attention(q_raw: torch.Tensor, k_raw: torch.Tensor, v_raw: torch.Tensor, pos: torch.Tensor | None,
+                   mask: torch.Tensor, q_heads: int, kv_heads: int, max_wavelength: float = 10000.0,
+                   head_dim: int = 64) -> torch.Tensor:
+    """Plugin semantics of SmolVLAFusedRopeAttention (deploy/cuda/fused_rope_layout.h:44-50): raw q / k / v,
+    positions [B, L] (int32 / int64; None with an fp32 mask = the implicit-position fp32 variant), keep-mask
+    [B, L, L] (bool, or fp32 > 0.5) -> fp32 context [B, Hq, L, D]."""
+    for t, n in ((q_raw, "q_raw"), (k_raw, "k_raw"), (v_raw, "v_raw"), (mask, "mask")):
+        _need(t, t.dtype, n)
+    if not (k_raw.dtype == v_raw.dtype == q_raw.dtype):
+        raise ValueError("q_raw, k_raw and v_raw must share a dtype")
+    b, l, _ = q_raw.shape
+    ctx = torch.empty(b, q_heads, l, head_dim, dtype=torch.float32, device=q_raw.device)
+    params = L.RopeParams(q_heads, kv_heads, head_dim, float(max_wavelength))
+    if pos is None:
+        _need(q_raw, torch.float32, "q_raw")
+        _need(mask, torch.float32, "mask")
+        check(lib().svla_fused_rope_attention_f32_mask_implicit_pos(_p(q_raw), _p(k_raw), _p(v_raw), _p(mask), _p(ctx),
+                                                                    b, l, ctypes.byref(params), _stream()),
+              "fused_rope_attention_f32_mask_implicit_pos")
+        return ctx
+    _need(pos, pos.dtype, "pos")
+    dt = _dtype_code(q_raw, (L.DT_FLOAT, L.DT_HALF, L.DT_BF16), "q_raw")
+    pt = _dtype_code(pos, (L.DT_INT32, L.DT_INT64), "pos")
+    if mask.dtype not in (torch.bool, torch.uint8):
+        raise ValueError("mask must be bool / uint8 (use pos=None for the fp32-mask variant)")
+    check(lib().svla_fused_rope_attention(_p(q_raw), _p(k_raw), _p(v_raw), _p(pos), _p(mask), _p(ctx), b, l,
+                                          ctypes.byref(params), dt, pt, _stream()), "fused_rope_attention")
+    return ctx
 
 
 def rope_table(max_pos: int, max_wavelength: float, device) -> torch.Tensor:
@@ -286,3 +333,23 @@ def _(x, qweight, wscale, bias):
 def _rope_layout_op(q_raw: torch.Tensor, k_raw: torch.Tensor, pos: torch.Tensor, q_heads: int, kv_heads: int,
                     max_wavelength: float) -> tuple[torch.Tensor, torch.Tensor]:
     return rope_layout(q_raw, k_raw, pos, q_heads, kv_heads, max_wavelength)
+
+
+@_rope_layout_op.register_fake
+def _(q_raw, k_raw, pos, q_heads, kv_heads, max_wavelength):
+    b, l, w = q_raw.shape
+    d = w // q_heads
+    return q_raw.new_empty(b, q_heads, l, d), q_raw.new_empty(b, q_heads, d, l)
+
+
+@torch.library.custom_op("svla::rope_attention", mutates_args=())
+def _rope_attention_op(q_raw: torch.Tensor, k_raw: torch.Tensor, v_raw: torch.Tensor, pos: torch.Tensor,
+                       mask: torch.Tensor, q_heads: int, kv_heads: int, max_wavelength: float) -> torch.Tensor:
+    return rope_attention(q_raw, k_raw, v_raw, pos, mask, q_heads, kv_heads, max_wavelength,
+                          head_dim=q_raw.shape[-1] // q_heads)
+
+
+@_rope_attention_op.register_fake
+def _(q_raw, k_raw, v_raw, pos, mask, q_heads, kv_heads, max_wavelength):
+    b, l, w = q_raw.shape
+    return q_raw.new_empty(b, q_heads, l, w // q_heads, dtype=torch.float32)

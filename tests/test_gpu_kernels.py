@@ -469,26 +469,116 @@ def test_attention_two_sources_and_quant_out():
 
 # ----------------------------------------------------------------------------- RoPE / layout
 
-def test_rope_layout_against_reference_kat(golden_dir):
-    """validate_fused_rope_layout_math.py inputs (seed 1000, L = 177) through the plugin-semantics kernel."""
+def _ulp(dtype) -> float:
+    return {torch.float32: 2.0 ** -23, torch.float16: 2.0 ** -10, torch.bfloat16: 2.0 ** -7}[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("pos_dtype", [torch.int32, torch.int64])
+def test_rope_layout_against_reference_kat(golden_dir, dtype, pos_dtype):
+    """validate_fused_rope_layout_math.py inputs (seed 1000, L = 177) through the plugin-semantics kernel, in
+    each data / position type the plugin takes (deploy/cuda/fused_rope_layout.cu:545-571).  fp32: within 1e-5
+    of the KAT's own values; fp16 / bf16: within one ulp of the output type of the fp32 rotation of the
+    same (rounded) inputs."""
+    from oracle.model import apply_rope
     torch.manual_seed(1000)
     q_raw = torch.randn(1, 177, 15 * 64)
     k_raw = torch.randn(1, 177, 5 * 64)
     d = np.load(golden_dir / "rope_kat.npz")
     rows = torch.from_numpy(d["rows"])
-    qb, kb = q_raw.to(torch.bfloat16), k_raw.to(torch.bfloat16)
-    pos = torch.arange(177, dtype=torch.int32)[None]
-    q_out, k_out = ops.rope_layout(qb.to(DEV), kb.to(DEV), pos.to(DEV), 15, 5, 10000.0)
-    q_rot = q_out.cpu().float().transpose(1, 2)[0, rows]                 # [rows, 15, 64]
-    k_rot = k_out.cpu().float().permute(0, 3, 1, 2)[0, rows][:, ::3]     # [rows, 5, 64] (undo GQA expansion)
-    # the kernel rotates bf16 inputs: compare within bf16 rounding of the fp32 reference KAT values
-    assert cosine(q_rot, torch.from_numpy(d["q_rot"])) >= 0.9999
-    assert cosine(k_rot, torch.from_numpy(d["k_rot"])) >= 0.9999
-    assert float((q_rot - torch.from_numpy(d["q_rot"])).abs().max()) < 0.05
-    # GQA expansion: the three query heads of each kv head hold identical keys
+    qx, kx = q_raw.to(dtype), k_raw.to(dtype)
+    pos = torch.arange(177, dtype=pos_dtype)[None]
+    q_out, k_out = ops.rope_layout(qx.to(DEV), kx.to(DEV), pos.to(DEV), 15, 5, 10000.0)
+    assert q_out.dtype == dtype and q_out.shape == (1, 15, 177, 64) and k_out.shape == (1, 15, 64, 177)
+    q_rot = q_out.cpu().float().transpose(1, 2)[0]                 # [177, 15, 64]
+    k_rot = k_out.cpu().float().permute(0, 3, 1, 2)[0][:, ::3]     # [177, 5, 64] (undo the GQA expansion)
+    if dtype == torch.float32:
+        assert float((q_rot[rows] - torch.from_numpy(d["q_rot"])).abs().max()) <= 1e-5
+        assert float((k_rot[rows] - torch.from_numpy(d["k_rot"])).abs().max()) <= 1e-5
+    ref_q = apply_rope(qx.float().view(1, 177, 15, 64), pos, 10000.0)[0]
+    ref_k = apply_rope(kx.float().view(1, 177, 5, 64), pos, 10000.0)[0]
+    for got, ref in ((q_rot, ref_q), (k_rot, ref_k)):
+        tol = ref.abs() * _ulp(dtype) + 2e-6
+        assert bool(((got - ref).abs() <= tol + 1e-6 + (ref.abs() * 2e-6)).all())
     kk = k_out.cpu()
     for j in range(5):
         assert torch.equal(kk[0, 3 * j], kk[0, 3 * j + 1]) and torch.equal(kk[0, 3 * j], kk[0, 3 * j + 2])
+
+
+def test_rope_layout_batched_positions_and_head_width():
+    """Two samples with padded (repeated) positions and a 32-wide head."""
+    from oracle.model import apply_rope
+    g = synthetic.generator(44)
+    b, l, hq, hkv, dh = 2, 50, 4, 2, 32
+    q = torch.randn(b, l, hq * dh, generator=g)
+    k = torch.randn(b, l, hkv * dh, generator=g)
+    pad = torch.ones(b, l, dtype=torch.bool)
+    pad[1, 30:40] = False
+    pos = (torch.cumsum(pad.to(torch.int64), 1) - 1)
+    q_out, k_out = ops.rope_layout(q.to(DEV), k.to(DEV), pos.to(DEV), hq, hkv, 100000.0, head_dim=dh)
+    ref_q = apply_rope(q.view(b, l, hq, dh), pos, 100000.0).transpose(1, 2)
+    ref_k = apply_rope(k.view(b, l, hkv, dh), pos, 100000.0).repeat_interleave(hq // hkv, 2).permute(0, 2, 3, 1)
+    assert float((q_out.cpu() - ref_q).abs().max()) <= 1e-5
+    assert float((k_out.cpu() - ref_k).abs().max()) <= 1e-5
+
+
+def _rope_attention_case(b, l, hq, hkv, seed):
+    from oracle.model import make_att_2d_masks
+    g = synthetic.generator(seed)
+    q = torch.randn(b, l, hq * 64, generator=g)
+    k = torch.randn(b, l, hkv * 64, generator=g)
+    v = torch.randn(b, l, hkv * 64, generator=g)
+    pad = torch.ones(b, l, dtype=torch.bool)
+    if b > 1:
+        pad[1, l - 21:l - 1] = False   # padded language tokens: their rows are fully masked
+    att = torch.zeros(b, l, dtype=torch.bool)
+    att[:, -1] = True                  # the state token
+    mask = make_att_2d_masks(pad, att)
+    pos = torch.cumsum(pad.to(torch.int64), 1) - 1
+    return q, k, v, pos, mask, pad
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("pos_dtype", [torch.int32, torch.int64])
+def test_fused_rope_attention_plugin_semantics(dtype, pos_dtype):
+    """raw q / k / v + position ids + bool mask -> fp32 context [B, 15, L, 64]
+    (deploy/cuda/fused_rope_layout.h:44-46; the v3 plugin, deploy/cuda/fused_attention_v3_real.cpp:104-116).
+    Bar: max-abs <= 2e-5 against the fp32 restatement on the same (rounded) inputs -- fp32 summation order and
+    the sin / cos / exp last bits differ; fully masked query rows are the mean of V."""
+    from oracle.model import fused_rope_attention
+    q, k, v, pos, mask, pad = _rope_attention_case(2, 177, 15, 5, 61)
+    qx, kx, vx = q.to(dtype), k.to(dtype), v.to(dtype)
+    ctx = ops.rope_attention(qx.to(DEV), kx.to(DEV), vx.to(DEV), pos.to(pos_dtype).to(DEV), mask.to(DEV), 15, 5)
+    assert ctx.dtype == torch.float32 and ctx.shape == (2, 15, 177, 64)
+    ref = fused_rope_attention(qx, kx, vx, pos, mask, 15, 5)
+    assert float((ctx.cpu() - ref).abs().max()) <= 2e-5
+    mean_v = vx.float().view(2, 177, 5, 64).mean(1).repeat_interleave(3, 1)    # [B, 15, 64]
+    dead = (~pad[1]).nonzero().flatten()
+    assert float((ctx.cpu()[1][:, dead] - mean_v[1][:, None]).abs().max()) <= 2e-5
+
+
+def test_fused_rope_attention_fp32_mask_implicit_positions():
+    """launchFusedRopeAttentionFp32MaskImplicitPos (deploy/cuda/fused_rope_layout.cu:433-543, :790-800):
+    positions 0..L-1, fp32 mask with keep = value > 0.5."""
+    from oracle.model import fused_rope_attention
+    q, k, v, _, mask, _ = _rope_attention_case(1, 130, 15, 5, 62)
+    pos = torch.arange(130)[None]
+    mf = mask.float() * 0.75 + torch.rand(mask.shape, generator=synthetic.generator(2)) * 0.2
+    ctx = ops.rope_attention(q.to(DEV), k.to(DEV), v.to(DEV), None, mf.to(DEV), 15, 5)
+    ref = fused_rope_attention(q, k, v, pos, mf > 0.5, 15, 5)
+    assert float((ctx.cpu() - ref).abs().max()) <= 2e-5
+
+
+def test_rope_entry_points_reject_what_the_plugin_rejects():
+    x = torch.zeros(1, 4, 64, device=DEV)
+    pos = torch.zeros(1, 4, dtype=torch.int16, device=DEV)
+    with pytest.raises(ValueError):
+        ops.rope_layout(x, x, pos, 1, 1)            # int16 positions
+    with pytest.raises(L.SvlaError):
+        ops.rope_layout(x, x, pos.int(), 3, 2)      # 3 query heads over 2 kv heads
+    with pytest.raises(L.SvlaError):
+        ops.rope_attention(x, x, x, pos.int(), torch.ones(1, 4, 4, dtype=torch.bool, device=DEV), 1, 1,
+                           head_dim=48)           # head_dim not a multiple of 32
 
 
 # ----------------------------------------------------------------------------- W8A16 epilogues (the expert's)
