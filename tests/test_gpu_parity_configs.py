@@ -146,8 +146,9 @@ def test_text_decoder_layer_at_prefix_length_177(wavelength):
 
     # RMSNorm + q/k/v quantisation: bf16 rows within one ulp of the oracle's, int8 bit-exact given them
     q_mod, k_mod, v_mod = (f"{p}.self_attn.{n}" for n in ("q_proj", "k_proj", "v_proj"))
+    # RMSNorm rounds twice (x * rsqrt to bf16, then * weight): a flipped first rounding can leave two ulps
     y = t(q_mod)[:177]
-    ulp_close(y, rms_norm(h, w[f"{p}.input_layernorm.weight"], cfg.rms_eps), max_mismatch=1e-3)
+    ulp_close(y, rms_norm(h, w[f"{p}.input_layernorm.weight"], cfg.rms_eps), ulps=2.0, max_mismatch=1e-3)
     q8 = {}
     for mod in (q_mod, k_mod, v_mod):
         q8[mod] = t(f"{mod}#int8")[:177]
@@ -184,7 +185,7 @@ def test_text_decoder_layer_at_prefix_length_177(wavelength):
     # post-attention RMSNorm + gate / up quantisation
     g_mod, u_mod, d_mod = (f"{p}.mlp.{n}" for n in ("gate_proj", "up_proj", "down_proj"))
     y2 = t(g_mod)[:177]
-    ulp_close(y2, rms_norm(h1, w[f"{p}.post_attention_layernorm.weight"], cfg.rms_eps), max_mismatch=1e-3)
+    ulp_close(y2, rms_norm(h1, w[f"{p}.post_attention_layernorm.weight"], cfg.rms_eps), ulps=2.0, max_mismatch=1e-3)
     for mod in (g_mod, u_mod):
         assert torch.equal(t(f"{mod}#int8")[:177], lin[mod].quantize_input(y2)), mod
     # SiLU gate (three bf16 roundings) and the W8A16 down projection + residual
@@ -206,7 +207,8 @@ def test_text_decoder_layer_at_prefix_length_177(wavelength):
     assert cosine(r.kcache[0].cpu()[:177], k_ref[0]) >= 0.999
     assert cosine(r.vcache[0].cpu()[:177], v_ref2[0]) >= 0.999
     # the final RMSNorm (prefix_out)
-    ulp_close(r.prefix_out.cpu()[:177], rms_norm(out, w[f"{TEXT}.norm.weight"], cfg.rms_eps), max_mismatch=1e-3)
+    ulp_close(r.prefix_out.cpu()[:177], rms_norm(out, w[f"{TEXT}.norm.weight"], cfg.rms_eps), ulps=2.0,
+              max_mismatch=1e-3)
 
 
 # ----------------------------------------------------------------------------- benchmark architecture
@@ -223,13 +225,18 @@ def bench():
 
 
 def _prefix_check(feats, taps, row, ref_row=0):
+    """16 quantized layers deep the two paths (exact int32 GEMMs on the GPU, bf16 fake-dequant GEMMs in the
+    oracle) round differently and some int8 activations flip, so the bar is relative: cosine >= 0.999 and
+    relative L2 <= 5% on the final prefix hidden states and on every layer's K and V."""
     z = feats["z"][row].cpu()
     ref = taps["prefix_out"][ref_row].float()
-    assert cosine(z, ref) >= 0.999
-    assert max_abs(z, ref) <= 2e-2 * float(ref.abs().max()) + 2e-2
+    rel = float((z - ref).norm() / ref.norm())
+    assert cosine(z, ref) >= 0.999 and rel <= 0.05, (row, cosine(z, ref), rel, max_abs(z, ref))
     for layer, ((k, v), (rk, rv)) in enumerate(zip(feats["kv_cache"], taps["kv"])):
         for got, want in ((k[row], rk[ref_row]), (v[row], rv[ref_row])):
-            assert cosine(got, want) >= 0.999, layer
+            got, want = got.float().cpu(), want.float()
+            rel = float((got - want).norm() / want.norm())
+            assert cosine(got, want) >= 0.999 and rel <= 0.05, (row, layer, cosine(got, want), rel)
 
 
 def test_prefix_kv_cache_bench_architecture_batch1_and_batch64(bench):
