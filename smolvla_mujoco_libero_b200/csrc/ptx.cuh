@@ -216,6 +216,13 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// The same descriptor with a leading byte offset: for an MN-major operand, the distance between successive
+// 64-element (128-byte) blocks along M/N, each an 8-row x 128-byte atom stack like the first.
+__device__ __forceinline__ uint64_t smem_desc_sw128_lbo(uint32_t saddr, uint32_t lbo_bytes) {
+  return (smem_desc_sw128(saddr) & ~(static_cast<uint64_t>(0x3FFF) << 16)) |
+         (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16);
+}
+
 // Instruction descriptors (cta_group::1, both operands K-major, dense).
 //   bits 4-5 D format (1 = f32, 2 = s32)   bits 7-9 / 10-12 A / B format
 //   bits 17-22 N >> 3                       bits 24-28 M >> 4

@@ -573,15 +573,15 @@ int32_t svla_norm_quant(const svla_norm_desc* d, svla_stream_t stream) {
   return fail(SVLA_ERR_ARG, "svla_norm_quant: k=%d too large (max 3072)", d->k);
 }
 
-// 3-D bf16 tensor map (column, row, batch) with a 64 x 128 x 1 box and the 128-byte swizzle; rows past
+// 3-D bf16 tensor map (column, row, batch) with a 64 x box_rows x 1 box and the 128-byte swizzle; rows past
 // `rows` (of each batch) read as zeros
 static int32_t make_tmap_bhd(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t batch,
-                             uint64_t rs, uint64_t bs) {
+                             uint64_t rs, uint64_t bs, uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(SVLA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {cols, rows, batch};
   cuuint64_t strides[2] = {rs * 2, bs * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -593,11 +593,13 @@ static int32_t make_tmap_bhd(CUtensorMap* map, const void* base, uint64_t cols, 
 static int32_t run_attention_tc(const svla_attn_desc* d, float scale, cudaStream_t stream) {
   AttnTcArgs a;
   std::memset(&a, 0, sizeof(a));
-  int32_t rc = make_tmap_bhd(&a.tq, d->q, static_cast<uint64_t>(d->hq) * 64, d->lq, d->batch, d->q_rs, d->q_bs);
+  int32_t rc = make_tmap_bhd(&a.tq, d->q, static_cast<uint64_t>(d->hq) * 64, d->lq, d->batch, d->q_rs, d->q_bs, 128);
   if (rc) return rc;
-  rc = make_tmap_bhd(&a.tk, d->k1, static_cast<uint64_t>(d->hkv) * 64, d->l1, d->batch, d->kv1_rs, d->kv1_bs);
+  rc = make_tmap_bhd(&a.tk, d->k1, static_cast<uint64_t>(d->hkv) * 64, d->l1, d->batch, d->kv1_rs, d->kv1_bs,
+                     atc::kKeys);
   if (rc) return rc;
-  rc = make_tmap_bhd(&a.tv, d->v1, static_cast<uint64_t>(d->hkv) * 64, d->l1, d->batch, d->kv1_rs, d->kv1_bs);
+  rc = make_tmap_bhd(&a.tv, d->v1, static_cast<uint64_t>(d->hkv) * 64, d->l1, d->batch, d->kv1_rs, d->kv1_bs,
+                     atc::kKeys);
   if (rc) return rc;
   a.o = static_cast<__nv_bfloat16*>(d->o);
   a.o_bs = d->o_bs;
@@ -619,17 +621,16 @@ static int32_t run_attention_tc(const svla_attn_desc* d, float scale, cudaStream
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
-  // one 128-query tile per CTA, two CTAs per SM: each CTA's softmax overlaps the other's MMAs, and one CTA's
+  // one 128-query tile per CTA, two CTAs per SM: one CTA's exponentials fill the other's gaps, and one CTA's
   // set-up and epilogue overlap the other's key loop
-  using C = atc::Cfg<false>;
+  auto kern = attention_tc_kernel;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, atc::kSmemBytes);
     if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
   dim3 grid(static_cast<unsigned>((d->lq + 127) / 128), d->hq, d->batch);
-  return launch(attention_tc_kernel<false>, grid, dim3(C::kThreads), C::kSmemBytes, stream, "attention_tc_kernel", a);
+  return launch(kern, grid, dim3(atc::kThreads), atc::kSmemBytes, stream, "attention_tc_kernel", a);
 }
 
 int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
