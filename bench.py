@@ -61,11 +61,12 @@ def dist_env():
 PG_TIMEOUT_S = 120  # ranks that wait for a missing peer end with an error instead of hanging
 
 
-def init_ranks(world: int, backend: str, device=None) -> None:
-    """One process per GPU (nccl) or per CPU rank (gloo, tests); rendezvous from the torchrun environment."""
+def init_ranks(world: int, backend: str, device=None, timeout_s: float = PG_TIMEOUT_S) -> None:
+    """One process per GPU (nccl) or per CPU rank (gloo, tests); rendezvous from the torchrun environment.  A
+    collective that waits for a rank which has died or hangs ends with an error after `timeout_s`."""
     if world > 1:
         kw = {"device_id": device} if device is not None else {}
-        dist.init_process_group(backend, timeout=timedelta(seconds=PG_TIMEOUT_S), **kw)
+        dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s), **kw)
 
 
 def max_over_ranks(value: float, world: int, device="cpu") -> float:

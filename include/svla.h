@@ -155,7 +155,7 @@ typedef struct svla_gemm_desc {
   float dt;               /* EPI_EULER */
   float* xt;
   void* xt_bf16;
-  uint64_t* debug_clock;  /* optional [16]: SM clock stamps of the first CTA's phases (profiling), else NULL */
+  uint64_t* debug_clock;  /* optional [32]: SM clock stamps of the first CTA's phases (profiling), else NULL */
   int32_t weights_resident; /* 1: every B operand was written before the previously launched kernel started
                                (packed weights), so its first tiles are fetched before waiting for that kernel */
   /* Split-K for GEMMs with few output tiles: split_k 0 = automatic (when a workspace is given and the
@@ -168,6 +168,10 @@ typedef struct svla_gemm_desc {
   int32_t split_k;
   void* workspace;
   size_t workspace_bytes;
+  /* CTA pairs: 0 or 1 = one CTA per 128-row tile, 2 = two CTAs per 256-row tile (tcgen05 cta_group::2:
+   * each SM loads its own A rows and half of B, 2/3 of the operand bytes per SM for the same MMA work;
+   * I8 / BF16 operands, block_n 128 or 256, no split-K, m > 128).  Bit-identical results either way. */
+  int32_t cta_pair;
 } svla_gemm_desc;
 
 #define SVLA_SPLITK_COUNTER_BYTES 65536
@@ -383,6 +387,9 @@ typedef struct svla_flow_desc {
   void* a_emb; void* a_t; void* eh; void* eq; void* ek; void* ev; void* ectx; void* emlp;
   uint32_t* sync;          /* 8 bytes (8-byte aligned), zero before the first launch; every completed launch leaves
                               it valid.  After a device error (svla_device_error) zero it again. */
+  uint32_t spin_limit;     /* polls of a grid barrier before the kernel gives up with device error 103 and returns
+                              (the other CTAs return at their next barrier); 0 = the library default (about 4M
+                              polls of ~32 ns: seconds) */
   uint64_t* debug_clock;   /* profiling, or NULL: 2 x 1024 (event, globaltimer ns) pairs of the first and last CTA
                               (events 1/2 barrier enter/exit, 3 rows staged, 4 products done, 5 epilogue done,
                               6 attention task done) */

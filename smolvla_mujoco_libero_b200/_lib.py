@@ -33,7 +33,7 @@ class GemmDesc(ctypes.Structure):
         ("resid_rows", c_int32), ("rope_cs", c_void_p), ("pos", c_void_p), ("max_pos", c_int32),
         ("q_smooth", c_void_p), ("q_rsmooth", c_void_p), ("q_act", c_float), ("qout", c_void_p), ("ldq", c_int32), ("dt", c_float),
         ("xt", c_void_p), ("xt_bf16", c_void_p), ("debug_clock", c_void_p), ("weights_resident", c_int32),
-        ("split_k", c_int32), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("split_k", c_int32), ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("cta_pair", c_int32),
     ]
 
 
@@ -65,6 +65,7 @@ class AttnDesc(ctypes.Structure):
 
 
 FLOW_MAX_LAYERS, FLOW_MAX_ROWS = 32, 64
+ERR_MBAR_TIMEOUT, ERR_BAD_SHAPE, ERR_FLOW_BARRIER = 101, 102, 103  # device error word codes
 
 
 class FlowLayer(ctypes.Structure):
@@ -85,7 +86,8 @@ class FlowDesc(ctypes.Structure):
         ("w_action_out", c_void_p), ("b_action_out", c_void_p), ("key_mask", c_void_p), ("key_mask_bs", c_int64),
         ("suffix_pos", c_void_p), ("cross_pos", c_void_p), ("rope_cs", c_void_p), ("max_pos", c_int32),
         ("a_emb", c_void_p), ("a_t", c_void_p), ("eh", c_void_p), ("eq", c_void_p), ("ek", c_void_p), ("ev", c_void_p),
-        ("ectx", c_void_p), ("emlp", c_void_p), ("sync", c_void_p), ("debug_clock", c_void_p),
+        ("ectx", c_void_p), ("emlp", c_void_p), ("sync", c_void_p), ("spin_limit", ctypes.c_uint32),
+        ("debug_clock", c_void_p),
         ("layer", FlowLayer * FLOW_MAX_LAYERS),
     ]
 

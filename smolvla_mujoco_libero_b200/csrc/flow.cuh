@@ -23,7 +23,7 @@
 //
 // Grid barrier: a monotonic 64-bit arrival counter in a caller-provided 8-byte buffer (zero before first use;
 // every completed launch leaves it at a multiple of the grid size).  Every wait is bounded: a barrier that
-// does not open within kSpinLimit polls records kErrFlowBarrier in the device error word; the other CTAs see
+// does not open within spin_limit polls (kSpinLimit unless the caller sets a shorter one) records kErrFlowBarrier in the device error word; the other CTAs see
 // the error word at their next wait and return, so the kernel always ends (and later launches refuse to run
 // while the error word is set).  A rows are staged with bulk copies completing on an mbarrier, also waited
 // for with a bound.
@@ -85,6 +85,7 @@ struct FlowArgs {
   int max_pos;
   __nv_bfloat16 *a_emb, *a_t, *eh, *eq, *ek, *ev, *ectx, *emlp;  // scratch rows
   unsigned long long* sync;    // monotonic arrival counter (a multiple of gridDim.x between launches)
+  uint32_t spin_limit;         // polls of a grid barrier before it gives up (kErrFlowBarrier)
   int* err;
   unsigned long long* dbg;     // profiling: (event, globaltimer ns) pairs of CTA 0 and the last CTA, or nullptr
   FlowLayer layer[kFlowMaxLayers];
@@ -169,7 +170,7 @@ __device__ bool grid_sync(const FlowArgs& a, FlowSmem& sm) {
     const unsigned long long target = (old / n + 1ull) * n;
     uint32_t spins = 0;
     while (ld_acquire_u64(a.sync) < target) {
-      if (++spins >= kSpinLimit) {
+      if (++spins >= a.spin_limit) {
         record_error(a.err, kErrFlowBarrier);
         ok = 0;
         break;

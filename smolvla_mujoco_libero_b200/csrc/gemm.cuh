@@ -6,7 +6,13 @@
 //   W8A16  A bf16 (TMA), B int8 (TMA into a staging buffer), converted by the epilogue warps to
 //          bf16(q * w_s[n]) in the 128B-swizzled layout the MMA reads, then kind::f16.  W8A16 linears.
 //
-// Persistent: one CTA per SM walks output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... in N-fastest
+// CTA pairs (CG = 2): a cluster of two CTAs computes 256-row tiles with tcgen05.mma.cta_group::2 (M = 256);
+// each CTA loads its own 128 A rows and half of the tile's B rows, so a k-stage brings 32 KB into each SM
+// instead of 48 KB for the same MMA work.  The main loop is bound by that per-SM operand ingest (measured
+// about 70 bytes per clock), so the pair form runs it faster.  The even CTA issues the MMAs and commits to
+// both CTAs' barriers; every load is a plain TMA load of the CTA's own tile.
+//
+// Persistent: one CTA (pair) per SM (pair) walks output tiles t = cluster, cluster + clusters, ... in N-fastest
 // order (the CTAs running at one time share A row-blocks; the weights stay L2-resident).  Accumulators
 // are double-buffered in TMEM (2 x P x BN columns) so the epilogue of one tile overlaps the MMAs of the next.
 // Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma (one lane), the next 8 or 16 warps
@@ -113,10 +119,10 @@ struct KindTraits<Kind::W8A16> {
   static __device__ __forceinline__ uint32_t idesc(int n) { return idesc_bf16(128, n); }
 };
 
-template <Kind KIND, int BN, int P, int STAGES>
+template <Kind KIND, int BN, int P, int STAGES, int CG = 1>
 struct GemmSmem {
   static constexpr int kATile = 128 * 128;            // bytes
-  static constexpr int kBTile = BN * 128;             // bytes (bf16 or int8 MMA operand)
+  static constexpr int kBTile = (BN / CG) * 128;      // bytes (bf16 or int8 MMA operand; a CTA pair splits B)
   static constexpr int kRawTile = KindTraits<KIND>::kConvert ? BN * 64 : 0;  // int8 staging, W8A16
   static constexpr int kStage = P * (kATile + kBTile + kRawTile);
   static constexpr int kBarOff = STAGES * kStage;
@@ -169,8 +175,8 @@ __device__ __forceinline__ float2 gelu_tanh_f2(float2 x) {
   return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
 }
 
-template <int BN, int P>
-__device__ __forceinline__ void tile_coord(const GemmArgs& a, int t, int& si, int& m0, int& n0) {
+template <int BN, int P, int CG = 1>
+__device__ __forceinline__ void tile_coord(const GemmArgs& a, int t, int& si, int& m0, int& n0, int rank = 0) {
   if (a.splits > 1) t /= a.splits;
   const int nt = t % a.tiles_n, mt = t / a.tiles_n;
   si = 0;
@@ -179,7 +185,7 @@ __device__ __forceinline__ void tile_coord(const GemmArgs& a, int t, int& si, in
     for (int s = 1; s < 3; ++s)
       if (s < a.nseg && nt >= a.seg[s].tile_begin) si = s;
   }
-  m0 = mt * 128;
+  m0 = mt * 128 * CG + rank * 128;
   n0 = (nt - a.seg[si].tile_begin) * BN;
 }
 
@@ -590,11 +596,12 @@ __device__ __forceinline__ bool splitk_reduce(const GemmArgs& args, int t, int m
   return true;
 }
 
-template <Kind KIND, int BN, int P, int STAGES, Epi EPI>
+template <Kind KIND, int BN, int P, int STAGES, Epi EPI, int CG>
 __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_kernel(const __grid_constant__ GemmArgs args) {
   constexpr int kEpiWarps = epi_warps<KIND, P, EPI>();
   using T = KindTraits<KIND>;
-  using S = GemmSmem<KIND, BN, P, STAGES>;
+  using S = GemmSmem<KIND, BN, P, STAGES, CG>;
+  static_assert(CG == 1 || (!T::kConvert && BN >= 128), "CTA pairs: I8 / BF16 operands, 128- or 256-column tiles");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
@@ -610,6 +617,12 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
   const int lane = threadIdx.x & 31;
   const int k_tiles = (args.K + T::kBK - 1) / T::kBK;
   const int n_tiles_total = args.tiles_m * args.tiles_n * (args.splits > 1 ? args.splits : 1);
+  // work units: tiles of 128 * CG rows, walked by clusters (single CTAs when CG = 1)
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  const int cl = blockIdx.x / CG, n_cl = gridDim.x / CG;
+  const bool leader = rank == 0;
+  // the leader's copy of a barrier (cluster address); the MMA issuer and its commits use these
+  auto leader_bar = [&](uint64_t* bar) -> uint32_t { return CG == 2 ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar); };
 
   if (threadIdx.x == 0) stamp(args.dbg, 0);
   if (threadIdx.x == 0) {
@@ -620,17 +633,23 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps);
+      mbar_init(&tempty[b], CG * kEpiWarps);  // a pair: the leader's counts both CTAs' epilogue warps
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, S::kTmemCols);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, S::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, S::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // both CTAs' barriers are initialised before either uses the other's
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (threadIdx.x == 0) stamp(args.dbg, 1);
@@ -652,32 +671,41 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
         prefetch_tmap(&args.tb[p]);
       }
       constexpr uint32_t kBBytes = T::kConvert ? S::kRawTile : S::kBTile;
+      constexpr uint32_t kStageTx = CG * P * (S::kATile + kBBytes);  // bytes both CTAs of the unit bring in
       auto b_dst = [&](uint8_t* st, int p) {
         return T::kConvert ? st + P * (S::kATile + S::kBTile) + p * S::kRawTile : st + P * S::kATile + p * S::kBTile;
       };
+      // a load of this CTA's tile that completes on the leader's full barrier of stage s
+      auto load = [&](void* dst, const CUtensorMap* map, int s, int x, int y) {
+        if constexpr (CG == 2)
+          tma_load_2d_pair(dst, map, leader_bar(&full[s]), x, y);
+        else
+          tma_load_2d(dst, map, &full[s], x, y);
+      };
+      const int b_row0 = static_cast<int>(rank) * (BN / CG);  // a pair: this CTA's half of the B rows
       // Weights packed before the previous kernel started (weights_resident) do not depend on it: the first
       // tile's first STAGES weight tiles are requested before waiting, so they stream in while it finishes.
       int pre = 0;
-      if (args.weights_resident && blockIdx.x < n_tiles_total) {
+      if (args.weights_resident && cl < n_tiles_total) {
         int si, m0, n0, kb, ke;
-        tile_coord<BN, P>(args, blockIdx.x, si, m0, n0);
-        k_range(args, blockIdx.x, k_tiles, kb, ke);
+        tile_coord<BN, P, CG>(args, cl, si, m0, n0, rank);
+        k_range(args, cl, k_tiles, kb, ke);
         pre = ke - kb < STAGES ? ke - kb : STAGES;
         for (int i = 0; i < pre; ++i) {
           uint8_t* st = smem + i * S::kStage;
-          mbar_arrive_expect_tx(&full[i], P * (S::kATile + kBBytes));
+          if (leader) mbar_arrive_expect_tx(&full[i], kStageTx);
 #pragma unroll
           for (int p = 0; p < P; ++p)
-            tma_load_2d(b_dst(st, p), &args.tb[(P == 1) ? si : p], &full[i], (kb + i) * T::kBK, n0);
+            load(b_dst(st, p), &args.tb[(P == 1) ? si : p], i, (kb + i) * T::kBK, n0 + b_row0);
         }
       }
       pdl_wait();
       pdl_trigger();
       uint32_t g = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x) {
+      for (int t = cl; t < n_tiles_total && ok; t += n_cl) {
         int si, m0, n0, kb, ke;
-        tile_coord<BN, P>(args, t, si, m0, n0);
+        tile_coord<BN, P, CG>(args, t, si, m0, n0, rank);
         k_range(args, t, k_tiles, kb, ke);
         for (int kt = kb; kt < ke; ++kt, ++g) {
           const int s = g % STAGES;
@@ -685,31 +713,42 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
           uint8_t* st = smem + s * S::kStage;
           if (static_cast<int>(g) < pre) {  // weights already requested: only the activations remain
 #pragma unroll
-            for (int p = 0; p < P; ++p)
-              tma_load_2d(st + p * S::kATile, &args.ta[(P == 1) ? si : p], &full[s], kt * T::kBK, m0);
+            for (int p = 0; p < P; ++p) load(st + p * S::kATile, &args.ta[(P == 1) ? si : p], s, kt * T::kBK, m0);
             if (g == 0) stamp(args.dbg, 2);
             continue;
           }
           if (!(ok = bounded_wait(&empty[s], ph ^ 1))) break;
-          mbar_arrive_expect_tx(&full[s], P * (S::kATile + kBBytes));
+          if (leader) mbar_arrive_expect_tx(&full[s], kStageTx);
 #pragma unroll
           for (int p = 0; p < P; ++p) {
             const int mi = (P == 1) ? si : p;
-            tma_load_2d(st + p * S::kATile, &args.ta[mi], &full[s], kt * T::kBK, m0);
-            tma_load_2d(b_dst(st, p), &args.tb[mi], &full[s], kt * T::kBK, n0);
+            load(st + p * S::kATile, &args.ta[mi], s, kt * T::kBK, m0);
+            load(b_dst(st, p), &args.tb[mi], s, kt * T::kBK, n0 + b_row0);
           }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = T::idesc(BN);
+    // ---------------- MMA issuer (a pair: the leader only, for both CTAs)
+    if (lane == 0 && leader) {
+      // M = 128 per CTA, 256 for a pair
+      const uint32_t idesc = (KIND == Kind::I8) ? idesc_i8(128 * CG, BN) : idesc_bf16(128 * CG, BN);
+      // a commit to the barrier `bar` of both CTAs of the unit
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (CG == 2) {
+          mma_commit_pair(mapa_shared(smem_u32(bar), 0));
+          mma_commit_pair(mapa_shared(smem_u32(bar), 1));
+        } else {
+          mma_commit(bar);
+        }
+      };
       uint32_t g = 0, lt = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < n_tiles_total && ok; t += gridDim.x, ++lt) {
+      for (int t = cl; t < n_tiles_total && ok; t += n_cl, ++lt) {
         const uint32_t ab = lt & 1, use = lt >> 1;
+        if (lt < 8) stamp(args.dbg, 16 + 2 * lt);  // profiling: waits here mean the epilogue sets the pace
         if (!(ok = bounded_wait(&tempty[ab], (use & 1) ^ 1))) break;
+        if (lt < 8) stamp(args.dbg, 17 + 2 * lt);
         tc_fence_after();
         const uint32_t d_base = tmem_base + ab * S::kAccCols;
         int kb, ke;
@@ -734,15 +773,21 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
               const uint64_t ad = smem_desc_sw128(a_addr + kk * 32);
               const uint64_t bd = smem_desc_sw128(b_addr + kk * 32);
               const uint32_t acc = (kt > kb || kk > 0) ? 1u : 0u;
-              if constexpr (KIND == Kind::I8)
+              if constexpr (CG == 2) {
+                if constexpr (KIND == Kind::I8)
+                  mma_i8_pair(d_tmem, ad, bd, idesc, acc);
+                else
+                  mma_bf16_pair(d_tmem, ad, bd, idesc, acc);
+              } else if constexpr (KIND == Kind::I8) {
                 mma_i8(d_tmem, ad, bd, idesc, acc);
-              else
+              } else {
                 mma_bf16(d_tmem, ad, bd, idesc, acc);
+              }
             }
           }
-          mma_commit(&empty[s]);  // stage s free once these MMAs have read it
+          commit(&empty[s]);  // stage s free (in both CTAs) once these MMAs have read it
         }
-        mma_commit(&tfull[ab]);  // the tile's accumulator is complete
+        commit(&tfull[ab]);  // the tile's accumulator is complete
         if (lt == 0) stamp(args.dbg, 5);
       }
     }
@@ -764,7 +809,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
     auto fetch_consts = [&](int t) {
       if (t >= n_tiles_total || etid >= BN) return;
       int si, m0, n0;
-      tile_coord<BN, P>(args, t, si, m0, n0);
+      tile_coord<BN, P, CG>(args, t, si, m0, n0, rank);
       const int n = n0 + etid;
 #pragma unroll
       for (int set = 0; set < P; ++set) {
@@ -794,22 +839,23 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
     };
     // scales and biases are written with the weights: when those predate the previous kernel the first
     // tile's constants are requested before waiting for it
-    if (args.weights_resident) fetch_consts(blockIdx.x);
+    if (args.weights_resident) fetch_consts(cl);
     pdl_wait();  // residuals / outputs may be touched by the previous kernel
-    if (!args.weights_resident) fetch_consts(blockIdx.x);
-    put_consts(blockIdx.x, 0);
+    if (!args.weights_resident) fetch_consts(cl);
+    put_consts(cl, 0);
     asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
     if (etid == 0) stamp(args.dbg, 6);
     // Every epilogue warp runs every iteration (also after a failed wait) so that the named barrier
     // below is reached the same number of times by all of them.
-    for (int t = blockIdx.x; t < n_tiles_total; t += gridDim.x, ++lt) {
+    const uint32_t tempty_leader[2] = {leader_bar(&tempty[0]), leader_bar(&tempty[1])};
+    for (int t = cl; t < n_tiles_total; t += n_cl, ++lt) {
       const uint32_t ab = lt & 1, use = lt >> 1;
       int si, m0, n0;
-      tile_coord<BN, P>(args, t, si, m0, n0);
+      tile_coord<BN, P, CG>(args, t, si, m0, n0, rank);
       // this tile's constants are in buffer ab (written before the barrier that ended the previous
       // iteration); the next tile's are requested now
       const float* cst = const_base + ab * S::kConstArrays * BN;
-      fetch_consts(t + gridDim.x);
+      fetch_consts(t + n_cl);
       bool acc_waited = false, acc_ok = true;
       auto wait_acc = [&]() -> bool {
         if (acc_waited) return acc_ok;
@@ -829,11 +875,16 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
       if (lt == 0 && etid == 0) stamp(args.dbg, 8);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[ab]);
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbar_arrive_cluster(tempty_leader[ab]);
+        else
+          mbar_arrive(&tempty[ab]);
+      }
       ok = ok_t;
       // the other buffer was last read by the previous tile, which every warp finished before the barrier
       // that ended the previous iteration
-      put_consts(t + gridDim.x, ab ^ 1u);
+      put_consts(t + n_cl, ab ^ 1u);
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
     }
   } else if constexpr (T::kConvert) {
@@ -899,11 +950,16 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
 
   tc_fence_before();
   __syncthreads();
+  // a pair: neither CTA leaves while the other may still arrive on its barriers or read its shared memory
+  if constexpr (CG == 2) cluster_sync();
   if (threadIdx.x == 0) stamp(args.dbg, 9);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, S::kTmemCols);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem_base, S::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, S::kTmemCols);
     if (lane == 0) stamp(args.dbg, 10);
   }
 }

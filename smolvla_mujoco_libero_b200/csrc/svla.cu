@@ -61,6 +61,35 @@ bool pdl_enabled() {
 }
 
 template <typename... KArgs, typename... Args>
+int32_t launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       const char* name, unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster_x > 1) {  // CTA pairs: clusters of cluster_x consecutive CTAs along x
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster_x;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+  return check_launch(name);
+}
+
+template <typename... KArgs, typename... Args>
 int32_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* name,
                Args&&... args) {
   cudaLaunchConfig_t cfg = {};
@@ -130,19 +159,19 @@ int32_t make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt, in
 }
 
 // ---------------------------------------------------------------- GEMM dispatch
-template <Kind K, int BN, int P>
+template <Kind K, int BN, int P, int CG = 1>
 constexpr int stages_for() {
-  constexpr int a = 128 * 128, b = BN * 128, raw = KindTraits<K>::kConvert ? BN * 64 : 0;
+  constexpr int a = 128 * 128, b = (BN / CG) * 128, raw = KindTraits<K>::kConvert ? BN * 64 : 0;
   constexpr int stage = P * (a + b + raw);
   constexpr int s = (200 * 1024) / stage;
   return s > 8 ? 8 : (s < 2 ? 2 : s);
 }
 
-template <Kind K, int BN, int P, Epi E>
+template <Kind K, int BN, int P, Epi E, int CG = 1>
 int32_t launch_gemm_inst(const GemmArgs& args, dim3 grid, cudaStream_t stream) {
-  constexpr int ST = stages_for<K, BN, P>();
-  using S = GemmSmem<K, BN, P, ST>;
-  auto kern = gemm_sm100_kernel<K, BN, P, ST, E>;
+  constexpr int ST = stages_for<K, BN, P, CG>();
+  using S = GemmSmem<K, BN, P, ST, CG>;
+  auto kern = gemm_sm100_kernel<K, BN, P, ST, E, CG>;
   static bool configured[64] = {false};  // the attribute is per function and per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -152,45 +181,47 @@ int32_t launch_gemm_inst(const GemmArgs& args, dim3 grid, cudaStream_t stream) {
     if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  return launch(kern, grid, dim3(gemm_threads<K, P, E>()), S::kBytes, stream, "gemm_sm100_kernel", args);
+  return launch_cluster(kern, grid, dim3(gemm_threads<K, P, E>()), S::kBytes, stream, "gemm_sm100_kernel", CG, args);
 }
 
-template <Kind K, int BN, int P>
+template <Kind K, int BN, int P, int CG>
 int32_t dispatch_epi(Epi e, const GemmArgs& args, dim3 grid, cudaStream_t st) {
-  if constexpr (P == 2) {
-    if (e == Epi::SiluMul) return launch_gemm_inst<K, BN, 2, Epi::SiluMul>(args, grid, st);
+  if constexpr (CG == 2 && (K == Kind::W8A16 || BN < 128)) {
+    return fail(SVLA_ERR_ARG, "CTA pairs take I8 / BF16 operands and 128- or 256-column tiles");
+  } else if constexpr (P == 2) {
+    if (e == Epi::SiluMul) return launch_gemm_inst<K, BN, 2, Epi::SiluMul, CG>(args, grid, st);
     return fail(SVLA_ERR_ARG, "pair GEMMs support only the SILU_MUL epilogue");
   } else {
     switch (e) {
-      case Epi::Bf16: return launch_gemm_inst<K, BN, 1, Epi::Bf16>(args, grid, st);
-      case Epi::Rope: return launch_gemm_inst<K, BN, 1, Epi::Rope>(args, grid, st);
-      case Epi::Resid: return launch_gemm_inst<K, BN, 1, Epi::Resid>(args, grid, st);
-      case Epi::F32: return launch_gemm_inst<K, BN, 1, Epi::F32>(args, grid, st);
+      case Epi::Bf16: return launch_gemm_inst<K, BN, 1, Epi::Bf16, CG>(args, grid, st);
+      case Epi::Rope: return launch_gemm_inst<K, BN, 1, Epi::Rope, CG>(args, grid, st);
+      case Epi::Resid: return launch_gemm_inst<K, BN, 1, Epi::Resid, CG>(args, grid, st);
+      case Epi::F32: return launch_gemm_inst<K, BN, 1, Epi::F32, CG>(args, grid, st);
       default: break;
     }
-    if (e == Epi::GeluQuant) return launch_gemm_inst<K, BN, 1, Epi::GeluQuant>(args, grid, st);
+    if (e == Epi::GeluQuant) return launch_gemm_inst<K, BN, 1, Epi::GeluQuant, CG>(args, grid, st);
     if constexpr (K == Kind::I8) {
-      if (e == Epi::I32) return launch_gemm_inst<K, BN, 1, Epi::I32>(args, grid, st);
+      if (e == Epi::I32) return launch_gemm_inst<K, BN, 1, Epi::I32, CG>(args, grid, st);
     }
     if constexpr (K == Kind::BF16) {
-      if (e == Epi::SiluBf16) return launch_gemm_inst<K, BN, 1, Epi::SiluBf16>(args, grid, st);
-      if (e == Epi::Euler) return launch_gemm_inst<K, BN, 1, Epi::Euler>(args, grid, st);
+      if (e == Epi::SiluBf16) return launch_gemm_inst<K, BN, 1, Epi::SiluBf16, CG>(args, grid, st);
+      if (e == Epi::Euler) return launch_gemm_inst<K, BN, 1, Epi::Euler, CG>(args, grid, st);
     }
     return fail(SVLA_ERR_ARG, "epilogue %d not available for operand kind %d", static_cast<int>(e),
                 static_cast<int>(K));
   }
 }
 
-template <Kind K>
+template <Kind K, int CG>
 int32_t dispatch_bn(int bn, int pair, Epi e, const GemmArgs& args, dim3 grid, cudaStream_t st) {
   if (pair) {
-    if (bn == 64) return dispatch_epi<K, 64, 2>(e, args, grid, st);
-    if (bn == 128) return dispatch_epi<K, 128, 2>(e, args, grid, st);
+    if (bn == 64) return dispatch_epi<K, 64, 2, CG>(e, args, grid, st);
+    if (bn == 128) return dispatch_epi<K, 128, 2, CG>(e, args, grid, st);
     return fail(SVLA_ERR_ARG, "pair GEMMs use block_n 64 or 128 (got %d)", bn);
   }
-  if (bn == 64) return dispatch_epi<K, 64, 1>(e, args, grid, st);
-  if (bn == 128) return dispatch_epi<K, 128, 1>(e, args, grid, st);
-  if (bn == 256) return dispatch_epi<K, 256, 1>(e, args, grid, st);
+  if (bn == 64) return dispatch_epi<K, 64, 1, CG>(e, args, grid, st);
+  if (bn == 128) return dispatch_epi<K, 128, 1, CG>(e, args, grid, st);
+  if (bn == 256) return dispatch_epi<K, 256, 1, CG>(e, args, grid, st);
   return fail(SVLA_ERR_ARG, "block_n must be 64, 128 or 256 (got %d)", bn);
 }
 
@@ -279,6 +310,17 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   }
   const int sms = sm_count();
   const int bn = d->block_n ? d->block_n : choose_block_n(d, sms);
+  // CTA pairs (256-row tiles over two SMs, half the B rows per SM), on request only: measured on the
+  // benchmark's GEMMs they are bit-identical but not faster (SigLIP q/k/v 0.288 -> 0.298 ms, fc1 0.549 ->
+  // 0.593 ms, fc2 0.288 -> 0.283 ms, expert down 21.0 -> 22.9 us), so the main loop is not bound by the
+  // per-SM operand bytes they save
+  if (d->cta_pair < 0 || d->cta_pair > 2) return fail(SVLA_ERR_ARG, "cta_pair must be 0, 1 or 2");
+  int cg = 1;
+  if (d->cta_pair == 2) {
+    if (kind == Kind::W8A16 || bn < 128 || d->split_k > 1 || d->m <= 128 || sms < 2)
+      return fail(SVLA_ERR_ARG, "cta_pair 2 needs I8 / BF16 operands, block_n >= 128, no split-K and m > 128");
+    cg = 2;
+  }
   const int elem_a = (kind == Kind::I8) ? 1 : 2;
   const int elem_b = (kind == Kind::BF16) ? 2 : 1;
   const int bk = (kind == Kind::I8) ? 128 : 64;
@@ -303,7 +345,7 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
                      CU_TENSOR_MAP_SWIZZLE_NONE);
     } else {
       const CUtensorMapDataType dtb = (kind == Kind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-      rc = make_tmap(&args.tb[s], g.b, dtb, elem_b, d->k, g.n, g.ldb, bk, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+      rc = make_tmap(&args.tb[s], g.b, dtb, elem_b, d->k, g.n, g.ldb, bk, bn / cg, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (rc) return rc;
     GemmSeg& o = args.seg[s];
@@ -325,7 +367,7 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   args.nseg = d->nseg;
   args.M = d->m;
   args.K = d->k;
-  args.tiles_m = (d->m + 127) / 128;
+  args.tiles_m = (d->m + 128 * cg - 1) / (128 * cg);
   args.tiles_n = tiles;
   args.rows_per_group = d->rows_per_group;
   args.group_stride = d->group_stride;
@@ -400,11 +442,20 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
     }
   }
   const long long total_tiles = out_tiles * args.splits;
-  dim3 grid(static_cast<unsigned>(total_tiles < sms ? total_tiles : sms));
+  const long long units = sms / cg;  // CTAs (pairs) resident at once, one per SM (pair of SMs)
+  dim3 grid(static_cast<unsigned>(cg * (total_tiles < units ? total_tiles : units)));
+  if (cg == 2) {
+    if (args.splits > 1) return fail(SVLA_ERR_ARG, "CTA pairs do not split K");
+    switch (kind) {
+      case Kind::I8: return dispatch_bn<Kind::I8, 2>(bn, d->pair, epi, args, grid, stream);
+      case Kind::BF16: return dispatch_bn<Kind::BF16, 2>(bn, d->pair, epi, args, grid, stream);
+      default: return fail(SVLA_ERR_ARG, "CTA pairs take I8 / BF16 operands");
+    }
+  }
   switch (kind) {
-    case Kind::I8: return dispatch_bn<Kind::I8>(bn, d->pair, epi, args, grid, stream);
-    case Kind::BF16: return dispatch_bn<Kind::BF16>(bn, d->pair, epi, args, grid, stream);
-    case Kind::W8A16: return dispatch_bn<Kind::W8A16>(bn, d->pair, epi, args, grid, stream);
+    case Kind::I8: return dispatch_bn<Kind::I8, 1>(bn, d->pair, epi, args, grid, stream);
+    case Kind::BF16: return dispatch_bn<Kind::BF16, 1>(bn, d->pair, epi, args, grid, stream);
+    case Kind::W8A16: return dispatch_bn<Kind::W8A16, 1>(bn, d->pair, epi, args, grid, stream);
   }
   return fail(SVLA_ERR_ARG, "unreachable");
 }
@@ -1016,6 +1067,7 @@ int32_t svla_flow(const svla_flow_desc* d, svla_stream_t stream) {
                       d->key_mask_bs < (d->prefix_len + 15) / 16 * 16))
     return fail(SVLA_ERR_ARG, "svla_flow: key flag rows must be 16-byte aligned and hold prefix_len rounded up to 16");
   a.sync = reinterpret_cast<unsigned long long*>(d->sync);
+  a.spin_limit = d->spin_limit ? d->spin_limit : kSpinLimit;
   a.dbg = reinterpret_cast<unsigned long long*>(d->debug_clock);
   a.err = device_error_ptr();
   if (!a.err) return fail(SVLA_ERR_CUDA, "svla_flow: device error word unavailable");

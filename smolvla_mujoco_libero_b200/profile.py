@@ -76,10 +76,10 @@ def op_gemm(a) -> dict:
     if a.split_k != 1:
         ws = ops.splitk_workspace(64 << 20, dev)
         extra.update(split_k=a.split_k, workspace=ws, workspace_bytes=ws.numel())
-    d = ops.gemm_desc(kind, epi, a.m, a.k, segs, block_n=a.block_n, **extra)
+    d = ops.gemm_desc(kind, epi, a.m, a.k, segs, block_n=a.block_n, cta_pair=a.cta_pair, **extra)
     ms = time_op(lambda: ops.gemm(d), a.iters)
     # phase clock stamps of CTA 0 from one more launch
-    dbg = torch.zeros(16, dtype=torch.int64, device=dev)
+    dbg = torch.zeros(32, dtype=torch.int64, device=dev)
     d.debug_clock = dbg.data_ptr()
     ops.gemm(d)
     torch.cuda.synchronize()
@@ -87,10 +87,13 @@ def op_gemm(a) -> dict:
     d.debug_clock = None
     names = ["entry", "setup", "tma0", "full0", "conv0", "commit0", "epi_consts", "epi_acc", "epi_done", "sync_end", "dealloc",
              "sk_stored", "sk_bar", "sk_counted", "sk_last", "sk_notlast"]
+    # MMA warp, accumulator buffer of tile i: wait begins / ends (a long wait = the epilogue sets the pace)
+    names += [f"acc{i}_{w}" for i in range(8) for w in ("wait", "free")]
     phases = {names[i]: (c[i] - c[0]) if c[i] else None for i in range(len(names))}
     ops_count = 2.0 * a.m * a.n * a.k * (2 if epi == 4 else 1)
     best = min(ms)
-    return {"op": "gemm", "kind": a.kind, "epi": a.epi, "m": a.m, "n": a.n, "k": a.k, "split_k": a.split_k, "ms": ms,
+    return {"op": "gemm", "kind": a.kind, "epi": a.epi, "m": a.m, "n": a.n, "k": a.k, "split_k": a.split_k,
+            "cta_pair": a.cta_pair, "ms": ms,
             "tflops_best": ops_count / (best / 1e3) / 1e12, "cta0_cycles": phases}
 
 
@@ -199,6 +202,7 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=768)
     ap.add_argument("--block-n", type=int, default=0)
     ap.add_argument("--split-k", type=int, default=1, help="GEMM split-K: 1 off, 0 automatic, n splits")
+    ap.add_argument("--cta-pair", type=int, default=0, help="GEMM CTA pairs: 0 automatic, 1 off, 2 on")
     ap.add_argument("--lq", type=int, default=1024)
     ap.add_argument("--lk", type=int, default=1024)
     ap.add_argument("--heads", type=int, default=12)

@@ -1,12 +1,15 @@
 """The multi-rank path of bench.py on CPU: two gloo ranks (torchrun-style environment, 127.0.0.1) take the
 same collective steps; the slowest rank's time and the whole-job rate come out the same on every rank; the
-reference arm runs on rank 0 only."""
+reference arm runs on rank 0 only; a rank that dies or hangs between steps ends the survivor's next collective
+with an error within the process-group timeout instead of a hang."""
 
 import os
 import socket
 import sys
+import time
 from pathlib import Path
 
+import pytest
 import torch.multiprocessing as mp
 
 REPO = Path(__file__).resolve().parent.parent
@@ -53,3 +56,43 @@ def test_reference_arm_runs_on_rank_zero_only(capsys):
     import bench
     assert bench.run_reference(None, 1, 2) == 0
     assert capsys.readouterr().out == ""
+
+
+def _failing_rank(rank: int, world: int, port: int, mode: str, q) -> None:
+    """Step 1 together; then rank 1 exits ("exit") or stops answering ("hang"), and rank 0 takes step 2."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    sys.path.insert(0, str(REPO))
+    import bench
+    r, w, _ = bench.dist_env()
+    bench.init_ranks(w, "gloo", timeout_s=5)
+    bench.max_over_ranks(1.0, w)                 # step 1: both ranks
+    if r == 1:
+        if mode == "exit":
+            os._exit(0)                           # dies between steps, no collective in flight
+        time.sleep(60)                            # hangs between steps
+        os._exit(0)
+    t0 = time.perf_counter()
+    try:
+        bench.max_over_ranks(2.0, w)             # step 2: the peer is gone
+        q.put(("no error", time.perf_counter() - t0))
+    except Exception as exc:  # noqa: BLE001 - any error ends the step, which is the point
+        q.put((type(exc).__name__, time.perf_counter() - t0))
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exit", "hang"])
+def test_survivor_errors_within_the_timeout_when_a_rank_dies_or_hangs(mode):
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_failing_rank, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    kind, elapsed = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=90)
+        if p.is_alive():
+            p.kill()
+    assert kind != "no error"
+    assert elapsed < 60, elapsed                  # the 5 s timeout (plus teardown), not a hang

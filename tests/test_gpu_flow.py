@@ -113,3 +113,31 @@ def test_engine_uses_the_flow_kernel_at_batch_one(tiny, tmp_path):
     assert torch.equal(got, want) and torch.equal(again, want)
     _close(got, eng_off.sample_actions(*args), 0.9999, 2e-2)
     assert _lib.device_error() == 0
+
+
+def test_flow_grid_barrier_that_runs_out_reports_an_error_and_the_context_survives(tiny):
+    """Every wait in the flow kernel is bounded.  With a poll limit of 1 the first CTA to reach a grid barrier
+    gives up before the others arrive: it records device error 103 (kErrFlowBarrier), every CTA returns at
+    its next barrier, and the launch ends.  The host reads the error, clears it and the arrival counter, and
+    the next call on the same context gives the same actions as before."""
+    import ctypes
+
+    from smolvla_mujoco_libero_b200.model import DeviceWeights
+    w, _js, scales = tiny
+    dw = DeviceWeights(TINY, w, scales)
+    _o, args = _args(TINY, 1, 25)
+    r, want = _run(dw, 1, args, flow=True)
+    assert _lib.device_error() == 0
+    d = next(a[0] for fn, a in r.launches if fn is _lib.lib().svla_flow)
+    d.spin_limit = 1
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(_lib.lib().svla_flow(ctypes.byref(d), stream), "svla_flow")
+    torch.cuda.synchronize()
+    assert _lib.device_error(reset=True) == _lib.ERR_FLOW_BARRIER
+    assert _lib.device_error() == 0
+    d.spin_limit = 0
+    r.flow_sync.zero_()
+    got = r(*args).clone()
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.equal(got, want)

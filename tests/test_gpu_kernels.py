@@ -348,6 +348,79 @@ def test_epilogues_on_16_byte_aligned_rows_equal_32_byte_aligned(layout):
     assert torch.equal(r_ref.cpu(), (y_ref.float() + res.float()).to(torch.bfloat16).cpu())
 
 
+# ----------------------------------------------------------------------------- CTA pairs
+
+def _pair_case(kind, epi, m, n, k, g, nseg=1, pair=False):
+    """Operands and a descriptor builder for one GEMM; build(cta_pair) returns (descriptor, outputs)."""
+    if kind == L.KIND_I8:
+        a = [_rand_i8((m, k), g).to(DEV) for _ in range(nseg)]
+        b = [_rand_i8((n, k), g).to(DEV) for _ in range(nseg)]
+    else:
+        a = [torch.randn(m, k, generator=g).to(torch.bfloat16).to(DEV) for _ in range(nseg)]
+        b = [(torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16).to(DEV) for _ in range(nseg)]
+    ws = [(torch.rand(n, generator=g) * 1e-3).to(DEV) for _ in range(nseg)]
+    bias = [(torch.randn(n, generator=g) * 0.1).to(torch.bfloat16).to(DEV) for _ in range(nseg)]
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16).to(DEV)
+    smooth = (torch.rand(n, generator=g) + 0.5).to(DEV)
+    pos = torch.randint(0, 227, (m,), generator=g, dtype=torch.int32).to(DEV)
+    cs = ops.rope_table(227, 10000.0, DEV)
+    odt = torch.int32 if epi == L.EPI_I32 else torch.bfloat16
+
+    def build(cta_pair):
+        outs = [torch.zeros(m, n, dtype=odt, device=DEV) for _ in range(1 if pair else nseg)]
+        if epi == L.EPI_RESID:
+            outs[0].copy_(res)
+        segs = [ops.Seg(a=a[i], b=b[i], out=outs[0 if pair else i], n=n, wscale=ws[i], act_scale=0.01 + 0.01 * i,
+                        bias=None if epi == L.EPI_I32 else bias[i], rope=1 if (epi == L.EPI_ROPE and i < 2) else 0)
+                for i in range(nseg)]
+        extra = {}
+        if epi == L.EPI_RESID:
+            extra = dict(resid=outs[0], ldr=n)
+        if epi == L.EPI_ROPE:
+            extra = dict(rope_cs=cs, pos=pos, max_pos=227)
+        qout = None
+        if epi == L.EPI_GELU_QUANT:
+            qout = torch.zeros(m, n, dtype=torch.int8, device=DEV)
+            extra = dict(q_smooth=smooth, q_rsmooth=ops.reciprocal(smooth), q_act=0.02, qout=qout, ldq=n)
+        d = ops.gemm_desc(kind, epi, m, k, segs, pair=pair, cta_pair=cta_pair, block_n=128, **extra)
+        return d, outs + ([qout] if qout is not None else [])
+    return build
+
+
+@pytest.mark.parametrize("kind,epi,m,n,k,nseg,pair", [
+    (L.KIND_I8, L.EPI_I32, 1000, 512, 768, 1, False),        # 8 row tiles: 4 pairs, the last partly past M
+    (L.KIND_I8, L.EPI_BF16, 2048, 768, 768, 3, False),       # SigLIP q/k/v segments
+    (L.KIND_I8, L.EPI_GELU_QUANT, 1280, 3072, 768, 1, False),
+    (L.KIND_I8, L.EPI_RESID, 768, 768, 3072, 1, False),
+    (L.KIND_I8, L.EPI_ROPE, 1416, 320, 960, 3, False),       # text q/k/v with RoPE, 8 x 177 rows
+    (L.KIND_BF16, L.EPI_RESID, 3200, 720, 2048, 1, False),   # expert down_proj
+    (L.KIND_BF16, L.EPI_SILU_MUL, 3200, 2048, 720, 2, True),  # expert gate / up pair
+    (L.KIND_BF16, L.EPI_ROPE, 3200, 320, 720, 3, False),     # expert q/k/v
+])
+def test_cta_pairs_equal_single_ctas(kind, epi, m, n, k, nseg, pair):
+    """tcgen05 cta_group::2 (256-row tiles over two SMs, each loading half of B) against one CTA per 128-row
+    tile: every output bit-identical (the same MMA K order per output element)."""
+    g = synthetic.generator(m + n + k + epi)
+    build = _pair_case(kind, epi, m, n, k, g, nseg, pair)
+    d1, o1 = build(1)
+    ops.gemm(d1)
+    d2, o2 = build(2)
+    ops.gemm(d2)
+    torch.cuda.synchronize()
+    for x, y in zip(o1, o2):
+        assert torch.equal(x, y)
+
+
+def test_cta_pair_int32_matches_oracle():
+    g = synthetic.generator(77)
+    m, n, k = 1000, 512, 768
+    qx, qw = _rand_i8((m, k), g), _rand_i8((n, k), g)
+    acc = torch.zeros(m, n, dtype=torch.int32, device=DEV)
+    ops.gemm(ops.gemm_desc(L.KIND_I8, L.EPI_I32, m, k, [ops.Seg(a=qx.to(DEV), b=qw.to(DEV), out=acc, n=n)],
+                           cta_pair=2, block_n=256))
+    assert torch.equal(acc.cpu(), Q.int_gemm(qx, qw))
+
+
 # ----------------------------------------------------------------------------- norms
 
 def test_rmsnorm_quant_three_outputs():
