@@ -80,6 +80,16 @@ int32_t svla_dequant_weight_bf16(const int8_t* qweight, const float* wscale, int
 int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, float act_scale, int8_t* q,
                              int32_t ldq, int32_t m, int32_t k, svla_stream_t stream);
 
+/* Calibration statistics of `calls` linear calls of `rows` tokens each (call c = rows [c*rows, (c+1)*rows)
+ * of x, bf16 [calls*rows, ldx], 2-byte aligned, ldx >= k); replaces the forward pre-hook of
+ * PerChannelLinearInputCollector (deploy/calibrate_smolvla_activation_channel_scales.py:68-84).  Per call and
+ * channel: a = max(max_t |x|, 1e-8) and p = max(torch.quantile(|x[:, k]|, q), 1e-8), linear interpolation,
+ * bit-identical to torch.quantile on fp32 (NaN inputs are skipped, not propagated); both are max-accumulated
+ * into amax / pamax fp32 [k], which the caller zero-fills before the first call of a module.
+ * 1 <= rows <= 4096, 1 <= calls <= 65535, 0 <= q <= 1. */
+int32_t svla_channel_percentile(const void* x, int64_t ldx, int32_t calls, int32_t rows, int32_t k, float q,
+                                float* amax, float* pamax, svla_stream_t stream);
+
 /* int8 x int8 -> int32 GEMM acc[m,n] = sum_k qx[m,k] * qw[n,k]; replaces int8GemmInt32Kernel
  * (deploy/cuda/smoothquant_linear_epilogue.cu:121-137) and the cuBLASLt CUBLAS_COMPUTE_32I call
  * (deploy/cuda/smoothquant_linear_cublaslt.cu:230-306).  tcgen05 kind::i8. */

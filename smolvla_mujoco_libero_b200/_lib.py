@@ -120,6 +120,8 @@ SIGNATURES = {
     "svla_dequant_weight_bf16": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "svla_quantize_smooth": (c_int32, [c_void_p, c_int32, c_void_p, c_float, c_void_p, c_int32, c_int32, c_int32,
                                        c_void_p]),
+    "svla_channel_percentile": (c_int32, [c_void_p, c_int64, c_int32, c_int32, c_int32, c_float, c_void_p, c_void_p,
+                                          c_void_p]),
     "svla_gemm_i8_i32": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "svla_sq_linear_w8a8_workspace_size": (c_size_t, [c_int32, c_int32]),
     "svla_sq_linear_w8a8": (c_int32, [c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_int32, c_int32,

@@ -10,7 +10,7 @@ mode "bf16") and observes the input of every W8A8-recipe linear, with the semant
     a = max(amax_x / s) / 127.
 One "call" is one sample's pass through a module, as the reference hook sees it: per image for the vision
 tower and connector (embed_image runs once per camera, deploy/trt_sample_actions_core_deploy.py:296-297),
-per sample for the text layers.  The percentile runs on the GPU (torch.quantile).
+per sample for the text layers.  The statistics run on the GPU (svla_channel_percentile).
 """
 
 from __future__ import annotations
@@ -21,27 +21,35 @@ from typing import Any, Iterable
 
 import torch
 
+from . import ops
 from .config import SmolVLAConfig
 from .model import DeviceWeights, SmolVLARunner
 from .weights import linear_specs
 
 
 class ChannelStats:
+    """Per module: elementwise max over calls of the per-call channel amax / percentile-amax, each call's
+    statistics computed by the channel-percentile kernel (exact torch.quantile interpolation)."""
+
     def __init__(self, percentile: float):
         self.p = percentile
         self.calls: dict[str, dict[str, Any]] = {}
 
-    def observe(self, module: str, x: torch.Tensor) -> None:
-        flat = x.detach().to(torch.float32).abs().reshape(-1, x.shape[-1])
-        amax = flat.amax(dim=0).clamp_min(1e-8)
-        pamax = torch.quantile(flat, self.p / 100.0, dim=0).clamp_min(1e-8)
-        c = self.calls.get(module)
-        if c is None:
-            self.calls[module] = {"amax": amax, "pamax": pamax, "n": 1, "shape": list(x.shape)}
-        else:
-            c["amax"] = torch.maximum(c["amax"], amax)
-            c["pamax"] = torch.maximum(c["pamax"], pamax)
-            c["n"] += 1
+    def observe(self, modules: Iterable[str], x: torch.Tensor, rows_per_call: int) -> None:
+        """x: [calls * rows_per_call, K] bf16, the input every module in `modules` sees."""
+        k = x.shape[-1]
+        amax = torch.zeros(k, dtype=torch.float32, device=x.device)
+        pamax = torch.zeros_like(amax)
+        ops.channel_percentile(x.reshape(-1, k), rows_per_call, self.p / 100.0, amax, pamax)
+        n = x.reshape(-1, k).shape[0] // rows_per_call
+        for module in modules:
+            c = self.calls.get(module)
+            if c is None:
+                self.calls[module] = {"amax": amax, "pamax": pamax, "n": n, "shape": [rows_per_call, k]}
+            else:
+                c["amax"] = torch.maximum(c["amax"], amax)
+                c["pamax"] = torch.maximum(c["pamax"], pamax)
+                c["n"] += n
 
 
 def smoothquant_entry(module: str, scale_list: torch.Tensor, weight: torch.Tensor, alpha: float,
@@ -83,10 +91,7 @@ def calibrate(cfg: SmolVLAConfig, state: dict[str, torch.Tensor], observations: 
                 per = cfg.n_patches
             else:
                 per = cfg.prefix_len
-            for start in range(0, rows, per):
-                chunk = buf[start:start + per]
-                for m in mods:
-                    stats.observe(m, chunk)
+            stats.observe(mods, buf, per)
 
         runner(obs.images, obs.img_masks, obs.lang_tokens, obs.lang_masks, obs.state, obs.noise, observer=observe)
     torch.cuda.synchronize()

@@ -18,6 +18,7 @@
 #include "../../include/svla.h"
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "calib.cuh"
 #include "gemm.cuh"
 #include "misc.cuh"
 #include "norm.cuh"
@@ -514,6 +515,42 @@ int32_t svla_quantize_smooth(const void* x, int32_t ldx, const float* smooth, fl
   const long long total = static_cast<long long>(m) * (k / 8);
   return launch(smooth_quant_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, cs(stream), "smooth_quant_kernel",
                 static_cast<const __nv_bfloat16*>(x), ldx, smooth, act_scale, q, ldq, m, k);
+}
+
+int32_t svla_channel_percentile(const void* x, int64_t ldx, int32_t calls, int32_t rows, int32_t k, float q,
+                                float* amax, float* pamax, svla_stream_t stream) {
+  if (!x || !amax || !pamax || k <= 0 || ldx < k || rows < 1 || rows > kPctMaxRows || calls < 1 || calls > 65535 ||
+      !(q >= 0.f && q <= 1.f))
+    return fail(SVLA_ERR_ARG, "svla_channel_percentile: bad args (1 <= rows <= %d, 1 <= calls <= 65535, ldx >= k, "
+                "0 <= q <= 1)", kPctMaxRows);
+  if (reinterpret_cast<uintptr_t>(x) % 2 || reinterpret_cast<uintptr_t>(amax) % 4 ||
+      reinterpret_cast<uintptr_t>(pamax) % 4)
+    return fail(SVLA_ERR_ARG, "svla_channel_percentile: misaligned x / amax / pamax");
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(channel_percentile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(percentile_smem(kPctMaxRows)));
+    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  // torch.quantile's interpolation point, in fp32 as torch computes it for an fp32 input
+  const float rank = q * static_cast<float>(rows - 1);
+  PercentileArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.calls = calls;
+  a.rows = rows;
+  a.K = k;
+  a.lo = static_cast<int>(std::floor(rank));
+  a.hi = static_cast<int>(std::ceil(rank));
+  a.w = rank - static_cast<float>(a.lo);
+  a.amax = amax;
+  a.pamax = pamax;
+  return launch(channel_percentile_kernel, dim3(static_cast<unsigned>((k + kPctCols - 1) / kPctCols), calls),
+                dim3(kPctCols * 32), percentile_smem(rows), cs(stream), "channel_percentile_kernel", a);
 }
 
 int32_t svla_gemm(const svla_gemm_desc* desc, svla_stream_t stream) { return run_gemm(desc, cs(stream)); }

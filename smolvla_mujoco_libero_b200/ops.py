@@ -75,6 +75,23 @@ def quantize_smooth(x: torch.Tensor, smooth: torch.Tensor | None, act_scale: flo
     return q
 
 
+def channel_percentile(x: torch.Tensor, rows: int, q: float, amax: torch.Tensor, pamax: torch.Tensor) -> None:
+    """Max-accumulate per-channel max(|x|) and torch.quantile(|x|, q) of each `rows`-token call of x (bf16
+    [calls * rows, K], unit stride along K) into amax / pamax (fp32 [K], zero-filled before the first call)."""
+    _need(x, torch.bfloat16, "x", contiguous=False)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("channel_percentile: x must be 2-D with unit stride along channels")
+    m, k = x.shape
+    if rows <= 0 or m % rows:
+        raise ValueError(f"channel_percentile: {m} rows are not a whole number of {rows}-token calls")
+    for t, n in ((amax, "amax"), (pamax, "pamax")):
+        _need(t, torch.float32, n)
+        if t.numel() != k or t.device != x.device:
+            raise ValueError(f"channel_percentile: {n} must be fp32 [{k}] on {x.device}")
+    check(lib().svla_channel_percentile(_p(x), x.stride(0), m // rows, rows, k, float(q), _p(amax), _p(pamax),
+                                        _stream()), "channel_percentile")
+
+
 def gemm_i8_i32(qx: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
     _need(qx, torch.int8, "qx")
     _need(qw, torch.int8, "qw")

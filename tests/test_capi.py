@@ -142,3 +142,16 @@ def test_quantize_and_linear_alignment_is_checked_before_any_launch():
     assert lib.svla_sq_linear_w8a8(0x100002, None, 1.0, 0x300000, 0x400000, None, 4, 64, 64, 0x500000, 0x600000,
                                    4096, None) == 1
     assert b"aligned" in lib.svla_last_error()
+
+
+def test_channel_percentile_arguments_are_checked_before_any_launch():
+    lib = _lib.lib()
+    f = lib.svla_channel_percentile
+    assert f(0x100000, 64, 1, 4097, 64, 0.5, 0x200000, 0x300000, None) == 1  # more than 4096 rows a call
+    assert b"rows" in lib.svla_last_error()
+    assert f(0x100000, 32, 1, 16, 64, 0.5, 0x200000, 0x300000, None) == 1    # ldx < k
+    assert f(0x100000, 64, 1, 16, 64, -0.1, 0x200000, 0x300000, None) == 1   # q outside [0, 1]
+    assert f(0x100000, 64, 0, 16, 64, 0.5, 0x200000, 0x300000, None) == 1    # no calls
+    assert f(0x100001, 64, 1, 16, 64, 0.5, 0x200000, 0x300000, None) == 1    # odd bf16 address
+    assert b"misaligned" in lib.svla_last_error()
+    assert f(0x100000, 64, 1, 16, 64, 0.5, None, 0x300000, None) == 1

@@ -862,3 +862,44 @@ def test_structured_mask_equals_byte_mask(two_sources):
     key_rows[:, :l1] = pad.to(torch.uint8)
     o_key = ops.attention(q, k1, v1, hq, hkv, key_mask=key_rows.to(DEV)[:, :l1], mask_keys=l1, **srcs)
     assert torch.equal(o_byte.cpu(), o_key.cpu())
+
+
+@pytest.mark.parametrize("rows,k,calls", [(1, 8, 3), (2, 13, 2), (177, 960, 4), (1024, 768, 2), (4096, 40, 1)])
+@pytest.mark.parametrize("q", [0.9999, 0.5, 0.0, 1.0, 0.37])
+def test_channel_percentile_bit_exact_with_torch_quantile(rows, k, calls, q):
+    """svla_channel_percentile: per call, amax and torch.quantile(|x|, q) (the oracle's collector statistic),
+    max-accumulated over calls -- bit-exact in fp32.  Inputs carry ties (bf16 rounding of a narrow range),
+    exact zeros and a ragged channel count."""
+    g = torch.Generator().manual_seed(rows * 7 + k)
+    x = (torch.randn(calls * rows, k, generator=g) * torch.linspace(0.01, 40.0, k)).to(torch.bfloat16)
+    x[::5, ::3] = 0
+    x[1::7] = x[1::7].float().clamp(-0.5, 0.5).to(torch.bfloat16)  # many equal values
+    amax = torch.zeros(k, device=DEV)
+    pamax = torch.zeros(k, device=DEV)
+    ops.channel_percentile(x.to(DEV), rows, q, amax, pamax)
+    ref_a = torch.zeros(k)
+    ref_p = torch.zeros(k)
+    for c in range(calls):
+        a, p = Q.per_channel_percentile_amax(x[c * rows:(c + 1) * rows], q * 100.0)
+        ref_a = torch.maximum(ref_a, a)
+        ref_p = torch.maximum(ref_p, p)
+    assert torch.equal(amax.cpu(), ref_a)
+    assert torch.equal(pamax.cpu(), ref_p)
+
+
+def test_channel_percentile_strided_rows_and_rejects():
+    """A row-strided view (a column slice of a wider buffer) reads only its own channels; bad shapes are
+    refused by the C ABI before any launch."""
+    x = torch.randn(354, 1000, dtype=torch.bfloat16)
+    v = x[:, 16:976]
+    amax = torch.zeros(960, device=DEV)
+    pamax = torch.zeros(960, device=DEV)
+    xd = x.to(DEV)
+    ops.channel_percentile(xd[:, 16:976], 177, 0.9999, amax, pamax)
+    ra, rp = [torch.maximum(*t) for t in zip(Q.per_channel_percentile_amax(v[:177], 99.99),
+                                              Q.per_channel_percentile_amax(v[177:], 99.99))]
+    assert torch.equal(amax.cpu(), ra) and torch.equal(pamax.cpu(), rp)
+    lib = L.lib()
+    assert lib.svla_channel_percentile(ops._p(xd), 1000, 1, 4097, 8, 0.5, ops._p(amax), ops._p(pamax), 0) != 0
+    assert lib.svla_channel_percentile(ops._p(xd), 4, 1, 8, 8, 0.5, ops._p(amax), ops._p(pamax), 0) != 0
+    assert lib.svla_channel_percentile(ops._p(xd), 1000, 1, 8, 8, 1.5, ops._p(amax), ops._p(pamax), 0) != 0
