@@ -46,7 +46,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--calib-samples", type=int, default=4)
     ap.add_argument("--b1-iters", type=int, default=30)
-    ap.add_argument("--cpu-iters", type=int, default=3)
+    ap.add_argument("--cpu-iters", type=int, default=30)
+    ap.add_argument("--cpu-warmup", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -153,23 +154,27 @@ def make_observations(cfg, batch, seed):
     return synthetic.observations(batch, seed=seed, image_size=cfg.image_size, n_tokens=cfg.n_lang)
 
 
-def cpu_baseline(cfg, state, scales_json, iters: int):
-    """The oracle (CPU restatement of the reference fake-quant path) on the host cores, batch 1."""
+def cpu_baseline(cfg, state, scales_json, iters: int, warmup: int):
+    """The oracle (CPU restatement of the reference fake-quant path) on the host cores, batch 1: `warmup`
+    untimed calls, then `iters` timed calls (value from the median; p50 / p95 reported)."""
     from oracle import quant as Q
     from oracle.model import OracleSmolVLA
     torch.set_num_threads(os.cpu_count() or 1)
     m = OracleSmolVLA(cfg, state, Q.load_activation_scales_by_module(scales_json))
     o = make_observations(cfg, 1, 10_000)
     times = []
-    for i in range(iters + 1):
+    for i in range(warmup + iters):
         t0 = time.perf_counter()
         m.sample_actions(o.images, o.img_masks, o.lang_tokens, o.lang_masks, o.state, o.noise)
-        if i > 0:
+        if i >= warmup:
             times.append(time.perf_counter() - t0)
-    med = statistics.median(times)
-    return {"value": 1.0 / med, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{iters} timed batch-1 sample_actions calls after 1 warm-up (the bs64 workload per "
-                      f"observation), median {med:.2f} s/chunk, fp32/bf16 torch CPU oracle"}
+    times.sort()
+    p50 = statistics.median(times)
+    p95 = times[min(len(times) - 1, int(round(0.95 * (len(times) - 1))))]
+    return {"value": 1.0 / p50, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "p50_s_per_chunk": p50, "p95_s_per_chunk": p95, "iters": iters, "warmup": warmup,
+            "sample": f"{iters} timed batch-1 sample_actions calls after {warmup} warm-up calls (the bs64 workload "
+                      f"per observation): p50 {p50:.3f} s/chunk, p95 {p95:.3f} s/chunk, fp32/bf16 torch CPU oracle"}
 
 
 def run_reference(args, rank, world):
@@ -361,7 +366,7 @@ def main():
         "clocks": clk,
     }
     if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, state, js, args.cpu_iters)
+        line["cpu_baseline"] = cpu_baseline(cfg, state, js, args.cpu_iters, args.cpu_warmup)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -383,15 +388,14 @@ def measure_int8_peak(dev) -> float | None:
 
 
 def profile_traffic(name: str) -> float | None:
-    """DRAM bytes per full-size launch from a committed ncu summary (profiles/<name>.md, line
-    `traffic_bytes_per_launch: N`), or None when that summary is absent."""
-    f = REPO / "profiles" / f"{name}.md"
+    """DRAM bytes (read + write) of one full-size launch of kernel `name` from the committed traffic table
+    (profiles/traffic.json, written by `python -m smolvla_mujoco_libero_b200.profile --ncu-traffic` from an ncu
+    capture), or None when the table has no entry."""
+    f = REPO / "profiles" / "traffic.json"
     if not f.exists():
         return None
-    for line in f.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            return float(line.split(":", 1)[1].strip())
-    return None
+    entry = json.loads(f.read_text()).get(name)
+    return None if entry is None else float(entry["dram_bytes_per_launch"])
 
 
 def attention_roofline(runner, peaks):

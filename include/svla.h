@@ -350,23 +350,37 @@ int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n,
  * RMSNorm, action_out_proj, x_t += dt * v] (lerobot VLAFlowMatching.sample_actions / denoise_step) in one
  * cooperative launch (one CTA per SM, grid barriers between phases, every wait bounded).  Same arithmetic
  * and rounding points as the per-layer launches (svla_gemm / svla_norm_quant / svla_attention with the
- * structured expert masks); only the fp32 summation order inside dot products differs.  Expert linears
- * are bf16 weights (the W8A16 linears' bf16(q * w_s) weights).  No counterpart launch in the reference,
- * whose TensorRT engine runs the loop as separate layers (deploy/trt_sample_actions_core_deploy.py:108-237).
+ * structured expert masks); only the fp32 summation order inside dot products differs.  The weights are
+ * read in the MMA fragment order svla_flow_pack_weight writes (each warp load is one contiguous run): the
+ * expert layers' W8A16 linears as int8 with their per-output-channel scales, dequantised in registers to
+ * bf16(q * w_s) -- the W8A16Linear weight (deploy/linear_only_quant.py:122-124, :147-148) bit for bit at half
+ * the bytes of the bf16 copy -- and the bf16 linears (action / time projections) as bf16.  No counterpart
+ * launch in the reference, whose TensorRT engine runs the loop as separate layers
+ * (deploy/trt_sample_actions_core_deploy.py:108-237).
  * ------------------------------------------------------------------------------------------------*/
 #define SVLA_FLOW_MAX_LAYERS 32
 #define SVLA_FLOW_MAX_ROWS 64
 
+/* Bytes of the fragment-packed copy of an [n, k] weight (n, k multiples of 16): n * k * elem_bytes. */
+size_t svla_flow_packed_bytes(int32_t n, int32_t k, int32_t elem_bytes);
+/* Writes the fragment-packed copy of w ([n, k], row stride ld elements; elem_bytes 1 = int8, 2 = bf16) to out
+ * (svla_flow_packed_bytes, 16-byte aligned): 16-row slices, each K/16 steps x 32 lanes x 8 elements in the
+ * order of the mma.m16n8k16 B fragments of the slice's two 8-row tiles. */
+int32_t svla_flow_pack_weight(const void* w, int32_t elem_bytes, int64_t ld, int32_t n, int32_t k, void* out,
+                              svla_stream_t stream);
+
 typedef struct svla_flow_layer {
   const void* input_norm;  /* bf16 [E] */
   const void* post_norm;   /* bf16 [E] */
-  const void* wq;          /* bf16 [heads * 64, E] */
-  const void* wk;          /* bf16 [kv_heads * 64, E] (self-attention layers; NULL on cross-attention layers) */
-  const void* wv;
-  const void* wo;          /* bf16 [E, heads * 64] */
-  const void* wg;          /* bf16 [mlp, E] */
-  const void* wu;          /* bf16 [mlp, E] */
-  const void* wd;          /* bf16 [E, mlp] */
+  /* int8 weights, fragment-packed (svla_flow_pack_weight, elem_bytes 1), each with its fp32 per-output-channel
+   * scale w_s [n] (svla_pack_weight_i8) */
+  const void* wq; const float* sq;  /* [heads * 64, E] */
+  const void* wk; const float* sk;  /* [kv_heads * 64, E] (self-attention layers; NULL on cross-attention layers) */
+  const void* wv; const float* sv;
+  const void* wo; const float* so;  /* [E, heads * 64] */
+  const void* wg; const float* sg;  /* [mlp, E] */
+  const void* wu; const float* su;  /* [mlp, E] */
+  const void* wd; const float* sd;  /* [E, mlp] */
   const void* keys;        /* bf16 [batch * prefix_len, kv_heads * 64]: the layer's prefix KV cache (self) or */
   const void* values;      /*   its cross-attention K/V projections (cross) */
   int32_t cross;
@@ -381,12 +395,13 @@ typedef struct svla_flow_desc {
   const float* noise;      /* fp32 [batch * chunk, A] */
   float* xt;               /* fp32 [batch * chunk, A]: the actions on return */
   void* xt_bf16;           /* bf16 [batch * chunk, A] scratch */
-  const void* w_action_in; const void* b_action_in;       /* bf16 [E, A], [E] */
-  const void* w_time_in; int32_t ld_time_in;              /* bf16 [E, >= E]: the first E columns are used */
+  /* bf16 weights, fragment-packed (svla_flow_pack_weight, elem_bytes 2); biases bf16 */
+  const void* w_action_in; const void* b_action_in;       /* [E, A], [E] */
+  const void* w_time_in;                                  /* the first E columns of action_time_mlp_in, [E, E] */
   const float* time_in_const;                             /* fp32 [num_steps, E]: W[:, E:] . time_emb(t_k) + b */
-  const void* w_time_out; const void* b_time_out;         /* bf16 [E, E], [E] */
+  const void* w_time_out; const void* b_time_out;         /* [E, E], [E] */
   const void* final_norm;                                 /* bf16 [E] */
-  const void* w_action_out; const void* b_action_out;     /* bf16 [A, E], [A] */
+  const void* w_action_out; const void* b_action_out;     /* [A, E], [A] */
   const uint8_t* key_mask; int64_t key_mask_bs;           /* prefix key flags of sample b at key_mask + b * bs
                                                              (16-byte aligned rows of >= prefix_len rounded up to
                                                              16 bytes), or NULL */
@@ -395,6 +410,9 @@ typedef struct svla_flow_desc {
   /* scratch (bf16): a_emb, a_t, eh [rows, E]; eq, ectx [rows, heads * 64]; ek, ev [rows, kv_heads * 64];
    * emlp [rows, mlp] */
   void* a_emb; void* a_t; void* eh; void* eq; void* ek; void* ev; void* ectx; void* emlp;
+  float* norm_part;        /* fp32 scratch [64 * 64]: per action row and 16-column slice of E, the sum of squares
+                              of the expert hidden state (the RMSNorm statistics, written by the phase that writes
+                              the rows and summed in slice order by the next) */
   uint32_t* sync;          /* 8 bytes (8-byte aligned), zero before the first launch; every completed launch leaves
                               it valid.  After a device error (svla_device_error) zero it again. */
   uint32_t spin_limit;     /* polls of a grid barrier before the kernel gives up with device error 103 and returns

@@ -70,9 +70,10 @@ ERR_MBAR_TIMEOUT, ERR_BAD_SHAPE, ERR_FLOW_BARRIER = 101, 102, 103  # device erro
 
 class FlowLayer(ctypes.Structure):
     _fields_ = [
-        ("input_norm", c_void_p), ("post_norm", c_void_p), ("wq", c_void_p), ("wk", c_void_p), ("wv", c_void_p),
-        ("wo", c_void_p), ("wg", c_void_p), ("wu", c_void_p), ("wd", c_void_p), ("keys", c_void_p),
-        ("values", c_void_p), ("cross", c_int32),
+        ("input_norm", c_void_p), ("post_norm", c_void_p), ("wq", c_void_p), ("sq", c_void_p), ("wk", c_void_p),
+        ("sk", c_void_p), ("wv", c_void_p), ("sv", c_void_p), ("wo", c_void_p), ("so", c_void_p), ("wg", c_void_p),
+        ("sg", c_void_p), ("wu", c_void_p), ("su", c_void_p), ("wd", c_void_p), ("sd", c_void_p),
+        ("keys", c_void_p), ("values", c_void_p), ("cross", c_int32),
     ]
 
 
@@ -81,12 +82,12 @@ class FlowDesc(ctypes.Structure):
         ("batch", c_int32), ("chunk", c_int32), ("prefix_len", c_int32), ("hidden", c_int32), ("action_dim", c_int32),
         ("heads", c_int32), ("kv_heads", c_int32), ("mlp", c_int32), ("n_layers", c_int32), ("num_steps", c_int32),
         ("eps", c_float), ("noise", c_void_p), ("xt", c_void_p), ("xt_bf16", c_void_p),
-        ("w_action_in", c_void_p), ("b_action_in", c_void_p), ("w_time_in", c_void_p), ("ld_time_in", c_int32),
+        ("w_action_in", c_void_p), ("b_action_in", c_void_p), ("w_time_in", c_void_p),
         ("time_in_const", c_void_p), ("w_time_out", c_void_p), ("b_time_out", c_void_p), ("final_norm", c_void_p),
         ("w_action_out", c_void_p), ("b_action_out", c_void_p), ("key_mask", c_void_p), ("key_mask_bs", c_int64),
         ("suffix_pos", c_void_p), ("cross_pos", c_void_p), ("rope_cs", c_void_p), ("max_pos", c_int32),
         ("a_emb", c_void_p), ("a_t", c_void_p), ("eh", c_void_p), ("eq", c_void_p), ("ek", c_void_p), ("ev", c_void_p),
-        ("ectx", c_void_p), ("emlp", c_void_p), ("sync", c_void_p), ("spin_limit", ctypes.c_uint32),
+        ("ectx", c_void_p), ("emlp", c_void_p), ("norm_part", c_void_p), ("sync", c_void_p), ("spin_limit", ctypes.c_uint32),
         ("debug_clock", c_void_p),
         ("layer", FlowLayer * FLOW_MAX_LAYERS),
     ]
@@ -156,6 +157,8 @@ SIGNATURES = {
     "svla_f32_to_bf16": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
     "svla_euler_init": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "svla_reciprocal": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "svla_flow_packed_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "svla_flow_pack_weight": (c_int32, [c_void_p, c_int32, c_int64, c_int32, c_int32, c_void_p, c_void_p]),
     "svla_flow": (c_int32, [POINTER(FlowDesc), c_void_p]),
     "svla_engine_inspect": (c_int32, [c_char_p, POINTER(EngineInfo)]),
     "svla_engine_create": (c_int32, [c_char_p, c_int32, c_int32, c_void_p, POINTER(c_void_p)]),

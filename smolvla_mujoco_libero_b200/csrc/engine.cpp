@@ -583,6 +583,7 @@ struct Buffers {
   void* splitk_ws;
   size_t splitk_bytes;
   uint32_t* flow_sync;  // grid-barrier words of the persistent flow kernel
+  float* flow_norm;     // its RMSNorm statistics scratch
   float* rope_cs;
   float* c_step;
 };
@@ -601,6 +602,8 @@ struct svla_engine {
   PackedFile file;
   char* weights = nullptr;  // device arena of the file's tensors
   char* arena = nullptr;    // device arena of the buffers
+  char* flow_frag = nullptr;  // fragment-order copies of the weights the persistent flow kernel reads
+  std::map<std::string, const void*> frag;  // linear -> its copy in flow_frag
   uint64_t arena_bytes = 0;
   Buffers buf{};
   std::map<std::string, Lin> lin;
@@ -822,6 +825,7 @@ uint64_t layout_buffers(const Cfg& c, int B, char* base, Buffers* b) {
   b->splitk_bytes = kSplitKBytes;
   b->splitk_ws = take(kSplitKBytes);
   b->flow_sync = reinterpret_cast<uint32_t*>(take(8));
+  b->flow_norm = reinterpret_cast<float*>(take(64 * 64 * 4));
   const int max_pos = c.prefix_len() + c.chunk;
   b->rope_cs = reinterpret_cast<float*>(take(static_cast<uint64_t>(max_pos) * 32 * 2 * 4));
   b->c_step = reinterpret_cast<float*>(take(static_cast<uint64_t>(c.num_steps) * E * 4));
@@ -1106,21 +1110,11 @@ class Builder {
 
   static svla_stream_t st(cudaStream_t s) { return reinterpret_cast<svla_stream_t>(s); }
 
-  // the persistent flow kernel applies: few action rows and bf16 / W8A16 expert linears
-  bool use_flow() const {
-    if ((e_.flags & SVLA_ENGINE_NO_FLOW) || B_ * c_.chunk > SVLA_FLOW_MAX_ROWS || c_.expert_layers > SVLA_FLOW_MAX_LAYERS)
-      return false;
-    if (c_.expert_hidden % 16 || c_.expert_hidden > 1024 || c_.max_action_dim % 16 || c_.expert_mlp % 16) return false;
-    const std::string ep = std::string(kExpert) + ".";
-    for (const auto& kv : e_.lin)
-      if (kv.first.compare(0, ep.size(), ep) == 0 && kv.second.kind == "w8a8") return false;
-    return true;
-  }
+  // the persistent flow kernel applies: few action rows and its weights packed (flow_weights_packed)
+  bool use_flow() const { return !e_.frag.empty() && B_ * c_.chunk <= SVLA_FLOW_MAX_ROWS; }
 
-  const void* bf16_weight(const std::string& name) const {
-    const Lin& p = e_.lin.at(name);
-    return p.kind == "w8a16" ? p.weight_deq : p.weight;
-  }
+  const void* frag(const std::string& name) const { return e_.frag.at(name); }
+  const float* wscale(const std::string& name) const { return e_.lin.at(name).wscale; }
 
   void flow(int MS) {
     const Cfg& c = c_;
@@ -1141,15 +1135,14 @@ class Builder {
     d.noise = b.in_noise;
     d.xt = b.xt;
     d.xt_bf16 = b.xt_bf;
-    d.w_action_in = bf16_weight("model.action_in_proj");
+    d.w_action_in = frag("model.action_in_proj");
     d.b_action_in = e_.lin.at("model.action_in_proj").bias;
-    d.w_time_in = e_.lin.at("model.action_time_mlp_in").weight;
-    d.ld_time_in = 2 * c.expert_hidden;
+    d.w_time_in = frag("model.action_time_mlp_in");
     d.time_in_const = b.c_step;
-    d.w_time_out = bf16_weight("model.action_time_mlp_out");
+    d.w_time_out = frag("model.action_time_mlp_out");
     d.b_time_out = e_.lin.at("model.action_time_mlp_out").bias;
     d.final_norm = tensor(std::string(kExpert) + ".norm.weight");
-    d.w_action_out = bf16_weight("model.action_out_proj");
+    d.w_action_out = frag("model.action_out_proj");
     d.b_action_out = e_.lin.at("model.action_out_proj").bias;
     d.key_mask = b.cross_mask;
     d.key_mask_bs = static_cast<int64_t>(c.chunk) * ld16(c.prefix_len());
@@ -1165,24 +1158,32 @@ class Builder {
     d.ev = b.ev;
     d.ectx = b.ectx;
     d.emlp = b.emlp;
+    d.norm_part = b.flow_norm;
     d.sync = b.flow_sync;
     for (int i = 0; i < c.expert_layers; ++i) {
       const std::string p = std::string(kExpert) + ".layers." + std::to_string(i);
       svla_flow_layer& l = d.layer[i];
       l.input_norm = tensor(p + ".input_layernorm.weight");
       l.post_norm = tensor(p + ".post_attention_layernorm.weight");
-      l.wq = bf16_weight(p + ".self_attn.q_proj");
-      l.wo = bf16_weight(p + ".self_attn.o_proj");
-      l.wg = bf16_weight(p + ".mlp.gate_proj");
-      l.wu = bf16_weight(p + ".mlp.up_proj");
-      l.wd = bf16_weight(p + ".mlp.down_proj");
+      l.wq = frag(p + ".self_attn.q_proj");
+      l.sq = wscale(p + ".self_attn.q_proj");
+      l.wo = frag(p + ".self_attn.o_proj");
+      l.so = wscale(p + ".self_attn.o_proj");
+      l.wg = frag(p + ".mlp.gate_proj");
+      l.sg = wscale(p + ".mlp.gate_proj");
+      l.wu = frag(p + ".mlp.up_proj");
+      l.su = wscale(p + ".mlp.up_proj");
+      l.wd = frag(p + ".mlp.down_proj");
+      l.sd = wscale(p + ".mlp.down_proj");
       l.cross = c.is_cross(i) ? 1 : 0;
       if (l.cross) {
         l.keys = b.ck[i];
         l.values = b.cv[i];
       } else {
-        l.wk = bf16_weight(p + ".self_attn.k_proj");
-        l.wv = bf16_weight(p + ".self_attn.v_proj");
+        l.wk = frag(p + ".self_attn.k_proj");
+        l.sk = wscale(p + ".self_attn.k_proj");
+        l.wv = frag(p + ".self_attn.v_proj");
+        l.sv = wscale(p + ".self_attn.v_proj");
         l.keys = b.kcache[i];
         l.values = b.vcache[i];
       }
@@ -1455,6 +1456,60 @@ int32_t compute_constants(svla_engine* e, cudaStream_t stream) {
   return err == cudaSuccess ? SVLA_OK : cuda_fail(err, "computing the engine constants");
 }
 
+// Fragment-order copies (svla_flow_pack_weight) of the weights the persistent flow kernel reads: the expert
+// layers' W8A16 linears as int8, the action / time projections as bf16.  Left empty (the flow loop then runs as
+// per-layer launches) when the kernel cannot take the configuration or the engine was created with NO_FLOW.
+int32_t pack_flow_weights(svla_engine* e, cudaStream_t stream) {
+  const Cfg& c = e->cfg;
+  if ((e->flags & SVLA_ENGINE_NO_FLOW) || c.chunk > SVLA_FLOW_MAX_ROWS || c.expert_layers > SVLA_FLOW_MAX_LAYERS ||
+      c.expert_hidden % 16 || c.expert_hidden > 1024 || c.max_action_dim % 16 || c.expert_mlp % 16)
+    return SVLA_OK;
+  struct Job {
+    std::string name;
+    const void* w;
+    int eb, n, k;
+    int64_t ld;
+  };
+  std::vector<Job> jobs;
+  const std::string ep = std::string(kExpert) + ".";
+  for (const auto& kv : e->lin) {
+    if (kv.first.compare(0, ep.size(), ep) != 0) continue;
+    if (kv.second.kind != "w8a16") return SVLA_OK;  // the kernel reads int8 expert weights only
+    jobs.push_back({kv.first, kv.second.weight, 1, kv.second.n, kv.second.k, kv.second.k});
+  }
+  const int E = c.expert_hidden;
+  for (const char* n : {"model.action_in_proj", "model.action_time_mlp_out", "model.action_out_proj"}) {
+    const Lin& l = e->lin.at(n);
+    if (l.kind != "bf16") return SVLA_OK;
+    jobs.push_back({n, l.weight, 2, l.n, l.k, l.k});
+  }
+  const Lin& ti = e->lin.at("model.action_time_mlp_in");  // its first E columns (the rest is a per-step constant)
+  if (ti.kind != "bf16") return SVLA_OK;
+  jobs.push_back({"model.action_time_mlp_in", ti.weight, 2, ti.n, E, ti.k});
+  size_t total = 0;
+  std::vector<size_t> off;
+  for (const Job& j : jobs) {
+    const size_t nb = svla_flow_packed_bytes(j.n, j.k, j.eb);
+    if (nb == 0) return SVLA_OK;
+    off.push_back(total);
+    total += (nb + kAlign - 1) / kAlign * kAlign;
+  }
+  cudaError_t err = cudaMalloc(&e->flow_frag, total);
+  if (err != cudaSuccess) {
+    e->flow_frag = nullptr;
+    return cuda_fail(err, "cudaMalloc(flow weights)");
+  }
+  for (size_t i = 0; i < jobs.size(); ++i) {
+    const Job& j = jobs[i];
+    const int32_t rc = svla_flow_pack_weight(j.w, j.eb, j.ld, j.n, j.k, e->flow_frag + off[i],
+                                             reinterpret_cast<svla_stream_t>(stream));
+    if (rc != SVLA_OK) return rc;
+    e->frag[j.name] = e->flow_frag + off[i];
+  }
+  err = cudaStreamSynchronize(stream);
+  return err == cudaSuccess ? SVLA_OK : cuda_fail(err, "packing the flow weights");
+}
+
 void release(svla_engine* e) {
   if (!e) return;
   cudaDeviceSynchronize();
@@ -1462,6 +1517,7 @@ void release(svla_engine* e) {
     if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
   if (e->capture_stream) cudaStreamDestroy(e->capture_stream);
   if (e->arena) cudaFree(e->arena);
+  if (e->flow_frag) cudaFree(e->flow_frag);
   if (e->weights) cudaFree(e->weights);
   delete e;
 }
@@ -1526,6 +1582,8 @@ int32_t svla_engine_create(const char* packed_path, int32_t max_batch, int32_t f
   ce = cudaMemsetAsync(e->arena, 0, e->arena_bytes, s);
   if (ce != cudaSuccess) return cuda_fail(ce, "svla_engine_create: clearing the buffers");
   rc = compute_constants(e.get(), s);
+  if (rc != SVLA_OK) return rc;
+  rc = pack_flow_weights(e.get(), s);
   if (rc != SVLA_OK) return rc;
   ce = cudaStreamCreateWithFlags(&e->capture_stream, cudaStreamNonBlocking);
   if (ce != cudaSuccess) return cuda_fail(ce, "svla_engine_create: cudaStreamCreate");

@@ -13,7 +13,10 @@
 // slice x a row block, tasks spread over the CTAs; the 8 warps of a CTA split K and add their partial tiles in
 // a fixed order), mma.sync m16n8k16 bf16 with fp32 accumulators, the A rows staged in shared memory by bulk
 // copies (RMSNorm applied there with the stand-alone norm kernel's arithmetic and operation order), weights
-// read straight from global memory.  Epilogues round exactly where the GEMM kernel's epilogues do (bias, SiLU,
+// read straight from global memory in MMA fragment order (pack_fragments_kernel): one k16 step of a 16-column
+// slice is 32 lanes x 8 elements, so a warp's load is one contiguous 256-byte (int8) or 512-byte (bf16) run.
+// The expert layers' W8A16 weights stay int8 and are dequantised in registers to bf16(q * w_s), the bf16
+// weight of the per-layer path bit for bit, at half the bytes.  Epilogues round exactly where the GEMM kernel's epilogues do (bias, SiLU,
 // RoPE, residual, SiLU-gate, Euler update), so the only difference from the per-layer launch list is the
 // fp32 summation order inside each dot product.
 // Attention: one CTA per (sample, query head, 16-query tile); the 8 warps take consecutive key ranges with
@@ -22,12 +25,15 @@
 // phase (they are final before the kernel starts).
 //
 // Grid barrier: a monotonic 64-bit arrival counter in a caller-provided 8-byte buffer (zero before first use;
-// every completed launch leaves it at a multiple of the grid size).  Every wait is bounded: a barrier that
+// every completed launch leaves it at a multiple of the grid size); each CTA arrives with a release reduction
+// and polls for its own precomputed target.  Every wait is bounded: a barrier that
 // does not open within spin_limit polls (kSpinLimit unless the caller sets a shorter one) records kErrFlowBarrier in the device error word; the other CTAs see
 // the error word at their next wait and return, so the kernel always ends (and later launches refuse to run
 // while the error word is set).  A rows are staged with bulk copies completing on an mbarrier, also waited
 // for with a bound.
 #pragma once
+
+#include <type_traits>
 
 #include "attention.cuh"
 #include "gemm.cuh"
@@ -43,19 +49,22 @@ constexpr int kFlowRows = 64;             // most action rows per call (four m16
 constexpr int kFlowKC = 1024;             // A columns staged for 64 rows (twice as many for 32-row blocks)
 constexpr int kFlowLda = kFlowKC + 16;    // largest staged row stride (elements) of 64 rows
 constexpr int kFlowRedStride = 40;        // fp32 row stride of the per-warp partial tiles (conflict-free)
+constexpr int kFlowMaxSlices = kFlowKC / 16;  // 16-column slices of a row of E
 constexpr int kFlowAttnStride = 72;       // fp32 row stride of the per-warp attention partials
 constexpr int kErrFlowBarrier = 103;
 
+// int8 weights in fragment order, each with its per-output-channel scales
 struct FlowLayer {
   const __nv_bfloat16* ln1;  // input RMSNorm weight [E]
   const __nv_bfloat16* ln2;  // post-attention RMSNorm weight [E]
-  const __nv_bfloat16* wq;   // [q_dim, E]
-  const __nv_bfloat16* wk;   // [kv_dim, E] (self-attention layers)
-  const __nv_bfloat16* wv;
-  const __nv_bfloat16* wo;   // [E, q_dim]
-  const __nv_bfloat16* wg;   // [mlp, E]
-  const __nv_bfloat16* wu;
-  const __nv_bfloat16* wd;   // [E, mlp]
+  const uint8_t* wq;         // [q_dim, E]
+  const uint8_t* wk;         // [kv_dim, E] (self-attention layers)
+  const uint8_t* wv;
+  const uint8_t* wo;         // [E, q_dim]
+  const uint8_t* wg;         // [mlp, E]
+  const uint8_t* wu;
+  const uint8_t* wd;         // [E, mlp]
+  const float *sq, *sk, *sv, *so, *sg, *su, *sd;
   const __nv_bfloat16* k1;   // prefix keys [B * Lp, kv_dim]: the KV cache (self) or its cross projection
   const __nv_bfloat16* v1;
   int cross;
@@ -67,15 +76,15 @@ struct FlowArgs {
   const float* noise;
   float* xt;
   __nv_bfloat16* xt_bf;
-  const __nv_bfloat16* w_in;   // action_in_proj [E, A] + bias [E]
+  // bf16 weights in fragment order
+  const uint8_t* w_in;         // action_in_proj [E, A] + bias [E]
   const __nv_bfloat16* b_in;
-  const __nv_bfloat16* w_tin;  // action_time_mlp_in, its first E columns (row stride ld_tin)
-  int ld_tin;
+  const uint8_t* w_tin;        // action_time_mlp_in, its first E columns [E, E]
   const float* c_step;         // [n_steps, E]: W_tin[:, E:] . time_emb(t_step) + b_tin
-  const __nv_bfloat16* w_tout;  // action_time_mlp_out [E, E] + bias
+  const uint8_t* w_tout;       // action_time_mlp_out [E, E] + bias
   const __nv_bfloat16* b_tout;
   const __nv_bfloat16* ln_f;   // final RMSNorm [E]
-  const __nv_bfloat16* w_out;  // action_out_proj [A, E] + bias [A]
+  const uint8_t* w_out;        // action_out_proj [A, E] + bias [A]
   const __nv_bfloat16* b_out;
   const uint8_t* key_mask;     // prefix key flags, row b at key_mask + b * key_mask_bs
   long long key_mask_bs;
@@ -84,6 +93,7 @@ struct FlowArgs {
   const float* rope_cs;        // [max_pos][32] (cos, sin)
   int max_pos;
   __nv_bfloat16 *a_emb, *a_t, *eh, *eq, *ek, *ev, *ectx, *emlp;  // scratch rows
+  float* norm_part;            // [kFlowRows][kFlowMaxSlices]: per row and 16-column slice, sum of squares of eh
   unsigned long long* sync;    // monotonic arrival counter (a multiple of gridDim.x between launches)
   uint32_t spin_limit;         // polls of a grid barrier before it gives up (kErrFlowBarrier)
   int* err;
@@ -107,6 +117,8 @@ struct FlowSmem {
   float red[kFlowWarps * kFlowRows * kFlowRedStride];    // per-warp partial tiles / attention partials
   float ml[kFlowWarps * 32];                             // attention: per-warp row max (16) and sum (16)
   uint8_t kf[kFlowWarps * 32];                           // attention: the staged keys' padding flags
+  float rstd[kFlowRows];                                 // RMSNorm: 1 / rms of the staged rows
+  unsigned long long target;                             // arrival count that opens the next grid barrier
   int ok;
   int n_ev;                                              // profiling events recorded by this CTA
 };
@@ -142,6 +154,12 @@ __device__ __forceinline__ uint32_t ldcg_u32(const __nv_bfloat16* p) {
 __device__ __forceinline__ void store2(__nv_bfloat16* p, float x, float y) {
   *reinterpret_cast<uint32_t*>(p) = pack_bf16_rn(x, y);
 }
+// store2, returning the sum of squares of the two stored (bf16) values: a row's RMSNorm statistics
+__device__ __forceinline__ float store2_ss(__nv_bfloat16* p, float x, float y) {
+  const float xr = bf16_round(x), yr = bf16_round(y);
+  store2(p, xr, yr);
+  return __fmaf_rn(yr, yr, __fmul_rn(xr, xr));
+}
 
 // profiling: thread 0 of CTA 0 and of the last CTA append (event, globaltimer) while there is room
 __device__ __forceinline__ void event(const FlowArgs& a, FlowSmem& sm, int code) {
@@ -156,18 +174,23 @@ __device__ __forceinline__ void event(const FlowArgs& a, FlowSmem& sm, int code)
   ++sm.n_ev;
 }
 
-// Grid barrier on a monotonic 64-bit arrival counter: barrier k of a launch opens when the counter reaches
-// the next multiple of gridDim.x above this CTA's arrival.  False when it timed out or another CTA recorded an
+// Grid barrier on a monotonic 64-bit arrival counter: barrier k (1, 2, ...) of a launch opens when the counter
+// reaches base + k * gridDim.x, base = the counter at launch (a multiple of gridDim.x: no barrier of this launch
+// can open before every CTA has read it, since each must arrive first).  False when it timed out or another CTA recorded an
 // error (then the caller returns).
-__device__ bool grid_sync(const FlowArgs& a, FlowSmem& sm) {
+// during(): work of every thread between its CTA's arrival and its wait that depends on no other CTA's writes
+// of the phase (L2 prefetches of the next phase's weights, staging of constant keys).
+template <typename During>
+__device__ bool grid_sync(const FlowArgs& a, FlowSmem& sm, During&& during) {
   __syncthreads();
   event(a, sm, kEvBarrierIn);
+  // arrive: a release reduction publishes this CTA's writes (ordered before it by the CTA barrier)
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(a.sync) : "memory");
+  during();
   if (threadIdx.x == 0) {
     int ok = 1;
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");  // this CTA's writes (ordered by the CTA barrier) first
-    const unsigned long long n = gridDim.x;
-    const unsigned long long old = atomicAdd(a.sync, 1ull);
-    const unsigned long long target = (old / n + 1ull) * n;
+    const unsigned long long target = sm.target;
+    sm.target = target + gridDim.x;
     uint32_t spins = 0;
     while (ld_acquire_u64(a.sync) < target) {
       if (++spins >= a.spin_limit) {
@@ -179,13 +202,31 @@ __device__ bool grid_sync(const FlowArgs& a, FlowSmem& sm) {
         ok = 0;
         break;
       }
-      __nanosleep(32);
     }
     sm.ok = ok;
   }
   __syncthreads();
   event(a, sm, kEvBarrierOut);
   return sm.ok != 0;
+}
+__device__ __forceinline__ bool grid_sync(const FlowArgs& a, FlowSmem& sm) {
+  return grid_sync(a, sm, [] {});
+}
+
+// L2 prefetch of the weight slices of this CTA's first task of a GEMM phase (n_col slices x row blocks of
+// rows_t rows, K columns), issued while it waits at the barrier before the phase
+template <int G, bool I8, typename WFn>
+__device__ __forceinline__ void prefetch_first(WFn&& wslices, int n_col, int M, int rows_t, int K) {
+  const int blocks = (M + rows_t - 1) / rows_t;
+  if (static_cast<int>(blockIdx.x) >= n_col * blocks || static_cast<int>(threadIdx.x) >= G) return;
+  const uint8_t* w[G];
+  const float* sc[G];
+  wslices(static_cast<int>(blockIdx.x) / blocks, w, sc);
+  const uint32_t bytes = static_cast<uint32_t>(K) * 16u * (I8 ? 1u : 2u);
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi)
+    if (gi == static_cast<int>(threadIdx.x))
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w[gi]), "r"(bytes) : "memory");
 }
 
 // row stride (elements) of a staged chunk of kc columns: 16-byte rows whose 8-row ldmatrix groups hit
@@ -200,16 +241,21 @@ __device__ __forceinline__ int staged_ld(int kc) {
 // flight at once, completing on the CTA's mbarrier (stage_wait: bounded; a timeout records an error that ends
 // the kernel at its next grid barrier).  Rows M..63 are left as they are: they only feed output rows that are
 // not stored.
-__device__ void stage_issue(FlowSmem& sm, const __nv_bfloat16* A, int lda, int M, int k0, int kc, int ldsa) {
-  if (threadIdx.x == 0) mbar_arrive_expect_tx(&sm.bar, static_cast<uint32_t>(M * kc * 2));
+__device__ void stage_issue(FlowSmem& sm, const __nv_bfloat16* A, int lda, int M, int k0, int kc, int ldsa,
+                            const float* part = nullptr) {
+  const uint32_t part_bytes = part != nullptr ? static_cast<uint32_t>(M * kFlowMaxSlices * 4) : 0u;
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(&sm.bar, static_cast<uint32_t>(M * kc * 2) + part_bytes);
   __syncthreads();
-  if (static_cast<int>(threadIdx.x) < M) {
+  const bool row = static_cast<int>(threadIdx.x) < M, parts = part != nullptr && threadIdx.x == kFlowRows;
+  if (row || parts) {
     // order other CTAs' earlier (generic) writes of A and this CTA's earlier reads of the buffer before the copy
     asm volatile("fence.proxy.async.global;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (row)
     bulk_g2s(&sm.a[threadIdx.x * ldsa], A + static_cast<size_t>(threadIdx.x) * lda + k0, static_cast<uint32_t>(kc * 2),
              &sm.bar);
-  }
+  if (parts) bulk_g2s(sm.red, part, part_bytes, &sm.bar);  // the rows' slice sums of squares (RMSNorm phases)
 }
 __device__ __forceinline__ void stage_wait(FlowSmem& sm, uint32_t& parity, int* err) {
   mbar_wait(&sm.bar, parity, err);
@@ -217,138 +263,133 @@ __device__ __forceinline__ void stage_wait(FlowSmem& sm, uint32_t& parity, int* 
 }
 
 
-// RMSNorm of the staged rows [0, M) (K <= 256 * NV) in place, one warp per row, with the arithmetic of the
-// stand-alone norm kernel's RMSNorm rows (norm_quant_row) in the same order, so the same bf16 results:
-//   ss = sum_k x^2 (fma, lane elements in order, then a butterfly over the lanes); rstd = 1 / sqrt(ss / K + eps)
-//   y = bf16(w * bf16(x * rstd)).  The weight stays in registers across rows.
-template <int NV>
-__device__ void norm_staged_rows(FlowSmem& sm, int K, const __nv_bfloat16* w, float eps, int M, int ldsa) {
-  constexpr int R = 2;  // rows per warp in flight (rows warp + 8 r)
+// RMSNorm of the staged rows, folded into the GEMM: the phase that wrote the rows left, per row and 16-column
+// slice, the sum of squares of the stored bf16 values (reduce_tiles, a fixed butterfly over the slice); they are
+// staged with the rows (stage_issue), added here in a fixed order (4 threads per row, consecutive slice runs,
+// then a butterfly) into rstd = 1 / sqrt(ss / K + eps), and mma_w applies y = bf16(w * bf16(x * rstd)) to each
+// A fragment it loads -- the rounding points of the stand-alone norm kernel's RMSNorm rows (norm_quant_row); only
+// the fp32 order of the sum of squares differs.  Rows M.. of the tile get rstd 0 (they feed no stored output).
+__device__ void rstd_from_parts(FlowSmem& sm, int K, float eps, int M, int tile_rows) {
+  const int m = threadIdx.x >> 2, q = threadIdx.x & 3, ns = K / 16, nq = (ns + 3) / 4;
+  float ss = 0.f;
+  if (m < M) {
+    const float* p = sm.red + m * kFlowMaxSlices;
+    const int end = (q + 1) * nq < ns ? (q + 1) * nq : ns;
+    for (int sl = q * nq; sl < end; ++sl) ss = __fadd_rn(ss, p[sl]);
+  }
+  ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, 1));
+  ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, 2));
+  if (q == 0 && m < tile_rows) {
+    const float var = __fdiv_rn(ss, static_cast<float>(K));
+    sm.rstd[m] = m < M ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps))) : 0.f;
+  }
+}
+// y = bf16(w * bf16(x * r)) of a bf16x2 pair x with weights w (the product of two bf16 values is exact in fp32,
+// so one bf16x2 multiply rounds it exactly as bf16(fp32(w) * fp32(h)) does)
+__device__ __forceinline__ uint32_t norm_pair(uint32_t x, float r, uint32_t w) {
+  const __nv_bfloat162 xb = *reinterpret_cast<const __nv_bfloat162*>(&x);
+  const __nv_bfloat162 wb = *reinterpret_cast<const __nv_bfloat162*>(&w);
+  const __nv_bfloat162 h = __float22bfloat162_rn(__fmul2_rn(__bfloat1622float2(xb), make_float2(r, r)));
+  const __nv_bfloat162 y = __hmul2(wb, h);
+  return *reinterpret_cast<const uint32_t*>(&y);
+}
+
+// One lane's weight fragments of one k16 step of a 16-column slice: the B fragments (b0, b1) of the slice's two
+// 8-column tiles, as int8 (8 bytes) or bf16 (16 bytes).
+template <bool I8>
+using Frag = typename std::conditional<I8, uint2, uint4>::type;
+
+// bf16x2 of two int8 weights (bytes sh / 8 and sh / 8 + 1 of w) dequantised as bf16(float(q) * s): the rounding
+// of the bf16 weight the per-layer path multiplies by
+__device__ __forceinline__ uint32_t deq_pair(uint32_t w, int sh, float s) {
+  const float q0 = static_cast<float>(static_cast<int8_t>((w >> sh) & 0xFFu));
+  const float q1 = static_cast<float>(static_cast<int8_t>((w >> (sh + 8)) & 0xFFu));
+  return pack_bf16_rn(__fmul_rn(q0, s), __fmul_rn(q1, s));
+}
+
+// the four bf16x2 B registers (tile 0: b0, b1; tile 1: b0, b1) of a fragment; sc: the scales of the lane's
+// columns in tiles 0 and 1 (int8 only)
+__device__ __forceinline__ void frag_regs(const uint2& f, const float (&sc)[2], uint32_t (&r)[4]) {
+  r[0] = deq_pair(f.x, 0, sc[0]);
+  r[1] = deq_pair(f.x, 16, sc[0]);
+  r[2] = deq_pair(f.y, 0, sc[1]);
+  r[3] = deq_pair(f.y, 16, sc[1]);
+}
+__device__ __forceinline__ void frag_regs(const uint4& f, const float (&)[2], uint32_t (&r)[4]) {
+  r[0] = f.x;
+  r[1] = f.y;
+  r[2] = f.z;
+  r[3] = f.w;
+}
+
+// this warp's weight fragments of one chunk (k16 steps w, w + 8, ..., at most U) of the slices ws[G], loaded
+// before they are needed so that their latency overlaps the staging of A
+template <int G, int U, bool I8>
+__device__ __forceinline__ void load_w(const uint8_t* const (&ws)[G], int k0, int kc, Frag<I8> (&b)[U][G]) {
+  constexpr int kLaneBytes = I8 ? 8 : 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __nv_bfloat162 w2[NV][4];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int k = (i * 32 + lane) * 8;
-    const int4 wr = k < K ? *reinterpret_cast<const int4*>(w + k) : make_int4(0, 0, 0, 0);
-    const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wr);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w2[i][j] = wh[j];
-  }
-  for (int m0 = warp; m0 < M; m0 += R * kFlowWarps) {
-    float2 v[R][NV][4];
-    float ss[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int m = m0 + r * kFlowWarps;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int k = (i * 32 + lane) * 8;
-        const int4 raw = (m < M && k < K) ? *reinterpret_cast<const int4*>(&sm.a[m * ldsa + k]) : make_int4(0, 0, 0, 0);
-        const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[r][i][j] = __bfloat1622float2(hx[j]);
-      }
-      ss[r] = 0.f;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        if ((i * 32 + lane) * 8 < K) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            ss[r] = fmaf(v[r][i][j].x, v[r][i][j].x, ss[r]);
-            ss[r] = fmaf(v[r][i][j].y, v[r][i][j].y, ss[r]);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-      for (int r = 0; r < R; ++r) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], o);
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int m = m0 + r * kFlowWarps;
-      if (m >= M) continue;
-      const float var = __fdiv_rn(ss[r], static_cast<float>(K));
-      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-      const float2 rs = make_float2(rstd, rstd);
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int k = (i * 32 + lane) * 8;
-        if (k >= K) continue;
-        uint32_t out[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          // h = bf16(x * rstd); y = bf16(w * h): the product of two bf16 values is exact in fp32, so one bf16x2
-          // multiply rounds it exactly as bf16(fp32(w) * fp32(h)) does
-          const __nv_bfloat162 h = __float22bfloat162_rn(__fmul2_rn(v[r][i][j], rs));
-          const __nv_bfloat162 y = __hmul2(w2[i][j], h);
-          out[j] = *reinterpret_cast<const uint32_t*>(&y);
-        }
-        *reinterpret_cast<int4*>(&sm.a[m * ldsa + k]) = make_int4(out[0], out[1], out[2], out[3]);
-      }
-    }
-  }
-}
-
-// finish staging A (optionally RMSNorm-ed; K <= 1024 then) for a phase whose K fits one chunk
-__device__ void stage_single_finish(const FlowArgs& fa, FlowSmem& sm, int K, const __nv_bfloat16* norm_w, float eps,
-                                    int M, int ldsa, uint32_t& parity) {
-  stage_wait(sm, parity, fa.err);
-  event(fa, sm, kEvCopied);
-  if (norm_w != nullptr) {
-    if (K <= 256) norm_staged_rows<1>(sm, K, norm_w, eps, M, ldsa);
-    else if (K <= 512) norm_staged_rows<2>(sm, K, norm_w, eps, M, ldsa);
-    else if (K <= 768) norm_staged_rows<3>(sm, K, norm_w, eps, M, ldsa);
-    else norm_staged_rows<4>(sm, K, norm_w, eps, M, ldsa);
-    __syncthreads();
-  }
-}
-
-// this warp's weight fragments of one chunk (k16 steps w, w + 8, ..., at most U), loaded before they are
-// needed so that their latency overlaps the staging of A
-template <int G, int U>
-__device__ __forceinline__ void load_w(const __nv_bfloat16* const (&wrow)[G], int ldw, int k0, int kc,
-                                       uint32_t (&b)[U][G][2][2]) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int steps = kc / 16;
+  const int steps = kc / 16, s0 = k0 / 16;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int s = warp + u * kFlowWarps;
 #pragma unroll
     for (int gi = 0; gi < G; ++gi) {
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        if (s < steps) {
-          const __nv_bfloat16* p = wrow[gi] + static_cast<size_t>(nt * 8 + g) * ldw + k0 + s * 16 + 2 * t;
-          b[u][gi][nt][0] = __ldg(reinterpret_cast<const unsigned int*>(p));
-          b[u][gi][nt][1] = __ldg(reinterpret_cast<const unsigned int*>(p + 8));
-        } else {
-          b[u][gi][nt][0] = b[u][gi][nt][1] = 0u;
-        }
+      if (s < steps) {
+        b[u][gi] = __ldg(reinterpret_cast<const Frag<I8>*>(ws[gi] + (static_cast<size_t>(s0 + s) * 32 + lane) * kLaneBytes));
+      } else {
+        b[u][gi] = Frag<I8>{};
       }
     }
   }
 }
 
-// this warp's partial products over its k16 steps of the staged chunk
-template <int G, int MT, int U>
-__device__ __forceinline__ void mma_w(const FlowSmem& sm, int ldsa, int kc, const uint32_t (&b)[U][G][2][2],
-                                      float (&acc)[G][2][MT][4]) {
+// the norm weights of this warp's k16 steps (columns k0 + s*16 + 2t, + 1 and + 8, + 9), loaded with the weights
+template <int U>
+__device__ __forceinline__ void load_nw(const __nv_bfloat16* nw, int k0, int kc, uint32_t (&nv)[U][2]) {
+  const int warp = threadIdx.x >> 5, t = threadIdx.x & 3;
+  const int steps = kc / 16;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int s = warp + u * kFlowWarps;
+    if (s < steps) {
+      nv[u][0] = __ldg(reinterpret_cast<const unsigned int*>(nw + k0 + s * 16 + 2 * t));
+      nv[u][1] = __ldg(reinterpret_cast<const unsigned int*>(nw + k0 + s * 16 + 2 * t + 8));
+    } else {
+      nv[u][0] = nv[u][1] = 0u;
+    }
+  }
+}
+
+// this warp's partial products over its k16 steps of the staged chunk; NORM: RMSNorm each A fragment first
+// (norm weights nv from load_nw, the fragment rows' rstd in rs[mt][0 / 1] for rows g / g + 8)
+template <int G, int MT, int U, bool I8, bool NORM>
+__device__ __forceinline__ void mma_w(const FlowSmem& sm, int ldsa, int kc, const Frag<I8> (&b)[U][G],
+                                      const float (&sc)[G][2], float (&acc)[G][2][MT][4],
+                                      const uint32_t (&nv)[U][2], const float (&rs)[MT][2]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int steps = kc / 16;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int s = warp + u * kFlowWarps;
     if (s >= steps) break;
+    uint32_t r[G][4];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) frag_regs(b[u][gi], sc[gi], r[gi]);
+    const uint32_t w_lo = nv[u][0], w_hi = nv[u][1];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
       uint32_t af[4];
       ldmatrix_x4(af, &sm.a[(mt * 16 + (lane & 15)) * ldsa + s * 16 + (lane >> 4) * 8]);
+      if constexpr (NORM) {  // a0: row g, k 2t | a1: row g + 8 | a2: row g, k 2t + 8 | a3: row g + 8, k 2t + 8
+        af[0] = norm_pair(af[0], rs[mt][0], w_lo);
+        af[1] = norm_pair(af[1], rs[mt][1], w_lo);
+        af[2] = norm_pair(af[2], rs[mt][0], w_hi);
+        af[3] = norm_pair(af[3], rs[mt][1], w_hi);
+      }
 #pragma unroll
       for (int gi = 0; gi < G; ++gi) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) mma16816(acc[gi][nt][mt], af, b[u][gi][nt][0], b[u][gi][nt][1]);
+        mma16816(acc[gi][0][mt], af, r[gi][0], r[gi][1]);
+        mma16816(acc[gi][1][mt], af, r[gi][2], r[gi][3]);
       }
     }
   }
@@ -356,12 +397,20 @@ __device__ __forceinline__ void mma_w(const FlowSmem& sm, int ldsa, int kc, cons
 
 // adds the 8 warps' partial tiles (warp order) and hands each (row, column pair) to the epilogue together
 // with the four words pre(m, j) fetched for it before the partial tiles were exchanged (residuals, biases:
-// their load latency overlaps the exchange)
-template <int G, int MT, typename Pre, typename Epi>
+// their load latency overlaps the exchange).  An epilogue that returns a SqSums<G> returns, per group, the sum of
+// squares of the two values it stored: the 8 pairs of a row of each group's 16 columns are then added by a fixed
+// butterfly and handed to stat(m, gi, ss) -- the RMSNorm statistics of the rows for the next phase.
+template <int G>
+struct SqSums {
+  float s[G];
+};
+template <int G, int MT, typename Pre, typename Epi, typename Stat>
 __device__ __forceinline__ void reduce_tiles(FlowSmem& sm, int M, const float (&acc)[G][2][MT][4], Pre&& pre,
-                                             Epi&& epi) {
+                                             Epi&& epi, Stat&& stat) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   constexpr int kItems = (MT * 16 * 8 + kFlowThreads - 1) / kFlowThreads;  // (row, column pair) items per thread
+  using R = decltype(epi(0, 0, std::declval<float (&)[G][2]>(), std::declval<const uint4&>()));
+  constexpr bool kStats = std::is_same<R, SqSums<G>>::value;
   uint4 pv[kItems];
 #pragma unroll
   for (int u = 0; u < kItems; ++u) {
@@ -387,32 +436,51 @@ __device__ __forceinline__ void reduce_tiles(FlowSmem& sm, int M, const float (&
 #pragma unroll
   for (int u = 0; u < kItems; ++u) {
     const int idx = threadIdx.x + u * kFlowThreads;
-    if (idx >= M * 8) break;
+    const bool valid = idx < M * 8;  // every thread takes every u (the butterfly below needs whole warps)
     const int m = idx >> 3, j = (idx & 7) * 2;
-    float v[G][2];
+    SqSums<G> ss{};
+    if (valid) {
+      float v[G][2];
 #pragma unroll
-    for (int gi = 0; gi < G; ++gi) {
-      v[gi][0] = v[gi][1] = 0.f;
+      for (int gi = 0; gi < G; ++gi) {
+        v[gi][0] = v[gi][1] = 0.f;
 #pragma unroll
-      for (int w = 0; w < kFlowWarps; ++w) {
-        const float2 p = *reinterpret_cast<const float2*>(
-            &sm.red[(w * kFlowRows + m) * kFlowRedStride + gi * 16 + j]);
-        v[gi][0] = __fadd_rn(v[gi][0], p.x);
-        v[gi][1] = __fadd_rn(v[gi][1], p.y);
+        for (int w = 0; w < kFlowWarps; ++w) {
+          const float2 p = *reinterpret_cast<const float2*>(
+              &sm.red[(w * kFlowRows + m) * kFlowRedStride + gi * 16 + j]);
+          v[gi][0] = __fadd_rn(v[gi][0], p.x);
+          v[gi][1] = __fadd_rn(v[gi][1], p.y);
+        }
+      }
+      if constexpr (kStats) {
+        ss = epi(m, j, v, pv[u]);
+      } else {
+        epi(m, j, v, pv[u]);
       }
     }
-    epi(m, j, v, pv[u]);
+    if constexpr (kStats) {
+#pragma unroll
+      for (int gi = 0; gi < G; ++gi) {
+        float x = ss.s[gi];
+        x = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, 1));
+        x = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, 2));
+        x = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, 4));
+        if (valid && (idx & 7) == 0) stat(m, gi, x);
+      }
+    }
   }
   __syncthreads();
 }
 
 // One GEMM phase: out[rows, slice] = epi(A[rows, :K] . W[slice, :K]^T) for n_col slices of G x 16 columns,
 // each split into blocks of MT * 16 rows (a task = a slice x a row block: with MT = 2 a CTA stages, normalises
-// and multiplies half of the rows, at twice the tasks); wrows(slice, w) gives each group's first weight row.
-// norm_w: RMSNorm the A rows while staging (K <= 1024).
-template <int G, int MT, typename WFn, typename PreFn, typename EpiFn>
+// and multiplies half of the rows, at twice the tasks); wslices(slice, w, s) gives each group's packed 16-column
+// slice (K * 16 elements, int8 when I8, else bf16) and, for int8, the slice's 16 per-column scales.
+// NORM: RMSNorm the A rows with norm_w (K <= 1024; rstd_from_parts).  An epilogue that returns SqSums<G> leaves
+// the RMSNorm statistics of its rows for the next phase: group gi of task ct is slice ct * G + gi of the output.
+template <int G, int MT, bool I8, bool NORM, typename WFn, typename PreFn, typename EpiFn>
 __device__ void gemm_phase(const FlowArgs& fa, FlowSmem& sm, uint32_t& parity, int M, const __nv_bfloat16* A, int K,
-                           const __nv_bfloat16* norm_w, float eps, int n_col, int ldw, WFn&& wrows, PreFn&& pre,
+                           const __nv_bfloat16* norm_w, float eps, int n_col, WFn&& wslices, PreFn&& pre,
                            EpiFn&& epi) {
   constexpr int kRowsT = MT * 16;
   // columns staged per chunk: as many as the A buffer holds for kRowsT rows, at most U k16 steps per warp
@@ -420,19 +488,30 @@ __device__ void gemm_phase(const FlowArgs& fa, FlowSmem& sm, uint32_t& parity, i
   constexpr int KC0 = U * 16 * kFlowWarps, KC1 = (kFlowRows * kFlowLda) / kRowsT - 16;
   constexpr int KC = KC0 < KC1 ? KC0 : KC1;
   static_assert(KC % 16 == 0 && KC >= 1024, "chunk width");
+  if (NORM && K > KC) return;  // a normed phase stages its rows whole (svla_flow checks K <= 1024)
   const int blocks = (M + kRowsT - 1) / kRowsT;
   const int n_tasks = n_col * blocks;
   if (static_cast<int>(blockIdx.x) >= n_tasks) return;
   const bool single = K <= KC;
   const int ldsa = staged_ld(single ? K : KC);
+  float rs[MT][2] = {};
+  uint32_t nv[U][2] = {};
   int staged = -1;  // row block in shared memory (single-chunk phases)
-  uint32_t b[U][G][2][2];
+  Frag<I8> b[U][G];
+  const int g8 = (threadIdx.x & 31) >> 2;
   for (int task = blockIdx.x; task < n_tasks; task += gridDim.x) {
     const int ct = task / blocks, rb = task % blocks;
     const int row0 = rb * kRowsT, rows = (M - row0) < kRowsT ? (M - row0) : kRowsT;
     const __nv_bfloat16* Ab = A + static_cast<size_t>(row0) * K;
-    const __nv_bfloat16* wr[G];
-    wrows(ct, wr);
+    const uint8_t* wr[G];
+    const float* wsc[G];
+    wslices(ct, wr, wsc);
+    float sc[G][2];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      sc[gi][0] = I8 ? __ldg(wsc[gi] + g8) : 0.f;
+      sc[gi][1] = I8 ? __ldg(wsc[gi] + 8 + g8) : 0.f;
+    }
     float acc[G][2][MT][4];
 #pragma unroll
     for (int gi = 0; gi < G; ++gi)
@@ -446,24 +525,35 @@ __device__ void gemm_phase(const FlowArgs& fa, FlowSmem& sm, uint32_t& parity, i
       const bool stage = !single || staged != rb;
       if (stage) {
         if (!single) __syncthreads();  // every warp is done with the previous chunk
-        stage_issue(sm, Ab, K, rows, k0, kc, ldsa);
+        stage_issue(sm, Ab, K, rows, k0, kc, ldsa,
+                    NORM ? fa.norm_part + static_cast<size_t>(row0) * kFlowMaxSlices : nullptr);
       }
-      load_w<G, U>(wr, ldw, k0, kc, b);
+      load_w<G, U, I8>(wr, k0, kc, b);
+      if constexpr (NORM) load_nw<U>(norm_w, k0, kc, nv);
       if (stage) {
-        if (single) {
-          stage_single_finish(fa, sm, K, norm_w, eps, rows, ldsa, parity);
-          staged = rb;
-          event(fa, sm, kEvStaged);
-        } else {
-          stage_wait(sm, parity, fa.err);
+        stage_wait(sm, parity, fa.err);
+        event(fa, sm, kEvCopied);
+        if (single) staged = rb;
+        if constexpr (NORM) {
+          rstd_from_parts(sm, K, eps, rows, kRowsT);
+          __syncthreads();
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            rs[mt][0] = sm.rstd[mt * 16 + g8];
+            rs[mt][1] = sm.rstd[mt * 16 + 8 + g8];
+          }
         }
+        event(fa, sm, kEvStaged);
       }
-      mma_w<G, MT, U>(sm, ldsa, kc, b, acc);
+      mma_w<G, MT, U, I8, NORM>(sm, ldsa, kc, b, sc, acc, nv, rs);
     }
     event(fa, sm, kEvMma);
     reduce_tiles<G, MT>(
         sm, rows, acc, [&](int m, int j) { return pre(ct, row0 + m, j); },
-        [&](int m, int j, float (&v)[G][2], const uint4& p) { epi(ct, row0 + m, j, v, p); });
+        [&](int m, int j, float (&v)[G][2], const uint4& p) { return epi(ct, row0 + m, j, v, p); },
+        [&](int m, int gi, float ss) {
+          fa.norm_part[static_cast<size_t>(row0 + m) * kFlowMaxSlices + ct * G + gi] = ss;
+        });
     event(fa, sm, kEvEpilogue);
   }
 }
@@ -695,6 +785,30 @@ __device__ void attention_phase(FlowSmem& sm, const FlowArgs& a, const FlowLayer
 
 }  // namespace flow_detail
 
+// Fragment-order copy of a weight w [n, k] (row stride ld elements of eb bytes; n, k multiples of 16), the
+// layout the flow kernel's weight loads read: thread i writes lane (i % 32) of k16 step s of 16-row slice sl
+// (i / 32 = sl * k / 16 + s), 8 elements: rows sl*16 + g (e < 4) or + 8 + g (e >= 4), g = lane / 4, columns
+// s*16 + 2 (lane % 4) + (e % 2) + 8 ((e / 2) % 2) -- the B fragments b0, b1 of mma.m16n8k16 for both 8-row tiles.
+__global__ void pack_fragments_kernel(const uint8_t* w, int eb, long long ld, int n, int k, uint8_t* out) {
+  const long long total = static_cast<long long>(n) * k / 8;
+  const int ks = k / 16;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int lane = static_cast<int>(i % 32);
+    const long long r = i / 32;
+    const int s = static_cast<int>(r % ks), sl = static_cast<int>(r / ks);
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const long long row = sl * 16 + (e >= 4 ? 8 : 0) + g;
+      const long long col = s * 16 + 2 * t + (e & 1) + ((e >> 1) & 1) * 8;
+      const uint8_t* src = w + (row * ld + col) * eb;
+      uint8_t* dst = out + (i * 8 + e) * eb;
+      for (int bb = 0; bb < eb; ++bb) dst[bb] = src[bb];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a) {
   using namespace flow_detail;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -706,6 +820,8 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
     fence_mbar_init();
     // a device error left by an earlier launch may have left the barrier counter between multiples: do not run
     sm.ok = *reinterpret_cast<volatile int*>(a.err) == 0;
+    const unsigned long long n = gridDim.x;
+    sm.target = (ld_acquire_u64(a.sync) / n + 1ull) * n;
   }
   __syncthreads();
   if (!sm.ok) return;
@@ -718,6 +834,9 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
     a.xt_bf[i] = __float2bfloat16_rn(x);
   }
 
+  // 16-column slice `i` of a fragment-packed weight with k columns
+  auto slice_i8 = [](const uint8_t* w, int i, int k) { return w + static_cast<size_t>(i) * 16 * k; };
+  auto slice_bf16 = [](const uint8_t* w, int i, int k) { return w + static_cast<size_t>(i) * 32 * k; };
   auto no_pre = [](int, int, int) { return make_uint4(0u, 0u, 0u, 0u); };
   // two bf16 biases of columns c, c + 1 (one word)
   auto bias_pre = [](const __nv_bfloat16* bias, int c) {
@@ -727,28 +846,92 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
   auto hi = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };  // bf16 in the high half
   // residual epilogue: p.x holds eh[m, c..c+1]
   auto resid_store = [&](int c, int m, const float (&v)[1][2], const uint4& p) {
-    store2(a.eh + static_cast<size_t>(m) * E + c, __fadd_rn(bf16_round(v[0][0]), lo(p.x)),
-           __fadd_rn(bf16_round(v[0][1]), hi(p.x)));
+    return SqSums<1>{{store2_ss(a.eh + static_cast<size_t>(m) * E + c, __fadd_rn(bf16_round(v[0][0]), lo(p.x)),
+                                __fadd_rn(bf16_round(v[0][1]), hi(p.x)))}};
   };
 
-  if (!grid_sync(a, sm)) return;
+  // weight slices of each GEMM phase: task -> the packed 16-column slices of its G groups (and their scales)
+  auto w_in = [&](int task, const uint8_t* (&w)[1], const float* (&s)[1]) {
+    w[0] = slice_bf16(a.w_in, task, Ad);
+    s[0] = nullptr;
+  };
+  auto w_tin = [&](int task, const uint8_t* (&w)[1], const float* (&s)[1]) {
+    w[0] = slice_bf16(a.w_tin, task, E);
+    s[0] = nullptr;
+  };
+  auto w_tout = [&](int task, const uint8_t* (&w)[1], const float* (&s)[1]) {
+    w[0] = slice_bf16(a.w_tout, task, E);
+    s[0] = nullptr;
+  };
+  auto w_out = [&](int task, const uint8_t* (&w)[1], const float* (&s)[1]) {
+    w[0] = slice_bf16(a.w_out, task, E);
+    s[0] = nullptr;
+  };
+  // q (and k, v on self-attention layers) with RoPE; a task is the column pairs (c, c + 32) of 16 consecutive
+  // rotation pairs of one head: c0 = head * 64 + half * 16
+  auto qkv_cols = [&](const FlowLayer& L) { return 2 * a.Hq + (L.cross ? 0 : 4 * a.Hkv); };
+  auto qkv_seg = [&](const FlowLayer& L, int task, int& seg, int& c0) {
+    const int q_tasks = 2 * a.Hq, kv_tasks = L.cross ? 0 : 2 * a.Hkv;
+    int t = task;
+    seg = 0;
+    if (t >= q_tasks) {
+      t -= q_tasks;
+      seg = 1;
+      if (t >= kv_tasks) {
+        t -= kv_tasks;
+        seg = 2;
+      }
+    }
+    c0 = (t >> 1) * 64 + (t & 1) * 16;
+  };
+  auto w_qkv = [&](const FlowLayer& L, int task, const uint8_t* (&w)[2], const float* (&s)[2]) {
+    int seg, c0;
+    qkv_seg(L, task, seg, c0);
+    const uint8_t* W = seg == 0 ? L.wq : (seg == 1 ? L.wk : L.wv);
+    const float* S = seg == 0 ? L.sq : (seg == 1 ? L.sk : L.sv);
+    w[0] = slice_i8(W, c0 / 16, E);
+    w[1] = slice_i8(W, (c0 + 32) / 16, E);
+    s[0] = S + c0;
+    s[1] = S + c0 + 32;
+  };
+  auto w_o = [&](const FlowLayer& L, int task, const uint8_t* (&w)[1], const float* (&s)[1]) {
+    w[0] = slice_i8(L.wo, task, qd);
+    s[0] = L.so + task * 16;
+  };
+  auto w_gu = [&](const FlowLayer& L, int task, const uint8_t* (&w)[2], const float* (&s)[2]) {
+    w[0] = slice_i8(L.wg, task, E);
+    w[1] = slice_i8(L.wu, task, E);
+    s[0] = L.sg + task * 16;
+    s[1] = L.su + task * 16;
+  };
+  auto w_d = [&](const FlowLayer& L, int task, const uint8_t* (&w)[1], const float* (&s)[1]) {
+    w[0] = slice_i8(L.wd, task, a.mlp);
+    s[0] = L.sd + task * 16;
+  };
+  auto bind = [](auto& f, const FlowLayer& L) { return [&f, &L](int t, auto& w, auto& s) { f(L, t, w, s); }; };
+  // L2 prefetches of a phase's first-task weights, issued while waiting at the barrier before it
+  auto pf_in = [&] { prefetch_first<1, false>(w_in, E / 16, M, 32, Ad); };
+  auto pf_qkv = [&](const FlowLayer& L) { prefetch_first<2, true>(bind(w_qkv, L), qkv_cols(L), M, 32, E); };
+  auto pf_o = [&](const FlowLayer& L) { prefetch_first<1, true>(bind(w_o, L), E / 16, M, 32, qd); };
+  auto pf_gu = [&](const FlowLayer& L) { prefetch_first<2, true>(bind(w_gu, L), a.mlp / 16, M, 64, E); };
+  auto pf_d = [&](const FlowLayer& L) { prefetch_first<1, true>(bind(w_d, L), E / 16, M, 32, a.mlp); };
+
+  if (!grid_sync(a, sm, pf_in)) return;
 
   for (int step = 0; step < a.n_steps; ++step) {
     // action_in_proj: a_emb = bf16(x_t . W_in^T + b)
-    gemm_phase<1, 2>(
-        a, sm, parity, M, a.xt_bf, Ad, nullptr, 0.f, E / 16, Ad,
-        [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_in + static_cast<size_t>(task) * 16 * Ad; },
+    gemm_phase<1, 2, false, false>(
+        a, sm, parity, M, a.xt_bf, Ad, nullptr, 0.f, E / 16, w_in,
         [&](int task, int, int j) { return bias_pre(a.b_in, task * 16 + j); },
         [&](int task, int m, int j, float (&v)[1][2], const uint4& p) {
           store2(a.a_emb + static_cast<size_t>(m) * E + task * 16 + j, __fadd_rn(v[0][0], lo(p.x)),
                  __fadd_rn(v[0][1], hi(p.x)));
         });
-    if (!grid_sync(a, sm)) return;
+    if (!grid_sync(a, sm, [&] { prefetch_first<1, false>(w_tin, E / 16, M, 32, E); })) return;
     // time MLP in: a_t = bf16(silu(bf16(a_emb . W_tin[:, :E]^T + c_step)))
     const float* cst = a.c_step + static_cast<size_t>(step) * E;
-    gemm_phase<1, 2>(
-        a, sm, parity, M, a.a_emb, E, nullptr, 0.f, E / 16, a.ld_tin,
-        [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_tin + static_cast<size_t>(task) * 16 * a.ld_tin; },
+    gemm_phase<1, 2, false, false>(
+        a, sm, parity, M, a.a_emb, E, nullptr, 0.f, E / 16, w_tin,
         [&](int task, int, int j) {
           const float2 c2 = __ldg(reinterpret_cast<const float2*>(cst + task * 16 + j));
           return make_uint4(__float_as_uint(c2.x), __float_as_uint(c2.y), 0u, 0u);
@@ -758,51 +941,26 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
           const float x1 = bf16_round(__fadd_rn(v[0][1], __uint_as_float(p.y)));
           store2(a.a_t + static_cast<size_t>(m) * E + task * 16 + j, silu_f(x0), silu_f(x1));
         });
-    if (!grid_sync(a, sm)) return;
+    if (!grid_sync(a, sm, [&] { prefetch_first<1, false>(w_tout, E / 16, M, 32, E); })) return;
     // time MLP out: eh = bf16(a_t . W_tout^T + b)
-    gemm_phase<1, 2>(
-        a, sm, parity, M, a.a_t, E, nullptr, 0.f, E / 16, E,
-        [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_tout + static_cast<size_t>(task) * 16 * E; },
+    gemm_phase<1, 2, false, false>(
+        a, sm, parity, M, a.a_t, E, nullptr, 0.f, E / 16, w_tout,
         [&](int task, int, int j) { return bias_pre(a.b_tout, task * 16 + j); },
         [&](int task, int m, int j, float (&v)[1][2], const uint4& p) {
-          store2(a.eh + static_cast<size_t>(m) * E + task * 16 + j, __fadd_rn(v[0][0], lo(p.x)),
-                 __fadd_rn(v[0][1], hi(p.x)));
+          return SqSums<1>{{store2_ss(a.eh + static_cast<size_t>(m) * E + task * 16 + j, __fadd_rn(v[0][0], lo(p.x)),
+                                      __fadd_rn(v[0][1], hi(p.x)))}};
         });
-    if (!grid_sync(a, sm)) return;
+    if (!grid_sync(a, sm, [&] { pf_qkv(a.layer[0]); })) return;
 
     for (int li = 0; li < a.n_layers; ++li) {
       const FlowLayer& L = a.layer[li];
-      // q (and k, v on self-attention layers) with RoPE; a task is the column pairs (c, c + 32) of 16
-      // consecutive rotation pairs of one head: c0 = head * 64 + half * 16
-      const int q_tasks = 2 * a.Hq, kv_tasks = L.cross ? 0 : 2 * a.Hkv;
       const int* pos = L.cross ? a.cross_pos : a.suffix_pos;
-      auto seg_of = [&](int task, int& seg, int& c0) {
-        if (task < q_tasks) {
-          seg = 0;
-          c0 = (task >> 1) * 64 + (task & 1) * 16;
-        } else if (task < q_tasks + kv_tasks) {
-          seg = 1;
-          const int tk = task - q_tasks;
-          c0 = (tk >> 1) * 64 + (tk & 1) * 16;
-        } else {
-          seg = 2;
-          const int tv = task - q_tasks - kv_tasks;
-          c0 = (tv >> 1) * 64 + (tv & 1) * 16;
-        }
-      };
-      gemm_phase<2, 2>(
-          a, sm, parity, M, a.eh, E, L.ln1, a.eps, q_tasks + 2 * kv_tasks, E,
-          [&](int task, const __nv_bfloat16* (&w)[2]) {
-            int seg, c0;
-            seg_of(task, seg, c0);
-            const __nv_bfloat16* W = seg == 0 ? L.wq : (seg == 1 ? L.wk : L.wv);
-            w[0] = W + static_cast<size_t>(c0) * E;
-            w[1] = W + static_cast<size_t>(c0 + 32) * E;
-          },
+      gemm_phase<2, 2, true, true>(
+          a, sm, parity, M, a.eh, E, L.ln1, a.eps, qkv_cols(L), bind(w_qkv, L),
           [&](int task, int m, int j) {
             // (cos, sin) of rotation pairs i0, i0 + 1 at this row's position
             int seg, c0;
-            seg_of(task, seg, c0);
+            qkv_seg(L, task, seg, c0);
             if (seg == 2) return make_uint4(0u, 0u, 0u, 0u);
             int ps = pos[m];
             ps = ps < 0 ? 0 : (ps >= a.max_pos ? a.max_pos - 1 : ps);
@@ -812,7 +970,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
           },
           [&](int task, int m, int j, float (&v)[2][2], const uint4& p) {
             int seg, c0;
-            seg_of(task, seg, c0);
+            qkv_seg(L, task, seg, c0);
             __nv_bfloat16* out = seg == 0 ? a.eq : (seg == 1 ? a.ek : a.ev);
             const int ld = seg == 0 ? qd : kvd;
             float x1a = bf16_round(v[0][0]), x1b = bf16_round(v[0][1]);
@@ -832,48 +990,45 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
             store2(out + static_cast<size_t>(m) * ld + c0 + j, x1a, x1b);
             store2(out + static_cast<size_t>(m) * ld + c0 + 32 + j, x2a, x2b);
           });
-      attention_prestage(sm, a, L);  // prefix keys / values do not depend on this phase
-      if (!grid_sync(a, sm)) return;
+      // the prefix keys / values do not depend on this phase: staged while waiting at the barrier
+      if (!grid_sync(a, sm, [&] { attention_prestage(sm, a, L); })) return;
       attention_phase(sm, a, L);
-      if (!grid_sync(a, sm)) return;
+      if (!grid_sync(a, sm, [&] { pf_o(L); })) return;
       // o_proj + residual: eh = bf16(bf16(ectx . W_o^T) + eh)
-      gemm_phase<1, 2>(
-          a, sm, parity, M, a.ectx, qd, nullptr, 0.f, E / 16, qd,
-          [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = L.wo + static_cast<size_t>(task) * 16 * qd; },
+      gemm_phase<1, 2, true, false>(
+          a, sm, parity, M, a.ectx, qd, nullptr, 0.f, E / 16, bind(w_o, L),
           [&](int task, int m, int j) {
             return make_uint4(ldcg_u32(a.eh + static_cast<size_t>(m) * E + task * 16 + j), 0u, 0u, 0u);
           },
-          [&](int task, int m, int j, float (&v)[1][2], const uint4& p) { resid_store(task * 16 + j, m, v, p); });
-      if (!grid_sync(a, sm)) return;
+          [&](int task, int m, int j, float (&v)[1][2], const uint4& p) { return resid_store(task * 16 + j, m, v, p); });
+      if (!grid_sync(a, sm, [&] { pf_gu(L); })) return;
       // gate / up + SiLU gate: emlp = bf16(bf16(silu(bf16(gate))) * bf16(up))
-      gemm_phase<2, 4>(
-          a, sm, parity, M, a.eh, E, L.ln2, a.eps, a.mlp / 16, E,
-          [&](int task, const __nv_bfloat16* (&w)[2]) {
-            w[0] = L.wg + static_cast<size_t>(task) * 16 * E;
-            w[1] = L.wu + static_cast<size_t>(task) * 16 * E;
-          },
-          no_pre,
+      gemm_phase<2, 4, true, true>(
+          a, sm, parity, M, a.eh, E, L.ln2, a.eps, a.mlp / 16, bind(w_gu, L), no_pre,
           [&](int task, int m, int j, float (&v)[2][2], const uint4&) {
             const float g0 = bf16_round(silu_f(bf16_round(v[0][0])));
             const float g1 = bf16_round(silu_f(bf16_round(v[0][1])));
             store2(a.emlp + static_cast<size_t>(m) * a.mlp + task * 16 + j, __fmul_rn(g0, bf16_round(v[1][0])),
                    __fmul_rn(g1, bf16_round(v[1][1])));
           });
-      if (!grid_sync(a, sm)) return;
+      if (!grid_sync(a, sm, [&] { pf_d(L); })) return;
       // down_proj + residual
-      gemm_phase<1, 2>(
-          a, sm, parity, M, a.emlp, a.mlp, nullptr, 0.f, E / 16, a.mlp,
-          [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = L.wd + static_cast<size_t>(task) * 16 * a.mlp; },
+      gemm_phase<1, 2, true, false>(
+          a, sm, parity, M, a.emlp, a.mlp, nullptr, 0.f, E / 16, bind(w_d, L),
           [&](int task, int m, int j) {
             return make_uint4(ldcg_u32(a.eh + static_cast<size_t>(m) * E + task * 16 + j), 0u, 0u, 0u);
           },
-          [&](int task, int m, int j, float (&v)[1][2], const uint4& p) { resid_store(task * 16 + j, m, v, p); });
-      if (!grid_sync(a, sm)) return;
+          [&](int task, int m, int j, float (&v)[1][2], const uint4& p) { return resid_store(task * 16 + j, m, v, p); });
+      const bool last = li + 1 == a.n_layers;
+      if (!grid_sync(a, sm, [&] {
+            if (last) prefetch_first<1, false>(w_out, Ad / 16, M, 32, E);
+            else pf_qkv(a.layer[li + 1]);
+          }))
+        return;
     }
     // final RMSNorm + action_out_proj + Euler: x_t += dt * (y . W_out^T + b), x_t_bf16 = bf16(x_t)
-    gemm_phase<1, 2>(
-        a, sm, parity, M, a.eh, E, a.ln_f, a.eps, Ad / 16, E,
-        [&](int task, const __nv_bfloat16* (&w)[1]) { w[0] = a.w_out + static_cast<size_t>(task) * 16 * E; },
+    gemm_phase<1, 2, false, true>(
+        a, sm, parity, M, a.eh, E, a.ln_f, a.eps, Ad / 16, w_out,
         [&](int task, int m, int j) {
           const int c = task * 16 + j;
           const float2 x = __ldcg(reinterpret_cast<const float2*>(a.xt + static_cast<size_t>(m) * Ad + c));
@@ -887,7 +1042,10 @@ __global__ void __launch_bounds__(kFlowThreads, 1) flow_kernel(const FlowArgs a)
           *reinterpret_cast<float2*>(a.xt + i) = make_float2(x0, x1);
           store2(a.xt_bf + i, x0, x1);
         });
-    if (!grid_sync(a, sm)) return;
+    if (!grid_sync(a, sm, [&] {
+          if (step + 1 < a.n_steps) pf_in();
+        }))
+      return;
   }
 }
 

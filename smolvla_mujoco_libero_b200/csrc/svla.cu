@@ -1056,6 +1056,24 @@ int32_t svla_euler_init(const float* noise, float* xt, void* xt_bf16, int64_t n,
                                                                                     static_cast<__nv_bfloat16*>(xt_bf16), n);
 }
 
+size_t svla_flow_packed_bytes(int32_t n, int32_t k, int32_t elem_bytes) {
+  if (n <= 0 || k <= 0 || n % 16 || k % 16 || (elem_bytes != 1 && elem_bytes != 2)) return 0;
+  return static_cast<size_t>(n) * k * elem_bytes;
+}
+
+int32_t svla_flow_pack_weight(const void* w, int32_t elem_bytes, int64_t ld, int32_t n, int32_t k, void* out,
+                              svla_stream_t stream) {
+  if (!w || !out || svla_flow_packed_bytes(n, k, elem_bytes) == 0 || ld < k)
+    return fail(SVLA_ERR_ARG, "svla_flow_pack_weight: bad args (n, k multiples of 16, ld >= k, elem_bytes 1 or 2)");
+  if (reinterpret_cast<uintptr_t>(out) % 16 != 0 || reinterpret_cast<uintptr_t>(w) % elem_bytes != 0)
+    return fail(SVLA_ERR_ARG, "svla_flow_pack_weight: out must be 16-byte aligned");
+  const long long total = static_cast<long long>(n) * k / 8;
+  const unsigned grid = static_cast<unsigned>(std::min<long long>((total + 255) / 256, 1 << 16));
+  return launch(pack_fragments_kernel, dim3(grid), dim3(256), 0, cs(stream), "pack_fragments_kernel",
+                static_cast<const uint8_t*>(w), static_cast<int>(elem_bytes), static_cast<long long>(ld),
+                static_cast<int>(n), static_cast<int>(k), static_cast<uint8_t*>(out));
+}
+
 int32_t svla_flow(const svla_flow_desc* d, svla_stream_t stream) {
   if (!d) return fail(SVLA_ERR_ARG, "svla_flow: null descriptor");
   const int rows = d->batch * d->chunk;
@@ -1070,16 +1088,17 @@ int32_t svla_flow(const svla_flow_desc* d, svla_stream_t stream) {
   if (d->n_layers < 1 || d->n_layers > SVLA_FLOW_MAX_LAYERS || d->num_steps < 1 || d->prefix_len < 1)
     return fail(SVLA_ERR_ARG, "svla_flow: n_layers %d (1..%d), num_steps %d, prefix_len %d", d->n_layers,
                 SVLA_FLOW_MAX_LAYERS, d->num_steps, d->prefix_len);
-  if (d->ld_time_in < d->hidden || d->ld_time_in % 8 != 0 || d->max_pos < 1)
-    return fail(SVLA_ERR_ARG, "svla_flow: ld_time_in %d / max_pos %d", d->ld_time_in, d->max_pos);
+  if (d->max_pos < 1) return fail(SVLA_ERR_ARG, "svla_flow: max_pos %d", d->max_pos);
   const void* need[] = {d->noise, d->xt, d->xt_bf16, d->w_action_in, d->b_action_in, d->w_time_in, d->time_in_const,
                         d->w_time_out, d->b_time_out, d->final_norm, d->w_action_out, d->b_action_out, d->suffix_pos,
                         d->cross_pos, d->rope_cs, d->a_emb, d->a_t, d->eh, d->eq, d->ek, d->ev, d->ectx, d->emlp,
-                        d->sync};
+                        d->norm_part, d->sync};
   for (const void* p : need)
     if (!p) return fail(SVLA_ERR_ARG, "svla_flow: null pointer argument");
   // 16-byte rows for the staged A loads and the packed stores
-  const void* aligned[] = {d->xt_bf16, d->a_emb, d->a_t, d->eh, d->eq, d->ek, d->ev, d->ectx, d->emlp, d->rope_cs};
+  // and the fragment-packed weights (16-byte lane loads)
+  const void* aligned[] = {d->xt_bf16, d->a_emb, d->a_t, d->eh, d->eq, d->ek, d->ev, d->ectx, d->emlp, d->rope_cs,
+                           d->w_action_in, d->w_time_in, d->w_time_out, d->w_action_out};
   for (const void* p : aligned)
     if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return fail(SVLA_ERR_ARG, "svla_flow: buffers must be 16-byte aligned");
   FlowArgs a{};
@@ -1090,15 +1109,16 @@ int32_t svla_flow(const svla_flow_desc* d, svla_stream_t stream) {
   a.scale = 0.125f;  // head_dim^-1/2
   a.noise = d->noise; a.xt = d->xt; a.xt_bf = static_cast<__nv_bfloat16*>(d->xt_bf16);
   auto bfp = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
-  a.w_in = bfp(d->w_action_in); a.b_in = bfp(d->b_action_in);
-  a.w_tin = bfp(d->w_time_in); a.ld_tin = d->ld_time_in; a.c_step = d->time_in_const;
-  a.w_tout = bfp(d->w_time_out); a.b_tout = bfp(d->b_time_out);
-  a.ln_f = bfp(d->final_norm); a.w_out = bfp(d->w_action_out); a.b_out = bfp(d->b_action_out);
+  auto u8p = [](const void* p) { return static_cast<const uint8_t*>(p); };
+  a.w_in = u8p(d->w_action_in); a.b_in = bfp(d->b_action_in);
+  a.w_tin = u8p(d->w_time_in); a.c_step = d->time_in_const;
+  a.w_tout = u8p(d->w_time_out); a.b_tout = bfp(d->b_time_out);
+  a.ln_f = bfp(d->final_norm); a.w_out = u8p(d->w_action_out); a.b_out = bfp(d->b_action_out);
   a.key_mask = d->key_mask; a.key_mask_bs = d->key_mask_bs;
   a.suffix_pos = d->suffix_pos; a.cross_pos = d->cross_pos; a.rope_cs = d->rope_cs; a.max_pos = d->max_pos;
   auto bfw = [](void* p) { return static_cast<__nv_bfloat16*>(p); };
   a.a_emb = bfw(d->a_emb); a.a_t = bfw(d->a_t); a.eh = bfw(d->eh); a.eq = bfw(d->eq); a.ek = bfw(d->ek);
-  a.ev = bfw(d->ev); a.ectx = bfw(d->ectx); a.emlp = bfw(d->emlp);
+  a.ev = bfw(d->ev); a.ectx = bfw(d->ectx); a.emlp = bfw(d->emlp); a.norm_part = d->norm_part;
   if (reinterpret_cast<uintptr_t>(d->sync) % 8 != 0) return fail(SVLA_ERR_ARG, "svla_flow: sync must be 8-byte aligned");
   if (d->key_mask && (reinterpret_cast<uintptr_t>(d->key_mask) % 16 != 0 || d->key_mask_bs % 16 != 0 ||
                       d->key_mask_bs < (d->prefix_len + 15) / 16 * 16))
@@ -1111,11 +1131,16 @@ int32_t svla_flow(const svla_flow_desc* d, svla_stream_t stream) {
   for (int i = 0; i < d->n_layers; ++i) {
     const svla_flow_layer& s = d->layer[i];
     if (!s.input_norm || !s.post_norm || !s.wq || !s.wo || !s.wg || !s.wu || !s.wd || !s.keys || !s.values ||
-        (!s.cross && (!s.wk || !s.wv)))
-      return fail(SVLA_ERR_ARG, "svla_flow: layer %d lacks a weight or its keys / values", i);
+        !s.sq || !s.so || !s.sg || !s.su || !s.sd || (!s.cross && (!s.wk || !s.wv || !s.sk || !s.sv)))
+      return fail(SVLA_ERR_ARG, "svla_flow: layer %d lacks a weight, a weight scale or its keys / values", i);
+    const void* packed[] = {s.wq, s.wk, s.wv, s.wo, s.wg, s.wu, s.wd};
+    for (const void* p : packed)
+      if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+        return fail(SVLA_ERR_ARG, "svla_flow: layer %d: packed weights must be 16-byte aligned", i);
     FlowLayer& L = a.layer[i];
-    L.ln1 = bfp(s.input_norm); L.ln2 = bfp(s.post_norm); L.wq = bfp(s.wq); L.wk = bfp(s.wk); L.wv = bfp(s.wv);
-    L.wo = bfp(s.wo); L.wg = bfp(s.wg); L.wu = bfp(s.wu); L.wd = bfp(s.wd); L.k1 = bfp(s.keys); L.v1 = bfp(s.values);
+    L.ln1 = bfp(s.input_norm); L.ln2 = bfp(s.post_norm); L.wq = u8p(s.wq); L.wk = u8p(s.wk); L.wv = u8p(s.wv);
+    L.wo = u8p(s.wo); L.wg = u8p(s.wg); L.wu = u8p(s.wu); L.wd = u8p(s.wd); L.k1 = bfp(s.keys); L.v1 = bfp(s.values);
+    L.sq = s.sq; L.sk = s.sk; L.sv = s.sv; L.so = s.so; L.sg = s.sg; L.su = s.su; L.sd = s.sd;
     L.cross = s.cross ? 1 : 0;
   }
   // one CTA per SM, all resident at once (a cooperative launch refuses a grid that cannot be)

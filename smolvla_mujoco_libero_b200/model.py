@@ -51,6 +51,7 @@ class PackedLinear:
     act_scale: float = 1.0              # w8a8
     weight_bf16: torch.Tensor | None = None  # original bf16 weight (bf16 / calibration mode)
     weight_deq: torch.Tensor | None = None   # w8a16: bf16(q * wscale), the weight W8A16Linear multiplies by
+    flow_frag: torch.Tensor | None = None    # the fragment-order copy the persistent flow kernel reads (lazy)
 
 
 def time_embedding_bf16(cfg: SmolVLAConfig) -> torch.Tensor:
@@ -121,7 +122,7 @@ class DeviceWeights:
     def nbytes(self) -> int:
         tot = 0
         for p in self.lin.values():
-            for t in (p.weight, p.wscale, p.bias, p.smooth, p.weight_deq):
+            for t in (p.weight, p.wscale, p.bias, p.smooth, p.weight_deq, p.flow_frag):
                 if t is not None:
                     tot += t.numel() * t.element_size()
         return tot + sum(t.numel() * t.element_size() for t in self.t.values())
@@ -161,7 +162,7 @@ class SmolVLARunner:
         can_flow = self._flow_supported(weights.cfg, batch, mode, debug_taps)
         if flow and not can_flow:
             raise ValueError("the persistent flow kernel needs quant mode, batch * chunk <= 64, no taps and "
-                             "bf16 / W8A16 expert linears")
+                             "W8A16 expert linears")
         self.flow = can_flow if flow is None else bool(flow)
         self.dev = weights.device
         self.graph: torch.cuda.CUDAGraph | None = None
@@ -177,7 +178,7 @@ class SmolVLARunner:
         if c.expert_hidden % 16 or c.expert_hidden > 1024 or c.max_action_dim % 16 or c.expert_mlp % 16:
             return False
         expert = [p for n, p in self.w.lin.items() if n.startswith(EXPERT + ".")]
-        return all(p.kind == "bf16" or (p.kind == "w8a16" and p.weight_deq is not None) for p in expert)
+        return all(p.kind == "w8a16" for p in expert)
 
     # ------------------------------------------------------------------ buffers
     def _alloc(self):
@@ -577,9 +578,14 @@ class SmolVLARunner:
         c, B, w = self.cfg, self.B, self.w
         E = c.expert_hidden
 
-        def wt(name):  # the bf16 weight a linear multiplies by
+        def wt(name, cols=None):  # fragment-order copy of the weight (int8 for W8A16, else bf16), made once
             p = w.lin[name]
-            return (p.weight if p.kind == "bf16" else p.weight_deq).data_ptr()
+            if p.flow_frag is None:
+                p.flow_frag = ops.flow_pack_weight(p.weight if cols is None else p.weight[:, :cols])
+            return p.flow_frag.data_ptr()
+
+        def ws(name):
+            return w.lin[name].wscale.data_ptr()
 
         d = L.FlowDesc()
         d.batch, d.chunk, d.prefix_len, d.hidden, d.action_dim = B, c.chunk, c.prefix_len, E, c.max_action_dim
@@ -588,7 +594,7 @@ class SmolVLARunner:
         d.noise, d.xt, d.xt_bf16 = self.in_noise.data_ptr(), self.xt.data_ptr(), self.xt_bf.data_ptr()
         d.w_action_in, d.b_action_in = wt("model.action_in_proj"), w.lin["model.action_in_proj"].bias.data_ptr()
         mi = w.lin["model.action_time_mlp_in"]
-        d.w_time_in, d.ld_time_in, d.time_in_const = mi.weight.data_ptr(), mi.weight.stride(0), self.c_step.data_ptr()
+        d.w_time_in, d.time_in_const = wt("model.action_time_mlp_in", cols=E), self.c_step.data_ptr()
         d.w_time_out, d.b_time_out = wt("model.action_time_mlp_out"), w.lin["model.action_time_mlp_out"].bias.data_ptr()
         d.final_norm = w.t[f"{EXPERT}.norm.weight"].data_ptr()
         d.w_action_out, d.b_action_out = wt("model.action_out_proj"), w.lin["model.action_out_proj"].bias.data_ptr()
@@ -597,6 +603,8 @@ class SmolVLARunner:
         d.rope_cs, d.max_pos = self.rope_cs.data_ptr(), self.max_pos
         d.a_emb, d.a_t, d.eh, d.eq = self.a_emb.data_ptr(), self.a_t.data_ptr(), self.eh.data_ptr(), self.eq.data_ptr()
         d.ek, d.ev, d.ectx, d.emlp = self.ek.data_ptr(), self.ev.data_ptr(), self.ectx.data_ptr(), self.emlp.data_ptr()
+        self.flow_norm = torch.zeros(64 * 64, dtype=torch.float32, device=self.dev)
+        d.norm_part = self.flow_norm.data_ptr()
         self.flow_sync = torch.zeros(2, dtype=torch.int32, device=self.dev)
         d.sync = self.flow_sync.data_ptr()
         for i in range(c.expert_layers):
@@ -604,13 +612,17 @@ class SmolVLARunner:
             ly = d.layer[i]
             ly.input_norm = w.t[f"{p}.input_layernorm.weight"].data_ptr()
             ly.post_norm = w.t[f"{p}.post_attention_layernorm.weight"].data_ptr()
-            ly.wq, ly.wo = wt(f"{p}.self_attn.q_proj"), wt(f"{p}.self_attn.o_proj")
-            ly.wg, ly.wu, ly.wd = wt(f"{p}.mlp.gate_proj"), wt(f"{p}.mlp.up_proj"), wt(f"{p}.mlp.down_proj")
+            ly.wq, ly.sq = wt(f"{p}.self_attn.q_proj"), ws(f"{p}.self_attn.q_proj")
+            ly.wo, ly.so = wt(f"{p}.self_attn.o_proj"), ws(f"{p}.self_attn.o_proj")
+            ly.wg, ly.sg = wt(f"{p}.mlp.gate_proj"), ws(f"{p}.mlp.gate_proj")
+            ly.wu, ly.su = wt(f"{p}.mlp.up_proj"), ws(f"{p}.mlp.up_proj")
+            ly.wd, ly.sd = wt(f"{p}.mlp.down_proj"), ws(f"{p}.mlp.down_proj")
             ly.cross = int(c.is_cross_layer(i))
             if ly.cross:
                 ly.keys, ly.values = self.ck[i].data_ptr(), self.cv[i].data_ptr()
             else:
-                ly.wk, ly.wv = wt(f"{p}.self_attn.k_proj"), wt(f"{p}.self_attn.v_proj")
+                ly.wk, ly.sk = wt(f"{p}.self_attn.k_proj"), ws(f"{p}.self_attn.k_proj")
+                ly.wv, ly.sv = wt(f"{p}.self_attn.v_proj"), ws(f"{p}.self_attn.v_proj")
                 ly.keys, ly.values = self.kcache[i].data_ptr(), self.vcache[i].data_ptr()
         return d
 

@@ -92,6 +92,24 @@ def channel_percentile(x: torch.Tensor, rows: int, q: float, amax: torch.Tensor,
                                         _stream()), "channel_percentile")
 
 
+def flow_pack_weight(w: torch.Tensor) -> torch.Tensor:
+    """The fragment-order copy of an int8 or bf16 weight [n, k] (any row stride, unit column stride) that the
+    persistent flow kernel reads (svla_flow_pack_weight)."""
+    if w.dtype not in (torch.int8, torch.bfloat16):
+        raise ValueError(f"flow_pack_weight: int8 or bf16 weight expected, got {w.dtype}")
+    _need(w, w.dtype, "w", contiguous=False)
+    if w.dim() != 2 or w.stride(1) != 1:
+        raise ValueError("flow_pack_weight: w must be 2-D with unit column stride")
+    n, k = w.shape
+    eb = w.element_size()
+    nbytes = lib().svla_flow_packed_bytes(n, k, eb)
+    if nbytes == 0:
+        raise ValueError(f"flow_pack_weight: [{n}, {k}] is not a multiple of 16 in both dimensions")
+    out = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+    check(lib().svla_flow_pack_weight(_p(w), eb, w.stride(0), n, k, _p(out), _stream()), "flow_pack_weight")
+    return out
+
+
 def gemm_i8_i32(qx: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
     _need(qx, torch.int8, "qx")
     _need(qw, torch.int8, "qw")

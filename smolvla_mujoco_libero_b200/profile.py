@@ -18,6 +18,7 @@ import json
 
 import torch
 
+from . import _lib as L
 from . import ops, synthetic
 from .calibrate import calibrate, load_scale_json
 from .config import BENCH
@@ -187,6 +188,89 @@ def summarize_launches(csv_path: str, top: int = 30) -> str:
     return "\n".join(out)
 
 
+_BYTE_UNITS = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1e3, "MB": 1e6, "GB": 1e9}
+
+
+def ncu_traffic(csv_path: str, kernel: str) -> tuple[float, int]:
+    """Mean dram__bytes_read.sum + dram__bytes_write.sum per launch of the kernels whose name contains `kernel`
+    in an `ncu -i <rep> --page raw --csv` export, and the number of launches."""
+    import csv
+    with open(csv_path, newline="") as f:
+        rows = list(csv.DictReader(f))
+    units = rows[0] if rows and not rows[0].get("ID", "").strip().isdigit() else {}
+    tot, n = 0.0, 0
+    for r in rows:
+        if not r.get("ID", "").strip().isdigit() or kernel not in r.get("Kernel Name", ""):
+            continue
+        b = 0.0
+        for m in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            b += float(r[m].replace(",", "")) * _BYTE_UNITS.get(units.get(m, "byte").strip(), 1.0)
+        tot += b
+        n += 1
+    if n == 0:
+        raise ValueError(f"no launch of {kernel!r} in {csv_path}")
+    return tot / n, n
+
+
+def update_traffic(json_path: str, key: str, csv_path: str, kernel: str, scale: float, note: str) -> dict:
+    """Writes traffic[key] = {dram_bytes_per_launch: mean bytes x scale, ...} into the machine-readable traffic
+    table that bench.py reads (the DRAM bytes of one full-size launch, from a capture of a smaller case scaled by
+    the units processed when scale != 1)."""
+    from pathlib import Path
+    b, n = ncu_traffic(csv_path, kernel)
+    path = Path(json_path)
+    table = json.loads(path.read_text()) if path.exists() else {}
+    table[key] = {"dram_bytes_per_launch": b * scale, "captured_bytes_per_launch": b, "scale": scale,
+                  "launches": n, "kernel": kernel, "note": note}
+    path.write_text(json.dumps(table, indent=1, sort_keys=True) + "\n")
+    return table[key]
+
+
+FLOW_EVENTS = {1: "barrier_in", 2: "barrier_out", 3: "staged", 4: "mma", 5: "epilogue", 6: "attn", 7: "copied",
+               8: "keys", 9: "attn_done"}
+
+
+def flow_phase_names(cfg) -> list[str]:
+    """Phase names of one flow step in kernel order (the kernel puts one grid barrier after each)."""
+    names = ["action_in", "time_in", "time_out"]
+    for _ in range(cfg.expert_layers):
+        names += ["qkv", "attention", "o_proj", "gate_up", "down"]
+    return names + ["action_out"]
+
+
+def flow_events(r, cta: int = 0) -> dict:
+    """Per-phase breakdown of one persistent flow kernel launch from its own globaltimer events (CTA 0 or the last
+    CTA): for each phase kind, the mean microseconds from the barrier exit to each event, the barrier wait and
+    the whole phase (barrier exit to next barrier exit)."""
+    fd = next(args[0] for fn, args in r.launches if fn is L.lib().svla_flow)
+    dbg = torch.zeros(2 * 1024 * 2, dtype=torch.int64, device=r.dev)
+    fd.debug_clock = dbg.data_ptr()
+    r._run_launches()
+    torch.cuda.synchronize()
+    fd.debug_clock = None
+    ev = dbg.view(2, 1024, 2)[cta].cpu().tolist()
+    ev = [(c, t) for c, t in ev if c]
+    names = flow_phase_names(r.cfg)
+    # phases start at each barrier exit (the first barrier, after x_t = noise, opens phase 0)
+    starts = [i for i, (c, _) in enumerate(ev) if c == 2]
+    acc: dict[str, dict[str, list[float]]] = {}
+    for pi in range(len(starts) - 1):
+        i0, i1 = starts[pi], starts[pi + 1]
+        t0 = ev[i0][1]
+        kind = names[pi % len(names)]
+        d = acc.setdefault(kind, {})
+        seen = set()
+        for c, t in ev[i0 + 1:i1 + 1]:
+            key = FLOW_EVENTS.get(c, str(c))
+            if key in seen:
+                continue
+            seen.add(key)
+            d.setdefault(key, []).append((t - t0) / 1e3)
+        d.setdefault("phase", []).append((ev[i1][1] - t0) / 1e3)
+    out = {k: {e: round(sum(v) / len(v), 3) for e, v in d.items()} | {"n": len(d["phase"])} for k, d in acc.items()}
+    return {"cta": cta, "events": len(ev), "phases": len(starts) - 1, "mean_us_from_barrier_exit": out}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", default="sample_actions", choices=["sample_actions", "gemm", "attn", "norm"])
@@ -212,9 +296,20 @@ def main() -> None:
     ap.add_argument("--prefix", type=int, default=0, help="--op attn: structured mask, key padding over this many "
                     "prefix keys and causal order over the rest")
     ap.add_argument("--summarize", default=None, help="print the per-kernel summary of an ncu launch-list CSV")
+    ap.add_argument("--ncu-traffic", nargs=3, metavar=("CSV", "KERNEL", "KEY"), default=None,
+                    help="update the traffic table (--traffic-json) entry KEY from an ncu raw CSV export")
+    ap.add_argument("--traffic-json", default="profiles/traffic.json")
+    ap.add_argument("--scale", type=float, default=1.0, help="--ncu-traffic: full-size units / captured units")
+    ap.add_argument("--note", default="", help="--ncu-traffic: the capture (case, command)")
+    ap.add_argument("--flow-events", action="store_true", help="sample_actions at batch 1: per-phase breakdown of "
+                    "the persistent flow kernel from its own globaltimer events")
     a = ap.parse_args()
     if a.summarize:
         print(summarize_launches(a.summarize))
+        return
+    if a.ncu_traffic:
+        csv_path, kernel, key = a.ncu_traffic
+        print(json.dumps(update_traffic(a.traffic_json, key, csv_path, kernel, a.scale, a.note)))
         return
     if a.op == "gemm":
         print(json.dumps(op_gemm(a)))
@@ -249,6 +344,9 @@ def main() -> None:
         torch.cuda.synchronize()
         times.append(s.elapsed_time(e))
     print(json.dumps({"batch": a.batch, "launches_per_call": r.n_launches, "ms_per_call": times, "graph": a.graph}))
+    if a.flow_events and r.flow:
+        for cta in (0, 1):
+            print(json.dumps(flow_events(r, cta)))
 
 
 if __name__ == "__main__":

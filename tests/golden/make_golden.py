@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures under tests/golden/ from the reference's OWN code.
 
-Run in a container that has the reference checkout (read-only) at
-/root/reference:
+Run in a container that has a checkout of the reference (read-only is enough), naming its root
+with --reference or the SVLA_REFERENCE environment variable:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 The reference modules are imported unchanged from <reference>/deploy:
   * linear_only_quant.W8A8Linear / W8A16Linear / quantize_weight_per_out_channel
@@ -25,6 +25,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import sys
 import types
 from pathlib import Path
@@ -107,8 +108,11 @@ def run_reference_linear(ref, case: synthetic.LinearCase, alpha: float, percenti
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SVLA_REFERENCE"),
+                    help="root of the reference checkout (default: $SVLA_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or SVLA_REFERENCE")
     deploy = Path(args.reference) / "deploy"
     sys.path.insert(0, str(deploy))
     install_lerobot_stubs()

@@ -79,7 +79,7 @@ def test_flow_arguments_are_checked_before_any_launch():
         d = _lib.FlowDesc()
         d.batch, d.chunk, d.prefix_len, d.hidden, d.action_dim = 1, 50, 177, 720, 32
         d.heads, d.kv_heads, d.mlp, d.n_layers, d.num_steps = 15, 5, 2048, 16, 10
-        d.ld_time_in, d.max_pos, d.eps = 1440, 227, 1e-5
+        d.max_pos, d.eps = 227, 1e-5
         for k, v in kw.items():
             setattr(d, k, v)
         return d
@@ -90,13 +90,25 @@ def test_flow_arguments_are_checked_before_any_launch():
         (dict(mlp=2040), "multiples of 16"),
         (dict(kv_heads=4), "kv_heads"),            # 15 heads over 4 kv heads
         (dict(n_layers=33), "n_layers"),
-        (dict(ld_time_in=700), "ld_time_in"),
+        (dict(max_pos=0), "max_pos"),
         (dict(), "null pointer"),                  # no buffers at all
     ]
     for kw, word in cases:
         d = desc(**kw)
         assert lib.svla_flow(ctypes.byref(d), None) == 1, kw
         assert word.encode() in lib.svla_last_error(), (kw, lib.svla_last_error())
+
+
+def test_flow_weight_packing_arguments_are_checked_before_any_launch():
+    lib = _lib.lib()
+    assert lib.svla_flow_packed_bytes(720, 960, 1) == 720 * 960
+    assert lib.svla_flow_packed_bytes(720, 960, 2) == 2 * 720 * 960
+    assert lib.svla_flow_packed_bytes(720, 968, 1) == 0   # k not a multiple of 16
+    assert lib.svla_flow_packed_bytes(720, 960, 4) == 0   # int8 or bf16 only
+    assert lib.svla_flow_pack_weight(0x100000, 1, 960, 720, 968, 0x200000, None) == 1
+    assert lib.svla_flow_pack_weight(0x100000, 1, 900, 720, 960, 0x200000, None) == 1  # ld < k
+    assert lib.svla_flow_pack_weight(0x100000, 1, 960, 720, 960, 0x200008, None) == 1  # out not 16-byte aligned
+    assert b"aligned" in lib.svla_last_error()
 
 
 def test_gemm_epilogue_pointers_are_checked_before_any_launch():
