@@ -426,9 +426,10 @@ def attention_roofline(runner, peaks):
 
 
 def flow_roofline(runner, peaks):
-    """The batch-1 call's dominant kernel (svla_flow: the whole flow-matching loop, 64% of the batch-1 launch
-    list) timed on its own with CUDA events on the launch stream.  Algorithmic bytes: the expert's bf16 weights
-    read once per flow step (they exceed L2) plus the prefix K/V once."""
+    """The batch-1 call's dominant kernel (svla_flow: the whole flow-matching loop, about two thirds of the batch-1
+    launch list) timed on its own with CUDA events on the launch stream.  Algorithmic bytes: per flow step the
+    expert layers' int8 weights (fragment order) with their fp32 scales, and the bf16 action / time projections,
+    each read once; the prefix K/V once per call."""
     import ctypes
 
     from smolvla_mujoco_libero_b200 import _lib as L
@@ -443,7 +444,7 @@ def flow_roofline(runner, peaks):
         if name.startswith(EXPERT + ".layers."):
             if c.is_cross_layer(int(name.split(".layers.")[1].split(".")[0])) and (".k_proj" in name or ".v_proj" in name):
                 continue  # cross layers read the precomputed K/V projections, not these weights
-            per_step += p.n * p.k * 2
+            per_step += p.n * p.k + p.n * 4  # int8 weight + fp32 per-channel scale
     per_step += (E * c.max_action_dim * 2) * 2 + E * E * 2 * 2  # action in / out, time MLP (in: first E columns)
     kv = c.expert_layers * c.prefix_len * c.kv_dim * 2 * 2
     nbytes = per_step * c.num_steps + kv

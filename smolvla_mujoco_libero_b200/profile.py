@@ -74,6 +74,17 @@ def op_gemm(a) -> dict:
     elif epi == 4:
         segs.append(ops.Seg(a=A, b=B, out=out, n=a.n, wscale=ws, act_scale=0.01))
         extra = dict(pair=True)
+    elif epi == 2:
+        # q (n columns) and k, v (kv_n columns each) of one input, RoPE on q and k: the QKV projection
+        segs[0].rope = 1
+        for rope in (1, 0):
+            Bk = mk(a.kv_n, a.k, torch.bfloat16 if kind == 1 else torch.int8)
+            wk = torch.rand(a.kv_n, generator=g).to(dev) * 1e-3
+            ok = torch.empty(a.m, a.kv_n, dtype=torch.bfloat16, device=dev)
+            segs.append(ops.Seg(a=A, b=Bk, out=ok, n=a.kv_n, wscale=wk, act_scale=0.01, rope=rope))
+        max_pos = 256
+        pos = torch.randint(0, max_pos, (a.m,), generator=g, dtype=torch.int32).to(dev)
+        extra = dict(rope_cs=ops.rope_table(max_pos, 100000.0, dev), pos=pos, max_pos=max_pos)
     if a.split_k != 1:
         ws = ops.splitk_workspace(64 << 20, dev)
         extra.update(split_k=a.split_k, workspace=ws, workspace_bytes=ws.numel())
@@ -91,7 +102,7 @@ def op_gemm(a) -> dict:
     # MMA warp, accumulator buffer of tile i: wait begins / ends (a long wait = the epilogue sets the pace)
     names += [f"acc{i}_{w}" for i in range(8) for w in ("wait", "free")]
     phases = {names[i]: (c[i] - c[0]) if c[i] else None for i in range(len(names))}
-    ops_count = 2.0 * a.m * a.n * a.k * (2 if epi == 4 else 1)
+    ops_count = 2.0 * a.m * a.k * (a.n * (2 if epi == 4 else 1) + (2 * a.kv_n if epi == 2 else 0))
     best = min(ms)
     return {"op": "gemm", "kind": a.kind, "epi": a.epi, "m": a.m, "n": a.n, "k": a.k, "split_k": a.split_k,
             "cta_pair": a.cta_pair, "ms": ms,
@@ -284,6 +295,7 @@ def main() -> None:
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=768)
+    ap.add_argument("--kv-n", type=int, default=320, help="--epi rope: columns of the k and v segments")
     ap.add_argument("--block-n", type=int, default=0)
     ap.add_argument("--split-k", type=int, default=1, help="GEMM split-K: 1 off, 0 automatic, n splits")
     ap.add_argument("--cta-pair", type=int, default=0, help="GEMM CTA pairs: 0 automatic, 1 off, 2 on")
