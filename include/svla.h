@@ -323,7 +323,7 @@ int32_t svla_rope_table(float* cs, int32_t max_pos, float max_wavelength, svla_s
 /* Masks and positions of one call (deploy/diagnose_3_4_numeric_baseline.py:42-46, :117-146, :171-172).
  * img_mask0/1 bool [B], lang_mask bool [B, n_lang]; prefix length Lp = 2*n_img + n_lang + 1, Ls = chunk.
  * prefix_mask [B, Lp, ld(Lp)], self_mask [B, Ls, ld(Lp + Ls)], cross_mask [B, Ls, ld(Lp)] bytes with the
- * row stride ld(L) = L rounded up to a multiple of 16 (padding bytes 0); prefix_pos [B, Lp],
+ * row stride ld(L) = L rounded up to a multiple of 16 (padding bytes 0), 16-byte aligned; prefix_pos [B, Lp],
  * suffix_pos / cross_pos [B, Ls]. */
 int32_t svla_build_masks(const uint8_t* img_mask0, const uint8_t* img_mask1, const uint8_t* lang_mask,
                          int32_t batch, int32_t n_img, int32_t n_lang, int32_t chunk, uint8_t* prefix_mask,

@@ -56,44 +56,65 @@ __device__ __forceinline__ int prefix_pad(const MaskArgs& a, int b, int i) {
   return 1;
 }
 
-// one block per batch row
+// grid (ceil((Lp + 2 Ls) / 8), B): one warp per mask row (prefix rows, then the suffix's self-attention rows,
+// then its cross-attention rows), 16 bytes per lane and store; warp 0 of block (0, b) also writes the
+// positions (a warp prefix sum of the padding flags)
 __global__ void masks_kernel(const MaskArgs a) {
   pdl_wait();
   pdl_trigger();
-  const int b = blockIdx.x;
-  const int Lp = 2 * a.n_img + a.n_lang + 1;
-  extern __shared__ int sh[];  // pad[Lp], cum[Lp]
-  int* pad = sh;
-  int* cum = sh + Lp;
-  for (int i = threadIdx.x; i < Lp; i += blockDim.x) {
-    pad[i] = prefix_pad(a, b, i);
-    cum[i] = (i == Lp - 1) ? 1 : 0;  // att cumsum: only the state token has att = 1
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int c = 0;
-    for (int i = 0; i < Lp; ++i) {
-      c += pad[i];
-      a.prefix_pos[b * Lp + i] = c - 1;
+  const int b = blockIdx.y;
+  const int Lp = 2 * a.n_img + a.n_lang + 1, Lt = Lp + a.Ls;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (blockIdx.x == 0 && warp == 0) {
+    int c = 0;  // cumsum(pad) before this run of 32
+    for (int base = 0; base < Lp; base += 32) {
+      const int i = base + lane;
+      int x = i < Lp ? prefix_pad(a, b, i) : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += t;
+      }
+      if (i < Lp) a.prefix_pos[b * Lp + i] = c + x - 1;
+      c += __shfl_sync(0xffffffffu, x, 31);
     }
-    for (int i = 0; i < a.Ls; ++i) {
+    for (int i = lane; i < a.Ls; i += 32) {
       a.suffix_pos[b * a.Ls + i] = c + i;
       a.cross_pos[b * a.Ls + i] = i;
     }
   }
-  const int ldp = mask_ld(Lp);
-  for (int idx = threadIdx.x; idx < Lp * ldp; idx += blockDim.x) {
-    const int q = idx / ldp, k = idx % ldp;
-    a.prefix_mask[static_cast<size_t>(b) * Lp * ldp + idx] = (k < Lp) && (cum[k] <= cum[q]) && pad[q] && pad[k];
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= Lp + 2 * a.Ls) return;
+  // att cumsum: only the state token (the last prefix token) has att = 1, so cum[k] <= cum[q] fails only for
+  // k = Lp - 1 with q != Lp - 1
+  int kind, q, ld;
+  uint8_t* dst;
+  if (row < Lp) {
+    kind = 0, q = row, ld = mask_ld(Lp);
+    dst = a.prefix_mask + (static_cast<size_t>(b) * Lp + q) * ld;
+  } else if (row < Lp + a.Ls) {
+    kind = 1, q = row - Lp, ld = mask_ld(Lt);
+    dst = a.self_mask + (static_cast<size_t>(b) * a.Ls + q) * ld;
+  } else {
+    kind = 2, q = row - Lp - a.Ls, ld = mask_ld(Lp);
+    dst = a.cross_mask + (static_cast<size_t>(b) * a.Ls + q) * ld;
   }
-  const int Lt = Lp + a.Ls, ldt = mask_ld(Lt);
-  for (int idx = threadIdx.x; idx < a.Ls * ldt; idx += blockDim.x) {
-    const int q = idx / ldt, k = idx % ldt;
-    a.self_mask[static_cast<size_t>(b) * a.Ls * ldt + idx] = (k < Lp) ? pad[k] : (k < Lt && (k - Lp) <= q);
-  }
-  for (int idx = threadIdx.x; idx < a.Ls * ldp; idx += blockDim.x) {
-    const int k = idx % ldp;
-    a.cross_mask[static_cast<size_t>(b) * a.Ls * ldp + idx] = (k < Lp) && pad[k];
+  const int pad_q = kind == 0 ? prefix_pad(a, b, q) : 1;
+  for (int c0 = lane * 16; c0 < ld; c0 += 32 * 16) {
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int k = c0 + j;
+      int v;
+      if (kind == 0)
+        v = (k < Lp) && !(k == Lp - 1 && q != Lp - 1) && pad_q && prefix_pad(a, b, k);
+      else if (kind == 1)
+        v = (k < Lp) ? prefix_pad(a, b, k) : (k < Lt && (k - Lp) <= q);
+      else
+        v = (k < Lp) && prefix_pad(a, b, k);
+      w[j / 4] |= static_cast<uint32_t>(v != 0) << (8 * (j % 4));
+    }
+    *reinterpret_cast<int4*>(dst + c0) = make_int4(w[0], w[1], w[2], w[3]);
   }
 }
 

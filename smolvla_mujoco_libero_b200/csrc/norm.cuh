@@ -174,6 +174,22 @@ __device__ __forceinline__ void norm_quant_row(const NormQuantArgs& a, int m, in
 // so each warp keeps two rows of loads in flight.
 template <int NV, bool LAYERNORM>
 __global__ void __launch_bounds__(256) norm_quant_kernel(const NormQuantArgs a) {
+  // the row constants (norm weight, bias, reciprocal smooth vectors) do not depend on the previous kernel:
+  // their cache lines are requested into L1 before waiting for it, one 128-byte line per thread
+  {
+    const int line = threadIdx.x, wl = (a.K * 2 + 127) / 128, fl = (a.K * 4 + 127) / 128;
+    const void* p = nullptr;
+    if (line < wl) {
+      p = reinterpret_cast<const char*>(a.w) + line * 128;
+    } else if (LAYERNORM && line < 2 * wl) {
+      p = reinterpret_cast<const char*>(a.b) + (line - wl) * 128;
+    } else {
+      const int r = line - (LAYERNORM ? 2 : 1) * wl, qi = r / fl;
+      if (r >= 0 && qi < a.nq && a.rsmooth[qi] != nullptr)
+        p = reinterpret_cast<const char*>(a.rsmooth[qi]) + (r - qi * fl) * 128;
+    }
+    if (p != nullptr) asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+  }
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;

@@ -1012,10 +1012,16 @@ int32_t svla_build_masks(const uint8_t* img_mask0, const uint8_t* img_mask1, con
   if (!img_mask0 || !img_mask1 || !lang_mask || !prefix_mask || !prefix_pos || !self_mask || !cross_mask ||
       !suffix_pos || !cross_pos || batch <= 0 || n_img < 0 || n_lang < 0 || chunk <= 0)
     return fail(SVLA_ERR_ARG, "svla_build_masks: bad args");
+  // mask rows are written as 16-byte runs
+  if ((reinterpret_cast<uintptr_t>(prefix_mask) | reinterpret_cast<uintptr_t>(self_mask) |
+       reinterpret_cast<uintptr_t>(cross_mask)) % 16 != 0)
+    return fail(SVLA_ERR_ARG, "svla_build_masks: masks must be 16-byte aligned");
   MaskArgs a{img_mask0, img_mask1, lang_mask, batch, n_img, n_lang, chunk, prefix_mask, prefix_pos,
              self_mask, cross_mask, suffix_pos, cross_pos};
   const int lp = 2 * n_img + n_lang + 1;
-  return launch(masks_kernel, dim3(batch), dim3(256), 2 * lp * sizeof(int), cs(stream), "masks_kernel", a);
+  const int rows = lp + 2 * chunk;  // prefix, self-attention and cross-attention mask rows of a sample
+  return launch(masks_kernel, dim3(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(batch)), dim3(256), 0,
+                cs(stream), "masks_kernel", a);
 }
 
 int32_t svla_embed_tokens(const int64_t* tokens, int32_t batch, int32_t t, const void* table, int32_t vocab,

@@ -903,3 +903,42 @@ def test_channel_percentile_strided_rows_and_rejects():
     assert lib.svla_channel_percentile(ops._p(xd), 1000, 1, 4097, 8, 0.5, ops._p(amax), ops._p(pamax), 0) != 0
     assert lib.svla_channel_percentile(ops._p(xd), 4, 1, 8, 8, 0.5, ops._p(amax), ops._p(pamax), 0) != 0
     assert lib.svla_channel_percentile(ops._p(xd), 1000, 1, 8, 8, 1.5, ops._p(amax), ops._p(pamax), 0) != 0
+
+
+@pytest.mark.parametrize("batch,n_img,n_lang,chunk", [(1, 64, 48, 50), (3, 64, 48, 50), (2, 5, 7, 3)])
+def test_build_masks_match_the_reference_mask_formulas(batch, n_img, n_lang, chunk):
+    """svla_build_masks against make_att_2d_masks / cumsum(pad) - 1 (deploy/diagnose_3_4_numeric_baseline.py:42-46)
+    and the suffix rules; padding bytes of every 16-byte row stay 0."""
+    from oracle.model import make_att_2d_masks
+    g = torch.Generator().manual_seed(batch * 100 + n_img)
+    m0 = torch.randint(0, 2, (batch,), generator=g, dtype=torch.uint8)
+    m1 = torch.ones(batch, dtype=torch.uint8)
+    lang = (torch.rand(batch, n_lang, generator=g) > 0.3).to(torch.uint8)
+    Lp, Ls = 2 * n_img + n_lang + 1, chunk
+    ld = lambda n: (n + 15) // 16 * 16  # noqa: E731
+    pm = torch.full((batch, Lp, ld(Lp)), 7, dtype=torch.uint8, device=DEV)
+    sm = torch.full((batch, Ls, ld(Lp + Ls)), 7, dtype=torch.uint8, device=DEV)
+    cm = torch.full((batch, Ls, ld(Lp)), 7, dtype=torch.uint8, device=DEV)
+    pp = torch.empty(batch, Lp, dtype=torch.int32, device=DEV)
+    sp = torch.empty(batch, Ls, dtype=torch.int32, device=DEV)
+    cp = torch.empty(batch, Ls, dtype=torch.int32, device=DEV)
+    d = [t.to(DEV) for t in (m0, m1, lang)]
+    rc = L.lib().svla_build_masks(d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(), batch, n_img, n_lang, chunk,
+                                  pm.data_ptr(), pp.data_ptr(), sm.data_ptr(), cm.data_ptr(), sp.data_ptr(),
+                                  cp.data_ptr(), ops._stream())
+    assert rc == 0, L.lib().svla_last_error()
+    pad = torch.cat([m0[:, None].expand(batch, n_img), m1[:, None].expand(batch, n_img), lang,
+                     torch.ones(batch, 1, dtype=torch.uint8)], dim=1).bool()
+    att = torch.zeros(batch, Lp, dtype=torch.bool)
+    att[:, -1] = True
+    pm, sm, cm = pm.cpu(), sm.cpu(), cm.cpu()
+    assert torch.equal(pm[:, :, :Lp].bool(), make_att_2d_masks(pad, att))
+    assert torch.equal(pp.cpu().long(), torch.cumsum(pad.long(), dim=1) - 1)
+    causal = torch.arange(Ls)[None, :] <= torch.arange(Ls)[:, None]
+    want_self = torch.cat([pad[:, None, :].expand(batch, Ls, Lp), causal[None].expand(batch, Ls, Ls)], dim=2)
+    assert torch.equal(sm[:, :, :Lp + Ls].bool(), want_self)
+    assert torch.equal(cm[:, :, :Lp].bool(), pad[:, None, :].expand(batch, Ls, Lp))
+    assert torch.equal(sp.cpu().long(), pad.long().sum(1, keepdim=True) + torch.arange(Ls)[None])
+    assert torch.equal(cp.cpu().long(), torch.arange(Ls)[None].expand(batch, Ls))
+    for t, n in ((pm, Lp), (sm, Lp + Ls), (cm, Lp)):
+        assert int(t[:, :, n:].sum()) == 0 and int(t.max()) <= 1
