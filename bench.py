@@ -365,7 +365,9 @@ def main():
         "roofline_batch1": roof_b1,
         "clocks": clk,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    # the CPU baseline runs on rank 0 at N = 1 only: under torchrun the other ranks would wait for it at the
+    # closing barrier for longer than the process-group timeout
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, state, js, args.cpu_iters, args.cpu_warmup)
     if rank == 0:
         print(json.dumps(line), flush=True)
