@@ -232,8 +232,9 @@ typedef struct svla_attn_desc {
   const float* qo_smooth; const float* qo_rsmooth; float qo_act; /* qo_rsmooth optional, as in svla_norm_desc */
   int32_t batch, lq, hq, hkv;
   float scale;                                           /* 0 = head_dim^-1/2 */
-  int32_t impl; /* SVLA_ATTN_AUTO, or force SVLA_ATTN_MMA_SYNC / SVLA_ATTN_TCGEN05 (the latter only for
-                   unmasked single-source calls with lq >= 128, aligned strides) */
+  int32_t impl; /* SVLA_ATTN_AUTO (tcgen05 for unmasked calls, mma.sync for masked ones), or force
+                   SVLA_ATTN_MMA_SYNC / SVLA_ATTN_TCGEN05 (the latter needs 16-byte aligned operands and strides;
+                   byte masks only on a single key source with rows padded to a multiple of 16 keys) */
   void* debug_clock; /* profiling: uint64 [96] phase clock stamps of one CTA of the tcgen05 kernel, or NULL */
   /* Structured mask, instead of `mask` (same result as the equivalent byte mask, far less mask traffic):
    * query i may see key k iff k < mask_keys ? key_mask[b*key_mask_bs + k] != 0 : k - mask_keys <= i

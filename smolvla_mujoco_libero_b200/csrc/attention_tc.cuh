@@ -1,8 +1,14 @@
-// Unmasked attention on the 5th-generation tensor cores (tcgen05), head_dim 64, bf16 in / bf16 out:
-// the SigLIP encoder's self-attention (deploy/export_6f_layer0_attention_tensors.py:100-119 semantics,
-// without a mask):  o = bf16(softmax((q . k) * scale) @ v), fp32 scores, softmax and accumulation.
+// Attention on the 5th-generation tensor cores (tcgen05), head_dim 64, bf16 in / bf16 (or int8) out, with the
+// semantics of the reference's eager attention (deploy/export_6f_layer0_attention_tensors.py:100-119):
+//   s = (q . k) * scale (fp32);  s = mask ? s : finfo(f32).min;  o = bf16(softmax(s) @ v)
+// (a fully masked row becomes uniform over all keys).  MASK: none (the SigLIP encoder), a byte mask
+// [B, Lq, Lk] (the VLM prefix), or the structured mask of the action expert (key padding flags over the first
+// mask_keys keys, causal order over the rest).
 //
-// CTA: one 128-query tile of one (batch, head); 192 threads; two CTAs per SM.
+// CTA: 128 packed rows of one (batch, kv head): its G = Hq / Hkv query heads x QT = 128 / G consecutive
+// queries, row r = (query q0 + r / G, head kh * G + r % G) -- one 4-D TMA box (dim, head, query, batch) of Q,
+// so every key / value tile is loaded once for the whole GQA group.  Keys come from up to two sources (the
+// cached prefix, then the current suffix), each a sequence of 64-key tiles.  192 threads; two CTAs per SM.
 //   warp 0       TMA: the Q tile once, then K and V tiles of 64 keys through a 3-stage ring
 //   warp 1       TMEM owner (256 columns) and MMA issuer (one lane):
 //                  S_j = Q K_j^T   (M 128, N 64, K 64; both operands from shared memory, K-major)
@@ -39,12 +45,15 @@
 namespace svla {
 
 struct AttnTcArgs {
-  CUtensorMap tq;          // 3-D map (column, row, batch), box 64 x 128 x 1, 128-byte swizzle
-  CUtensorMap tk, tv;      // 3-D maps, box 64 x 64 x 1, 128-byte swizzle
+  CUtensorMap tq;          // 4-D map (dim, head, query, batch), box 64 x G x QT x 1, 128-byte swizzle
+  CUtensorMap tk, tv;      // source 1: 3-D maps (column, key, batch), box 64 x 64 x 1, 128-byte swizzle
+  CUtensorMap tk2, tv2;    // source 2 (L2 > 0)
+  const uint8_t* mask;     long long mask_bs; int mask_rs;   // byte mask (single source), rows 16-byte padded
+  const uint8_t* key_mask; long long key_mask_bs; int mask_keys;  // structured mask
   __nv_bfloat16* o;        long long o_bs; int o_rs;
   int8_t* qo;              long long qo_bs; int qo_rs;
   const float* qo_smooth;  const float* qo_rsmooth;  float qo_act;
-  int Lq, Lk, Hq, Hkv;
+  int Lq, L1, L2, Hq, Hkv, G, QT;
   float scale_log2;  // scale * log2(e)
   unsigned long long* dbg;  // optional phase clock stamps of the CTA (0, 0, batch / 2) (profiling)
   int* err;
@@ -63,8 +72,13 @@ constexpr int kQBytes = 128 * 128;          // 128 query rows x 64 bf16
 constexpr int kKVBytes = kKeys * 128;       // 64 key rows x 64 bf16
 constexpr int kStages = 3;
 constexpr int kVStage = 2 * kKVBytes;  // V tile, then a tile of bf16 ones (the row-sum columns of the P.V MMA)
-constexpr int kQ = 0, kK = kQBytes, kV = kK + kStages * kKVBytes, kBar = kV + kStages * kVStage;
+constexpr int kKeepBytes = 128 * 8;  // byte mask: one 64-bit keep mask per packed row of a key tile
+constexpr int kQ = 0, kK = kQBytes, kV = kK + kStages * kKVBytes, kKeep = kV + kStages * kVStage;
+constexpr int kBar = kKeep + kStages * kKeepBytes;
 constexpr int kSmemBytes = kBar + 256 + 1024;  // + barriers + alignment slack
+// the scaled (log2-domain) score of a masked key: below any real score by far, exactly representable, and
+// exp2(kMaskedLog2 - m) is 0 for any real running max m and 1 for m == kMaskedLog2
+constexpr float kMaskedLog2 = -1.0e30f;
 constexpr int kThreads = 192;
 constexpr int kSBufs = 2;
 constexpr uint32_t kS = 0, kO = kSBufs * kKeys, kTmemCols = 256;  // O: 64 columns + 16 row-sum columns
@@ -77,6 +91,9 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, i
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+enum TcMask : int { kTcMaskNone = 0, kTcMaskBytes = 1, kTcMaskStructured = 2 };
+
+template <int MASK>
 __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __grid_constant__ AttnTcArgs a) {
   using namespace atc;
   extern __shared__ uint8_t smem_raw[];
@@ -90,13 +107,13 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
   uint64_t* o_done = p_full + kSBufs;     // [2] P.V of key tile j (and all before it) done: o_done[j % 2]
   uint64_t* o_full = o_done + 2;          // the last P.V has completed
   uint64_t* mma_done = o_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* m_full = mma_done + 1;        // [kStages] byte mask: the keep masks of key tile j are in the ring
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m_full + kStages);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int kh = h / (a.Hq / a.Hkv);
-  const int q0 = blockIdx.x * 128;
-  const int n_kv = (a.Lk + kKeys - 1) / kKeys;
+  const int kh = blockIdx.y, b = blockIdx.z;
+  const int q0 = blockIdx.x * a.QT;
+  const int n1 = (a.L1 + kKeys - 1) / kKeys, n_kv = n1 + (a.L2 + kKeys - 1) / kKeys;
   unsigned long long* dbg = (a.dbg && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == gridDim.z / 2) ? a.dbg : nullptr;
   auto stamp = [&](int slot) {
     if (dbg) dbg[slot] = clock64();
@@ -118,6 +135,7 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
     mbar_init(&o_done[1], 1);
     mbar_init(o_full, 1);
     mbar_init(mma_done, 1);
+    for (int s = 0; s < kStages; ++s) mbar_init(&m_full[s], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -141,20 +159,57 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
   if (threadIdx.x == 0) stamp(1);
 
   if (warp == 0) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer (lane 0); with a byte mask the whole warp also turns each key tile's mask
+    // bytes into one 64-bit keep mask per packed row (lane l: rows 4l .. 4l + 3)
     if (lane == 0) {
       prefetch_tmap(&a.tq);
       prefetch_tmap(&a.tk);
       prefetch_tmap(&a.tv);
-      mbar_arrive_expect_tx(q_full, kQBytes);
-      tma_load_3d(smem + kQ, &a.tq, q_full, h * 64, q0, b);
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, a.err)) break;
+      // rows G * QT.. of the Q tile are not loaded: they feed only rows that are never stored
+      mbar_arrive_expect_tx(q_full, static_cast<uint32_t>(a.G * a.QT * 128));
+      tma_load_4d(smem + kQ, &a.tq, q_full, 0, kh * a.G, q0, b);
+    }
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j % kStages;
+      bool ok = true;
+      if (lane == 0 && j >= kStages) ok = mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, a.err);
+      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+      const bool src1 = j < n1;
+      const int key = (src1 ? j : j - n1) * kKeys;
+      if constexpr (MASK == kTcMaskBytes) {
+        // single key source: key j * 64 + e of row (query q0 + r / G); the host checked 16-byte aligned rows
+        // padded to a multiple of 16 keys, so every 16-key run below L1 is one aligned load
+        uint64_t* keep = reinterpret_cast<uint64_t*>(smem + kKeep + s * kKeepBytes);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rr = lane * 4 + i, qi = q0 + rr / a.G;
+          uint64_t kb = ~0ull;
+          if (rr < a.G * a.QT && qi < a.Lq) {
+            const uint8_t* mrow = a.mask + static_cast<size_t>(b) * a.mask_bs + static_cast<size_t>(qi) * a.mask_rs;
+            kb = 0ull;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              if (key + c * 16 >= a.L1) continue;
+              const uint4 w = __ldg(reinterpret_cast<const uint4*>(mrow + key + c * 16));
+              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const uint32_t nz = __vcmpne4(ww[u], 0u) & 0x08040201u;  // bit b of byte b: key nonzero
+                const uint32_t b4 = (nz | (nz >> 8) | (nz >> 16) | (nz >> 24)) & 0xFu;
+                kb |= static_cast<uint64_t>(b4) << (c * 16 + u * 4);
+              }
+            }
+          }
+          keep[rr] = kb;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&m_full[s]);
+      }
+      if (lane == 0) {
         mbar_arrive_expect_tx(&k_full[s], kKVBytes);
-        tma_load_3d(smem + kK + s * kKVBytes, &a.tk, &k_full[s], kh * 64, j * kKeys, b);
+        tma_load_3d(smem + kK + s * kKVBytes, src1 ? &a.tk : &a.tk2, &k_full[s], kh * 64, key, b);
         mbar_arrive_expect_tx(&v_full[s], kKVBytes);
-        tma_load_3d(smem + kV + s * kVStage, &a.tv, &v_full[s], kh * 64, j * kKeys, b);
+        tma_load_3d(smem + kV + s * kVStage, src1 ? &a.tv : &a.tv2, &v_full[s], kh * 64, key, b);
       }
     }
   } else if (warp == 1) {
@@ -211,7 +266,9 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
   } else {
     // ---------------- softmax warpgroup
     const int wq = warp & 3;  // TMEM lane quarter
-    const int row = q0 + wq * 32 + lane;
+    const int rr = wq * 32 + lane;  // packed row: query q0 + rr / G of head kh * G + rr % G
+    const int qi = q0 + rr / a.G, hq = kh * a.G + rr % a.G;
+    const bool row_in = rr < a.G * a.QT && qi < a.Lq;
     const uint32_t lanes = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tO = tmem + lanes + kO;
     const float c = a.scale_log2;
@@ -224,11 +281,73 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
       const bool st0 = (wq == 0 && lane == 0 && j < 8);
       if (st0) stamp(32 + j);
       tc_fence_after();
-      const int kvalid = a.Lk - j * kKeys;  // keys of this tile inside Lk
+      const bool src1 = j < n1;
+      const int kvalid = src1 ? a.L1 - j * kKeys : a.L2 - (j - n1) * kKeys;  // keys of this tile in its source
+      uint64_t keep = ~0ull;  // keys of the tile this row may see (bits past kvalid: don't care, set)
+      if constexpr (MASK == kTcMaskStructured) {
+        // global key index kg0 + e: flags below kend, causal order (kg - mask_keys <= query) from mask_keys on
+        const int kg0 = src1 ? j * kKeys : a.L1 + (j - n1) * kKeys;
+        const int kend = a.mask_keys < a.L1 + a.L2 ? a.mask_keys : a.L1 + a.L2;
+        const uint8_t* fl = a.key_mask + static_cast<size_t>(b) * a.key_mask_bs;
+        keep = 0ull;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int k16 = kg0 + c * 16;
+          uint32_t bits = 0u;
+          if (k16 < kend) {
+            if (((k16 & 15) == 0) && (k16 + 16 <= kend || a.key_mask_bs >= ((kend + 15) & ~15))) {
+              const uint4 w = __ldg(reinterpret_cast<const uint4*>(fl + k16));
+              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const uint32_t nz = __vcmpne4(ww[u], 0u) & 0x08040201u;
+                bits |= ((nz | (nz >> 8) | (nz >> 16) | (nz >> 24)) & 0xFu) << (u * 4);
+              }
+            } else {
+              for (int e = 0; e < 16 && k16 + e < kend; ++e) bits |= (fl[k16 + e] != 0 ? 1u : 0u) << e;
+            }
+            if (k16 + 16 > kend) bits &= (1u << (kend - k16)) - 1u;  // keys from kend on: causal rule below
+          }
+          keep |= static_cast<uint64_t>(bits) << (c * 16);
+        }
+        // causal part: keys kg >= kend with kg - mask_keys <= qi, i.e. e <= qi + mask_keys - kg0
+        const int lo = kend - kg0, hi = qi + a.mask_keys - kg0;  // e in [max(lo, 0), hi]
+        const int e0 = lo > 0 ? lo : 0;
+        if (hi >= e0 && e0 < kKeys) {
+          const int e1 = hi < kKeys - 1 ? hi : kKeys - 1;
+          const uint64_t upto = e1 >= 63 ? ~0ull : ((2ull << e1) - 1ull);
+          const uint64_t from = (e0 >= 64) ? 0ull : ~((1ull << e0) - 1ull);
+          keep |= upto & from;
+        }
+      } else if constexpr (MASK == kTcMaskBytes) {
+        if (!mbar_wait_warp(&m_full[j % kStages], (j / kStages) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        keep = reinterpret_cast<const uint64_t*>(smem + kKeep + (j % kStages) * kKeepBytes)[rr];
+      }
+      // valid: the tile's keys inside its source; keep: the valid keys this row may see.  A masked key has the
+      // score finfo.min in the reference, i.e. probability exp(min - max) = 0 unless every key so far is
+      // masked, where all scores tie and the weights are uniform: masked keys take the scaled score
+      // kMaskedLog2 below (far under any real score) through the running max, probability
+      // exp2(kMaskedLog2 - m) -- 0 against a real maximum, 1 while the row has seen only masked keys.
+      const uint64_t valid = kvalid >= kKeys ? ~0ull : ((1ull << kvalid) - 1ull);
+      keep &= valid;
+      const bool any_masked = keep != valid;
       uint32_t r[kKeys];
 #pragma unroll
       for (int ch = 0; ch < kKeys / 32; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[ch * 32]));
       tmem_ld_wait();
+      if constexpr (MASK != kTcMaskNone) {
+        if (any_masked) {  // masked keys leave the max and the exponentials (their weight is set below)
+          const uint32_t klo = static_cast<uint32_t>(keep), khi = static_cast<uint32_t>(keep >> 32);
+#pragma unroll
+          for (int e = 0; e < kKeys; ++e) {
+            const uint32_t kw = e < 32 ? klo : khi;
+            if (((kw >> (e & 31)) & 1u) == 0u) r[e] = __float_as_uint(-INFINITY);
+          }
+        }
+      }
       if (st0) stamp(56 + j);
       // row max with 8 independent partial maxima (short dependency chains); the three-input max does two
       // comparisons per instruction at the two-input rate
@@ -243,7 +362,8 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
         for (int e = 0; e < kKeys; ++e) mp[e & 7] = (e < kvalid) ? fmaxf(mp[e & 7], __uint_as_float(r[e])) : mp[e & 7];
       }
       const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-      const float m_new = fmaxf(m, __fmul_rn(mx, c));  // max of s * c (rounding is monotonic)
+      float m_new = fmaxf(m, __fmul_rn(mx, c));  // max of s * c (rounding is monotonic)
+      if (MASK != kTcMaskNone && any_masked) m_new = fmaxf(m_new, kMaskedLog2);
       float alpha = 1.0f;
       bool grow = false;
       if (st0) stamp(64 + j);
@@ -287,6 +407,9 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
       // packed fp32 pipe (FFMA2).  Keys past Lk (last tile only) get probability 0; full tiles take a loop
       // without those selects.
       const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
+      const float pm = (MASK != kTcMaskNone && any_masked) ? ex2_approx(kMaskedLog2 - m) : 0.f;
+      const uint32_t klo = static_cast<uint32_t>(keep), khi = static_cast<uint32_t>(keep >> 32);
+      const uint32_t vlo = static_cast<uint32_t>(valid), vhi = static_cast<uint32_t>(valid >> 32);
       auto exps = [&](auto masked) {
 #pragma unroll
         for (int ch = 0; ch < kKeys / 32; ++ch) {
@@ -298,15 +421,20 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
             float p0 = ex2_approx(z.x);
             float p1 = ex2_approx(z.y);
             if constexpr (decltype(masked)::value) {
-              p0 = (k0 < kvalid) ? p0 : 0.f;
-              p1 = (k0 + 1 < kvalid) ? p1 : 0.f;
+              // kept: its own weight; masked but valid: pm; past the source's keys: 0
+              const uint32_t kw = k0 < 32 ? klo : khi, vw = k0 < 32 ? vlo : vhi;
+              const int b0 = k0 & 31;
+              p0 = ((kw >> b0) & 1u) ? p0 : (((vw >> b0) & 1u) ? pm : 0.f);
+              p1 = ((kw >> (b0 + 1)) & 1u) ? p1 : (((vw >> (b0 + 1)) & 1u) ? pm : 0.f);
             }
             pk[e / 2] = pack_bf16_rn(p0, p1);
           }
           tmem_st16(tS + ch * 16, pk);
         }
       };
-      if (kvalid >= kKeys)
+      // the choice is warp-uniform: each variant's tcgen05.st is a warp-collective instruction, and the rows of
+      // a warp may differ in whether they see a masked key
+      if (__all_sync(0xffffffffu, kvalid >= kKeys && !any_masked))
         exps(std::false_type{});
       else
         exps(std::true_type{});
@@ -328,7 +456,7 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
         tmem_ld_wait();
         const float inv = __frcp_rn(__uint_as_float(l16[0]));
         const float ra = (a.qo && a.qo_rsmooth) ? __frcp_rn(a.qo_act) : 0.f;
-        const bool in = row < a.Lq;
+        const bool in = row_in;
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch) {
           uint32_t r[32];
@@ -342,9 +470,9 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
             v[e + 1] = __fmul_rn(__uint_as_float(r[e + 1]), inv);
             bf16_round2(v[e], v[e + 1]);
           }
-          const int col = h * 64 + ch * 32;
+          const int col = hq * 64 + ch * 32;
           if (a.o) {
-            __nv_bfloat16* op = a.o + static_cast<size_t>(b) * a.o_bs + static_cast<size_t>(row) * a.o_rs + col;
+            __nv_bfloat16* op = a.o + static_cast<size_t>(b) * a.o_bs + static_cast<size_t>(qi) * a.o_rs + col;
 #pragma unroll
             for (int u = 0; u < 4; ++u)
               *reinterpret_cast<int4*>(op + u * 8) =
@@ -372,7 +500,7 @@ __global__ void __launch_bounds__(atc::kThreads, 2) attention_tc_kernel(const __
                 }
               }
             }
-            int8_t* qp = a.qo + static_cast<size_t>(b) * a.qo_bs + static_cast<size_t>(row) * a.qo_rs + col;
+            int8_t* qp = a.qo + static_cast<size_t>(b) * a.qo_bs + static_cast<size_t>(qi) * a.qo_rs + col;
             *reinterpret_cast<int4*>(qp) = make_int4(w[0], w[1], w[2], w[3]);
             *reinterpret_cast<int4*>(qp + 16) = make_int4(w[4], w[5], w[6], w[7]);
           }

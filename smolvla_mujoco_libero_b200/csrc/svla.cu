@@ -678,10 +678,47 @@ static int32_t make_tmap_bhd(CUtensorMap* map, const void* base, uint64_t cols, 
   return SVLA_OK;
 }
 
+// 4-D bf16 tensor map of Q [batch][query][head][64] (dim, head, query, batch) with a 64 x G x QT x 1 box and the
+// 128-byte swizzle: one box is the packed rows (query-major, then head) of a kv head's G query heads
+static int32_t make_tmap_q4(CUtensorMap* map, const void* base, uint64_t heads, uint64_t lq, uint64_t batch,
+                            uint64_t rs, uint64_t bs, uint32_t g, uint32_t qt) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SVLA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[4] = {64, heads, lq, batch};
+  cuuint64_t strides[3] = {128, rs * 2, bs * 2};
+  cuuint32_t box[4] = {64, g, qt, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SVLA_ERR_ARG, "cuTensorMapEncodeTiled (4-D) failed (%d)", static_cast<int>(r));
+  return SVLA_OK;
+}
+
+}  // extern "C"
+
+template <int MASK>
+static int32_t launch_attention_tc(const AttnTcArgs& a, dim3 grid, cudaStream_t stream) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
+  auto kern = attention_tc_kernel<MASK>;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, atc::kSmemBytes);
+    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  return launch(kern, grid, dim3(atc::kThreads), atc::kSmemBytes, stream, "attention_tc_kernel", a);
+}
+
+extern "C" {
+
 static int32_t run_attention_tc(const svla_attn_desc* d, float scale, cudaStream_t stream) {
   AttnTcArgs a;
   std::memset(&a, 0, sizeof(a));
-  int32_t rc = make_tmap_bhd(&a.tq, d->q, static_cast<uint64_t>(d->hq) * 64, d->lq, d->batch, d->q_rs, d->q_bs, 128);
+  const int g = d->hq / d->hkv, qt = 128 / g;
+  int32_t rc = make_tmap_q4(&a.tq, d->q, d->hq, d->lq, d->batch, d->q_rs, d->q_bs, g, qt);
   if (rc) return rc;
   rc = make_tmap_bhd(&a.tk, d->k1, static_cast<uint64_t>(d->hkv) * 64, d->l1, d->batch, d->kv1_rs, d->kv1_bs,
                      atc::kKeys);
@@ -689,6 +726,20 @@ static int32_t run_attention_tc(const svla_attn_desc* d, float scale, cudaStream
   rc = make_tmap_bhd(&a.tv, d->v1, static_cast<uint64_t>(d->hkv) * 64, d->l1, d->batch, d->kv1_rs, d->kv1_bs,
                      atc::kKeys);
   if (rc) return rc;
+  if (d->l2 > 0) {
+    rc = make_tmap_bhd(&a.tk2, d->k2, static_cast<uint64_t>(d->hkv) * 64, d->l2, d->batch, d->kv2_rs, d->kv2_bs,
+                       atc::kKeys);
+    if (rc) return rc;
+    rc = make_tmap_bhd(&a.tv2, d->v2, static_cast<uint64_t>(d->hkv) * 64, d->l2, d->batch, d->kv2_rs, d->kv2_bs,
+                       atc::kKeys);
+    if (rc) return rc;
+  }
+  a.mask = d->mask;
+  a.mask_bs = d->mask_bs;
+  a.mask_rs = d->mask_rs;
+  a.key_mask = d->key_mask;
+  a.key_mask_bs = d->key_mask_bs;
+  a.mask_keys = d->mask_keys;
   a.o = static_cast<__nv_bfloat16*>(d->o);
   a.o_bs = d->o_bs;
   a.o_rs = d->o_rs;
@@ -699,26 +750,21 @@ static int32_t run_attention_tc(const svla_attn_desc* d, float scale, cudaStream
   a.qo_rsmooth = d->qo_rsmooth;
   a.qo_act = d->qo_act;
   a.Lq = d->lq;
-  a.Lk = d->l1;
+  a.L1 = d->l1;
+  a.L2 = d->l2 > 0 ? d->l2 : 0;
   a.Hq = d->hq;
   a.Hkv = d->hkv;
+  a.G = g;
+  a.QT = qt;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.dbg = static_cast<unsigned long long*>(d->debug_clock);
   a.err = device_error_ptr();
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return fail(SVLA_ERR_ARG, "device index %d out of range", dev);
-  // one 128-query tile per CTA, two CTAs per SM: one CTA's exponentials fill the other's gaps, and one CTA's
+  // one 128-row tile per CTA, two CTAs per SM: one CTA's exponentials fill the other's gaps, and one CTA's
   // set-up and epilogue overlap the other's key loop
-  auto kern = attention_tc_kernel;
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, atc::kSmemBytes);
-    if (e != cudaSuccess) return fail(SVLA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured[dev] = true;
-  }
-  dim3 grid(static_cast<unsigned>((d->lq + 127) / 128), d->hq, d->batch);
-  return launch(kern, grid, dim3(atc::kThreads), atc::kSmemBytes, stream, "attention_tc_kernel", a);
+  dim3 grid(static_cast<unsigned>((d->lq + qt - 1) / qt), d->hkv, d->batch);
+  if (d->key_mask) return launch_attention_tc<kTcMaskStructured>(a, grid, stream);
+  if (d->mask) return launch_attention_tc<kTcMaskBytes>(a, grid, stream);
+  return launch_attention_tc<kTcMaskNone>(a, grid, stream);
 }
 
 int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
@@ -773,11 +819,28 @@ int32_t svla_attention(const svla_attn_desc* d, svla_stream_t stream) {
            (!d->qo || (al(d->qo) && d->qo_rs % 16 == 0 && d->qo_bs % 16 == 0)) && d->q_bs % 8 == 0 &&
            d->kv1_bs % 8 == 0 && (!d->qo_rsmooth || al(d->qo_rsmooth));
   }();
-  const bool tc_ok = !d->mask && !d->key_mask && d->l2 <= 0 && d->lq >= 128 && a16;
+  // the tcgen05 kernel reads Q / K / V through tensor maps (16-byte aligned bases and strides), a byte mask as
+  // aligned 16-key runs of rows padded to a multiple of 16 keys (single key source), key flags as aligned runs
+  const bool tc_ok = [&] {
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!a16 || d->hq / d->hkv > 128) return false;
+    if (d->l2 > 0 && (!al(d->k2) || !al(d->v2) || d->kv2_rs % 8 || d->kv2_bs % 8)) return false;
+    if (d->mask && (d->l2 > 0 || !al(d->mask) || d->mask_rs % 16 || d->mask_bs % 16 ||
+                    d->mask_rs < ((d->l1 + 15) & ~15)))
+      return false;
+    if (d->key_mask && (!al(d->key_mask) || d->key_mask_bs % 16)) return false;
+    return true;
+  }();
   if (d->impl == SVLA_ATTN_TCGEN05 && !tc_ok)
-    return fail(SVLA_ERR_ARG, "svla_attention: the tcgen05 kernel needs an unmasked single-source call, lq >= 128 "
-                              "and 16-byte aligned operands");
-  if (tc_ok && d->impl != SVLA_ATTN_MMA_SYNC) return run_attention_tc(d, a.scale, cs(stream));
+    return fail(SVLA_ERR_ARG, "svla_attention: the tcgen05 kernel needs 16-byte aligned operands and strides, "
+                              "byte masks on a single key source with rows padded to 16 keys");
+  // automatic choice: the tcgen05 kernel for unmasked calls (the SigLIP encoder: 809 vs 1668 us at 128 images);
+  // masked calls stay on the mma.sync kernel, which measured as fast or faster at the path's masked shapes
+  // (expert self 35.3 vs 33.8 us, cross 28.8 vs 29.5 us, text prefix 76.4 vs 92.5 us at batch 64): a CTA there
+  // holds 3-4 key tiles, too few to amortise the tensor-memory setup, and GQA rows fill 128-row tiles unevenly
+  const bool masked = d->mask || d->key_mask;
+  if (tc_ok && (d->impl == SVLA_ATTN_TCGEN05 || (d->impl == SVLA_ATTN_AUTO && !masked)))
+    return run_attention_tc(d, a.scale, cs(stream));
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);

@@ -131,6 +131,7 @@ def op_norm(a) -> dict:
 
 
 def op_attn(a) -> dict:
+    from . import _lib as L
     from . import ops
     dev = torch.device("cuda", 0)
     g = torch.Generator(device="cpu").manual_seed(0)
@@ -151,8 +152,9 @@ def op_attn(a) -> dict:
         kf = torch.zeros(a.batch, (a.prefix + 15) // 16 * 16, dtype=torch.uint8)
         kf[:, : a.prefix - a.prefix // 10] = 1
         key_mask = kf.to(dev)
+    impl = {"auto": L.ATTN_AUTO, "mma": L.ATTN_MMA_SYNC, "tc": L.ATTN_TCGEN05}[a.impl]
     ms = time_op(lambda: ops.attention(q, k, v, a.heads, a.kv_heads, mask=mask, key_mask=key_mask,
-                                       mask_keys=a.prefix), a.iters)
+                                       mask_keys=a.prefix, impl=impl), a.iters)
     flops = 4.0 * a.batch * a.heads * a.lq * a.lk * 64
     # phase clock stamps of one CTA of the tcgen05 kernel (when that kernel runs)
     from . import _lib as L
@@ -305,6 +307,7 @@ def main() -> None:
     ap.add_argument("--kv-heads", type=int, default=12)
     ap.add_argument("--mask", action="store_true")
     ap.add_argument("--mask-ld", type=int, default=0)
+    ap.add_argument("--impl", default="auto", choices=["auto", "mma", "tc"], help="--op attn: kernel choice")
     ap.add_argument("--prefix", type=int, default=0, help="--op attn: structured mask, key padding over this many "
                     "prefix keys and causal order over the rest")
     ap.add_argument("--summarize", default=None, help="print the per-kernel summary of an ncu launch-list CSV")

@@ -510,11 +510,103 @@ def test_attention_tcgen05_kernel(b, lq, lk, hq, hkv):
     assert torch.equal(qo.cpu(), qo_ref)
 
 
-def test_attention_tcgen05_rejects_masked_calls():
+def test_attention_tcgen05_rejects_what_it_cannot_take():
+    """The tcgen05 kernel reads byte masks as aligned 16-key runs of rows padded to 16 keys, from one key source:
+    an unpadded mask row or a byte mask over two sources is refused (the automatic choice then takes the
+    mma.sync kernel)."""
     q = torch.zeros(1, 128, 64, dtype=torch.bfloat16, device=DEV)
-    mask = torch.ones(1, 128, 128, dtype=torch.bool, device=DEV)
+    k = torch.zeros(1, 100, 64, dtype=torch.bfloat16, device=DEV)
+    mask = torch.ones(1, 128, 100, dtype=torch.bool, device=DEV)  # row stride 100: not padded
     with pytest.raises(L.SvlaError):
-        ops.attention(q, q, q, 1, 1, mask=mask, impl=L.ATTN_TCGEN05)
+        ops.attention(q, k, k, 1, 1, mask=mask, impl=L.ATTN_TCGEN05)
+    padded = torch.ones(1, 128, 256, dtype=torch.bool, device=DEV)[:, :, :228]
+    with pytest.raises(L.SvlaError):
+        ops.attention(q, k, k, 1, 1, mask=padded, k2=k[:, :, :], v2=k[:, :, :], impl=L.ATTN_TCGEN05)
+    o = ops.attention(q, k, k, 1, 1, mask=mask)  # automatic: the mma.sync kernel takes it
+    assert torch.isfinite(o.float()).all()
+
+
+def _masked_case(seed, b, lq, l1, l2, hq, hkv):
+    g = synthetic.generator(seed)
+    q = torch.randn(b, lq, hq * 64, generator=g).to(torch.bfloat16)
+    k1 = torch.randn(b, l1, hkv * 64, generator=g).to(torch.bfloat16)
+    v1 = torch.randn(b, l1, hkv * 64, generator=g).to(torch.bfloat16)
+    k2 = torch.randn(b, max(l2, 1), hkv * 64, generator=g).to(torch.bfloat16)[:, :l2]
+    v2 = torch.randn(b, max(l2, 1), hkv * 64, generator=g).to(torch.bfloat16)[:, :l2]
+    pad = torch.rand(b, l1, generator=g) > 0.25
+    pad[:, -1] = True
+    return g, q, k1, v1, k2, v2, pad
+
+
+@pytest.mark.parametrize("b,lq,l1,l2,hq,hkv", [(3, 50, 177, 50, 15, 5), (2, 50, 177, 0, 15, 5),
+                                               (2, 7, 70, 9, 4, 2), (1, 130, 200, 30, 6, 6)])
+def test_attention_tcgen05_structured_mask(b, lq, l1, l2, hq, hkv):
+    """The action expert's structured mask on tcgen05 (GQA rows packed query-major, the prefix keys and the
+    chunk's own keys as two sources): against the reference attention on the equivalent byte mask and against
+    the mma.sync kernel; a sample whose prefix keys are all padding gives its queries only the causal keys."""
+    g, q, k1, v1, k2, v2, pad = _masked_case(b * 31 + lq + l1 + l2, b, lq, l1, l2, hq, hkv)
+    # sample 0's prefix keys are all padding: with one key source every key is masked (uniform weights over
+    # all keys, as the reference), with two its queries see only the causal chunk keys
+    pad[0, :] = False
+    full = torch.zeros(b, lq, l1 + l2, dtype=torch.bool)
+    full[:, :, :l1] = pad[:, None, :]
+    if l2:
+        full[:, :, l1:] = torch.tril(torch.ones(lq, l2, dtype=torch.bool))
+    key_rows = torch.zeros(b, (l1 + 15) // 16 * 16 + 16, dtype=torch.uint8)
+    key_rows[:, :l1] = pad.to(torch.uint8)
+    dev = lambda t: t.to(DEV)  # noqa: E731
+    srcs = dict(k2=dev(k2), v2=dev(v2)) if l2 else {}
+    kw = dict(key_mask=dev(key_rows)[:, :l1], mask_keys=l1, **srcs)
+    o_tc = ops.attention(dev(q), dev(k1), dev(v1), hq, hkv, impl=L.ATTN_TCGEN05, **kw)
+    o_ms = ops.attention(dev(q), dev(k1), dev(v1), hq, hkv, impl=L.ATTN_MMA_SYNC, **kw)
+    kk, vv = (torch.cat([k1, k2], 1), torch.cat([v1, v2], 1)) if l2 else (k1, v1)
+    ref = _attn_ref(q, kk, vv, full, hq, hkv)
+    assert cosine(o_tc, ref) >= 0.9999
+    assert float((o_tc.cpu().float() - ref.float()).abs().max()) <= 2e-2
+    assert float((o_tc.cpu().float() - o_ms.cpu().float()).abs().max()) <= 2e-2
+    assert _lib_device_error() == 0
+
+
+def _lib_device_error():
+    return L.device_error()
+
+
+@pytest.mark.parametrize("b,lq,lk,hq,hkv", [(2, 177, 177, 15, 5), (1, 40, 100, 3, 1), (2, 129, 64, 2, 2)])
+def test_attention_tcgen05_byte_mask(b, lq, lk, hq, hkv):
+    """The VLM prefix's byte mask on tcgen05 (rows padded to 16 keys), with a fully masked query row and the
+    fused int8 output: against the reference, the mma.sync kernel, and the same keys given as key flags."""
+    g = synthetic.generator(b * 17 + lq + lk)
+    q = torch.randn(b, lq, hq * 64, generator=g).to(torch.bfloat16)
+    k = torch.randn(b, lk, hkv * 64, generator=g).to(torch.bfloat16)
+    v = torch.randn(b, lk, hkv * 64, generator=g).to(torch.bfloat16)
+    mask = torch.rand(b, lq, lk, generator=g) > 0.3
+    mask[:, 0, :] = False
+    ld = (lk + 15) // 16 * 16
+    store = torch.zeros(b, lq, ld, dtype=torch.bool)
+    store[:, :, :lk] = mask
+    md = store.to(DEV)[:, :, :lk]
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    o_tc = ops.attention(qd, kd, vd, hq, hkv, mask=md, impl=L.ATTN_TCGEN05)
+    o_ms = ops.attention(qd, kd, vd, hq, hkv, mask=md, impl=L.ATTN_MMA_SYNC)
+    ref = _attn_ref(q, k, v, mask, hq, hkv)
+    assert cosine(o_tc, ref) >= 0.9999
+    assert float((o_tc.cpu().float() - ref.float()).abs().max()) <= 2e-2
+    assert float((o_tc.cpu().float() - o_ms.cpu().float()).abs().max()) <= 2e-2
+    smooth = torch.rand(hq * 64, generator=g) + 0.5
+    o2, qo = ops.attention(qd, kd, vd, hq, hkv, mask=md, qo_smooth=smooth.to(DEV), qo_act=0.01,
+                           qo_rsmooth=ops.reciprocal(smooth.to(DEV)), impl=L.ATTN_TCGEN05)
+    assert torch.equal(o2.cpu(), o_tc.cpu())
+    qo_ref = Q.smooth_quantize_activation(o2.cpu().reshape(-1, hq * 64), smooth, 0.01).reshape(b, lq, -1)
+    assert torch.equal(qo.cpu(), qo_ref)
+    # the same visibility as key flags for a mask that has the key-padding form
+    pad = torch.rand(b, lk, generator=g) > 0.25
+    fm = torch.zeros(b, lq, ld, dtype=torch.bool)
+    fm[:, :, :lk] = pad[:, None, :]
+    kr = torch.zeros(b, ld, dtype=torch.uint8)
+    kr[:, :lk] = pad.to(torch.uint8)
+    o_b = ops.attention(qd, kd, vd, hq, hkv, mask=fm.to(DEV)[:, :, :lk], impl=L.ATTN_TCGEN05)
+    o_k = ops.attention(qd, kd, vd, hq, hkv, key_mask=kr.to(DEV)[:, :lk], mask_keys=lk, impl=L.ATTN_TCGEN05)
+    assert torch.equal(o_b.cpu(), o_k.cpu())
 
 
 def test_attention_two_sources_and_quant_out():
@@ -857,10 +949,11 @@ def test_structured_mask_equals_byte_mask(two_sources):
     if two_sources:
         full[:, :, l1:] = torch.tril(torch.ones(lq, l2, dtype=torch.bool))
     srcs = dict(k2=k2, v2=v2) if two_sources else {}
-    o_byte = ops.attention(q, k1, v1, hq, hkv, mask=full.to(DEV), **srcs)
+    mma = L.ATTN_MMA_SYNC  # the same kernel on both forms (the byte mask here has unpadded rows)
+    o_byte = ops.attention(q, k1, v1, hq, hkv, mask=full.to(DEV), impl=mma, **srcs)
     key_rows = torch.zeros(b, 192, dtype=torch.uint8)
     key_rows[:, :l1] = pad.to(torch.uint8)
-    o_key = ops.attention(q, k1, v1, hq, hkv, key_mask=key_rows.to(DEV)[:, :l1], mask_keys=l1, **srcs)
+    o_key = ops.attention(q, k1, v1, hq, hkv, key_mask=key_rows.to(DEV)[:, :l1], mask_keys=l1, impl=mma, **srcs)
     assert torch.equal(o_byte.cpu(), o_key.cpu())
 
 
