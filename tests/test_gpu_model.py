@@ -104,6 +104,37 @@ def test_gpu_calibration_tracks_oracle_calibration(tiny):
         assert float(((s - rs).abs() / rs).max()) < 0.05, e["module"]
 
 
+def test_gpu_calibration_equals_the_oracle_collector_on_the_same_activations(tiny, monkeypatch):
+    """Given the same activations, the GPU calibration equals the reference's collector and SmoothQuant builder
+    exactly (deploy/calibrate_smolvla_activation_channel_scales.py:68-134, deploy/build_smoothquant_scales.py:
+    64-106 as restated in the oracle): every W8A8 input the GPU collector sees is also fed, one call at a time,
+    to the oracle collector, and each module's scale and smooth vector must match bit for bit."""
+    from oracle import quant as Q
+    from smolvla_mujoco_libero_b200 import calibrate as C
+    w, _js = tiny
+    seen = []
+    observe = C.ChannelStats.observe
+
+    def spy(self, modules, x, rows_per_call):
+        seen.append((list(modules), x.detach().reshape(-1, x.shape[-1]).cpu().clone(), rows_per_call))
+        return observe(self, modules, x, rows_per_call)
+
+    monkeypatch.setattr(C.ChannelStats, "observe", spy)
+    gj = C.calibrate(TINY, w, [_obs(TINY, 1, 100 + i) for i in range(2)])
+    col = Q.PerChannelCollector(TINY.percentile)
+    for mods, x, per in seen:
+        for r0 in range(0, x.shape[0], per):
+            for m in mods:
+                col.observe(m, x[r0:r0 + per])
+    rows = {r["module"]: r for r in col.rows()}
+    assert gj["linear_call_scales"]
+    for e in gj["linear_call_scales"]:
+        ref = Q.build_smoothquant_entry(rows[e["module"]], w[f"{e['module']}.weight"], gj["smoothquant_alpha"])
+        assert e["scale"] == ref["scale"], e["module"]
+        assert e["smooth_scale"] == ref["smooth_scale"], e["module"]
+        assert e["num_samples"] == ref["num_samples"], e["module"]
+
+
 def test_bench_architecture_batch1_matches_oracle():
     """The full benchmark architecture (SigLIP 12x768, text 16x960, expert 16x720, 10 steps) at batch 1."""
     torch.set_num_threads(8)
