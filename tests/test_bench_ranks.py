@@ -43,7 +43,7 @@ def test_two_gloo_ranks_agree_on_slowest_time_and_rate():
     procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = sorted(q.get(timeout=120) for _ in range(world))
+    out = sorted(q.get(timeout=600) for _ in range(world))  # a cold first torch import can take a minute
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -58,13 +58,16 @@ def test_reference_arm_runs_on_rank_zero_only(capsys):
     assert capsys.readouterr().out == ""
 
 
-def _failing_rank(rank: int, world: int, port: int, mode: str, q) -> None:
-    """Step 1 together; then rank 1 exits ("exit") or stops answering ("hang"), and rank 0 takes step 2."""
+def _failing_rank(rank: int, world: int, port: int, mode: str, q, start) -> None:
+    """Step 1 together; then rank 1 exits ("exit") or stops answering ("hang"), and rank 0 takes step 2.  The
+    ranks meet at `start` after their imports (a cold first torch import can take a minute) so that the 5 s
+    process-group timeout is not spent on one rank's start-up."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     sys.path.insert(0, str(REPO))
     import bench
     r, w, _ = bench.dist_env()
+    start.wait(timeout=600)
     bench.init_ranks(w, "gloo", timeout_s=5)
     bench.max_over_ranks(1.0, w)                 # step 1: both ranks
     if r == 1:
@@ -86,10 +89,11 @@ def test_survivor_errors_within_the_timeout_when_a_rank_dies_or_hangs(mode):
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_failing_rank, args=(r, world, port, mode, q)) for r in range(world)]
+    start = ctx.Barrier(world)
+    procs = [ctx.Process(target=_failing_rank, args=(r, world, port, mode, q, start)) for r in range(world)]
     for p in procs:
         p.start()
-    kind, elapsed = q.get(timeout=120)
+    kind, elapsed = q.get(timeout=660)
     for p in procs:
         p.join(timeout=90)
         if p.is_alive():
