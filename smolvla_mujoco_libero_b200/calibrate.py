@@ -100,7 +100,9 @@ def calibrate(cfg: SmolVLAConfig, state: dict[str, torch.Tensor], observations: 
     for module, c in stats.calls.items():
         if module not in specs:
             continue
-        scale_list = (c["pamax"] / 127.0).clamp_min(1e-8)
+        # on the CPU: a CUDA tensor divided by a Python scalar is multiplied by the scalar's reciprocal, which
+        # can differ by one ulp from the division the collector's arithmetic (and the golden fixtures) use
+        scale_list = (c["pamax"].cpu() / 127.0).clamp_min(1e-8)
         entries.append(smoothquant_entry(module, scale_list, state[f"{module}.weight"], alpha, num_samples=c["n"]))
     missing = set(specs) - {e["module"] for e in entries}
     if missing:
