@@ -80,6 +80,8 @@ struct GemmArgs {
   __nv_bfloat16* xt_bf16;           // Euler: bf16 copy
   unsigned long long* dbg;          // optional phase clock stamps of CTA 0 (profiling)
   int weights_resident;             // B operands were written before the previous kernel started
+  int shared_a;                     // pair over one A operand (P = 2, single CTAs): A is loaded once per
+                                    // stage and each k-step is ONE MMA of N = 2 * BN over the adjacent B tiles
   int out_v8;                       // every bf16 output row start is 32-byte aligned: 256-bit stores
   int resid_v8;                     // every residual row start is 32-byte aligned: 256-bit loads
   // split-K: work item t is split t % splits (k-tiles [split * kt_per_split, +kt_per_split)) of output
@@ -672,6 +674,8 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
       }
       constexpr uint32_t kBBytes = T::kConvert ? S::kRawTile : S::kBTile;
       constexpr uint32_t kStageTx = CG * P * (S::kATile + kBBytes);  // bytes both CTAs of the unit bring in
+      const bool one_a = P == 2 && args.shared_a;                        // the pair's A tile is loaded once
+      const uint32_t stage_tx = kStageTx - (one_a ? static_cast<uint32_t>(CG * S::kATile) : 0u);
       auto b_dst = [&](uint8_t* st, int p) {
         return T::kConvert ? st + P * (S::kATile + S::kBTile) + p * S::kRawTile : st + P * S::kATile + p * S::kBTile;
       };
@@ -693,7 +697,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
         pre = ke - kb < STAGES ? ke - kb : STAGES;
         for (int i = 0; i < pre; ++i) {
           uint8_t* st = smem + i * S::kStage;
-          if (leader) mbar_arrive_expect_tx(&full[i], kStageTx);
+          if (leader) mbar_arrive_expect_tx(&full[i], stage_tx);
 #pragma unroll
           for (int p = 0; p < P; ++p)
             load(b_dst(st, p), &args.tb[(P == 1) ? si : p], i, (kb + i) * T::kBK, n0 + b_row0);
@@ -713,16 +717,16 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
           uint8_t* st = smem + s * S::kStage;
           if (static_cast<int>(g) < pre) {  // weights already requested: only the activations remain
 #pragma unroll
-            for (int p = 0; p < P; ++p) load(st + p * S::kATile, &args.ta[(P == 1) ? si : p], s, kt * T::kBK, m0);
+            for (int p = 0; p < (one_a ? 1 : P); ++p) load(st + p * S::kATile, &args.ta[(P == 1) ? si : p], s, kt * T::kBK, m0);
             if (g == 0) stamp(args.dbg, 2);
             continue;
           }
           if (!(ok = bounded_wait(&empty[s], ph ^ 1))) break;
-          if (leader) mbar_arrive_expect_tx(&full[s], kStageTx);
+          if (leader) mbar_arrive_expect_tx(&full[s], stage_tx);
 #pragma unroll
           for (int p = 0; p < P; ++p) {
             const int mi = (P == 1) ? si : p;
-            load(st + p * S::kATile, &args.ta[mi], s, kt * T::kBK, m0);
+            if (p == 0 || !one_a) load(st + p * S::kATile, &args.ta[mi], s, kt * T::kBK, m0);
             load(b_dst(st, p), &args.tb[mi], s, kt * T::kBK, n0 + b_row0);
           }
         }
@@ -763,6 +767,28 @@ __global__ void __launch_bounds__(gemm_threads<KIND, P, EPI>(), 1) gemm_sm100_ke
           if (!ok) break;
           tc_fence_after();
           uint8_t* st = smem + s * S::kStage;
+          if constexpr (P == 2 && CG == 1 && 2 * BN <= 256) {
+            if (args.shared_a) {
+              // gate and up over the same A: their B tiles are adjacent in the stage (BN rows each), so one
+              // MMA of N = 2 * BN writes both accumulators (columns [0, BN) and [BN, 2 * BN) of the buffer)
+              // with half the MMA instructions
+              const uint32_t a_addr = smem_u32(st);
+              const uint32_t b_addr = smem_u32(st + P * S::kATile);
+              const uint32_t idesc2 = T::idesc(2 * BN);
+#pragma unroll
+              for (int kk = 0; kk < 128 / 32; ++kk) {
+                const uint64_t ad = smem_desc_sw128(a_addr + kk * 32);
+                const uint64_t bd = smem_desc_sw128(b_addr + kk * 32);
+                const uint32_t acc = (kt > kb || kk > 0) ? 1u : 0u;
+                if constexpr (KIND == Kind::I8)
+                  mma_i8(d_base, ad, bd, idesc2, acc);
+                else
+                  mma_bf16(d_base, ad, bd, idesc2, acc);
+              }
+              commit(&empty[s]);
+              continue;
+            }
+          }
 #pragma unroll
           for (int p = 0; p < P; ++p) {
             const uint32_t a_addr = smem_u32(st + p * S::kATile);

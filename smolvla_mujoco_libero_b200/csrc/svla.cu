@@ -396,6 +396,10 @@ int32_t run_gemm(const svla_gemm_desc* d, cudaStream_t stream) {
   for (int s = 0; s < d->nseg; ++s)
     if (d->seg[s].out && (reinterpret_cast<uintptr_t>(d->seg[s].out) % 32 != 0 || d->seg[s].ldo % 16 != 0)) args.out_v8 = 0;
   args.resid_v8 = (d->resid && reinterpret_cast<uintptr_t>(d->resid) % 32 == 0 && d->ldr % 16 == 0) ? 1 : 0;
+  // a pair over one A operand (the expert's gate / up on the same normalised rows): one MMA of N = 2 * BN
+  // per k-step instead of two of N = BN -- the tensor core takes about as long to issue either
+  args.shared_a = (d->pair && cg == 1 && kind != Kind::W8A16 && 2 * bn <= 256 && d->seg[0].a == d->seg[1].a &&
+                   d->seg[0].lda == d->seg[1].lda) ? 1 : 0;
   if (epi == Epi::Resid && !d->resid) return fail(SVLA_ERR_ARG, "RESID needs a residual");
   if (epi == Epi::Rope && (!d->rope_cs || !d->pos || d->max_pos <= 0)) return fail(SVLA_ERR_ARG, "ROPE needs rope_cs/pos");
   if (epi == Epi::GeluQuant && d->qout && (!d->q_smooth || d->q_act <= 0.f))

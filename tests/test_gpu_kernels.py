@@ -387,6 +387,35 @@ def _pair_case(kind, epi, m, n, k, g, nseg=1, pair=False):
     return build
 
 
+@pytest.mark.parametrize("kind,m,n,k,block_n", [
+    (L.KIND_BF16, 3200, 2048, 720, 128),   # expert gate / up at batch 64
+    (L.KIND_BF16, 50, 2048, 720, 64),      # batch 1, 64-column tiles
+    (L.KIND_I8, 300, 1024, 960, 128),      # W8A8 pair over one activation tensor
+])
+def test_pair_over_one_a_operand_equals_two_mmas(kind, m, n, k, block_n):
+    """A gate / up pair whose two linears read the same A tensor runs one MMA of N = 2 * block_n per k-step;
+    the same pair with A passed as two copies runs two MMAs of N = block_n.  Outputs must match bit for bit
+    (each output element sees the same products in the same K order)."""
+    g = synthetic.generator(m + n + k + block_n)
+    if kind == L.KIND_I8:
+        x = _rand_i8((m, k), g).to(DEV)
+        ws = [(_rand_i8((n, k), g).to(DEV), (torch.rand(n, generator=g) * 1e-3).to(DEV)) for _ in range(2)]
+        segs = lambda a0, a1, out: [ops.Seg(a=a, b=w, out=out, n=n, wscale=s, act_scale=0.02)
+                                    for a, (w, s) in zip((a0, a1), ws)]
+    else:
+        x = (torch.randn(m, k, generator=g) * 0.5).to(DEV, torch.bfloat16)
+        ws = [((torch.randn(n, k, generator=g) * 0.02).to(DEV, torch.bfloat16), None) for _ in range(2)]
+        segs = lambda a0, a1, out: [ops.Seg(a=a, b=w, out=out, n=n) for a, (w, _) in zip((a0, a1), ws)]
+    outs = []
+    for a1 in (x, x.clone()):
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+        ops.gemm(ops.gemm_desc(kind, L.EPI_SILU_MUL, m, k, segs(x, a1, out), pair=True, block_n=block_n))
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    assert bool(torch.isfinite(outs[0].float()).all())
+
+
 @pytest.mark.parametrize("kind,epi,m,n,k,nseg,pair", [
     (L.KIND_I8, L.EPI_I32, 1000, 512, 768, 1, False),        # 8 row tiles: 4 pairs, the last partly past M
     (L.KIND_I8, L.EPI_BF16, 2048, 768, 768, 3, False),       # SigLIP q/k/v segments
