@@ -1,6 +1,6 @@
 """End-to-end parity of the sm_100a sample_actions path with the CPU oracle.
 
-Bar (the north star's): on the same seeded inputs, weights and scale JSON, the final chunk matches the
+Bar: on the same seeded inputs, weights and scale JSON, the final chunk matches the
 oracle's SmoothQuant fake-dequant restatement with cosine >= 0.999 and max-abs <= 2e-2.  Batch rows are
 independent: a row's result is bit-identical whether it runs alone or in a batch.
 """

@@ -1,4 +1,4 @@
-"""Parity of the configurations the benchmark and the north star name, at their own shapes, with the oracle.
+"""Parity of the benchmarked workloads (single text layer, prefix encode, batch-64 call), at their own shapes, with the oracle.
 
 * one SmolVLM2 text decoder layer at prefix length 177 (hidden N(0,1) with 8 outlier channels x30, random
   N(0, 0.02) weights, SmoothQuant scales calibrated on that distribution), through the runner's own launch
