@@ -8,9 +8,9 @@
 //
 // CTA pairs (CG = 2): a cluster of two CTAs computes 256-row tiles with tcgen05.mma.cta_group::2 (M = 256);
 // each CTA loads its own 128 A rows and half of the tile's B rows, so a k-stage brings 32 KB into each SM
-// instead of 48 KB for the same MMA work.  The main loop is bound by that per-SM operand ingest (measured
-// about 70 bytes per clock), so the pair form runs it faster.  The even CTA issues the MMAs and commits to
-// both CTAs' barriers; every load is a plain TMA load of the CTA's own tile.
+// instead of 48 KB for the same MMA work.  The even CTA issues the MMAs and commits to both CTAs' barriers;
+// every load is a plain TMA load of the CTA's own tile.  Opt-in: the main loop is set by the issue rate of
+// the MMA thread (about one tcgen05.mma per 170-210 cycles at any N), which the pair form does not change.
 //
 // Persistent: one CTA (pair) per SM (pair) walks output tiles t = cluster, cluster + clusters, ... in N-fastest
 // order (the CTAs running at one time share A row-blocks; the weights stay L2-resident).  Accumulators
